@@ -1,0 +1,309 @@
+// Host side of the tcgen05 GEMM: TMA tensor-map construction, kernel instantiations,
+// launch helpers and the device-side builder of grouped (MoE) problem tables.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <vector>
+
+#include "gemm.cuh"
+
+namespace sv4 {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+// 3-D tiled map: dims/strides given inner-first; strides in bytes for dims 1 and 2.
+CUtensorMap make_map_3d(const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0, uint64_t d1,
+                        uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1,
+                        CUtensorMapSwizzle swz) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK(s1_bytes % 16 == 0 && s2_bytes % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  TORCH_CHECK((b0 * elem_bytes) % 16 == 0, "TMA inner box must span a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  return m;
+}
+
+// An operand view as (batch, outer, inner) with unit inner stride.
+struct OperandView {
+  const void* ptr;
+  int64_t inner, outer, batch;
+  int64_t outer_stride, batch_stride;  // elements
+};
+
+static OperandView view_of(const torch::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2 || t.dim() == 3, "operand must be 2-D or 3-D");
+  TORCH_CHECK(t.stride(-1) == 1, "operand needs a unit-stride innermost dimension");
+  OperandView v;
+  v.ptr = t.data_ptr();
+  v.inner = t.size(-1);
+  v.outer = t.size(-2);
+  v.outer_stride = t.stride(-2);
+  // A single row's stride is never used to step; give TMA a legal (16-byte multiple) value.
+  if (v.outer == 1) v.outer_stride = v.inner + (8 - v.inner % 8) % 8;
+  if (t.dim() == 3 && t.size(0) > 1) {
+    v.batch = t.size(0);
+    v.batch_stride = t.stride(0);
+  } else {
+    v.batch = 1;
+    v.batch_stride = v.outer * v.outer_stride;
+  }
+  return v;
+}
+
+// Box for an operand: K-major rows -> (64 x rows); MN-major -> (64 x 64).
+static CUtensorMap map_for(const OperandView& v, uint32_t box_outer) {
+  return make_map_3d(v.ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, v.inner, v.outer, v.batch, v.outer_stride * 2,
+                     v.batch_stride * 2, 64, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+static int num_sms(int dev) {
+  static int cached[64] = {0};
+  if (cached[dev] == 0) {
+    cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
+  }
+  return cached[dev];
+}
+
+template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
+static void launch(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1, const GemmParams& p,
+                   int grid, cudaStream_t stream) {
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, BMODE, EPI>;
+  constexpr int smem = GemmSmem<BN>::kTotal;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  kern<<<grid, 192, smem, stream>>>(ma, mb0, mb1, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+#define SV4_DISPATCH(A_MN, B_MN, BMODE, EPI)                                            \
+  if (a_mn == A_MN && b_mn == B_MN && bmode == BMODE && epi == EPI) {                   \
+    launch<256, A_MN, B_MN, BMODE, EPI>(ma, mb0, mb1, p, grid, stream);                 \
+    return;                                                                              \
+  }
+
+static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap& ma, const CUtensorMap& mb0,
+                     const CUtensorMap& mb1, const GemmParams& p, int grid, cudaStream_t stream) {
+  SV4_DISPATCH(false, false, kBSingle, kEpiBF16)
+  SV4_DISPATCH(false, false, kBSingle, kEpiF32)
+  SV4_DISPATCH(false, false, kBSingle, kEpiF32Acc)
+  SV4_DISPATCH(false, true, kBSingle, kEpiBF16)
+  SV4_DISPATCH(false, true, kBSingle, kEpiF32)
+  SV4_DISPATCH(true, true, kBSingle, kEpiF32Acc)
+  SV4_DISPATCH(true, true, kBSingle, kEpiF32)
+  SV4_DISPATCH(true, true, kBSingle, kEpiBF16)
+  SV4_DISPATCH(false, false, kBSplitN, kEpiSwiGLU)
+  SV4_DISPATCH(false, false, kBSingle, kEpiRowScaleBF16)
+  SV4_DISPATCH(false, true, kBSplitK, kEpiBF16)
+  TORCH_CHECK(false, "unsupported GEMM variant a_mn=", a_mn, " b_mn=", b_mn, " bmode=", bmode, " epi=", epi);
+}
+
+// ------------------------------------------------------------------ entry points
+// Dense / batched:  out[b, m, n] (+)= alpha * sum_k A[b, m, k] B[b, n, k]
+//   a: (.., M, K) if !a_mn  else (.., K, M)      (unit inner stride, bf16)
+//   b: (.., N, K) if !b_mn  else (.., K, N)
+//   out: (.., M, N) bf16 or fp32 with unit inner stride.
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate,
+          double alpha, torch::Tensor err) {
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "bf16 operands required");
+  TORCH_CHECK(out.stride(-1) == 1, "output needs unit inner stride");
+  c10::cuda::CUDAGuard guard(a.device());
+  OperandView va = view_of(a), vb = view_of(b);
+  const int64_t M = a_mn ? va.inner : va.outer;
+  const int64_t K = a_mn ? va.outer : va.inner;
+  const int64_t N = b_mn ? vb.inner : vb.outer;
+  TORCH_CHECK((b_mn ? vb.outer : vb.inner) == K, "K mismatch");
+  TORCH_CHECK(K % 64 == 0, "K must be a multiple of 64");
+  const int64_t batch = std::max(va.batch, vb.batch);
+  TORCH_CHECK(va.batch == vb.batch, "batch mismatch");
+  TORCH_CHECK(out.size(-1) == N && out.size(-2) == M, "output shape mismatch");
+  CUtensorMap ma = map_for(va, a_mn ? 64 : 128);
+  CUtensorMap mb = map_for(vb, b_mn ? 64 : 256);
+  GemmParams p{};
+  p.probs = nullptr;
+  p.total_tiles = nullptr;
+  p.n_probs = 1;
+  GemmProblem& s = p.single;
+  s.m = M; s.n = N; s.k = K;
+  s.a_m = 0; s.a_k = 0; s.a_b = 0;
+  s.b_n = 0; s.b_k = 0; s.b_b = 0;
+  s.tile_begin = 0;
+  s.batch = batch;
+  s.d_off = 0;
+  s.d_ld = out.stride(-2);
+  s.d_bstride = out.dim() == 3 ? out.stride(0) : 0;
+  s.aux_off = 0; s.aux_ld = 0;
+  p.d = out.data_ptr();
+  p.aux = nullptr;
+  p.rowscale = nullptr;
+  p.alpha = static_cast<float>(alpha);
+  p.err = err.data_ptr<int>();
+  int epi;
+  if (out.scalar_type() == at::kBFloat16) {
+    TORCH_CHECK(!accumulate, "accumulate needs an fp32 output");
+    epi = kEpiBF16;
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "output must be bf16 or fp32");
+    epi = accumulate ? kEpiF32Acc : kEpiF32;
+  }
+  const int tiles = batch * ((M + 127) / 128) * ((N + 255) / 256);
+  if (tiles == 0) return;
+  const int grid = std::min<int>(tiles, num_sms(a.get_device()));
+  dispatch(a_mn, b_mn, kBSingle, epi, ma, mb, mb, p, grid, at::cuda::getCurrentCUDAStream());
+}
+
+// Grouped GEMM driven by a device-side problem table (MoE).
+//   mode 0: SwiGLU fprop    A = x_perm (M_pad, D),    B0/B1 = W_gate/W_up (E, I, D)   -> out act (M_pad, I),
+//                                                                                       aux pre (M_pad, 2I)
+//   mode 1: down fprop      A = act (M_pad, I),       B = W_down (E, D, I)            -> out (M_pad, D) * rowscale
+//   mode 2: down dgrad      A = d_out (M_pad, D),     B = W_down (E, D, I) MN-major   -> out d_act (M_pad, I) bf16
+//   mode 3: gate/up dgrad   A = d_pre (M_pad, 2I),    B = [W_gate; W_up] split-K      -> out d_x (M_pad, D) bf16
+//   mode 4: wgrad           A = g (M_pad, *) MN-major, B = x (M_pad, *) MN-major      -> out fp32 (+=)
+void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor b1, torch::Tensor out,
+                  torch::Tensor aux, torch::Tensor rowscale, torch::Tensor probs, torch::Tensor total_tiles,
+                  int64_t n_probs, double gate_max, double lin_lo, double lin_hi, int64_t ksplit,
+                  bool accumulate, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(a.device());
+  OperandView va = view_of(a), vb0 = view_of(b0), vb1 = view_of(b1);
+  GemmParams p{};
+  p.probs = reinterpret_cast<const GemmProblem*>(probs.data_ptr());
+  p.total_tiles = total_tiles.data_ptr<int>();
+  p.n_probs = static_cast<int>(n_probs);
+  p.single = GemmProblem{};
+  p.d = out.data_ptr();
+  p.aux = aux.numel() ? aux.data_ptr() : nullptr;
+  p.rowscale = rowscale.numel() ? rowscale.data_ptr<float>() : nullptr;
+  p.alpha = 1.0f;
+  p.gate_max = static_cast<float>(gate_max);
+  p.lin_lo = static_cast<float>(lin_lo);
+  p.lin_hi = static_cast<float>(lin_hi);
+  p.ksplit = static_cast<int>(ksplit);
+  p.err = err.data_ptr<int>();
+  const int grid = num_sms(a.get_device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  switch (mode) {
+    case 0: {
+      CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 128), m1 = map_for(vb1, 128);
+      dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, p, grid, stream);
+      break;
+    }
+    case 1: {
+      CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 256);
+      dispatch(false, false, kBSingle, kEpiRowScaleBF16, ma, m0, m0, p, grid, stream);
+      break;
+    }
+    case 2: {
+      CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 64);
+      dispatch(false, true, kBSingle, kEpiBF16, ma, m0, m0, p, grid, stream);
+      break;
+    }
+    case 3: {
+      CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 64), m1 = map_for(vb1, 64);
+      dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, p, grid, stream);
+      break;
+    }
+    case 4: {
+      CUtensorMap ma = map_for(va, 64), m0 = map_for(vb0, 64);
+      dispatch(true, true, kBSingle, accumulate ? kEpiF32Acc : kEpiF32, ma, m0, m0, p, grid, stream);
+      break;
+    }
+    default:
+      TORCH_CHECK(false, "unknown grouped GEMM mode");
+  }
+}
+
+// ------------------------------------------------------------------------------
+// Device-side problem-table builders for the MoE grouped GEMMs.  `seg_start`/`seg_rows`
+// (int32, E) describe each expert's row segment in the padded permuted buffer.
+__global__ void build_moe_problems_kernel(const int* seg_start, const int* seg_rows, int n_experts, int mode,
+                                          int D, int I, int bn_out, GemmProblem* probs, int* total) {
+  // one thread: n_experts is small (<= a few hundred)
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int tiles = 0;
+  int np = 0;
+  for (int e = 0; e < n_experts; ++e) {
+    const int rows = seg_rows[e];
+    const int start = seg_start[e];
+    const int reps = (mode == 4) ? 2 : 1;  // wgrad of gate/up: two problems per expert
+    for (int r = 0; r < reps; ++r) {
+      GemmProblem pr{};
+      pr.batch = 1;
+      if (mode == 0) {         // SwiGLU fprop: m = rows, n = I, k = D
+        pr.m = rows; pr.n = I; pr.k = D;
+        pr.a_m = start; pr.a_k = 0; pr.a_b = 0;
+        pr.b_n = 0; pr.b_k = 0; pr.b_b = e;
+        pr.d_off = static_cast<long long>(start) * I; pr.d_ld = I;
+        pr.aux_off = static_cast<long long>(start) * 2 * I; pr.aux_ld = 2 * I;
+      } else if (mode == 1) {  // down fprop: m = rows, n = D, k = I
+        pr.m = rows; pr.n = D; pr.k = I;
+        pr.a_m = start; pr.b_b = e;
+        pr.d_off = static_cast<long long>(start) * D; pr.d_ld = D;
+        pr.aux_off = start;
+      } else if (mode == 2) {  // down dgrad: m = rows, n = I, k = D
+        pr.m = rows; pr.n = I; pr.k = D;
+        pr.a_m = start; pr.b_b = e;
+        pr.d_off = static_cast<long long>(start) * I; pr.d_ld = I;
+      } else if (mode == 3) {  // gate/up dgrad: m = rows, n = D, k = 2I
+        pr.m = rows; pr.n = D; pr.k = 2 * I;
+        pr.a_m = start; pr.b_b = e;
+        pr.d_off = static_cast<long long>(start) * D; pr.d_ld = D;
+      } else if (mode == 4) {  // gate/up wgrad: dW_{g|u}[e] (I x D) = dpre[:, r*I:(r+1)*I]^T x
+        pr.m = I; pr.n = D; pr.k = rows;
+        pr.a_m = r * I; pr.a_k = start; pr.b_n = 0; pr.b_k = start;
+        pr.d_off = (static_cast<long long>(r) * n_experts + e) * static_cast<long long>(I) * D; pr.d_ld = D;
+      } else {                 // mode 5: down wgrad: dWd[e] (D x I) = d_out^T act
+        pr.m = D; pr.n = I; pr.k = rows;
+        pr.a_m = 0; pr.a_k = start; pr.b_n = 0; pr.b_k = start;
+        pr.d_off = static_cast<long long>(e) * D * I; pr.d_ld = I;
+      }
+      pr.tile_begin = tiles;
+      const int tn = (pr.n + bn_out - 1) / bn_out;
+      const int tm = (pr.m + 127) / 128;
+      tiles += (pr.k == 0 && mode < 4) ? 0 : tm * tn;
+      probs[np++] = pr;
+    }
+  }
+  *total = tiles;
+}
+
+void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t mode, int64_t D, int64_t I,
+                        torch::Tensor probs, torch::Tensor total) {
+  c10::cuda::CUDAGuard guard(seg_start.device());
+  const int E = seg_start.numel();
+  const int bn_out = (mode == 0) ? 128 : 256;
+  build_moe_problems_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      seg_start.data_ptr<int>(), seg_rows.data_ptr<int>(), E, static_cast<int>(mode), static_cast<int>(D),
+      static_cast<int>(I), bn_out, reinterpret_cast<GemmProblem*>(probs.data_ptr()), total.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t problem_bytes() { return sizeof(GemmProblem); }
+
+}  // namespace sv4

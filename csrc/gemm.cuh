@@ -1,0 +1,359 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[m, n] = sum_k A[m, k] * B[n, k]        (fp32 accumulation in TMEM)
+//
+// One CTA per SM loops over output tiles of 128 x BN.  Roles (6 warps):
+//   warp 0      : TMA producer -- one elected lane streams A/B k-blocks into a
+//                 kStages-deep shared-memory ring (128B swizzle).
+//   warp 1      : MMA issuer   -- one elected lane issues tcgen05.mma (M=128, N=BN,
+//                 K=16 per instruction) into one of two TMEM accumulators, then
+//                 tcgen05.commit releases the smem stage / publishes the accumulator.
+//   warps 2..5  : epilogue     -- tcgen05.ld the accumulator (each warp owns its
+//                 32-lane TMEM quarter), apply the fused epilogue, store to global.
+// Two TMEM accumulators (2 x BN columns) let the epilogue of tile i overlap the
+// MMAs of tile i+1.
+//
+// Work is described by GemmProblem records: a single problem (optionally repeated
+// over a batch dimension, used by the batched Newton-Schulz GEMMs) or a device-side
+// table (MoE grouped GEMMs, filled on the GPU from the routing counts, so no host
+// sync).  A and B are read through 3-D TMA tensor maps (dims: inner, outer, batch)
+// that may be K-major or MN-major; the B operand can be split across two tensor
+// maps along N (fused SwiGLU gate|up) or along K (dgrad through [W_gate; W_up]).
+#pragma once
+#include "common.cuh"
+
+namespace sv4 {
+
+struct GemmProblem {
+  int m, n, k;            // logical problem size (k % 64 == 0)
+  int a_m, a_k, a_b;      // A tensor-map coordinates of element (0, 0) and batch index
+  int b_n, b_k, b_b;      // B tensor-map coordinates of element (0, 0) and batch index
+  int tile_begin;         // first global tile id of this problem (table mode)
+  int batch;              // single mode: number of repeats along the batch dims
+  long long d_off;        // element offset of D(0, 0)
+  long long d_ld;         // row stride of D in elements
+  long long d_bstride;    // single mode: D offset between batch repeats
+  long long aux_off;      // SwiGLU: element offset of the pre-activation rows; rowscale: row index base
+  long long aux_ld;       // SwiGLU: row stride of the pre-activation buffer
+};
+
+enum BMode : int { kBSingle = 0, kBSplitN = 1, kBSplitK = 2 };
+enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiSwiGLU = 3, kEpiRowScaleBF16 = 4 };
+
+struct GemmParams {
+  const GemmProblem* probs;   // device table or nullptr (single mode)
+  const int* total_tiles;     // device scalar (table mode)
+  int n_probs;
+  GemmProblem single;
+  void* d;
+  void* aux;                  // SwiGLU pre-activations (bf16)
+  const float* rowscale;      // kEpiRowScaleBF16
+  float alpha;
+  float gate_max, lin_lo, lin_hi;
+  int ksplit;                 // kBSplitK: K index where B switches from map 0 to map 1
+  int* err;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // bf16: 64 elements = 128 bytes = one swizzle row
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kTotal = kBarOffset + 256 + 1024;  // + barriers + alignment slack
+};
+
+__device__ __forceinline__ int tiles_m(const GemmProblem& p) { return (p.m + kBM - 1) / kBM; }
+
+template <int BN, int BMODE>
+__device__ __forceinline__ int tiles_n(const GemmProblem& p) {
+  constexpr int kOutN = BMODE == kBSplitN ? BN / 2 : BN;
+  return (p.n + kOutN - 1) / kOutN;
+}
+
+// Map a global tile id to (problem, m-tile, n-tile, batch).  `hint` carries the last
+// problem index (tile ids only increase per CTA, so the scan is amortised O(1)).
+template <int BN, int BMODE>
+__device__ __forceinline__ bool locate_tile(const GemmParams& P, int t, int& hint, GemmProblem& pr, int& mt,
+                                            int& nt, int& bt) {
+  if (P.probs == nullptr) {
+    pr = P.single;
+    const int per = tiles_m(pr) * tiles_n<BN, BMODE>(pr);
+    if (per == 0) return false;
+    bt = t / per;
+    if (bt >= pr.batch) return false;
+    const int local = t - bt * per;
+    mt = local / tiles_n<BN, BMODE>(pr);
+    nt = local % tiles_n<BN, BMODE>(pr);
+    return true;
+  }
+  while (hint + 1 < P.n_probs && P.probs[hint + 1].tile_begin <= t) ++hint;
+  pr = P.probs[hint];
+  const int tn = tiles_n<BN, BMODE>(pr);
+  const int local = t - pr.tile_begin;
+  if (local < 0 || tn == 0 || local >= tiles_m(pr) * tn) return false;
+  mt = local / tn;
+  nt = local % tn;
+  bt = 0;
+  return true;
+}
+
+template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
+__global__ void __launch_bounds__(192, 1)
+gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
+                 const __grid_constant__ CUtensorMap map_b1, const GemmParams P) {
+  using S = GemmSmem<BN>;
+  constexpr int kStages = S::kStages;
+  constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, 1, 1, A_MN, B_MN);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b0);
+    if (BMODE != kBSingle) tma_prefetch_desc(&map_b1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = P.probs == nullptr
+                        ? P.single.batch * tiles_m(P.single) * tiles_n<BN, BMODE>(P.single)
+                        : *P.total_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int hint = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        GemmProblem pr;
+        int mt, nt, bt;
+        if (!locate_tile<BN, BMODE>(P, t, hint, pr, mt, nt, bt)) continue;
+        const int nk = pr.k / kBK;
+        const int ab = pr.a_b + bt, bb = pr.b_b + bt;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, P.err, kErrTimeoutEmpty)) { ok = false; break; }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          const int ka = pr.a_k + kb * kBK;
+          const int m0 = pr.a_m + mt * kBM;
+          if (!A_MN) {
+            tma_load_3d(sa, &map_a, &full[stage], ka, m0, ab);
+          } else {
+            tma_load_3d(sa, &map_a, &full[stage], m0, ka, ab);
+            tma_load_3d(sa + kBM / 2 * kBK * 2, &map_a, &full[stage], m0 + 64, ka, ab);
+          }
+          int kbk = pr.b_k + kb * kBK;
+          const CUtensorMap* mb = &map_b0;
+          if (BMODE == kBSplitK && kbk >= P.ksplit) { mb = &map_b1; kbk -= P.ksplit; }
+          if (BMODE == kBSplitN) {
+            const int n0 = pr.b_n + nt * (BN / 2);
+            if (!B_MN) {
+              tma_load_3d(sb, &map_b0, &full[stage], kbk, n0, bb);
+              tma_load_3d(sb + (BN / 2) * kBK * 2, &map_b1, &full[stage], kbk, n0, bb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) {
+                tma_load_3d(sb + j * 64 * kBK * 2, &map_b0, &full[stage], n0 + j * 64, kbk, bb);
+                tma_load_3d(sb + (BN / 128 + j) * 64 * kBK * 2, &map_b1, &full[stage], n0 + j * 64, kbk, bb);
+              }
+            }
+          } else {
+            const int n0 = pr.b_n + nt * BN;
+            if (!B_MN) {
+              tma_load_3d(sb, mb, &full[stage], kbk, n0, bb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(sb + j * 64 * kBK * 2, mb, &full[stage], n0 + j * 64, kbk, bb);
+            }
+          }
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int hint = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        GemmProblem pr;
+        int mt, nt, bt;
+        if (!locate_tile<BN, BMODE>(P, t, hint, pr, mt, nt, bt)) continue;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, P.err, kErrTimeoutAccum)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        const int nk = pr.k / kBK;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[stage], phase, P.err, kErrTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // K-major: advance 16 elements (32 B) inside the swizzle row.
+            // MN-major: advance 16 K-rows (2 x 1024 B atoms); 64-wide MN blocks are 8 KB apart.
+            const uint64_t da = A_MN ? make_smem_desc(sa + kk * 2048, kBK * 128, 1024, 2)
+                                     : make_smem_desc(sa + kk * 32, 16, 1024, 2);
+            const uint64_t db = B_MN ? make_smem_desc(sb + kk * 2048, kBK * 128, 1024, 2)
+                                     : make_smem_desc(sb + kk * 32, 16, 1024, 2);
+            mma_bf16(d_tmem, da, db, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        mma_commit(&acc_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int hint = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      GemmProblem pr;
+      int mt, nt, bt;
+      if (!locate_tile<BN, BMODE>(P, t, hint, pr, mt, nt, bt)) continue;
+      if (!mbar_wait(&acc_full[acc], acc_phase, P.err, kErrTimeoutAccum)) break;
+      tc_fence_after();
+      const int row = mt * kBM + quarter * 32 + lane;
+      const bool row_ok = row < pr.m;
+      const bool zero_k = pr.k == 0;
+      const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      const long long dbase = pr.d_off + static_cast<long long>(bt) * pr.d_bstride + row * pr.d_ld;
+      if constexpr (EPI == kEpiSwiGLU) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d);
+        __nv_bfloat16* pre = reinterpret_cast<__nv_bfloat16*>(P.aux);
+        const int half = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < half; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_row + c, g);
+          tmem_ld32(t_row + half + c, u);
+          tmem_ld_wait();
+          const int col0 = nt * half + c;
+          if (row_ok) {
+            const long long pbase = pr.aux_off + row * pr.aux_ld;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = col0 + j;
+              if (col < pr.n) {
+                const float gv = zero_k ? 0.f : __uint_as_float(g[j]);
+                const float uv = zero_k ? 0.f : __uint_as_float(u[j]);
+                const float gc = fminf(gv, P.gate_max);
+                const float uc = fminf(fmaxf(uv, P.lin_lo), P.lin_hi);
+                out[dbase + col] = __float2bfloat16(silu_f(gc) * uc);
+                pre[pbase + col] = __float2bfloat16(gv);
+                pre[pbase + pr.n + col] = __float2bfloat16(uv);
+              }
+            }
+          }
+        }
+      } else {
+        const float rs = (EPI == kEpiRowScaleBF16 && row_ok) ? P.rowscale[pr.aux_off + row] : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_ld_wait();
+          const int col0 = nt * BN + c;
+          if (!row_ok) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = zero_k ? 0.f : __uint_as_float(r[j]) * P.alpha * rs;
+          const bool full_chunk = col0 + 32 <= pr.n;
+          if constexpr (EPI == kEpiBF16 || EPI == kEpiRowScaleBF16) {
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d) + dbase + col0;
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+                pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(out + j) = pk;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < pr.n) out[j] = __float2bfloat16(v[j]);
+            }
+          } else {
+            float* out = reinterpret_cast<float*>(P.d) + dbase + col0;
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if (EPI == kEpiF32Acc) {
+                  const float4 prev = *reinterpret_cast<const float4*>(out + j);
+                  o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+                }
+                *reinterpret_cast<float4*>(out + j) = o;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < pr.n) out[j] = (EPI == kEpiF32Acc) ? out[j] + v[j] : v[j];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace sv4

@@ -1,0 +1,265 @@
+"""Muon (+ MuonClip QK-Clip) and a combined Muon/AdamW optimizer.
+
+Muon per matrix W (n x m), reference ``optim/muon.py:57-192``::
+
+    M <- mu M + G ;  U = mu M + G                    (Nesterov look-ahead)
+    O = NS(U) * sqrt(max(n, m)) * gamma              (gamma = 0.18, RMS match to AdamW)
+    W <- W (1 - lr wd) - lr O
+
+Differences from the reference, each deliberate:
+
+* 3-D stacked expert weights (E, out, in) are orthogonalised per expert slice (the
+  reference raises; ``strict_2d=True`` restores that behaviour).
+* All matrices of one shape are orthogonalised in one batched call (on CUDA: the
+  native batched tensor-core GEMM, bf16 operands / fp32 accumulation).  On CPU the
+  default NS is the reference's fp32 per-matrix iteration, so CPU results match.
+* QK-Clip reads each attention layer's *device* max-logit buffer and rescales
+  ``q_up`` / ``k_proj`` by ``sqrt(tau / max)`` where ``max > tau`` without a host
+  sync; trigger counts are kept on the device and converted on access.
+
+``MuonAdamW`` is one ``torch.optim.Optimizer`` whose param groups carry
+``kind="muon"`` or ``kind="adamw"`` so a single object (and a single LR scheduler)
+drives both halves of the V4 recipe.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Iterable
+from typing import Any, Protocol, runtime_checkable
+
+import torch
+from torch import Tensor, nn
+
+from saint_llm_b200.optim.newton_schulz import STAGE1, STAGE2, batched_newton_schulz, hybrid_newton_schulz
+
+
+@runtime_checkable
+class _QKClippable(Protocol):
+    _last_max_attn_logit: float
+
+    def qk_clip_targets(self) -> list[Tensor]: ...
+
+
+def _orthogonalize(updates: list[Tensor], group: dict[str, Any], impl: str) -> list[Tensor]:
+    """NS-orthogonalise a list of same-shaped tensors (2-D or stacked 3-D)."""
+    kw = dict(n_iter_stage1=group["ns_iter_stage1"], n_iter_stage2=group["ns_iter_stage2"],
+              coeffs_stage1=tuple(group["ns_coeffs_stage1"]), coeffs_stage2=tuple(group["ns_coeffs_stage2"]))
+    if impl == "reference":
+        out = []
+        for u in updates:
+            out.append(hybrid_newton_schulz(u, **kw) if u.dim() == 2
+                       else torch.stack([hybrid_newton_schulz(s, **kw) for s in u]))
+        return out
+    stacked = torch.cat([u.reshape(-1, *u.shape[-2:]) for u in updates])
+    orth = batched_newton_schulz(stacked, precision="bf16" if impl == "batched_bf16" else "fp32", **kw)
+    res, i = [], 0
+    for u in updates:
+        cnt = u.numel() // (u.shape[-2] * u.shape[-1])
+        res.append(orth[i:i + cnt].reshape(u.shape))
+        i += cnt
+    return res
+
+
+class _QKClipMixin:
+    qk_clip_enabled: bool
+    qk_clip_tau: float
+    _qk_clip_layers: list[nn.Module]
+    _qk_clip_counts: dict[int, Tensor]
+
+    def _init_qk_clip(self, enabled: bool, tau: float, layers: Iterable[nn.Module] | None) -> None:
+        if tau <= 0.0:
+            raise ValueError(f"qk_clip_tau must be positive; got {tau}")
+        self.qk_clip_enabled = enabled
+        self.qk_clip_tau = tau
+        self._qk_clip_layers = list(layers or [])
+        self._qk_clip_counts = {}
+
+    def register_qk_clip_layer(self, layer: nn.Module) -> None:
+        if not isinstance(layer, _QKClippable):
+            raise TypeError(f"Layer {type(layer).__name__} does not satisfy _QKClippable "
+                            "protocol (needs _last_max_attn_logit and qk_clip_targets()).")
+        self._qk_clip_layers.append(layer)
+
+    @property
+    def qk_clip_count(self) -> dict[int, int]:
+        return {k: int(v) for k, v in self._qk_clip_counts.items() if int(v) > 0}
+
+    @torch.no_grad()
+    def _apply_qk_clip(self) -> None:
+        tau = self.qk_clip_tau
+        for layer in self._qk_clip_layers:
+            buf = getattr(layer, "max_attn_logit", None)
+            if isinstance(buf, Tensor):
+                mx = buf.float()
+                hit = mx > tau
+                scale = torch.where(hit, torch.sqrt(tau / mx.clamp(min=1e-30)), torch.ones_like(mx))
+                for w in layer.qk_clip_targets():
+                    w.mul_(scale.to(w.dtype))
+                cnt = self._qk_clip_counts.setdefault(id(layer), torch.zeros((), dtype=torch.long,
+                                                                             device=mx.device))
+                cnt.add_(hit.long())
+            else:
+                mxf = float(getattr(layer, "_last_max_attn_logit", 0.0))
+                if mxf <= tau:
+                    continue
+                for w in layer.qk_clip_targets():
+                    w.data.mul_((tau / mxf) ** 0.5)
+                cnt = self._qk_clip_counts.setdefault(id(layer), torch.zeros((), dtype=torch.long))
+                cnt.add_(1)
+
+
+def _muon_defaults(lr: float, momentum: float, weight_decay: float, rms_rescale: float,
+                   ns_iter_stage1: int, ns_iter_stage2: int, ns_coeffs_stage1: tuple[float, float, float],
+                   ns_coeffs_stage2: tuple[float, float, float]) -> dict[str, Any]:
+    if lr < 0.0:
+        raise ValueError(f"Invalid lr {lr}")
+    if not 0.0 <= momentum < 1.0:
+        raise ValueError(f"Invalid momentum {momentum} (must be in [0, 1))")
+    if weight_decay < 0.0:
+        raise ValueError(f"Invalid weight_decay {weight_decay}")
+    return dict(lr=lr, momentum=momentum, weight_decay=weight_decay, rms_rescale=rms_rescale,
+                ns_iter_stage1=ns_iter_stage1, ns_iter_stage2=ns_iter_stage2,
+                ns_coeffs_stage1=ns_coeffs_stage1, ns_coeffs_stage2=ns_coeffs_stage2)
+
+
+@torch.no_grad()
+def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: str, strict_2d: bool,
+                     chunk_elems: int = 1 << 28) -> None:
+    lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
+    by_shape: dict[tuple[Any, ...], list[Tensor]] = {}
+    for p in group["params"]:
+        if p.grad is None:
+            continue
+        if p.dim() != 2 and (strict_2d or p.dim() != 3):
+            raise ValueError(f"Muon expects 2D matrix params; got shape {tuple(p.shape)}. "
+                             "Use AdamW for 1D params (RMSNorm weights, biases, gating factors).")
+        st = opt.state[p]
+        if "momentum_buffer" not in st:
+            st["momentum_buffer"] = torch.zeros_like(p)
+        st["momentum_buffer"].mul_(mu).add_(p.grad.to(st["momentum_buffer"].dtype))
+        by_shape.setdefault((*p.shape[-2:], str(p.device)), []).append(p)
+    for params in by_shape.values():
+        # bounded working set: orthogonalise at most ~chunk_elems elements at a time
+        chunk: list[Tensor] = []
+        size = 0
+        for i, p in enumerate(params):
+            chunk.append(p)
+            size += p.numel()
+            if size >= chunk_elems or i == len(params) - 1:
+                upd = [opt.state[q]["momentum_buffer"].float() * mu + q.grad.float() for q in chunk]
+                for q, o in zip(chunk, _orthogonalize(upd, group, impl), strict=True):
+                    n, k = q.shape[-2:]
+                    q.mul_(1.0 - lr * wd).add_((o * (math.sqrt(max(n, k)) * gamma)).to(q.dtype), alpha=-lr)
+                chunk, size = [], 0
+
+
+def _resolve_impl(impl: str, params: Iterable[Tensor]) -> str:
+    if impl != "auto":
+        return impl
+    for p in params:
+        return "batched_bf16" if p.is_cuda else "reference"
+    return "reference"
+
+
+class Muon(_QKClipMixin, torch.optim.Optimizer):
+    """Muon for matrix parameters (2-D, or stacked 3-D experts)."""
+
+    def __init__(self, params: Iterable[nn.Parameter] | Iterable[dict[str, Any]], lr: float = 2.7e-4,
+                 momentum: float = 0.95, weight_decay: float = 0.1, rms_rescale: float = 0.18,
+                 ns_iter_stage1: int = 8, ns_iter_stage2: int = 2,
+                 ns_coeffs_stage1: tuple[float, float, float] = STAGE1,
+                 ns_coeffs_stage2: tuple[float, float, float] = STAGE2, *,
+                 qk_clip_enabled: bool = True, qk_clip_tau: float = 100.0,
+                 qk_clip_layers: Iterable[nn.Module] | None = None, ns_impl: str = "auto",
+                 strict_2d: bool = False) -> None:
+        super().__init__(params, _muon_defaults(lr, momentum, weight_decay, rms_rescale, ns_iter_stage1,
+                                                ns_iter_stage2, ns_coeffs_stage1, ns_coeffs_stage2))
+        self._init_qk_clip(qk_clip_enabled, qk_clip_tau, qk_clip_layers)
+        self.ns_impl = ns_impl
+        self.strict_2d = strict_2d
+
+    @torch.no_grad()
+    def step(self, closure: Callable[[], Tensor] | None = None) -> Tensor | None:
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            _muon_group_step(self, group, _resolve_impl(self.ns_impl, group["params"]), self.strict_2d)
+        if self.qk_clip_enabled and self._qk_clip_layers:
+            self._apply_qk_clip()
+        return loss
+
+
+class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
+    """One optimizer for the V4 split: groups with ``kind="muon"`` or ``kind="adamw"``."""
+
+    def __init__(self, muon_params: Iterable[nn.Parameter], adamw_params: Iterable[nn.Parameter], *,
+                 lr: float = 2.7e-4, momentum: float = 0.95, weight_decay: float = 0.1,
+                 rms_rescale: float = 0.18, adamw_lr: float | None = None,
+                 betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-20,
+                 adamw_weight_decay: float | None = None, qk_clip_enabled: bool = True,
+                 qk_clip_tau: float = 100.0, qk_clip_layers: Iterable[nn.Module] | None = None,
+                 ns_impl: str = "auto") -> None:
+        muon_defaults = _muon_defaults(lr, momentum, weight_decay, rms_rescale, 8, 2, STAGE1, STAGE2)
+        groups = [
+            {"params": list(muon_params), "kind": "muon", **muon_defaults},
+            {"params": list(adamw_params), "kind": "adamw", "lr": adamw_lr if adamw_lr is not None else lr,
+             "betas": betas, "eps": eps,
+             "weight_decay": adamw_weight_decay if adamw_weight_decay is not None else weight_decay},
+        ]
+        super().__init__([g for g in groups if g["params"]], {})
+        self._init_qk_clip(qk_clip_enabled, qk_clip_tau, qk_clip_layers)
+        self.ns_impl = ns_impl
+
+    @torch.no_grad()
+    def step(self, closure: Callable[[], Tensor] | None = None) -> Tensor | None:
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            if group["kind"] == "muon":
+                _muon_group_step(self, group, _resolve_impl(self.ns_impl, group["params"]), False)
+            else:
+                self._adamw_group_step(group)
+        if self.qk_clip_enabled and self._qk_clip_layers:
+            self._apply_qk_clip()
+        return loss
+
+    @torch.no_grad()
+    def _adamw_group_step(self, group: dict[str, Any]) -> None:
+        params = [p for p in group["params"] if p.grad is not None]
+        if not params:
+            return
+        b1, b2 = group["betas"]
+        lr, eps, wd = group["lr"], group["eps"], group["weight_decay"]
+        for p in params:
+            st = self.state[p]
+            if not st:
+                st["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                st["exp_avg"] = torch.zeros_like(p, dtype=torch.float32)
+                st["exp_avg_sq"] = torch.zeros_like(p, dtype=torch.float32)
+        if params[0].is_cuda:
+            from saint_llm_b200.ops import backend
+
+            if backend.native_for(params[0]):
+                from saint_llm_b200.ops import optim_kernels
+
+                optim_kernels.adamw_step(params, [self.state[p] for p in params], lr=lr, beta1=b1,
+                                         beta2=b2, eps=eps, weight_decay=wd)
+                return
+        for p in params:
+            st = self.state[p]
+            st["step"] += 1
+            t = float(st["step"])
+            g = p.grad.float()
+            st["exp_avg"].mul_(b1).add_(g, alpha=1 - b1)
+            st["exp_avg_sq"].mul_(b2).addcmul_(g, g, value=1 - b2)
+            denom = (st["exp_avg_sq"] / (1 - b2 ** t)).sqrt_().add_(eps)
+            upd = st["exp_avg"] / (1 - b1 ** t) / denom
+            p.mul_(1 - lr * wd).add_(upd.to(p.dtype), alpha=-lr)
+
+
+__all__ = ["Muon", "MuonAdamW"]

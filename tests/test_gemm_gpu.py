@@ -1,0 +1,51 @@
+"""Native tcgen05 GEMM vs a plain fp32 PyTorch reference."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(a, b):
+    return a.float() @ b.float().transpose(-1, -2)
+
+
+def _close(x, y, tol=2e-2):
+    err = (x.float() - y.float()).abs().max().item()
+    scale = y.float().abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (300, 200, 192), (4096, 2048, 2048),
+                                   (1, 17, 64), (1000, 1408, 2048)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, True), (True, False)])
+def test_gemm_layouts(cuda, m, n, k, a_t, b_t):
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(0)
+    a = torch.randn(k, m, device=cuda, dtype=torch.bfloat16).t() if a_t else torch.randn(m, k, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(k, n, device=cuda, dtype=torch.bfloat16).t() if b_t else torch.randn(n, k, device=cuda, dtype=torch.bfloat16)
+    out = gemm.gemm_nt(a, b, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    _close(out, _ref(a, b), 1e-3)
+    out16 = gemm.gemm_nt(a, b)
+    _close(out16, _ref(a, b))
+
+
+def test_gemm_accumulate_and_batched(cuda):
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(1)
+    a = torch.randn(5, 192, 320, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(5, 130, 320, device=cuda, dtype=torch.bfloat16)
+    acc = torch.randn(5, 192, 130, device=cuda, dtype=torch.float32)
+    want = acc + _ref(a, b)
+    gemm.gemm_nt(a, b, out=acc, accumulate=True)
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    _close(acc, want, 1e-3)
+    # batched a @ b with b row-major (MN-major operand)
+    x = torch.randn(7, 128, 256, device=cuda, dtype=torch.bfloat16)
+    y = torch.randn(7, 256, 384, device=cuda, dtype=torch.bfloat16)
+    _close(gemm.bmm(x, y), x.float() @ y.float(), 1e-3)

@@ -1,0 +1,237 @@
+"""Headline benchmark: training tokens/s of the ~16B FP8-class MoE.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (``torchrun`` for N > 1, expert parallel EP = N, data parallel for
+the replicated weights).  Per GPU a step is one optimizer step over ``seqs_per_gpu`` x
+4096 uniform-random tokens (weak scaling: 32 sequences per GPU, i.e. global batch
+256 x 4096 at N = 8).  The W warm-up steps are untimed; exactly K steps are timed with
+CUDA events between a barrier + synchronize on both sides; the per-rank time is
+max-reduced over ranks.  Every step copies its token batch from pinned host memory
+inside the timed region.  The model weights (tens of GB) stream through HBM every step,
+far beyond the 126 MB L2, so no explicit L2 flush is used.
+
+``e2e`` repeats the measurement through the public ``TrainStep`` call (host batch in,
+Python float loss out) timed by the host clock around the whole call.
+
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+if HERE not in sys.path:
+    sys.path.insert(0, HERE)
+
+METRIC = "train tokens/sec/box (max over ranks) FP8 MoE at 1/2/4/8 B200; decode tok/s"
+MODEL_DESC = ("V4-MoE ~16B total / ~2.7B active (BASELINE config 3): d2048 L28 H16x128, 64 routed top-6 + "
+              "2 shared, I1408, MTP1, vocab 32768")
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.lines: list[str] = []
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9], strict=True):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def count_native_launches(fn) -> int:
+    """Number of this framework's kernels (namespace sv4) launched by one call of fn."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return sum(1 for ev in prof.events()
+               if ev.device_type == torch.autograd.DeviceType.CUDA and "sv4::" in ev.name)
+
+
+def build_ours(args, device, world):
+    from saint_llm_b200.config import ModelConfig
+    from saint_llm_b200.models import SaintLLM
+    from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
+    from saint_llm_b200.train.engine import attach_main_grads, cast_params
+    from saint_llm_b200.train.step import TrainStep
+
+    upd = {"linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt}
+    if args.layers:
+        upd["n_layers"] = args.layers
+    cfg = ModelConfig.bench_16b().model_copy(update=upd)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = SaintLLM(cfg)
+    cast_params(model, torch.bfloat16)
+    grad_sync = None
+    if world > 1:
+        from saint_llm_b200.parallel import ep as ep_mod
+
+        grad_sync = ep_mod.setup_expert_parallel(model)
+        torch.cuda.empty_cache()
+    params = attach_main_grads(model)
+    muon, adamw = split_for_muon_adamw(model)
+    opt = MuonAdamW(muon, adamw, lr=2.7e-4, qk_clip_layers=model.attention_layers())
+    step = TrainStep(model, opt, micro_batches=args.seqs_per_gpu // args.micro_batch, params=params,
+                     grad_sync=grad_sync)
+    return cfg, model, step
+
+
+def run_ours(args) -> dict:
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    cfg, model, step = build_ours(args, device, world)
+    from saint_llm_b200.ops.gemm import check_errors
+    from saint_llm_b200.train.engine import SyntheticTokens
+
+    n_micro = args.seqs_per_gpu // args.micro_batch
+    host = SyntheticTokens(cfg.vocab_size, args.micro_batch, args.seq_len, n_micro, seed=rank).buf
+
+    def device_step():
+        return step.run_device(host.to(device, non_blocking=True))
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    check_errors(device)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            loss = device_step()
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    t_ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t_ms, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t_ms.item())
+    final_loss = float(loss.item())
+    check_errors(device)
+
+    # end-to-end through the public call: host batch in, float loss out
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step(host)
+    torch.cuda.synchronize()
+    t_e = torch.tensor([(time.perf_counter() - t0) * 1000 / args.steps], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t_e, op=torch.distributed.ReduceOp.MAX)
+    e2e_ms = float(t_e.item())
+
+    launches = count_native_launches(device_step) * args.steps
+    tokens_per_step = world * args.seqs_per_gpu * args.seq_len
+    result = {
+        "metric": METRIC, "value": tokens_per_step / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.linear_quant == "bf16" else "fp8",
+        "data": "synthetic uniform-random tokens; random-init weights N(0,0.02)",
+        "config": {"model": MODEL_DESC, "n_layers": cfg.n_layers, "global_batch": world * args.seqs_per_gpu,
+                   "seq_len": args.seq_len, "micro_batch": args.micro_batch,
+                   "parallelism": f"ep{world}+dp{world}" if world > 1 else "single-gpu",
+                   "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
+                   "l2": "inputs larger than L2 (the weights stream through HBM every step)",
+                   "final_loss": final_loss,
+                   "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)},
+        "clocks": clk.summary(),
+        "e2e": {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+    }
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return result if rank == 0 else {}
+
+
+def run_reference(args) -> dict:
+    from baseline import reference_arm
+
+    return reference_arm.run(args)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seqs-per-gpu", type=int, default=32)
+    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--linear-quant", default="bf16", choices=["bf16", "fp8"])
+    ap.add_argument("--ckpt", action="store_true", help="activation checkpointing per block")
+    ap.add_argument("--layers", type=int, default=0, help="(development only) override n_layers")
+    args = ap.parse_args()
+    res = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if res:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 
 namespace sv4 {
+// gemm.cu
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate,
           double alpha, torch::Tensor err);
 void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor b1, torch::Tensor out,
@@ -11,12 +12,66 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
 void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t mode, int64_t D, int64_t I,
                         torch::Tensor probs, torch::Tensor total);
 int64_t problem_bytes();
+void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Tensor act, torch::Tensor pre,
+                  double gmax, double lo, double hi, torch::Tensor err);
+void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, torch::Tensor dx, torch::Tensor err);
+// moe.cu
+void moe_route_plan(torch::Tensor idx, int64_t n_experts, int64_t k, torch::Tensor counts, torch::Tensor seg_start,
+                    torch::Tensor seg_rows, torch::Tensor total, torch::Tensor pos, torch::Tensor row_token,
+                    torch::Tensor err);
+void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out);
+void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out);
+void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor dy,
+                     torch::Tensor dw);
+void moe_zero_pad_rows(torch::Tensor row_token, torch::Tensor buf);
+void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi);
+// norm.cu
+void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor rstd, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dx);
+void rope_norm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor cosb, torch::Tensor sinb, torch::Tensor y,
+                   torch::Tensor rstd, int64_t heads, int64_t rd, bool norm_first, double eps);
+torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor cosb,
+                            torch::Tensor sinb, torch::Tensor rstd, torch::Tensor dx, int64_t heads, int64_t rd,
+                            bool norm_first);
+void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor p, torch::Tensor r, double eps);
+void mhc_gates_fwd(torch::Tensor p, torch::Tensor alpha, torch::Tensor s_pre, torch::Tensor s_res,
+                   torch::Tensor s_post, torch::Tensor a, torch::Tensor b, torch::Tensor c, int64_t n, int64_t iters);
+void mhc_gates_bwd(torch::Tensor p, torch::Tensor alpha, torch::Tensor s_pre, torch::Tensor s_res,
+                   torch::Tensor s_post, torch::Tensor da, torch::Tensor db, torch::Tensor dc, torch::Tensor dz,
+                   int64_t n, int64_t iters);
+void mhc_premix(torch::Tensor X, torch::Tensor a, torch::Tensor out, int64_t n);
+void mhc_combine(torch::Tensor X, torch::Tensor o, torch::Tensor B, torch::Tensor C, torch::Tensor Y, int64_t n);
+void mhc_combine_bwd(torch::Tensor dY, torch::Tensor X, torch::Tensor o, torch::Tensor B, torch::Tensor C,
+                     torch::Tensor dX, torch::Tensor dO, torch::Tensor dB, torch::Tensor dC, int64_t n);
+void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t n);
+void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
+                   torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
 }  // namespace sv4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "saint_llm_b200 sm_100a kernels";
-  m.def("gemm", &sv4::gemm, "tcgen05 GEMM / batched GEMM");
-  m.def("grouped_gemm", &sv4::grouped_gemm, "tcgen05 grouped GEMM (MoE)");
-  m.def("build_moe_problems", &sv4::build_moe_problems, "device-side MoE problem table");
+  m.def("gemm", &sv4::gemm);
+  m.def("grouped_gemm", &sv4::grouped_gemm);
+  m.def("build_moe_problems", &sv4::build_moe_problems);
   m.def("problem_bytes", &sv4::problem_bytes);
+  m.def("swiglu_dense", &sv4::swiglu_dense);
+  m.def("swiglu_dense_dgrad", &sv4::swiglu_dense_dgrad);
+  m.def("moe_route_plan", &sv4::moe_route_plan);
+  m.def("moe_gather", &sv4::moe_gather);
+  m.def("moe_combine", &sv4::moe_combine);
+  m.def("moe_combine_bwd", &sv4::moe_combine_bwd);
+  m.def("moe_zero_pad_rows", &sv4::moe_zero_pad_rows);
+  m.def("swiglu_bwd", &sv4::swiglu_bwd);
+  m.def("rmsnorm_fwd", &sv4::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &sv4::rmsnorm_bwd);
+  m.def("rope_norm_fwd", &sv4::rope_norm_fwd);
+  m.def("rope_norm_bwd", &sv4::rope_norm_bwd);
+  m.def("mhc_proj_fwd", &sv4::mhc_proj_fwd);
+  m.def("mhc_gates_fwd", &sv4::mhc_gates_fwd);
+  m.def("mhc_gates_bwd", &sv4::mhc_gates_bwd);
+  m.def("mhc_premix", &sv4::mhc_premix);
+  m.def("mhc_combine", &sv4::mhc_combine);
+  m.def("mhc_combine_bwd", &sv4::mhc_combine_bwd);
+  m.def("mhc_premix_da", &sv4::mhc_premix_da);
+  m.def("mhc_split_bwd", &sv4::mhc_split_bwd);
 }

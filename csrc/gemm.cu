@@ -89,39 +89,37 @@ static int num_sms(int dev) {
   return cached[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
-static void launch(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1, const GemmParams& p,
-                   int grid, cudaStream_t stream) {
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, BMODE, EPI>;
-  constexpr int smem = GemmSmem<BN>::kTotal;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
-  }
-  kern<<<grid, 192, smem, stream>>>(ma, mb0, mb1, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-#define SV4_DISPATCH(A_MN, B_MN, BMODE, EPI)                                            \
-  if (a_mn == A_MN && b_mn == B_MN && bmode == BMODE && epi == EPI) {                   \
-    launch<256, A_MN, B_MN, BMODE, EPI>(ma, mb0, mb1, p, grid, stream);                 \
-    return;                                                                              \
-  }
+// Kernel instantiations live in gemm_inst_*.cu (compiled in parallel).
+void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
+                         const GemmParams& p, int grid, cudaStream_t stream);
 
 static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap& ma, const CUtensorMap& mb0,
                      const CUtensorMap& mb1, const GemmParams& p, int grid, cudaStream_t stream) {
-  SV4_DISPATCH(false, false, kBSingle, kEpiBF16)
-  SV4_DISPATCH(false, false, kBSingle, kEpiF32)
-  SV4_DISPATCH(false, false, kBSingle, kEpiF32Acc)
-  SV4_DISPATCH(false, true, kBSingle, kEpiBF16)
-  SV4_DISPATCH(false, true, kBSingle, kEpiF32)
-  SV4_DISPATCH(true, true, kBSingle, kEpiF32Acc)
-  SV4_DISPATCH(true, true, kBSingle, kEpiF32)
-  SV4_DISPATCH(true, true, kBSingle, kEpiBF16)
-  SV4_DISPATCH(false, false, kBSplitN, kEpiSwiGLU)
-  SV4_DISPATCH(false, false, kBSingle, kEpiRowScaleBF16)
-  SV4_DISPATCH(false, true, kBSplitK, kEpiBF16)
+  struct V { bool a, b; int bm, ep; };
+  static const V table[] = {
+      {false, false, kBSingle, kEpiBF16},
+      {false, false, kBSingle, kEpiF32},
+      {false, false, kBSingle, kEpiF32Acc},
+      {false, true, kBSingle, kEpiBF16},
+      {false, true, kBSingle, kEpiF32},
+      {true, true, kBSingle, kEpiF32Acc},
+      {true, true, kBSingle, kEpiF32},
+      {true, true, kBSingle, kEpiBF16},
+      {false, false, kBSplitN, kEpiSwiGLU},
+      {false, false, kBSingle, kEpiRowScaleBF16},
+      {false, true, kBSplitK, kEpiBF16},
+      {true, false, kBSingle, kEpiBF16},
+      {true, false, kBSingle, kEpiF32},
+      {true, false, kBSingle, kEpiF32Acc},
+      {false, true, kBSingle, kEpiF32Acc},
+  };
+  for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
+    const V& v = table[i];
+    if (v.a == a_mn && v.b == b_mn && v.bm == bmode && v.ep == epi) {
+      gemm_launch_variant(i, ma, mb0, mb1, p, grid, stream);
+      return;
+    }
+  }
   TORCH_CHECK(false, "unsupported GEMM variant a_mn=", a_mn, " b_mn=", b_mn, " bmode=", bmode, " epi=", epi);
 }
 
@@ -216,7 +214,7 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
     }
     case 1: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 256);
-      dispatch(false, false, kBSingle, kEpiRowScaleBF16, ma, m0, m0, p, grid, stream);
+      dispatch(false, false, kBSingle, p.rowscale ? kEpiRowScaleBF16 : kEpiBF16, ma, m0, m0, p, grid, stream);
       break;
     }
     case 2: {
@@ -237,6 +235,46 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
     default:
       TORCH_CHECK(false, "unknown grouped GEMM mode");
   }
+}
+
+// Dense fused SwiGLU (shared experts):  pre = [x Wg^T | x Wu^T],  act = silu(min(g,gmax)) * clamp(u)
+void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Tensor act, torch::Tensor pre,
+                  double gmax, double lo, double hi, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(x.device());
+  OperandView vx = view_of(x), vg = view_of(wg), vu = view_of(wu);
+  const int64_t M = vx.outer, K = vx.inner, I = vg.outer;
+  TORCH_CHECK(K % 64 == 0 && vg.inner == K && vu.inner == K && vu.outer == I, "swiglu_dense shapes");
+  CUtensorMap ma = map_for(vx, 128), m0 = map_for(vg, 128), m1 = map_for(vu, 128);
+  GemmParams p{};
+  p.probs = nullptr;
+  GemmProblem& s = p.single;
+  s.m = M; s.n = I; s.k = K; s.batch = 1;
+  s.d_ld = act.stride(0); s.aux_ld = pre.stride(0);
+  p.d = act.data_ptr(); p.aux = pre.data_ptr();
+  p.alpha = 1.f; p.gate_max = gmax; p.lin_lo = lo; p.lin_hi = hi;
+  p.err = err.data_ptr<int>();
+  const int tiles = ((M + 127) / 128) * ((I + 127) / 128);
+  if (tiles == 0) return;
+  dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, p, std::min<int>(tiles, num_sms(x.get_device())),
+           at::cuda::getCurrentCUDAStream());
+}
+
+// dx = dpre[:, :I] Wg + dpre[:, I:] Wu   (B split along K between the two weights)
+void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, torch::Tensor dx, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(dpre.device());
+  OperandView va = view_of(dpre), vg = view_of(wg), vu = view_of(wu);
+  const int64_t M = va.outer, K2 = va.inner, D = vg.inner, I = vg.outer;
+  TORCH_CHECK(K2 == 2 * I && I % 64 == 0, "swiglu_dense_dgrad shapes");
+  CUtensorMap ma = map_for(va, 128), m0 = map_for(vg, 64), m1 = map_for(vu, 64);
+  GemmParams p{};
+  p.probs = nullptr;
+  GemmProblem& s = p.single;
+  s.m = M; s.n = D; s.k = K2; s.batch = 1; s.d_ld = dx.stride(0);
+  p.d = dx.data_ptr(); p.alpha = 1.f; p.ksplit = I; p.err = err.data_ptr<int>();
+  const int tiles = ((M + 127) / 128) * ((D + 255) / 256);
+  if (tiles == 0) return;
+  dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, p, std::min<int>(tiles, num_sms(dpre.get_device())),
+           at::cuda::getCurrentCUDAStream());
 }
 
 // ------------------------------------------------------------------------------
@@ -305,5 +343,26 @@ void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t
 }
 
 int64_t problem_bytes() { return sizeof(GemmProblem); }
+
+bool gemm_launch_group0(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group1(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group2(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group3(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group4(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group5(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group6(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+
+void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
+                         const GemmParams& p, int grid, cudaStream_t stream) {
+  const bool ok = gemm_launch_group0(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group1(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group2(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group3(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group4(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group5(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group6(variant, ma, mb0, mb1, p, grid, stream);
+  TORCH_CHECK(ok, "GEMM variant not instantiated");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 }  // namespace sv4

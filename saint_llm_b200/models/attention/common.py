@@ -30,6 +30,12 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: Tensor) -> Tensor:
+        from saint_llm_b200.ops import backend
+
+        if backend.native_for(x) and x.shape[-1] % 8 == 0:
+            from saint_llm_b200.ops.norm import rms_norm
+
+            return rms_norm(x, self.weight, self.eps)
         return self.weight * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps))
 
 

@@ -36,6 +36,7 @@ from saint_llm_b200.models.attention.common import (
     window_mask_at,
 )
 from saint_llm_b200.models.linear import LinearFactory, default_linear
+from saint_llm_b200.ops import backend
 
 
 class TokenLevelCompressor(nn.Module):
@@ -254,6 +255,10 @@ class CSA(_AttentionBase):
 
     def forward(self, h: Tensor, is_visual: Tensor | None = None, *,
                 kv_cache: Any | None = None) -> Tensor:
+        if kv_cache is None and backend.native_for(h):
+            from saint_llm_b200.ops.attention import attention_forward
+
+            return attention_forward(self, "csa", h, is_visual)
         off, cos, sin = self._positions(h, kv_cache)
         q = self._queries(h, cos, sin)
         k_new, v_new = self._sw_kv(h, cos, sin)

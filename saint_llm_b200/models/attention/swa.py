@@ -21,6 +21,7 @@ from saint_llm_b200.config import AttentionConfig, HCAConfig
 from saint_llm_b200.models.attention.common import scaled_dot_product
 from saint_llm_b200.models.attention.csa import TokenLevelCompressor, _AttentionBase
 from saint_llm_b200.models.linear import LinearFactory, default_linear
+from saint_llm_b200.ops import backend
 
 
 class SWAttention(_AttentionBase):
@@ -33,7 +34,10 @@ class SWAttention(_AttentionBase):
 
     def forward(self, h: Tensor, is_visual: Tensor | None = None, *,
                 kv_cache: Any | None = None) -> Tensor:
-        del is_visual
+        if kv_cache is None and backend.native_for(h):
+            from saint_llm_b200.ops.attention import attention_forward
+
+            return attention_forward(self, "swa", h, is_visual)
         off, cos, sin = self._positions(h, kv_cache)
         q = self._queries(h, cos, sin)
         k, v = self._sw_kv(h, cos, sin)
@@ -69,7 +73,10 @@ class HCA(_AttentionBase):
 
     def forward(self, h: Tensor, is_visual: Tensor | None = None, *,
                 kv_cache: Any | None = None) -> Tensor:
-        del is_visual
+        if kv_cache is None and backend.native_for(h):
+            from saint_llm_b200.ops.attention import attention_forward
+
+            return attention_forward(self, "hca", h, is_visual)
         off, cos, sin = self._positions(h, kv_cache)
         q = self._queries(h, cos, sin)
         k, v = self._sw_kv(h, cos, sin)

@@ -34,6 +34,16 @@ from saint_llm_b200.models.mtp import MTPStack
 from saint_llm_b200.models.multimodal import GenerationHeadHook, ModalityProjector, ResidualSideChannel
 
 
+def _apply_linear(mod: nn.Linear, x: Tensor) -> Tensor:
+    from saint_llm_b200.ops import backend
+
+    if backend.native_for(x):
+        from saint_llm_b200.ops.linear import linear
+
+        return linear(x, mod.weight, mod.bias)
+    return mod(x)
+
+
 class TransformerBlock(nn.Module):
     def __init__(self, cfg: ModelConfig, layer_idx: int, *, linear_factory: LinearFactory) -> None:
         super().__init__()
@@ -160,7 +170,7 @@ class SaintLLM(nn.Module):
         return self.final_norm(h), emb
 
     def logits(self, h: Tensor) -> Tensor:
-        out = self.lm_head(h)
+        out = _apply_linear(self.lm_head, h)
         c = self.cfg.final_logit_softcap
         return c * torch.tanh(out / c) if c is not None else out
 
@@ -185,7 +195,7 @@ class SaintLLM(nn.Module):
         return {
             "logits": self.logits(h),
             "mtp_logits": [self.logits(mh) for mh in mtp_hidden],
-            "generation_logits": self.generation_head(h),
+            "generation_logits": _apply_linear(self.generation_head.proj, h),
             "hidden": h,
             "aux_loss": self.aux_loss(),
         }

@@ -85,7 +85,12 @@ class LearnedRouter(nn.Module):
         self.update_aux_free_bias = False
 
     def affinity(self, x: Tensor) -> Tensor:
-        logits = self.score_proj(x)
+        if backend.native_for(x):
+            from saint_llm_b200.ops.linear import linear
+
+            logits = linear(x, self.score_proj.weight).float()
+        else:
+            logits = self.score_proj(x)
         if self.cfg.affinity_fn == "sqrt_softplus":
             return torch.sqrt(F.softplus(logits) + 1.0e-12)
         return torch.sigmoid(logits)
@@ -150,8 +155,10 @@ class DeepSeekMoE(nn.Module):
         )
         self._last_aux_loss: Tensor | None = None
         self.register_buffer("last_expert_counts", torch.zeros(cfg.routed_experts), persistent=False)
-        # expert-parallel group (set by parallel.ep.shard_experts); None = all local
+        # expert parallelism (set by parallel.ep.shard_grouped_experts); None = all experts local
         self.ep_group = None
+        self.ep_size = 1
+        self.ep_rank = 0
 
     def route(self, h: Tensor, token_ids: Tensor | None, is_visual: Tensor | None
               ) -> tuple[Tensor, Tensor, Tensor]:
@@ -167,6 +174,10 @@ class DeepSeekMoE(nn.Module):
 
     def forward(self, x: Tensor, token_ids: Tensor | None = None,
                 is_visual: Tensor | None = None) -> Tensor:
+        if self.ep_size > 1:
+            from saint_llm_b200.parallel import ep
+
+            return ep.moe_forward_ep(self, x, token_ids, is_visual)
         if backend.native_for(x):
             from saint_llm_b200.ops import moe as moe_ops
 

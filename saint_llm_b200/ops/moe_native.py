@@ -1,0 +1,250 @@
+"""Fused MoE layer on the native kernels (local experts; the EP wrapper is parallel.ep).
+
+Forward of ``DeepSeekMoE`` on CUDA::
+
+    h      = RMSNorm(x)                                    (native)
+    idx, g = router(h)                                     (learned or hash)
+    plan   = moe_route_plan(idx)                           expert segments padded to 128 rows,
+                                                           slot positions, row->token map (device)
+    x_p    = gather(h, plan)                               (M_pad, D)
+    act    = grouped GEMM [W_gate | W_up] + SwiGLU epilogue (M_pad, I)   (+ pre-acts saved)
+    y      = grouped GEMM W_down                           (M_pad, D)
+    out    = combine(y, plan, g) + sum_s SwiGLU_s(h)       shared experts: dense fused SwiGLU
+
+Backward reverses each step; weight gradients go straight into ``main_grad`` (fp32)
+through the accumulate epilogue of the grouped wgrad GEMMs.  No host synchronisation:
+problem tables for the grouped GEMMs are built on the device from the routing counts.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor, nn
+
+from saint_llm_b200.ops import backend, gemm
+from saint_llm_b200.ops.linear import accumulate_weight_grad
+
+_PROB_INTS: int | None = None
+
+
+def _prob_table(n: int, device: torch.device) -> Tensor:
+    global _PROB_INTS
+    if _PROB_INTS is None:
+        _PROB_INTS = backend.ext().problem_bytes() // 4
+    return torch.empty(n, _PROB_INTS, dtype=torch.int32, device=device)
+
+
+def _bf16c(t: Tensor) -> Tensor:
+    return (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)).contiguous()
+
+
+class RoutePlan:
+    """Device-side routing layout for one MoE call."""
+
+    def __init__(self, idx: Tensor, n_experts: int, k: int) -> None:
+        ext = backend.ext()
+        dev = idx.device
+        n_pairs = idx.numel()
+        self.n_experts = n_experts
+        self.k = k
+        self.m_cap = n_pairs + n_experts * 128
+        self.counts = torch.empty(n_experts, dtype=torch.int32, device=dev)
+        self.seg_start = torch.empty(n_experts, dtype=torch.int32, device=dev)
+        self.seg_rows = torch.empty(n_experts, dtype=torch.int32, device=dev)
+        self.total = torch.empty(1, dtype=torch.int32, device=dev)
+        self.pos = torch.empty(idx.shape[0], k, dtype=torch.int32, device=dev)
+        self.row_token = torch.full((self.m_cap,), -1, dtype=torch.int32, device=dev)
+        ext.moe_route_plan(idx.reshape(-1).to(torch.int64).contiguous(), n_experts, k, self.counts, self.seg_start,
+                           self.seg_rows, self.total, self.pos, self.row_token, gemm.error_word(dev))
+
+    def problems(self, mode: int, D: int, I: int) -> tuple[Tensor, Tensor, int]:
+        n = self.n_experts * (2 if mode == 4 else 1)
+        probs = _prob_table(n, self.pos.device)
+        total = torch.empty(1, dtype=torch.int32, device=self.pos.device)
+        backend.ext().build_moe_problems(self.seg_start, self.seg_rows, mode, D, I, probs, total)
+        return probs, total, n
+
+
+_EMPTY: dict[torch.device, Tensor] = {}
+
+
+def _empty(dev: torch.device) -> Tensor:
+    t = _EMPTY.get(dev)
+    if t is None:
+        t = torch.empty(0, device=dev)
+        _EMPTY[dev] = t
+    return t
+
+
+class _RoutedExpertsFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h: Tensor, idx: Tensor, gate: Tensor, wg: Tensor, wu: Tensor, wd: Tensor,  # type: ignore[override]
+                clamps: tuple[float, float, float]) -> Tensor:
+        ext = backend.ext()
+        dev = h.device
+        T, D = h.shape
+        E, I, _ = wg.shape
+        k = idx.shape[1]
+        gmax, lo, hi = clamps
+        err = gemm.error_word(dev)
+        plan = RoutePlan(idx, E, k)
+        hb = _bf16c(h)
+        x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+        ext.moe_gather(hb, plan.row_token, x_p)
+        wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
+        act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
+        pre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
+        e0 = _empty(dev)
+        pr, tot, n = plan.problems(0, D, I)
+        ext.grouped_gemm(0, x_p, wgb, wub, act, pre, e0, pr, tot, n, gmax, lo, hi, 0, False, err)
+        y = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+        pr, tot, n = plan.problems(1, D, I)
+        ext.grouped_gemm(1, act, wdb, wdb, y, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+        out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        gf = gate.float().contiguous()
+        ext.moe_combine(y, plan.pos, gf, out)
+        ctx.save_for_backward(hb, gf, act, pre, y, wg, wu, wd)
+        ctx.plan = plan
+        ctx.clamps = clamps
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        hb, gf, act, pre, y, wg, wu, wd = ctx.saved_tensors
+        plan: RoutePlan = ctx.plan
+        ext = backend.ext()
+        dev = hb.device
+        T, D = hb.shape
+        E, I, _ = wg.shape
+        gmax, lo, hi = ctx.clamps
+        err = gemm.error_word(dev)
+        e0 = _empty(dev)
+        dy = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+        dgate = torch.empty_like(gf)
+        ext.moe_combine_bwd(_bf16c(dout), y, plan.pos, gf, dy, dgate)
+        ext.moe_zero_pad_rows(plan.row_token, dy)
+        wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
+        # down projection: d_act = dy Wd ; dWd += dy^T act
+        dact = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
+        pr, tot, n = plan.problems(2, D, I)
+        ext.grouped_gemm(2, dy, wdb, wdb, dact, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+        dwd_buf = getattr(wd, "main_grad", None)
+        acc_d = dwd_buf is not None
+        if dwd_buf is None:
+            dwd_buf = torch.zeros(E, D, I, dtype=torch.float32, device=dev)
+        pr, tot, n = plan.problems(5, D, I)
+        ext.grouped_gemm(4, dy, act, act, dwd_buf, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
+        # SwiGLU backward
+        dpre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_bwd(dact, pre, dpre, gmax, lo, hi)
+        # gate/up: dx_p = dpre [Wg; Wu] ; d[Wg|Wu] += dpre^T x_p
+        dxp = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+        pr, tot, n = plan.problems(3, D, I)
+        ext.grouped_gemm(3, dpre, wgb, wub, dxp, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, I, False, err)
+        x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+        ext.moe_gather(hb, plan.row_token, x_p)
+        mg_g, mg_u = getattr(wg, "main_grad", None), getattr(wu, "main_grad", None)
+        if mg_g is not None and mg_u is not None and mg_u.data_ptr() == mg_g.data_ptr() + mg_g.numel() * 4:
+            joint, acc_gu = mg_g, True
+        else:
+            joint, acc_gu = torch.zeros(2, E, I, D, dtype=torch.float32, device=dev), False
+        pr, tot, n = plan.problems(4, D, I)
+        ext.grouped_gemm(4, dpre, x_p, x_p, joint, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
+        dh = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        ext.moe_combine(dxp, plan.pos, None, dh)
+        dwg = None if acc_gu else joint[0].to(wg.dtype)
+        dwu = None if acc_gu else joint[1].to(wu.dtype)
+        dwd = None if acc_d else dwd_buf.to(wd.dtype)
+        return dh, None, dgate, dwg, dwu, dwd, None
+
+
+class _SharedSwiGLUFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h: Tensor, wg: Tensor, wu: Tensor, wd: Tensor, clamps: tuple[float, float, float]):  # type: ignore[override]
+        ext = backend.ext()
+        dev = h.device
+        T, D = h.shape
+        I = wg.shape[0]
+        hb = _bf16c(h)
+        act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+        pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_dense(hb, _bf16c(wg), _bf16c(wu), act, pre, *clamps, gemm.error_word(dev))
+        y = gemm.gemm_nt(act, _bf16c(wd))
+        ctx.save_for_backward(hb, act, pre, wg, wu, wd)
+        ctx.clamps = clamps
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        hb, act, pre, wg, wu, wd = ctx.saved_tensors
+        ext = backend.ext()
+        dev = hb.device
+        I = wg.shape[0]
+        dyb = _bf16c(dy)
+        dact = gemm.gemm_nt(dyb, _bf16c(wd).t())
+        dwd = accumulate_weight_grad(wd, dyb, act)
+        dpre = torch.empty_like(pre)
+        ext.swiglu_bwd(dact, pre, dpre, *ctx.clamps)
+        dh = torch.empty_like(hb)
+        ext.swiglu_dense_dgrad(dpre, _bf16c(wg), _bf16c(wu), dh, gemm.error_word(dev))
+        dwg = accumulate_weight_grad(wg, dpre[:, :I], hb)
+        dwu = accumulate_weight_grad(wu, dpre[:, I:], hb)
+        return dh, dwg, dwu, dwd, None
+
+
+def shared_swiglu(h: Tensor, expert: nn.Module) -> Tensor:
+    lin = expert.clamp_linear
+    return _SharedSwiGLUFn.apply(h, expert.gate_proj.weight, expert.up_proj.weight, expert.down_proj.weight,
+                                 (float(expert.clamp_gate_max), float(lin[0]), float(lin[1])))
+
+
+def routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module) -> Tensor:
+    """h (T, D); idx / gate (T, k): sum_j gate[t,j] * expert_{idx[t,j]}(h[t]) over the local expert pool."""
+    return _RoutedExpertsFn.apply(h, idx, gate, experts.gate_weight, experts.up_weight, experts.down_weight,
+                                  (float(experts.clamp_gate_max), float(experts.clamp_linear[0]),
+                                   float(experts.clamp_linear[1])))
+
+
+def moe_forward(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
+    """CUDA forward of ``DeepSeekMoE``."""
+    if getattr(layer, "ep_size", 1) > 1:
+        from saint_llm_b200.parallel import ep
+
+        return ep.moe_forward_ep(layer, x, token_ids, is_visual)
+    if layer.grouped_experts is None or getattr(layer.grouped_experts, "linear_quant", "bf16") == "fp4":
+        return _moe_per_module(layer, x, token_ids, is_visual)
+    b, t, d = x.shape
+    h = layer.norm(x)
+    idx, gate, aux = layer.route(h, token_ids, is_visual)
+    layer._last_aux_loss = aux
+    k = layer.cfg.experts_per_token
+    h2 = h.reshape(b * t, d)
+    out = routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts)
+    for expert in layer.shared_experts:
+        out = out + shared_swiglu(h2, expert)
+    return out.view(b, t, d)
+
+
+def _moe_per_module(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
+    """Per-module expert layout on CUDA: the routed loop runs on native linears."""
+    h = layer.norm(x)
+    b, t, d = h.shape
+    idx, gate, aux = layer.route(h, token_ids, is_visual)
+    layer._last_aux_loss = aux
+    k = layer.cfg.experts_per_token
+    fh, fi, fg = h.reshape(b * t, d), idx.reshape(b * t, k), gate.reshape(b * t, k)
+    routed = torch.zeros_like(fh)
+    if layer.grouped_experts is not None:
+        routed = layer.grouped_experts(fh, fi, fg)
+    else:
+        for e, expert in enumerate(layer.routed_experts):
+            tok, slot = (fi == e).nonzero(as_tuple=True)
+            if tok.numel():
+                routed = routed.index_add(0, tok, expert(fh[tok]) * fg[tok, slot].unsqueeze(-1).to(fh.dtype))
+    out = routed
+    for expert in layer.shared_experts:
+        out = out + expert(fh)
+    return out.view(b, t, d)
+
+
+__all__ = ["RoutePlan", "moe_forward", "routed_experts", "shared_swiglu"]

@@ -34,6 +34,12 @@ from torch import Tensor, nn
 from saint_llm_b200.optim.newton_schulz import STAGE1, STAGE2, batched_newton_schulz, hybrid_newton_schulz
 
 
+def _grad(p: Tensor) -> Tensor | None:
+    """fp32 ``main_grad`` when the training engine attached one, else ``.grad``."""
+    mg = getattr(p, "main_grad", None)
+    return mg if mg is not None else p.grad
+
+
 @runtime_checkable
 class _QKClippable(Protocol):
     _last_max_attn_logit: float
@@ -129,7 +135,8 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
     lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
     by_shape: dict[tuple[Any, ...], list[Tensor]] = {}
     for p in group["params"]:
-        if p.grad is None:
+        g = _grad(p)
+        if g is None:
             continue
         if p.dim() != 2 and (strict_2d or p.dim() != 3):
             raise ValueError(f"Muon expects 2D matrix params; got shape {tuple(p.shape)}. "
@@ -137,7 +144,7 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
         st = opt.state[p]
         if "momentum_buffer" not in st:
             st["momentum_buffer"] = torch.zeros_like(p)
-        st["momentum_buffer"].mul_(mu).add_(p.grad.to(st["momentum_buffer"].dtype))
+        st["momentum_buffer"].mul_(mu).add_(g.to(st["momentum_buffer"].dtype))
         by_shape.setdefault((*p.shape[-2:], str(p.device)), []).append(p)
     for params in by_shape.values():
         # bounded working set: orthogonalise at most ~chunk_elems elements at a time
@@ -147,7 +154,7 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
             chunk.append(p)
             size += p.numel()
             if size >= chunk_elems or i == len(params) - 1:
-                upd = [opt.state[q]["momentum_buffer"].float() * mu + q.grad.float() for q in chunk]
+                upd = [opt.state[q]["momentum_buffer"].float() * mu + _grad(q).float() for q in chunk]
                 for q, o in zip(chunk, _orthogonalize(upd, group, impl), strict=True):
                     n, k = q.shape[-2:]
                     q.mul_(1.0 - lr * wd).add_((o * (math.sqrt(max(n, k)) * gamma)).to(q.dtype), alpha=-lr)
@@ -230,7 +237,7 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
 
     @torch.no_grad()
     def _adamw_group_step(self, group: dict[str, Any]) -> None:
-        params = [p for p in group["params"] if p.grad is not None]
+        params = [p for p in group["params"] if _grad(p) is not None]
         if not params:
             return
         b1, b2 = group["betas"]
@@ -254,7 +261,7 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
             st = self.state[p]
             st["step"] += 1
             t = float(st["step"])
-            g = p.grad.float()
+            g = _grad(p).float()
             st["exp_avg"].mul_(b1).add_(g, alpha=1 - b1)
             st["exp_avg_sq"].mul_(b2).addcmul_(g, g, value=1 - b2)
             denom = (st["exp_avg_sq"] / (1 - b2 ** t)).sqrt_().add_(eps)

@@ -1,0 +1,227 @@
+"""Expert parallelism (EP).
+
+Experts are partitioned contiguously: rank r of the EP group owns experts
+``[r*E/N, (r+1)*E/N)``.
+
+Reference-compatible API (``distributed/expert_parallel.py:47-276``):
+``dispatch_tokens_by_expert(tokens, expert_ids, n_experts=..., world_size=None,
+group=None) -> DispatchPlan`` (stable sort by destination rank, counts all-to-all,
+payload all-to-all; a ``world_size`` different from the process group's runs the same
+permutation without communication -- "simulation mode") and
+``combine_outputs_by_expert(expert_out, plan)`` (reverse all-to-all + un-permute).
+
+Training path (``moe_forward_ep``): router -> one row per (token, slot) sorted by
+destination rank -> autograd all-to-all -> the rank's local experts on the tensor
+cores (the grouped GEMMs of ``ops.moe_native`` with k = 1) -> reverse all-to-all ->
+gate-weighted sum per token.  The all-to-all here is NCCL (gloo on CPU); gradients
+flow through ``torch.distributed.nn`` all-to-alls.
+
+``setup_expert_parallel(model)`` shards every grouped expert pool to the local slice,
+marks the layers and returns the gradient synchroniser: replicated (non-expert)
+gradients are averaged across ranks (bucketed all-reduce); expert gradients, already
+complete on their owner, are divided by the world size so both follow the same
+global-mean loss.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+
+@dataclass(frozen=True)
+class DispatchPlan:
+    permuted_tokens: Tensor
+    send_counts: Tensor
+    recv_counts: Tensor
+    sort_indices: Tensor
+    local_expert_offsets: Tensor
+    n_local_tokens: int
+    world_size: int = 1
+    simulated: bool = True
+
+
+def _pg_size(group: dist.ProcessGroup | None) -> int:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1
+    return dist.get_world_size(group)
+
+
+def dispatch_tokens_by_expert(tokens: Tensor, expert_ids: Tensor, *, n_experts: int, world_size: int | None = None,
+                              group: dist.ProcessGroup | None = None) -> DispatchPlan:
+    if tokens.dim() != 2:
+        raise ValueError(f"tokens must be (N, D); got shape {tuple(tokens.shape)}")
+    if expert_ids.shape[0] != tokens.shape[0]:
+        raise ValueError(f"expert_ids length {expert_ids.shape[0]} != tokens batch {tokens.shape[0]}")
+    if n_experts <= 0:
+        raise ValueError(f"n_experts must be positive; got {n_experts}")
+    pg_ws = _pg_size(group)
+    ws = world_size if world_size is not None else pg_ws
+    if n_experts % ws:
+        raise ValueError(f"n_experts {n_experts} must be divisible by world_size {ws}")
+    real = ws == pg_ws and pg_ws > 1
+    per = n_experts // ws
+    dest = (expert_ids // per).clamp(0, ws - 1)
+    order = torch.argsort(dest, stable=True)
+    send = tokens.index_select(0, order)
+    send_counts = torch.bincount(dest, minlength=ws).to(torch.int64)
+    # per-local-expert offsets of the rows this rank receives (its own slice when simulated)
+    if real:
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=group)
+        rs, ss = recv_counts.tolist(), send_counts.tolist()
+        recv = tokens.new_empty(sum(rs), tokens.shape[1])
+        dist.all_to_all_single(recv, send.contiguous(), output_split_sizes=rs, input_split_sizes=ss, group=group)
+    else:
+        recv_counts, recv = send_counts.clone(), send
+    offsets = torch.zeros(per, dtype=torch.int64, device=tokens.device)
+    return DispatchPlan(recv, send_counts, recv_counts, order, offsets, tokens.shape[0], ws, not real)
+
+
+def combine_outputs_by_expert(expert_out: Tensor, plan: DispatchPlan, *,
+                              group: dist.ProcessGroup | None = None) -> Tensor:
+    if expert_out.shape[0] != plan.permuted_tokens.shape[0]:
+        raise ValueError("expert_out rows must match the dispatched rows")
+    if not plan.simulated:
+        back = expert_out.new_empty(plan.n_local_tokens, *expert_out.shape[1:])
+        dist.all_to_all_single(back, expert_out.contiguous(), output_split_sizes=plan.send_counts.tolist(),
+                               input_split_sizes=plan.recv_counts.tolist(), group=group)
+    else:
+        back = expert_out
+    out = torch.empty_like(back)
+    out.index_copy_(0, plan.sort_indices, back)
+    return out
+
+
+# ------------------------------------------------------------------ training path
+def _a2a(x: Tensor, out_splits: list[int], in_splits: list[int], group: dist.ProcessGroup | None) -> Tensor:
+    from torch.distributed.nn.functional import all_to_all_single
+
+    out = x.new_empty(sum(out_splits), *x.shape[1:])
+    return all_to_all_single(out, x.contiguous(), output_split_sizes=out_splits, input_split_sizes=in_splits,
+                             group=group)
+
+
+def moe_forward_ep(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
+    """``DeepSeekMoE`` forward with the routed experts sharded over the EP group."""
+    from saint_llm_b200.ops import backend
+
+    b, t, d = x.shape
+    h = layer.norm(x)
+    idx, gate, aux = layer.route(h, token_ids, is_visual)
+    layer._last_aux_loss = aux
+    k = layer.cfg.experts_per_token
+    T = b * t
+    h2 = h.reshape(T, d)
+    group = layer.ep_group
+    ws, rank = layer.ep_size, layer.ep_rank
+    e_loc = layer.cfg.routed_experts // ws
+    flat_e = idx.reshape(-1)
+    dest = flat_e // e_loc
+    order = torch.argsort(dest, stable=True)
+    send_counts = torch.bincount(dest, minlength=ws).to(torch.int64)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    ss, rs = send_counts.tolist(), recv_counts.tolist()
+    send_x = h2.index_select(0, order // k)
+    send_e = flat_e.index_select(0, order).contiguous()
+    recv_x = _a2a(send_x, rs, ss, group)
+    recv_e = send_e.new_empty(sum(rs))
+    dist.all_to_all_single(recv_e, send_e, output_split_sizes=rs, input_split_sizes=ss, group=group)
+    local_ids = (recv_e - rank * e_loc).view(-1, 1)
+    ge = layer.grouped_experts
+    native = backend.native_for(x)
+    if native:
+        from saint_llm_b200.ops.moe_native import routed_experts, shared_swiglu
+
+        ones = torch.ones(local_ids.shape[0], 1, dtype=torch.float32, device=x.device)
+        y_recv = routed_experts(recv_x, local_ids, ones, ge)
+    else:
+        ones = torch.ones(local_ids.shape[0], 1, dtype=torch.float32, device=x.device)
+        y_recv = ge(recv_x, local_ids, ones)
+    back = _a2a(y_recv, ss, rs, group)
+    inv = torch.empty_like(order)
+    inv[order] = torch.arange(order.numel(), device=order.device)
+    y_pair = back.index_select(0, inv).view(T, k, d)
+    out = (y_pair.float() * gate.reshape(T, k, 1).float()).sum(1).to(h2.dtype)
+    for expert in layer.shared_experts:
+        out = out + (shared_swiglu(h2, expert) if native else expert(h2))
+    return out.view(b, t, d)
+
+
+def shard_grouped_experts(model: nn.Module, rank: int, ws: int, group: dist.ProcessGroup | None) -> list[Tensor]:
+    """Keep only this rank's expert slice; returns the sharded (expert) parameters."""
+    from saint_llm_b200.models.moe import DeepSeekMoE
+
+    expert_params: list[Tensor] = []
+    for mod in model.modules():
+        if not isinstance(mod, DeepSeekMoE):
+            continue
+        ge = mod.grouped_experts
+        if ge is None:
+            raise ValueError("expert parallelism needs the stacked (moe_use_grouped_gemm) expert layout")
+        E = ge.n_experts
+        if E % ws:
+            raise ValueError(f"routed_experts {E} not divisible by EP size {ws}")
+        per = E // ws
+        for name in ("gate_weight", "up_weight", "down_weight"):
+            full = getattr(ge, name)
+            local = nn.Parameter(full.data[rank * per:(rank + 1) * per].clone(), requires_grad=full.requires_grad)
+            setattr(ge, name, local)
+            expert_params.append(local)
+        ge.n_global_experts = E
+        ge.n_experts = per
+        mod.ep_group = group
+        mod.ep_size = ws
+        mod.ep_rank = rank
+    return expert_params
+
+
+def make_grad_sync(expert_params: list[Tensor], group: dist.ProcessGroup | None,
+                   bucket_bytes: int = 256 << 20) -> Callable[[list[Tensor]], None]:
+    """Average replicated main_grads across ranks (bucketed all-reduce); scale expert grads by 1/N."""
+    ws = dist.get_world_size(group)
+    eids = {id(p) for p in expert_params}
+
+    def sync(params: list[Tensor]) -> None:
+        rep = [p.main_grad for p in params if id(p) not in eids]  # type: ignore[attr-defined]
+        bucket: list[Tensor] = []
+        size = 0
+        for i, g in enumerate(rep):
+            bucket.append(g)
+            size += g.numel() * 4
+            if size >= bucket_bytes or i == len(rep) - 1:
+                flat = torch.cat([x.reshape(-1) for x in bucket])
+                dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+                flat.div_(ws)
+                off = 0
+                for x in bucket:
+                    x.copy_(flat[off:off + x.numel()].view_as(x))
+                    off += x.numel()
+                bucket, size = [], 0
+        for p in params:
+            if id(p) in eids:
+                p.main_grad.div_(ws)  # type: ignore[attr-defined]
+
+    return sync
+
+
+def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None) -> Callable[[list[Tensor]], None]:
+    rank = dist.get_rank(group)
+    ws = dist.get_world_size(group)
+    return make_grad_sync(shard_grouped_experts(model, rank, ws, group), group)
+
+
+__all__ = [
+    "DispatchPlan",
+    "combine_outputs_by_expert",
+    "dispatch_tokens_by_expert",
+    "make_grad_sync",
+    "moe_forward_ep",
+    "setup_expert_parallel",
+    "shard_grouped_experts",
+]

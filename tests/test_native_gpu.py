@@ -1,0 +1,232 @@
+"""Native sm_100a kernels vs the fp32 eager PyTorch oracle of the same op (GPU)."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(x, y):
+    return ((x.float() - y.float()).norm() / (y.float().norm() + 1e-12)).item()
+
+
+def _bf(t):
+    return t.to(torch.bfloat16).float()
+
+
+def test_rmsnorm_native(cuda):
+    from saint_llm_b200.models.attention.common import RMSNorm
+    from saint_llm_b200.ops import backend
+
+    torch.manual_seed(0)
+    m = RMSNorm(2048).to(cuda)
+    m.weight.data.uniform_(0.5, 1.5)
+    x = torch.randn(300, 2048, device=cuda, requires_grad=True)
+    g = torch.randn(300, 2048, device=cuda)
+    with backend.eager_mode():
+        m(x).backward(g)
+    gx0, gw0 = x.grad.clone(), m.weight.grad.clone()
+    with backend.eager_mode():
+        y0 = m(x)
+    x.grad = None
+    m.weight.grad = None
+    y1 = m(x)
+    y1.backward(g.to(y1.dtype))
+    assert _rel(y1, y0) < 1e-2
+    assert _rel(x.grad, gx0) < 2e-2
+    assert _rel(m.weight.grad, gw0) < 1e-2
+
+
+@pytest.mark.parametrize("norm_first", [False, True])
+def test_rope_norm_native(cuda, norm_first):
+    from saint_llm_b200.models.attention.common import apply_partial_rope, rope_tables
+    from saint_llm_b200.ops.norm import rope_norm
+
+    torch.manual_seed(0)
+    T, H, d, rd = 64, 4, 128, 64
+    x = torch.randn(T, H, d, device=cuda, requires_grad=True)
+    w = (torch.rand(d, device=cuda) + 0.5).requires_grad_(True)
+    cos, sin = rope_tables(T, rd, 10000.0, cuda)
+
+    def ref(x, w):
+        xt = x.transpose(0, 1)
+
+        def norm(z):
+            return w * z * torch.rsqrt(z.pow(2).mean(-1, keepdim=True) + 1e-6)
+        y = apply_partial_rope(norm(xt), cos, sin, rd) if norm_first else norm(apply_partial_rope(xt, cos, sin, rd))
+        return y.transpose(0, 1)
+
+    g = torch.randn(T, H, d, device=cuda)
+    y0 = ref(x, w)
+    y0.backward(g)
+    gx0, gw0 = x.grad.clone(), w.grad.clone()
+    x.grad = None
+    w.grad = None
+    y1 = rope_norm(x, w, cos, sin, rd, norm_first=norm_first)
+    y1.backward(g.to(y1.dtype))
+    assert _rel(y1, y0) < 1e-2
+    assert _rel(x.grad, gx0) < 2e-2
+    assert _rel(w.grad, gw0) < 2e-2
+
+
+def test_mhc_native(cuda):
+    from saint_llm_b200.config import MHCConfig
+    from saint_llm_b200.models.mhc import MHC
+    from saint_llm_b200.ops import backend
+
+    torch.manual_seed(0)
+    n, d = 4, 256
+    m = MHC(d, MHCConfig(expansion_factor=n, sinkhorn_iters=20)).to(cuda)
+    with torch.no_grad():
+        for w in (m.w_pre, m.w_res, m.w_post):
+            w.weight.normal_(0, 0.02)
+        m.norm.weight.uniform_(0.5, 1.5)
+        for p in (m.alpha_pre, m.alpha_res, m.alpha_post):
+            p.fill_(0.5)
+        m.s_res.normal_(0, 0.3)
+    x = torch.randn(2, 70, n, d, device=cuda, requires_grad=True)
+    inner_w = torch.randn(d, d, device=cuda) / d ** 0.5
+    g = torch.randn(2, 70, n, d, device=cuda)
+
+    def run():
+        inner, a, b, c = m.split(x)
+        out = m.combine(x, torch.tanh(inner.float() @ inner_w), b, c)
+        out.float().backward(g)
+        return out
+
+    with backend.eager_mode():
+        y0 = run()
+    grads0 = {k: p.grad.clone() for k, p in m.named_parameters()}
+    gx0 = x.grad.clone()
+    m.zero_grad()
+    x.grad = None
+    y1 = run()
+    assert _rel(y1, y0) < 2e-2
+    assert _rel(x.grad, gx0) < 3e-2
+    for k, p in m.named_parameters():
+        assert _rel(p.grad, grads0[k]) < 5e-2, k
+
+
+def _expert_ref(h, idx, gate, wg, wu, wd, gmax=10.0, lo=-10.0, hi=10.0):
+    out = torch.zeros_like(h)
+    for e in range(wg.shape[0]):
+        tok, slot = (idx == e).nonzero(as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        x = h[tok]
+        y = (F.silu((x @ wg[e].t()).clamp(max=gmax)) * (x @ wu[e].t()).clamp(lo, hi)) @ wd[e].t()
+        out = out.index_add(0, tok, gate[tok, slot].unsqueeze(-1) * y)
+    return out
+
+
+@pytest.mark.parametrize("T,E,k,D,I", [(300, 8, 2, 256, 128), (1024, 16, 4, 512, 384)])
+def test_routed_experts_fixed_routing(cuda, T, E, k, D, I):
+    from saint_llm_b200.ops.moe import GroupedSwiGLUExperts
+    from saint_llm_b200.ops.moe_native import routed_experts
+
+    torch.manual_seed(0)
+    ex = GroupedSwiGLUExperts(D, I, E).to(cuda)
+    with torch.no_grad():
+        for w in (ex.gate_weight, ex.up_weight, ex.down_weight):
+            w.copy_(_bf(torch.randn_like(w) * 0.05))
+    h = _bf(torch.randn(T, D, device=cuda)).requires_grad_(True)
+    idx = torch.stack([torch.randperm(E, device=cuda)[:k] for _ in range(T)])
+    gate = torch.rand(T, k, device=cuda).requires_grad_(True)
+    g = torch.randn(T, D, device=cuda)
+    y0 = _expert_ref(h, idx, gate, ex.gate_weight, ex.up_weight, ex.down_weight)
+    y0.backward(g)
+    ref = {"h": h.grad.clone(), "gate": gate.grad.clone(), "wg": ex.gate_weight.grad.clone(),
+           "wu": ex.up_weight.grad.clone(), "wd": ex.down_weight.grad.clone()}
+    h.grad = None
+    gate.grad = None
+    ex.zero_grad()
+    y1 = routed_experts(h, idx, gate, ex)
+    y1.float().backward(g)
+    assert _rel(y1, y0) < 1e-2
+    assert _rel(h.grad, ref["h"]) < 2e-2
+    assert _rel(gate.grad, ref["gate"]) < 2e-2
+    assert _rel(ex.gate_weight.grad, ref["wg"]) < 2e-2
+    assert _rel(ex.up_weight.grad, ref["wu"]) < 2e-2
+    assert _rel(ex.down_weight.grad, ref["wd"]) < 2e-2
+
+
+def test_shared_swiglu_native(cuda):
+    from saint_llm_b200.models.moe import SwiGLU
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.moe_native import shared_swiglu
+
+    torch.manual_seed(0)
+    m = SwiGLU(512, 384, (-10.0, 10.0), 10.0).to(cuda)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(_bf(p * 3))
+    h = _bf(torch.randn(333, 512, device=cuda)).requires_grad_(True)
+    g = torch.randn(333, 512, device=cuda)
+    with backend.eager_mode():
+        y0 = m(h)
+        y0.backward(g)
+    ref = [h.grad.clone()] + [p.grad.clone() for p in m.parameters()]
+    h.grad = None
+    m.zero_grad()
+    y1 = shared_swiglu(h, m)
+    y1.float().backward(g)
+    assert _rel(y1, y0) < 1e-2
+    for got, want in zip([h.grad] + [p.grad for p in m.parameters()], ref, strict=True):
+        assert _rel(got, want) < 2e-2
+
+
+def test_fused_ce(cuda):
+    from saint_llm_b200.ops.ce import lm_head_cross_entropy
+
+    torch.manual_seed(0)
+    h = torch.randn(2, 300, 256, device=cuda, requires_grad=True)
+    w = (torch.randn(1000, 256, device=cuda) * 0.05).requires_grad_(True)
+    t = torch.randint(0, 1000, (2, 300), device=cuda)
+    for cap in (None, 30.0):
+        z = h @ w.t()
+        if cap:
+            z = cap * torch.tanh(z / cap)
+        l0 = F.cross_entropy(z.view(-1, 1000), t.view(-1))
+        gh0, gw0 = torch.autograd.grad(l0, (h, w))
+        l1 = lm_head_cross_entropy(h, w, t, softcap=cap)
+        gh1, gw1 = torch.autograd.grad(l1, (h, w))
+        assert abs(l1.item() - l0.item()) < 2e-2
+        assert _rel(gh1, gh0) < 3e-2 and _rel(gw1, gw0) < 3e-2
+
+
+def test_tiny_model_native_step(cuda):
+    """Whole tiny model on the native path: loss close to the eager oracle, grads aligned."""
+    from saint_llm_b200.config import ModelConfig
+    from saint_llm_b200.models import SaintLLM
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.gemm import check_errors
+    from saint_llm_b200.train.losses import make_loss_fn
+
+    torch.manual_seed(0)
+    cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+    model = SaintLLM(cfg).to(cuda)
+    x = torch.randint(0, cfg.vocab_size, (2, 64), device=cuda)
+    with backend.eager_mode():
+        l0 = make_loss_fn(cfg.mtp, moe_cfg=cfg.moe, fused=False)(model, x)
+        l0.backward()
+    g0 = {k: p.grad.clone() for k, p in model.named_parameters() if p.grad is not None}
+    model.zero_grad()
+    l1 = make_loss_fn(cfg.mtp, moe_cfg=cfg.moe)(model, x)
+    l1.backward()
+    torch.cuda.synchronize()
+    check_errors(cuda)
+    assert torch.isfinite(l1) and abs(l1.item() - l0.item()) < 0.05 * abs(l0.item())
+    cos = []
+    for k, ref in g0.items():
+        p = dict(model.named_parameters())[k]
+        assert p.grad is not None and torch.isfinite(p.grad).all(), k
+        if ref.norm() > 1e-6:
+            cos.append(F.cosine_similarity(p.grad.flatten().float(), ref.flatten(), dim=0).item())
+    assert sum(c > 0.9 for c in cos) >= 0.8 * len(cos), sorted(cos)[:10]
+
+
+def test_smoke_entry(cuda):
+    import __graft_entry__
+
+    __graft_entry__.smoke()

@@ -12,6 +12,13 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
 void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t mode, int64_t D, int64_t I,
                         torch::Tensor probs, torch::Tensor total);
 int64_t problem_bytes();
+void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor out, bool a_mn, bool b_mn,
+                double alpha, double beta, torch::Tensor err);
+// optim.cu
+void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_t slice, double mu);
+void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
+                    double eps);
+void muon_apply(torch::Tensor p, torch::Tensor o, double decay, double step);
 void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Tensor act, torch::Tensor pre,
                   double gmax, double lo, double hi, torch::Tensor err);
 void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, torch::Tensor dx, torch::Tensor err);
@@ -54,6 +61,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &sv4::grouped_gemm);
   m.def("build_moe_problems", &sv4::build_moe_problems);
   m.def("problem_bytes", &sv4::problem_bytes);
+  m.def("gemm_axpby", &sv4::gemm_axpby);
+  m.def("muon_momentum", &sv4::muon_momentum);
+  m.def("muon_normalize", &sv4::muon_normalize);
+  m.def("muon_apply", &sv4::muon_apply);
   m.def("swiglu_dense", &sv4::swiglu_dense);
   m.def("swiglu_dense_dgrad", &sv4::swiglu_dense_dgrad);
   m.def("moe_route_plan", &sv4::moe_route_plan);

@@ -112,6 +112,8 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
       {true, false, kBSingle, kEpiF32},
       {true, false, kBSingle, kEpiF32Acc},
       {false, true, kBSingle, kEpiF32Acc},
+      {false, false, kBSingle, kEpiAxpbyBF16},
+      {false, true, kBSingle, kEpiAxpbyBF16},
   };
   for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
     const V& v = table[i];
@@ -175,6 +177,39 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   if (tiles == 0) return;
   const int grid = std::min<int>(tiles, num_sms(a.get_device()));
   dispatch(a_mn, b_mn, kBSingle, epi, ma, mb, mb, p, grid, at::cuda::getCurrentCUDAStream());
+}
+
+// out = alpha * (A B^T) + beta * C, bf16 out and bf16 C with identical layout to out
+// (batched Newton-Schulz: P = c G G + b G and Y' = P Y + a Y in one pass each).
+void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor out, bool a_mn, bool b_mn,
+                double alpha, double beta, torch::Tensor err) {
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "bf16 operands required");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16, "bf16 out / C required");
+  TORCH_CHECK(c.sizes() == out.sizes() && c.strides() == out.strides(), "C must be laid out like out");
+  c10::cuda::CUDAGuard guard(a.device());
+  OperandView va = view_of(a), vb = view_of(b);
+  const int64_t M = a_mn ? va.inner : va.outer;
+  const int64_t K = a_mn ? va.outer : va.inner;
+  const int64_t N = b_mn ? vb.inner : vb.outer;
+  TORCH_CHECK((b_mn ? vb.outer : vb.inner) == K && K % 64 == 0, "K mismatch or K % 64");
+  TORCH_CHECK(va.batch == vb.batch, "batch mismatch");
+  TORCH_CHECK(out.size(-1) == N && out.size(-2) == M, "output shape mismatch");
+  CUtensorMap ma = map_for(va, a_mn ? 64 : 128);
+  CUtensorMap mb = map_for(vb, b_mn ? 64 : 256);
+  GemmParams p{};
+  GemmProblem& s = p.single;
+  s.m = M; s.n = N; s.k = K; s.batch = va.batch;
+  s.d_ld = out.stride(-2);
+  s.d_bstride = out.dim() == 3 ? out.stride(0) : 0;
+  p.d = out.data_ptr();
+  p.aux = c.data_ptr();
+  p.alpha = static_cast<float>(alpha);
+  p.beta = static_cast<float>(beta);
+  p.err = err.data_ptr<int>();
+  const int tiles = va.batch * ((M + 127) / 128) * ((N + 255) / 256);
+  if (tiles == 0) return;
+  dispatch(a_mn, b_mn, kBSingle, kEpiAxpbyBF16, ma, mb, mb, p, std::min<int>(tiles, num_sms(a.get_device())),
+           at::cuda::getCurrentCUDAStream());
 }
 
 // Grouped GEMM driven by a device-side problem table (MoE).
@@ -351,6 +386,7 @@ bool gemm_launch_group3(int, const CUtensorMap&, const CUtensorMap&, const CUten
 bool gemm_launch_group4(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group5(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group6(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group7(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 
 void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
                          const GemmParams& p, int grid, cudaStream_t stream) {
@@ -360,7 +396,8 @@ void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& 
                   gemm_launch_group3(variant, ma, mb0, mb1, p, grid, stream) ||
                   gemm_launch_group4(variant, ma, mb0, mb1, p, grid, stream) ||
                   gemm_launch_group5(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group6(variant, ma, mb0, mb1, p, grid, stream);
+                  gemm_launch_group6(variant, ma, mb0, mb1, p, grid, stream) ||
+                  gemm_launch_group7(variant, ma, mb0, mb1, p, grid, stream);
   TORCH_CHECK(ok, "GEMM variant not instantiated");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

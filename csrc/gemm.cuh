@@ -38,7 +38,8 @@ struct GemmProblem {
 };
 
 enum BMode : int { kBSingle = 0, kBSplitN = 1, kBSplitK = 2 };
-enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiSwiGLU = 3, kEpiRowScaleBF16 = 4 };
+// kEpiAxpbyBF16: D = alpha * acc + beta * C with C (bf16) laid out exactly like D (pointer `aux`).
+enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiSwiGLU = 3, kEpiRowScaleBF16 = 4, kEpiAxpbyBF16 = 5 };
 
 struct GemmParams {
   const GemmProblem* probs;   // device table or nullptr (single mode)
@@ -48,7 +49,7 @@ struct GemmParams {
   void* d;
   void* aux;                  // SwiGLU pre-activations (bf16)
   const float* rowscale;      // kEpiRowScaleBF16
-  float alpha;
+  float alpha, beta;
   float gate_max, lin_lo, lin_hi;
   int ksplit;                 // kBSplitK: K index where B switches from map 0 to map 1
   int* err;
@@ -302,7 +303,26 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = zero_k ? 0.f : __uint_as_float(r[j]) * P.alpha * rs;
           const bool full_chunk = col0 + 32 <= pr.n;
-          if constexpr (EPI == kEpiBF16 || EPI == kEpiRowScaleBF16) {
+          if constexpr (EPI == kEpiAxpbyBF16) {
+            const __nv_bfloat16* cin = reinterpret_cast<const __nv_bfloat16*>(P.aux) + dbase + col0;
+            if (full_chunk && ((reinterpret_cast<uintptr_t>(cin) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                const uint4 cv = *reinterpret_cast<const uint4*>(cin + j);
+                const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&cv);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float2 f = __bfloat1622float2(ch[q]);
+                  v[j + 2 * q] += P.beta * f.x;
+                  v[j + 2 * q + 1] += P.beta * f.y;
+                }
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
+            }
+          }
+          if constexpr (EPI == kEpiBF16 || EPI == kEpiRowScaleBF16 || EPI == kEpiAxpbyBF16) {
             __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d) + dbase + col0;
             if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
 #pragma unroll

@@ -102,6 +102,21 @@ def gemm_nt(a: Tensor, b: Tensor, *, out: Tensor | None = None, out_dtype: torch
     return out
 
 
+def gemm_axpby(a: Tensor, b: Tensor, c: Tensor, *, alpha: float = 1.0, beta: float = 1.0) -> Tensor:
+    """``alpha * a @ b^T + beta * c`` in one GEMM pass (bf16 in/out, fp32 accumulation)."""
+    a, b = a.to(torch.bfloat16), b.to(torch.bfloat16)
+    k = a.shape[-1]
+    if k % 64:
+        pad = 64 - k % 64
+        a, b = F.pad(a, (0, pad)), F.pad(b, (0, pad))
+    c = c.to(torch.bfloat16).contiguous()
+    out = torch.empty_like(c)
+    av, a_mn = _as_operand(a)
+    bv, b_mn = _as_operand(b)
+    backend.ext().gemm_axpby(av, bv, c, out, a_mn, b_mn, float(alpha), float(beta), error_word(a.device))
+    return out
+
+
 def matmul(a: Tensor, b: Tensor, *, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
     """``a @ b`` for (.., M, K) x (.., K, N)."""
     return gemm_nt(a, b.transpose(-1, -2), out_dtype=out_dtype)
@@ -127,4 +142,4 @@ def grouped_mm(a: Tensor, b: Tensor, offsets: Tensor) -> Tensor:
     return out.to(a.dtype)
 
 
-__all__ = ["bmm", "check_errors", "error_word", "gemm_nt", "grouped_mm", "matmul"]
+__all__ = ["bmm", "check_errors", "error_word", "gemm_axpby", "gemm_nt", "grouped_mm", "matmul"]

@@ -144,8 +144,13 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
         st = opt.state[p]
         if "momentum_buffer" not in st:
             st["momentum_buffer"] = torch.zeros_like(p)
-        st["momentum_buffer"].mul_(mu).add_(g.to(st["momentum_buffer"].dtype))
+        if impl != "native":
+            st["momentum_buffer"].mul_(mu).add_(g.to(st["momentum_buffer"].dtype))
         by_shape.setdefault((*p.shape[-2:], str(p.device)), []).append(p)
+    if impl == "native":
+        for params in by_shape.values():
+            _native_chunks(opt, params, group, chunk_elems)
+        return
     for params in by_shape.values():
         # bounded working set: orthogonalise at most ~chunk_elems elements at a time
         chunk: list[Tensor] = []
@@ -161,11 +166,53 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
                 chunk, size = [], 0
 
 
+@torch.no_grad()
+def _native_chunks(opt: torch.optim.Optimizer, params: list[Tensor], group: dict[str, Any], chunk_elems: int) -> None:
+    """CUDA Muon for same-shaped matrices: fused momentum / normalise / apply kernels around
+    the epilogue-fused batched Newton-Schulz (the momentum update happens here)."""
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.optim.newton_schulz import native_newton_schulz
+
+    ext = backend.ext()
+    lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
+    n, k = params[0].shape[-2:]
+    slice_ = n * k
+    i = 0
+    while i < len(params):
+        chunk, total = [], 0
+        while i < len(params) and (not chunk or total + params[i].numel() <= chunk_elems):
+            chunk.append(params[i])
+            total += params[i].numel()
+            i += 1
+        y = torch.empty(total // slice_, n, k, dtype=torch.bfloat16, device=chunk[0].device)
+        off = 0
+        for q in chunk:
+            cnt = q.numel() // slice_
+            st = opt.state[q]
+            g = _grad(q).float().contiguous()
+            sumsq = torch.empty(cnt, dtype=torch.float32, device=q.device)
+            ext.muon_momentum(st["momentum_buffer"], g, sumsq, slice_, float(mu))
+            ext.muon_normalize(st["momentum_buffer"], g, sumsq, y[off:off + cnt], slice_, float(mu), 1.0e-7)
+            off += cnt
+        y = native_newton_schulz(y, group["ns_iter_stage1"], group["ns_iter_stage2"],
+                                 tuple(group["ns_coeffs_stage1"]), tuple(group["ns_coeffs_stage2"]))
+        off = 0
+        scale = math.sqrt(max(n, k)) * gamma
+        for q in chunk:
+            cnt = q.numel() // slice_
+            ext.muon_apply(q.data, y[off:off + cnt].contiguous(), 1.0 - lr * wd, lr * scale)
+            off += cnt
+
+
 def _resolve_impl(impl: str, params: Iterable[Tensor]) -> str:
     if impl != "auto":
         return impl
     for p in params:
-        return "batched_bf16" if p.is_cuda else "reference"
+        if p.is_cuda:
+            from saint_llm_b200.ops import backend
+
+            return "native" if backend.native_for(p) else "batched_bf16"
+        return "reference"
     return "reference"
 
 

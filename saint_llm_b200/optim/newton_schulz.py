@@ -81,4 +81,31 @@ def batched_newton_schulz(x: Tensor, n_iter_stage1: int = 8, n_iter_stage2: int 
     return y.reshape(*lead, n, m).to(dtype)
 
 
-__all__ = ["STAGE1", "STAGE2", "batched_newton_schulz", "hybrid_newton_schulz"]
+def native_newton_schulz(y: Tensor, n_iter_stage1: int = 8, n_iter_stage2: int = 2,
+                         coeffs_stage1: tuple[float, float, float] = STAGE1,
+                         coeffs_stage2: tuple[float, float, float] = STAGE2) -> Tensor:
+    """Newton-Schulz on already-normalised bf16 matrices (B, r, c), three fused GEMMs per step.
+
+    Wide (r <= c):  G = Y Y^T ;  P = c G G + b G ;  Y <- P Y + a Y
+    Tall (r > c):   G = Y^T Y ;  P = c G G + b G ;  Y <- Y P + a Y
+    The "+ b G" and "+ a Y" terms ride in the GEMM epilogue (no element-wise passes),
+    and neither orientation needs a transpose copy: the tensor cores read Y^T directly.
+    """
+    from saint_llm_b200.ops import gemm
+
+    wide = y.shape[-2] <= y.shape[-1]
+    for steps, (a, b, c) in ((n_iter_stage1, coeffs_stage1), (n_iter_stage2, coeffs_stage2)):
+        for _ in range(steps):
+            if wide:
+                g = gemm.gemm_nt(y, y)
+                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b)
+                y = gemm.gemm_axpby(p, y.transpose(-1, -2), y, alpha=1.0, beta=a)
+            else:
+                yt = y.transpose(-1, -2)
+                g = gemm.gemm_nt(yt, yt)
+                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b)
+                y = gemm.gemm_axpby(y, p, y, alpha=1.0, beta=a)
+    return y
+
+
+__all__ = ["STAGE1", "STAGE2", "batched_newton_schulz", "hybrid_newton_schulz", "native_newton_schulz"]

@@ -230,3 +230,52 @@ def test_smoke_entry(cuda):
     import __graft_entry__
 
     __graft_entry__.smoke()
+
+
+def test_gemm_axpby(cuda):
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(0)
+    a = torch.randn(3, 192, 320, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(3, 256, 320, device=cuda, dtype=torch.bfloat16)
+    c = torch.randn(3, 192, 256, device=cuda, dtype=torch.bfloat16)
+    out = gemm.gemm_axpby(a, b, c, alpha=0.5, beta=-2.0)
+    want = 0.5 * (a.float() @ b.float().transpose(-1, -2)) - 2.0 * c.float()
+    assert _rel(out, want) < 1e-2
+    out2 = gemm.gemm_axpby(a, c.transpose(-1, -2)[:, :, :320] if False else b, c, alpha=1.0, beta=0.0)
+    assert _rel(out2, a.float() @ b.float().transpose(-1, -2)) < 1e-2
+
+
+@pytest.mark.parametrize("shape", [(3, 256, 512), (2, 512, 256), (4, 1408, 2048), (1, 16, 8192)])
+def test_native_newton_schulz(cuda, shape):
+    from saint_llm_b200.optim.newton_schulz import hybrid_newton_schulz, native_newton_schulz
+
+    torch.manual_seed(0)
+    g = torch.randn(*shape, device=cuda)
+    y = (g / (g.norm(dim=(-2, -1), keepdim=True) + 1e-7)).to(torch.bfloat16)
+    got = native_newton_schulz(y).float()
+    want = torch.stack([hybrid_newton_schulz(m) for m in g])
+    # bf16 Newton-Schulz: compare directions of the orthogonalised update
+    cos = F.cosine_similarity(got.flatten(1), want.flatten(1), dim=1)
+    assert (cos > 0.97).all(), cos
+
+
+def test_native_muon_step_matches_reference_direction(cuda):
+    from saint_llm_b200.optim import Muon
+
+    torch.manual_seed(0)
+    w0 = torch.randn(2, 384, 256, device=cuda) * 0.02
+    grads = [torch.randn(2, 384, 256, device=cuda) for _ in range(2)]
+    a = torch.nn.Parameter(w0.clone())
+    b = torch.nn.Parameter(w0.clone().to(torch.bfloat16))
+    b.main_grad = torch.zeros(2, 384, 256, device=cuda)
+    oa = Muon([a], lr=0.02, ns_impl="reference")
+    ob = Muon([b], lr=0.02)
+    for g in grads:
+        a.grad = g.clone()
+        b.main_grad.copy_(g)
+        oa.step()
+        ob.step()
+    da, db = (a.detach() - w0).flatten(1), (b.detach().float() - w0).flatten(1)
+    assert (F.cosine_similarity(da, db, dim=1) > 0.97).all()
+    assert abs(da.norm().item() / db.norm().item() - 1) < 0.05

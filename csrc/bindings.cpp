@@ -40,9 +40,10 @@ void rope_norm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor cosb, torch::
 torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor cosb,
                             torch::Tensor sinb, torch::Tensor rstd, torch::Tensor dx, int64_t heads, int64_t rd,
                             bool norm_first);
-void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor p, torch::Tensor r, double eps);
-void mhc_gates_fwd(torch::Tensor p, torch::Tensor alpha, torch::Tensor s_pre, torch::Tensor s_res,
-                   torch::Tensor s_post, torch::Tensor a, torch::Tensor b, torch::Tensor c, int64_t n, int64_t iters);
+void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor q, torch::Tensor ssq);
+void mhc_gates_fwd(torch::Tensor p, torch::Tensor ssq, torch::Tensor r, int64_t F, double eps, torch::Tensor alpha,
+                   torch::Tensor s_pre, torch::Tensor s_res, torch::Tensor s_post, torch::Tensor a, torch::Tensor b,
+                   torch::Tensor c, int64_t n, int64_t iters);
 void mhc_gates_bwd(torch::Tensor p, torch::Tensor alpha, torch::Tensor s_pre, torch::Tensor s_res,
                    torch::Tensor s_post, torch::Tensor da, torch::Tensor db, torch::Tensor dc, torch::Tensor dz,
                    int64_t n, int64_t iters);
@@ -53,10 +54,13 @@ void mhc_combine_bwd(torch::Tensor dY, torch::Tensor X, torch::Tensor o, torch::
 void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t n);
 void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
+// data.cpp
+void bind_data(pybind11::module_& m);
 }  // namespace sv4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "saint_llm_b200 sm_100a kernels";
+  sv4::bind_data(m);
   m.def("gemm", &sv4::gemm);
   m.def("grouped_gemm", &sv4::grouped_gemm);
   m.def("build_moe_problems", &sv4::build_moe_problems);

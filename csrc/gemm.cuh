@@ -275,17 +275,46 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           const int col0 = nt * half + c;
           if (row_ok) {
             const long long pbase = pr.aux_off + row * pr.aux_ld;
+            float av[32], gv[32], uv[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = col0 + j;
-              if (col < pr.n) {
-                const float gv = zero_k ? 0.f : __uint_as_float(g[j]);
-                const float uv = zero_k ? 0.f : __uint_as_float(u[j]);
-                const float gc = fminf(gv, P.gate_max);
-                const float uc = fminf(fmaxf(uv, P.lin_lo), P.lin_hi);
-                out[dbase + col] = __float2bfloat16(silu_f(gc) * uc);
-                pre[pbase + col] = __float2bfloat16(gv);
-                pre[pbase + pr.n + col] = __float2bfloat16(uv);
+            for (int q = 0; q < 32; ++q) {
+              gv[q] = zero_k ? 0.f : __uint_as_float(g[q]);
+              uv[q] = zero_k ? 0.f : __uint_as_float(u[q]);
+              av[q] = silu_f(fminf(gv[q], P.gate_max)) * fminf(fmaxf(uv[q], P.lin_lo), P.lin_hi);
+            }
+            __nv_bfloat16* o_act = out + dbase + col0;
+            __nv_bfloat16* o_g = pre + pbase + col0;
+            __nv_bfloat16* o_u = pre + pbase + pr.n + col0;
+            const bool vec = col0 + 32 <= pr.n &&
+                             ((reinterpret_cast<uintptr_t>(o_act) | reinterpret_cast<uintptr_t>(o_g) |
+                               reinterpret_cast<uintptr_t>(o_u)) & 15) == 0;
+            if (vec) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 8) {
+                uint4 pa, pg, pu;
+                uint32_t* wa = reinterpret_cast<uint32_t*>(&pa);
+                uint32_t* wg = reinterpret_cast<uint32_t*>(&pg);
+                uint32_t* wu = reinterpret_cast<uint32_t*>(&pu);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  __nv_bfloat162 ta = __floats2bfloat162_rn(av[q + 2 * h], av[q + 2 * h + 1]);
+                  __nv_bfloat162 tg = __floats2bfloat162_rn(gv[q + 2 * h], gv[q + 2 * h + 1]);
+                  __nv_bfloat162 tu = __floats2bfloat162_rn(uv[q + 2 * h], uv[q + 2 * h + 1]);
+                  wa[h] = *reinterpret_cast<uint32_t*>(&ta);
+                  wg[h] = *reinterpret_cast<uint32_t*>(&tg);
+                  wu[h] = *reinterpret_cast<uint32_t*>(&tu);
+                }
+                *reinterpret_cast<uint4*>(o_act + q) = pa;
+                *reinterpret_cast<uint4*>(o_g + q) = pg;
+                *reinterpret_cast<uint4*>(o_u + q) = pu;
+              }
+            } else {
+              for (int q = 0; q < 32; ++q) {
+                if (col0 + q < pr.n) {
+                  o_act[q] = __float2bfloat16(av[q]);
+                  o_g[q] = __float2bfloat16(gv[q]);
+                  o_u[q] = __float2bfloat16(uv[q]);
+                }
               }
             }
           }

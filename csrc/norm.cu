@@ -273,25 +273,29 @@ torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 
 // ---------------------------------------------------------------------- mHC
 // Stream X: (T, F) with F = n*D.  W: (P, F) fp32 gate projections with the RMSNorm weight
-// folded in (P = 2n + n^2).  Outputs p (T, P) = r * X W^T and r (T).
+// folded in (P = 2n + n^2).  Pass 1 (this kernel) accumulates the raw dots q = X W^T and the
+// row sums of squares into zero-initialised fp32 buffers; grid = (T/32, F-splits) so the
+// whole GPU participates.  The gates kernel turns them into r = 1/rms and p = r q.
 constexpr int kMhcTok = 32;    // tokens per CTA
 constexpr int kMhcChunk = 256; // K chunk
+constexpr int kMhcSplit = 1024; // features per CTA along F
 __global__ void mhc_proj_fwd_kernel(const __nv_bfloat16* __restrict__ X, const float* __restrict__ W,
-                                    float* __restrict__ p, float* __restrict__ r_out, int T, int F, int P,
-                                    float eps) {
+                                    float* __restrict__ q, float* __restrict__ ssq_out, int T, int F, int P) {
   extern __shared__ float sm[];
   constexpr int LD = kMhcChunk + 1;  // odd stride: no bank conflicts
   float* sw = sm;                    // P x LD
   float* sx = sm + P * LD;           // tok x LD
   __shared__ float ssq[kMhcTok];
   const int t0 = blockIdx.x * kMhcTok;
+  const int f_begin = blockIdx.y * kMhcSplit;
+  const int f_end = min(F, f_begin + kMhcSplit);
   const int n_out = kMhcTok * P;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   if (threadIdx.x < kMhcTok) ssq[threadIdx.x] = 0.f;
   float my_ss = 0.f;
-  for (int k0 = 0; k0 < F; k0 += kMhcChunk) {
+  for (int k0 = f_begin; k0 < f_end; k0 += kMhcChunk) {
     __syncthreads();
     for (int i = threadIdx.x; i < P * kMhcChunk; i += blockDim.x) {
       const int j = i / kMhcChunk, kk = i % kMhcChunk;
@@ -302,7 +306,7 @@ __global__ void mhc_proj_fwd_kernel(const __nv_bfloat16* __restrict__ X, const f
       float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       if (t0 + tt < T) load8(X + static_cast<int64_t>(t0 + tt) * F + k0 + kk, f);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) sx[tt * LD + kk + q] = f[q];
+      for (int qq = 0; qq < 8; ++qq) sx[tt * LD + kk + qq] = f[qq];
     }
     __syncthreads();
     {
@@ -321,10 +325,10 @@ __global__ void mhc_proj_fwd_kernel(const __nv_bfloat16* __restrict__ X, const f
         const int tt = o / P, j = o % P;
         const float* xs = sx + tt * LD;
         const float* ws = sw + j * LD;
-        float s = 0.f;
+        float s2 = 0.f;
 #pragma unroll 8
-        for (int kk = 0; kk < kMhcChunk; ++kk) s += xs[kk] * ws[kk];
-        acc[i] += s;
+        for (int kk = 0; kk < kMhcChunk; ++kk) s2 += xs[kk] * ws[kk];
+        acc[i] += s2;
       }
     }
   }
@@ -335,25 +339,26 @@ __global__ void mhc_proj_fwd_kernel(const __nv_bfloat16* __restrict__ X, const f
     const int o = threadIdx.x + i * blockDim.x;
     if (o < n_out) {
       const int tt = o / P, j = o % P;
-      if (t0 + tt < T) {
-        const float r = rsqrtf(ssq[tt] / F + eps);
-        p[static_cast<int64_t>(t0 + tt) * P + j] = acc[i] * r;
-        if (j == 0) r_out[t0 + tt] = r;
-      }
+      if (t0 + tt < T) atomicAdd(&q[static_cast<int64_t>(t0 + tt) * P + j], acc[i]);
     }
   }
+  if (threadIdx.x < kMhcTok && t0 + threadIdx.x < T) atomicAdd(&ssq_out[t0 + threadIdx.x], ssq[threadIdx.x]);
 }
 
-void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor p, torch::Tensor r, double eps) {
+// q (T, P) raw dots and ssq (T) are accumulated here; p = q * r and r are finalised by the gates kernel.
+void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor q, torch::Tensor ssq) {
   c10::cuda::CUDAGuard guard(X.device());
   const int T = X.size(0), F = X.size(1), P = W.size(0);
   TORCH_CHECK(F % kMhcChunk == 0 && P * kMhcTok <= 8 * 256, "mhc_proj shape");
+  q.zero_();
+  ssq.zero_();
   if (T == 0) return;
   const size_t smem = (P + kMhcTok) * (kMhcChunk + 1) * sizeof(float);
   cudaFuncSetAttribute(mhc_proj_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  mhc_proj_fwd_kernel<<<(T + kMhcTok - 1) / kMhcTok, 256, smem, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), W.data_ptr<float>(), p.data_ptr<float>(),
-      r.data_ptr<float>(), T, F, P, static_cast<float>(eps));
+  dim3 grid((T + kMhcTok - 1) / kMhcTok, (F + kMhcSplit - 1) / kMhcSplit);
+  mhc_proj_fwd_kernel<<<grid, 256, smem, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), W.data_ptr<float>(), q.data_ptr<float>(),
+      ssq.data_ptr<float>(), T, F, P);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -405,14 +410,19 @@ __device__ __forceinline__ void sinkhorn_fwd(float (&m)[N][N], int iters, float 
 }
 
 template <int N>
-__global__ void mhc_gates_fwd_kernel(const float* __restrict__ p, const float* __restrict__ alpha,
-                                     const float* __restrict__ s_pre, const float* __restrict__ s_res,
-                                     const float* __restrict__ s_post, float* __restrict__ a, float* __restrict__ b,
-                                     float* __restrict__ c, int T, int iters) {
+__global__ void mhc_gates_fwd_kernel(float* __restrict__ p, const float* __restrict__ ssq, float* __restrict__ r_out,
+                                     const float* __restrict__ alpha, const float* __restrict__ s_pre,
+                                     const float* __restrict__ s_res, const float* __restrict__ s_post,
+                                     float* __restrict__ a, float* __restrict__ b, float* __restrict__ c, int T,
+                                     int iters, float inv_f, float eps) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   constexpr int P = 2 * N + N * N;
-  const float* pr = p + static_cast<int64_t>(t) * P;
+  float* pr = p + static_cast<int64_t>(t) * P;
+  const float r = rsqrtf(ssq[t] * inv_f + eps);
+  r_out[t] = r;
+#pragma unroll
+  for (int j = 0; j < P; ++j) pr[j] *= r;
   const float ap = alpha[0], ar = alpha[1], ac = alpha[2];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
@@ -515,16 +525,18 @@ __global__ void mhc_gates_bwd_kernel(const float* __restrict__ p, const float* _
     default: TORCH_CHECK(false, "mHC expansion factor must be 1..4");                          \
   }
 
-void mhc_gates_fwd(torch::Tensor p, torch::Tensor alpha, torch::Tensor s_pre, torch::Tensor s_res,
-                   torch::Tensor s_post, torch::Tensor a, torch::Tensor b, torch::Tensor c, int64_t n,
-                   int64_t iters) {
+// p: raw dots in, p = r * dots out (in place); ssq: row sums of squares; r: 1/rms out.
+void mhc_gates_fwd(torch::Tensor p, torch::Tensor ssq, torch::Tensor r, int64_t F, double eps, torch::Tensor alpha,
+                   torch::Tensor s_pre, torch::Tensor s_res, torch::Tensor s_post, torch::Tensor a, torch::Tensor b,
+                   torch::Tensor c, int64_t n, int64_t iters) {
   c10::cuda::CUDAGuard guard(p.device());
   const int T = p.size(0);
   if (T == 0) return;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  SV4_MHC_N(n, (T + 127) / 128, mhc_gates_fwd_kernel, p.data_ptr<float>(), alpha.data_ptr<float>(),
-            s_pre.data_ptr<float>(), s_res.data_ptr<float>(), s_post.data_ptr<float>(), a.data_ptr<float>(),
-            b.data_ptr<float>(), c.data_ptr<float>(), T, static_cast<int>(iters));
+  SV4_MHC_N(n, (T + 127) / 128, mhc_gates_fwd_kernel, p.data_ptr<float>(), ssq.data_ptr<float>(),
+            r.data_ptr<float>(), alpha.data_ptr<float>(), s_pre.data_ptr<float>(), s_res.data_ptr<float>(),
+            s_post.data_ptr<float>(), a.data_ptr<float>(), b.data_ptr<float>(), c.data_ptr<float>(), T,
+            static_cast<int>(iters), 1.0f / static_cast<float>(F), static_cast<float>(eps));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -742,7 +754,7 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
     scoef[threadIdx.x][1] = rr * rr * rr / F * s;
   }
   __syncthreads();
-  for (int f0 = threadIdx.x * 4; f0 < F; f0 += blockDim.x * 4) {
+  for (int f0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; f0 < F; f0 += gridDim.y * blockDim.x * 4) {
     float wv[P][4];
 #pragma unroll
     for (int j = 0; j < P; ++j) {
@@ -840,7 +852,8 @@ void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::
   TORCH_CHECK(D % 4 == 0, "mhc_split_bwd: D % 4 == 0");
   if (T == 0) return;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  SV4_MHC_N(n, (T + kMhcTok - 1) / kMhcTok, mhc_split_bwd_kernel, reinterpret_cast<__nv_bfloat16*>(dX.data_ptr()),
+  const dim3 grid((T + kMhcTok - 1) / kMhcTok, std::max(1, (static_cast<int>(n) * D) / 512));
+  SV4_MHC_N(n, grid, mhc_split_bwd_kernel, reinterpret_cast<__nv_bfloat16*>(dX.data_ptr()),
             reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()),
             reinterpret_cast<const __nv_bfloat16*>(din.data_ptr()), a.data_ptr<float>(), dp.data_ptr<float>(),
             p.data_ptr<float>(), r.data_ptr<float>(), W.data_ptr<float>(), T, D);

@@ -33,15 +33,16 @@ class _SplitFn(torch.autograd.Function):
         ext = backend.ext()
         dev = X.device
         p = torch.empty(T, P, dtype=torch.float32, device=dev)
+        ssq = torch.empty(T, dtype=torch.float32, device=dev)
         r = torch.empty(T, dtype=torch.float32, device=dev)
         wf = w_fold.float().contiguous()
-        ext.mhc_proj_fwd(Xf, wf, p, r, float(eps))
+        ext.mhc_proj_fwd(Xf, wf, p, ssq)
         al = alpha.float().contiguous()
         sp, sr, so = s_pre.float().contiguous(), s_res.float().contiguous(), s_post.float().contiguous()
         a = torch.empty(T, n, dtype=torch.float32, device=dev)
         bm = torch.empty(T, n, n, dtype=torch.float32, device=dev)
         c = torch.empty(T, n, dtype=torch.float32, device=dev)
-        ext.mhc_gates_fwd(p, al, sp, sr, so, a, bm, c, n, iters)
+        ext.mhc_gates_fwd(p, ssq, r, n * d, float(eps), al, sp, sr, so, a, bm, c, n, iters)
         inner = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
         ext.mhc_premix(Xf, a, inner, n)
         ctx.save_for_backward(Xf, wf, al, sp, sr, so, p, r, a)

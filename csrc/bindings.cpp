@@ -40,7 +40,7 @@ void rope_norm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor cosb, torch::
 torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor cosb,
                             torch::Tensor sinb, torch::Tensor rstd, torch::Tensor dx, int64_t heads, int64_t rd,
                             bool norm_first);
-void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor q, torch::Tensor ssq);
+void row_sumsq(torch::Tensor X, torch::Tensor ssq);
 void mhc_gates_fwd(torch::Tensor p, torch::Tensor ssq, torch::Tensor r, int64_t F, double eps, torch::Tensor alpha,
                    torch::Tensor s_pre, torch::Tensor s_res, torch::Tensor s_post, torch::Tensor a, torch::Tensor b,
                    torch::Tensor c, int64_t n, int64_t iters);
@@ -81,7 +81,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &sv4::rmsnorm_bwd);
   m.def("rope_norm_fwd", &sv4::rope_norm_fwd);
   m.def("rope_norm_bwd", &sv4::rope_norm_bwd);
-  m.def("mhc_proj_fwd", &sv4::mhc_proj_fwd);
+  m.def("row_sumsq", &sv4::row_sumsq);
   m.def("mhc_gates_fwd", &sv4::mhc_gates_fwd);
   m.def("mhc_gates_bwd", &sv4::mhc_gates_bwd);
   m.def("mhc_premix", &sv4::mhc_premix);

@@ -81,6 +81,19 @@ static CUtensorMap map_for(const OperandView& v, uint32_t box_outer) {
                      v.batch_stride * 2, 64, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Map for writing D with TMA: 3-D (cols, rows, batch), box = 128 bytes x 32 rows, 128B swizzle.
+// Returns false (and leaves `m` unset) when the layout cannot be a TMA destination.
+static bool map_d_for(const void* base, bool f32, int64_t cols, int64_t rows, int64_t batch, int64_t ld,
+                      int64_t bstride, CUtensorMap& m) {
+  const int eb = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * eb) % 16 != 0 || cols <= 0 || rows <= 0) return false;
+  if (batch > 1 && (bstride * eb) % 16 != 0) return false;
+  const int64_t bs = batch > 1 ? bstride : rows * ld;
+  m = make_map_3d(base, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, eb, cols, rows,
+                  batch, ld * eb, bs * eb, 128 / eb, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  return true;
+}
+
 static int num_sms(int dev) {
   static int cached[64] = {0};
   if (cached[dev] == 0) {
@@ -91,10 +104,11 @@ static int num_sms(int dev) {
 
 // Kernel instantiations live in gemm_inst_*.cu (compiled in parallel).
 void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
-                         const GemmParams& p, int grid, cudaStream_t stream);
+                         const CUtensorMap& md, const GemmParams& p, int grid, cudaStream_t stream);
 
 static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap& ma, const CUtensorMap& mb0,
-                     const CUtensorMap& mb1, const GemmParams& p, int grid, cudaStream_t stream) {
+                     const CUtensorMap& mb1, const CUtensorMap& md, const GemmParams& p, int grid,
+                     cudaStream_t stream) {
   struct V { bool a, b; int bm, ep; };
   static const V table[] = {
       {false, false, kBSingle, kEpiBF16},
@@ -118,7 +132,7 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
   for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
     const V& v = table[i];
     if (v.a == a_mn && v.b == b_mn && v.bm == bmode && v.ep == epi) {
-      gemm_launch_variant(i, ma, mb0, mb1, p, grid, stream);
+      gemm_launch_variant(i, ma, mb0, mb1, md, p, grid, stream);
       return;
     }
   }
@@ -173,10 +187,33 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
     TORCH_CHECK(out.scalar_type() == at::kFloat, "output must be bf16 or fp32");
     epi = accumulate ? kEpiF32Acc : kEpiF32;
   }
-  const int tiles = batch * ((M + 127) / 128) * ((N + 255) / 256);
+  int tiles = batch * ((M + 127) / 128) * ((N + 255) / 256);
   if (tiles == 0) return;
-  const int grid = std::min<int>(tiles, num_sms(a.get_device()));
-  dispatch(a_mn, b_mn, kBSingle, epi, ma, mb, mb, p, grid, at::cuda::getCurrentCUDAStream());
+  CUtensorMap md = ma;
+  p.tma_d = map_d_for(out.data_ptr(), epi != kEpiBF16, N, M, batch, s.d_ld, s.d_bstride, md) ? 1 : 0;
+  const int sms = num_sms(a.get_device());
+  p.splitk = 1;
+  p.kc = static_cast<int>(K);
+  // Few output tiles and a long K (weight gradients of small layers, skinny projections):
+  // split K across SMs; every slice reduce-adds its partial tile into the fp32 output.
+  if (batch == 1 && epi != kEpiBF16 && p.tma_d && tiles * 2 <= sms && K >= 1024) {
+    int S = static_cast<int>(std::min<int64_t>(sms / tiles, K / 512));
+    if (S > 1) {
+      const int64_t kc = ((K + S - 1) / S + 63) / 64 * 64;
+      S = static_cast<int>((K + kc - 1) / kc);
+      if (S > 1) {
+        if (epi == kEpiF32) {
+          out.zero_();
+          epi = kEpiF32Acc;
+        }
+        p.splitk = S;
+        p.kc = static_cast<int>(kc);
+        tiles *= S;
+      }
+    }
+  }
+  const int grid = std::min<int>(tiles, sms);
+  dispatch(a_mn, b_mn, kBSingle, epi, ma, mb, mb, md, p, grid, at::cuda::getCurrentCUDAStream());
 }
 
 // out = alpha * (A B^T) + beta * C, bf16 out and bf16 C with identical layout to out
@@ -208,7 +245,9 @@ void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor
   p.err = err.data_ptr<int>();
   const int tiles = va.batch * ((M + 127) / 128) * ((N + 255) / 256);
   if (tiles == 0) return;
-  dispatch(a_mn, b_mn, kBSingle, kEpiAxpbyBF16, ma, mb, mb, p, std::min<int>(tiles, num_sms(a.get_device())),
+  CUtensorMap md = ma;
+  p.tma_d = map_d_for(out.data_ptr(), false, N, M, va.batch, s.d_ld, s.d_bstride, md) ? 1 : 0;
+  dispatch(a_mn, b_mn, kBSingle, kEpiAxpbyBF16, ma, mb, mb, md, p, std::min<int>(tiles, num_sms(a.get_device())),
            at::cuda::getCurrentCUDAStream());
 }
 
@@ -241,30 +280,37 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
   p.err = err.data_ptr<int>();
   const int grid = num_sms(a.get_device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  // D as one (rows, cols) row-major buffer; problems address it by row (d_off is a multiple of d_ld).
+  CUtensorMap md = map_for(va, 128);  // placeholder when D is not TMA-addressable
+  if (mode != 0 && out.is_contiguous() && out.numel() > 0) {
+    const int64_t cols = out.size(-1);
+    p.tma_d = map_d_for(out.data_ptr(), out.scalar_type() == at::kFloat, cols, out.numel() / cols, 1, cols, 0, md)
+                  ? 1 : 0;
+  }
   switch (mode) {
     case 0: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 128), m1 = map_for(vb1, 128);
-      dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, p, grid, stream);
+      dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, md, p, grid, stream);
       break;
     }
     case 1: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 256);
-      dispatch(false, false, kBSingle, p.rowscale ? kEpiRowScaleBF16 : kEpiBF16, ma, m0, m0, p, grid, stream);
+      dispatch(false, false, kBSingle, p.rowscale ? kEpiRowScaleBF16 : kEpiBF16, ma, m0, m0, md, p, grid, stream);
       break;
     }
     case 2: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 64);
-      dispatch(false, true, kBSingle, kEpiBF16, ma, m0, m0, p, grid, stream);
+      dispatch(false, true, kBSingle, kEpiBF16, ma, m0, m0, md, p, grid, stream);
       break;
     }
     case 3: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 64), m1 = map_for(vb1, 64);
-      dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, p, grid, stream);
+      dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, md, p, grid, stream);
       break;
     }
     case 4: {
       CUtensorMap ma = map_for(va, 64), m0 = map_for(vb0, 64);
-      dispatch(true, true, kBSingle, accumulate ? kEpiF32Acc : kEpiF32, ma, m0, m0, p, grid, stream);
+      dispatch(true, true, kBSingle, accumulate ? kEpiF32Acc : kEpiF32, ma, m0, m0, md, p, grid, stream);
       break;
     }
     default:
@@ -290,7 +336,7 @@ void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Te
   p.err = err.data_ptr<int>();
   const int tiles = ((M + 127) / 128) * ((I + 127) / 128);
   if (tiles == 0) return;
-  dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, p, std::min<int>(tiles, num_sms(x.get_device())),
+  dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, ma, p, std::min<int>(tiles, num_sms(x.get_device())),
            at::cuda::getCurrentCUDAStream());
 }
 
@@ -308,7 +354,9 @@ void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, 
   p.d = dx.data_ptr(); p.alpha = 1.f; p.ksplit = I; p.err = err.data_ptr<int>();
   const int tiles = ((M + 127) / 128) * ((D + 255) / 256);
   if (tiles == 0) return;
-  dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, p, std::min<int>(tiles, num_sms(dpre.get_device())),
+  CUtensorMap md = ma;
+  p.tma_d = map_d_for(dx.data_ptr(), false, D, M, 1, s.d_ld, 0, md) ? 1 : 0;
+  dispatch(false, true, kBSplitK, kEpiBF16, ma, m0, m1, md, p, std::min<int>(tiles, num_sms(dpre.get_device())),
            at::cuda::getCurrentCUDAStream());
 }
 
@@ -379,25 +427,33 @@ void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t
 
 int64_t problem_bytes() { return sizeof(GemmProblem); }
 
-bool gemm_launch_group0(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group1(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group2(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group3(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group4(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group5(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group6(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
-bool gemm_launch_group7(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group0(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group1(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group2(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group3(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group4(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group5(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group6(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
+bool gemm_launch_group7(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, int, cudaStream_t);
 
 void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
-                         const GemmParams& p, int grid, cudaStream_t stream) {
-  const bool ok = gemm_launch_group0(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group1(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group2(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group3(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group4(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group5(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group6(variant, ma, mb0, mb1, p, grid, stream) ||
-                  gemm_launch_group7(variant, ma, mb0, mb1, p, grid, stream);
+                         const CUtensorMap& md, const GemmParams& p, int grid, cudaStream_t stream) {
+  const bool ok = gemm_launch_group0(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group1(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group2(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group3(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group4(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group5(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group6(variant, ma, mb0, mb1, md, p, grid, stream) ||
+                  gemm_launch_group7(variant, ma, mb0, mb1, md, p, grid, stream);
   TORCH_CHECK(ok, "GEMM variant not instantiated");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

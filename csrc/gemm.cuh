@@ -52,11 +52,18 @@ struct GemmParams {
   float alpha, beta;
   float gate_max, lin_lo, lin_hi;
   int ksplit;                 // kBSplitK: K index where B switches from map 0 to map 1
+  int tma_d;                  // 1: D is written through map_d (TMA store / reduce-add) where possible
+  int splitk;                 // single mode: > 1 splits K into `splitk` slices of `kc` (reduce-add into D)
+  int kc;
   int* err;
 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // bf16: 64 elements = 128 bytes = one swizzle row
+
+// Epilogue staging: one 32-row x 128-byte buffer per epilogue warp (128B-swizzled, the
+// layout of a D tensor-map box), written by the warp and drained by a TMA store/reduce.
+constexpr int kEpiStageBytes = 32 * 128;
 
 template <int BN>
 struct GemmSmem {
@@ -64,7 +71,8 @@ struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kEpiOffset = kStages * kStageBytes;          // 1024-aligned
+  static constexpr int kBarOffset = kEpiOffset + 4 * kEpiStageBytes;
   static constexpr int kTotal = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
 
@@ -85,8 +93,8 @@ __device__ __forceinline__ bool locate_tile(const GemmParams& P, int t, int& hin
     pr = P.single;
     const int per = tiles_m(pr) * tiles_n<BN, BMODE>(pr);
     if (per == 0) return false;
-    bt = t / per;
-    if (bt >= pr.batch) return false;
+    bt = t / per;  // batch index, or K-slice index when split-K is on
+    if (bt >= (P.splitk > 1 ? P.splitk : pr.batch)) return false;
     const int local = t - bt * per;
     mt = local / tiles_n<BN, BMODE>(pr);
     nt = local % tiles_n<BN, BMODE>(pr);
@@ -106,7 +114,8 @@ __device__ __forceinline__ bool locate_tile(const GemmParams& P, int t, int& hin
 template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
 __global__ void __launch_bounds__(192, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
-                 const __grid_constant__ CUtensorMap map_b1, const GemmParams P) {
+                 const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_d,
+                 const GemmParams P) {
   using S = GemmSmem<BN>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, 1, 1, A_MN, B_MN);
@@ -141,6 +150,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b0);
     if (BMODE != kBSingle) tma_prefetch_desc(&map_b1);
+    if (P.tma_d) tma_prefetch_desc(&map_d);
   }
   tc_fence_before();
   __syncthreads();
@@ -148,8 +158,9 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   const uint32_t tmem_base = *tmem_slot;
 
   const int total = P.probs == nullptr
-                        ? P.single.batch * tiles_m(P.single) * tiles_n<BN, BMODE>(P.single)
+                        ? (P.splitk > 1 ? P.splitk : P.single.batch) * tiles_m(P.single) * tiles_n<BN, BMODE>(P.single)
                         : *P.total_tiles;
+  const bool split = P.probs == nullptr && P.splitk > 1;
 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA producer
@@ -162,14 +173,15 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         GemmProblem pr;
         int mt, nt, bt;
         if (!locate_tile<BN, BMODE>(P, t, hint, pr, mt, nt, bt)) continue;
-        const int nk = pr.k / kBK;
-        const int ab = pr.a_b + bt, bb = pr.b_b + bt;
+        const int k_begin = split ? bt * P.kc : 0;
+        const int nk = (split ? min(P.kc, pr.k - k_begin) : pr.k) / kBK;
+        const int ab = pr.a_b + (split ? 0 : bt), bb = pr.b_b + (split ? 0 : bt);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, P.err, kErrTimeoutEmpty)) { ok = false; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          const int ka = pr.a_k + kb * kBK;
+          const int ka = pr.a_k + k_begin + kb * kBK;
           const int m0 = pr.a_m + mt * kBM;
           if (!A_MN) {
             tma_load_3d(sa, &map_a, &full[stage], ka, m0, ab);
@@ -177,7 +189,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             tma_load_3d(sa, &map_a, &full[stage], m0, ka, ab);
             tma_load_3d(sa + kBM / 2 * kBK * 2, &map_a, &full[stage], m0 + 64, ka, ab);
           }
-          int kbk = pr.b_k + kb * kBK;
+          int kbk = pr.b_k + k_begin + kb * kBK;
           const CUtensorMap* mb = &map_b0;
           if (BMODE == kBSplitK && kbk >= P.ksplit) { mb = &map_b1; kbk -= P.ksplit; }
           if (BMODE == kBSplitN) {
@@ -222,7 +234,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, P.err, kErrTimeoutAccum)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int nk = pr.k / kBK;
+        const int nk = (split ? min(P.kc, pr.k - bt * P.kc) : pr.k) / kBK;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], phase, P.err, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
@@ -261,6 +273,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const bool row_ok = row < pr.m;
       const bool zero_k = pr.k == 0;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (split) bt = 0;  // every K-slice reduces into the same D
       const long long dbase = pr.d_off + static_cast<long long>(bt) * pr.d_bstride + row * pr.d_ld;
       if constexpr (EPI == kEpiSwiGLU) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d);
@@ -317,6 +330,62 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 }
               }
             }
+          }
+        }
+      } else if (P.tma_d && (P.probs == nullptr || mt * kBM + kBM <= pr.m)) {
+        // Stage 32 rows x 128 B per warp in swizzled smem, then one TMA store (or
+        // reduce-add for kEpiF32Acc) per chunk.  The tensor map clips the ragged edges
+        // (single mode: per batch, 3-D map); table-mode tiles are whole 128-row tiles.
+        constexpr bool kF32 = (EPI == kEpiF32 || EPI == kEpiF32Acc);
+        constexpr int kCW = kF32 ? 32 : 64;  // columns per 128-byte row chunk
+        uint8_t* stg = smem + S::kEpiOffset + quarter * kEpiStageBytes;
+        const float rs = (EPI == kEpiRowScaleBF16 && row_ok) ? P.rowscale[pr.aux_off + row] : 1.0f;
+        const int drow = static_cast<int>(pr.d_off / pr.d_ld) + mt * kBM + quarter * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += kCW) {
+          float v[kCW];
+#pragma unroll
+          for (int h = 0; h < kCW; h += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c + h, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[h + j] = zero_k ? 0.f : __uint_as_float(r[j]) * P.alpha * rs;
+          }
+          const int col0 = nt * BN + c;
+          if constexpr (EPI == kEpiAxpbyBF16) {
+            if (row_ok) {
+              const __nv_bfloat16* cin = reinterpret_cast<const __nv_bfloat16*>(P.aux) + dbase + col0;
+              for (int j = 0; j < kCW; ++j)
+                if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
+            }
+          }
+          if (lane == 0) bulk_wait_read_all();  // previous chunk's store has left the buffer
+          __syncwarp();
+          uint8_t* myrow = stg + lane * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // 16-byte chunk q of this row, 128B-swizzled
+            uint4 pk;
+            if constexpr (kF32) {
+              pk = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                              __float_as_uint(v[4 * q + 3]));
+            } else {
+              __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q], v[8 * q + 1]);
+              __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+              __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+              pk = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                              *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+            }
+            *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pk;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          // Boxes starting past the problem are skipped (never issue a fully clipped store).
+          if (lane == 0 && col0 < pr.n && mt * kBM + quarter * 32 < pr.m) {
+            if (EPI == kEpiF32Acc) tma_reduce_add_3d(&map_d, stg, col0, drow, bt);
+            else tma_store_3d(&map_d, stg, col0, drow, bt);
+            bulk_commit_group();
           }
         }
       } else {
@@ -395,6 +464,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores of this warp are complete before exit
   }
 
   tc_fence_before();

@@ -272,93 +272,36 @@ torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 }
 
 // ---------------------------------------------------------------------- mHC
-// Stream X: (T, F) with F = n*D.  W: (P, F) fp32 gate projections with the RMSNorm weight
-// folded in (P = 2n + n^2).  Pass 1 (this kernel) accumulates the raw dots q = X W^T and the
-// row sums of squares into zero-initialised fp32 buffers; grid = (T/32, F-splits) so the
-// whole GPU participates.  The gates kernel turns them into r = 1/rms and p = r q.
-constexpr int kMhcTok = 32;    // tokens per CTA
-constexpr int kMhcChunk = 256; // K chunk
-constexpr int kMhcSplit = 1024; // features per CTA along F
-__global__ void mhc_proj_fwd_kernel(const __nv_bfloat16* __restrict__ X, const float* __restrict__ W,
-                                    float* __restrict__ q, float* __restrict__ ssq_out, int T, int F, int P) {
-  extern __shared__ float sm[];
-  constexpr int LD = kMhcChunk + 1;  // odd stride: no bank conflicts
-  float* sw = sm;                    // P x LD
-  float* sx = sm + P * LD;           // tok x LD
-  __shared__ float ssq[kMhcTok];
-  const int t0 = blockIdx.x * kMhcTok;
-  const int f_begin = blockIdx.y * kMhcSplit;
-  const int f_end = min(F, f_begin + kMhcSplit);
-  const int n_out = kMhcTok * P;
-  float acc[8];
+// Stream X: (T, F) with F = n*D.  W: (P, F) gate projections with the RMSNorm weight folded
+// in (P = 2n + n^2).  The raw dots q = X W^T come from the GEMM, the row sums of squares from
+// row_sumsq; the gates kernel turns them into r = 1/rms and p = r q.
+constexpr int kMhcTok = 32;    // tokens per CTA (backward kernels)
+// ssq[t] = sum_k X[t, k]^2 (bf16 rows, fp32 result): one warp per row, 16-byte loads.
+// The mHC projection itself (X W^T, skinny N) runs on the tcgen05 GEMM with split-K.
+__global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ X, float* __restrict__ ssq, int T, int F) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= T) return;
+  const __nv_bfloat16* xr = X + static_cast<int64_t>(row) * F;
+  float s = 0.f;
+  for (int k = lane * 8; k < F; k += 32 * 8) {
+    float f[8];
+    load8(xr + k, f);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  if (threadIdx.x < kMhcTok) ssq[threadIdx.x] = 0.f;
-  float my_ss = 0.f;
-  for (int k0 = f_begin; k0 < f_end; k0 += kMhcChunk) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < P * kMhcChunk; i += blockDim.x) {
-      const int j = i / kMhcChunk, kk = i % kMhcChunk;
-      sw[j * LD + kk] = W[static_cast<int64_t>(j) * F + k0 + kk];
-    }
-    for (int i = threadIdx.x; i < kMhcTok * kMhcChunk / 8; i += blockDim.x) {
-      const int tt = i / (kMhcChunk / 8), kk = (i % (kMhcChunk / 8)) * 8;
-      float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (t0 + tt < T) load8(X + static_cast<int64_t>(t0 + tt) * F + k0 + kk, f);
-#pragma unroll
-      for (int qq = 0; qq < 8; ++qq) sx[tt * LD + kk + qq] = f[qq];
-    }
-    __syncthreads();
-    {
-      const int tt = threadIdx.x / 8, part = threadIdx.x % 8;
-      if (tt < kMhcTok) {
-        for (int kk = part; kk < kMhcChunk; kk += 8) {
-          const float v = sx[tt * LD + kk];
-          my_ss += v * v;
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int o = threadIdx.x + i * blockDim.x;
-      if (o < n_out) {
-        const int tt = o / P, j = o % P;
-        const float* xs = sx + tt * LD;
-        const float* ws = sw + j * LD;
-        float s2 = 0.f;
-#pragma unroll 8
-        for (int kk = 0; kk < kMhcChunk; ++kk) s2 += xs[kk] * ws[kk];
-        acc[i] += s2;
-      }
-    }
+    for (int q = 0; q < 8; ++q) s += f[q] * f[q];
   }
-  if (threadIdx.x / 8 < kMhcTok) atomicAdd(&ssq[threadIdx.x / 8], my_ss);
-  __syncthreads();
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int o = threadIdx.x + i * blockDim.x;
-    if (o < n_out) {
-      const int tt = o / P, j = o % P;
-      if (t0 + tt < T) atomicAdd(&q[static_cast<int64_t>(t0 + tt) * P + j], acc[i]);
-    }
-  }
-  if (threadIdx.x < kMhcTok && t0 + threadIdx.x < T) atomicAdd(&ssq_out[t0 + threadIdx.x], ssq[threadIdx.x]);
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) ssq[row] = s;
 }
 
-// q (T, P) raw dots and ssq (T) are accumulated here; p = q * r and r are finalised by the gates kernel.
-void mhc_proj_fwd(torch::Tensor X, torch::Tensor W, torch::Tensor q, torch::Tensor ssq) {
+void row_sumsq(torch::Tensor X, torch::Tensor ssq) {
   c10::cuda::CUDAGuard guard(X.device());
-  const int T = X.size(0), F = X.size(1), P = W.size(0);
-  TORCH_CHECK(F % kMhcChunk == 0 && P * kMhcTok <= 8 * 256, "mhc_proj shape");
-  q.zero_();
-  ssq.zero_();
+  const int T = X.size(0), F = X.size(1);
+  TORCH_CHECK(X.is_contiguous() && F % 8 == 0, "row_sumsq: contiguous rows, F % 8 == 0");
   if (T == 0) return;
-  const size_t smem = (P + kMhcTok) * (kMhcChunk + 1) * sizeof(float);
-  cudaFuncSetAttribute(mhc_proj_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  dim3 grid((T + kMhcTok - 1) / kMhcTok, (F + kMhcSplit - 1) / kMhcSplit);
-  mhc_proj_fwd_kernel<<<grid, 256, smem, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), W.data_ptr<float>(), q.data_ptr<float>(),
-      ssq.data_ptr<float>(), T, F, P);
+  row_sumsq_kernel<<<(T + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()), ssq.data_ptr<float>(), T, F);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -726,7 +669,7 @@ __global__ void mhc_premix_da_kernel(const __nv_bfloat16* __restrict__ X, const 
 }
 
 // Backward of split (pre-mix + norm-projection), accumulated onto dX (which holds the carry grad):
-//   dX[t,h] += a[t,h] * dinner[t]  +  r * (dp_t W)_h  -  (r^3 / F) * X[t,h] * sum_j dp_tj q_tj
+//   dX[t,h] = a[t,h] * dinner[t]  +  r * (dp_t W)_h  -  (r^3 / F) * X[t,h] * sum_j dp_tj q_tj
 // where q = p / r.  CTA per 32 tokens; each thread owns 4 features.
 template <int N>
 __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_bfloat16* __restrict__ X,
@@ -762,24 +705,21 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
       wv[j][0] = w4.x; wv[j][1] = w4.y; wv[j][2] = w4.z; wv[j][3] = w4.w;
     }
     const int h = f0 / D, d = f0 % D;
-    for (int tt = 0; tt < kMhcTok; ++tt) {
+    const int n_tok = min(kMhcTok, T - t0);
+#pragma unroll 4
+    for (int tt = 0; tt < n_tok; ++tt) {
       const int t = t0 + tt;
-      if (t >= T) break;
       const int64_t off = static_cast<int64_t>(t) * F + f0;
       const uint2 xv = *reinterpret_cast<const uint2*>(X + off);
-      const uint2 av = *reinterpret_cast<const uint2*>(dX + off);
       const uint2 gv = *reinterpret_cast<const uint2*>(din + static_cast<int64_t>(t) * D + d);
       const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
-      const __nv_bfloat162* ah2 = reinterpret_cast<const __nv_bfloat162*>(&av);
       const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv);
-      float x[4], acc[4], g[4];
+      float x[4], acc[4] = {0.f, 0.f, 0.f, 0.f}, g[4];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const float2 a2 = __bfloat1622float2(xh[q]);
-        const float2 b2 = __bfloat1622float2(ah2[q]);
         const float2 c2 = __bfloat1622float2(gh[q]);
         x[2 * q] = a2.x; x[2 * q + 1] = a2.y;
-        acc[2 * q] = b2.x; acc[2 * q + 1] = b2.y;
         g[2 * q] = c2.x; g[2 * q + 1] = c2.y;
       }
       const float ah = a[t * N + h];

@@ -32,6 +32,7 @@ from saint_llm_b200.models.mhc import MHC
 from saint_llm_b200.models.moe import DeepSeekMoE
 from saint_llm_b200.models.mtp import MTPStack
 from saint_llm_b200.models.multimodal import GenerationHeadHook, ModalityProjector, ResidualSideChannel
+from saint_llm_b200.ops import backend
 
 
 def _apply_linear(mod: nn.Linear, x: Tensor) -> Tensor:
@@ -115,7 +116,12 @@ class SaintLLM(nn.Module):
     # ---- inputs ------------------------------------------------------------------
     def _embed_inputs(self, token_ids: Tensor, vision_features: Tensor | None,
                       audio_features: Tensor | None) -> Tensor:
-        h = self.embed(token_ids)
+        if backend.native_for(self.embed.weight):
+            from saint_llm_b200.ops.embedding import embedding
+
+            h = embedding(token_ids, self.embed.weight)
+        else:
+            h = self.embed(token_ids)
         slots, mm = self.cfg.tokenizer_slots, self.cfg.multimodal
         if vision_features is not None and mm.enable_vision_projector:
             mask = token_ids == slots.image_pad

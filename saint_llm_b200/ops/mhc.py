@@ -1,7 +1,7 @@
 """mHC split / combine on the native kernels.
 
 split (one autograd node):
-    p, r  = mhc_proj_fwd(X, W_fold)       W_fold = [w_pre; w_res; w_post] * norm.weight
+    q = X W_fold^T (tcgen05 GEMM), ssq = row sums of X^2; W_fold = [w_pre; w_res; w_post] * norm.weight
     a,b,c = mhc_gates_fwd(p, alpha, s)    sigmoid / Sinkhorn (in registers) / 2 sigmoid
     inner = mhc_premix(X, a)
 combine:  X' = B X + C (x) out  (mhc_combine), backward in one pass (mhc_combine_bwd).
@@ -36,7 +36,8 @@ class _SplitFn(torch.autograd.Function):
         ssq = torch.empty(T, dtype=torch.float32, device=dev)
         r = torch.empty(T, dtype=torch.float32, device=dev)
         wf = w_fold.float().contiguous()
-        ext.mhc_proj_fwd(Xf, wf, p, ssq)
+        gemm.gemm_nt(Xf, wf.to(torch.bfloat16), out=p)  # skinny (T, P) projection, split-K on the GEMM
+        ext.row_sumsq(Xf, ssq)
         al = alpha.float().contiguous()
         sp, sr, so = s_pre.float().contiguous(), s_res.float().contiguous(), s_post.float().contiguous()
         a = torch.empty(T, n, dtype=torch.float32, device=dev)
@@ -73,7 +74,7 @@ class _SplitFn(torch.autograd.Function):
         d_alpha = torch.zeros(3, dtype=torch.float32, device=dev).index_add_(0, grp, (dz * p).sum(0))
         dzs = dz.sum(0)
         d_s_pre, d_s_res, d_s_post = dzs[:n], dzs[n:n + n * n].view(n, n), dzs[n + n * n:]
-        dXf = torch.zeros_like(Xf)
+        dXf = torch.empty_like(Xf)
         ext.mhc_split_bwd(dXf, Xf, din, a, dp.contiguous(), p, r, wf, n)
         dq = (dp * r[:, None]).to(torch.bfloat16)
         dW = gemm.gemm_nt(dq.t(), Xf.t(), out_dtype=torch.float32)

@@ -49,3 +49,36 @@ def test_gemm_accumulate_and_batched(cuda):
     x = torch.randn(7, 128, 256, device=cuda, dtype=torch.bfloat16)
     y = torch.randn(7, 256, 384, device=cuda, dtype=torch.bfloat16)
     _close(gemm.bmm(x, y), x.float() @ y.float(), 1e-3)
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+@pytest.mark.parametrize("m,n,k", [(1024, 256, 4096), (24, 8192, 4096), (4096, 24, 8192), (200, 100, 2048)])
+def test_gemm_split_k_skinny(cuda, m, n, k, accumulate):
+    """Few output tiles and long K: the K-split path (TMA reduce-add into fp32)."""
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(2)
+    # weight-gradient layout: both operands MN-major (token dimension is K)
+    a = torch.randn(k, m, device=cuda, dtype=torch.bfloat16).t()
+    b = torch.randn(k, n, device=cuda, dtype=torch.bfloat16).t()
+    base = torch.randn(m, n, device=cuda, dtype=torch.float32)
+    out = base.clone()
+    gemm.gemm_nt(a, b, out=out, accumulate=accumulate)
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    want = _ref(a, b) + (base if accumulate else 0)
+    _close(out, want, 1e-3)
+
+
+def test_gemm_bf16_output_view_with_row_stride(cuda):
+    """bf16 output written through a TMA map into a column slice of a wider buffer."""
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(3)
+    a = torch.randn(300, 256, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(200, 256, device=cuda, dtype=torch.bfloat16)
+    wide = torch.zeros(300, 520, device=cuda, dtype=torch.bfloat16)
+    gemm.gemm_nt(a, b, out=wide[:, 8:208])
+    torch.cuda.synchronize()
+    _close(wide[:, 8:208], _ref(a, b))
+    assert wide[:, :8].abs().sum() == 0 and wide[:, 208:].abs().sum() == 0

@@ -54,6 +54,15 @@ void mhc_combine_bwd(torch::Tensor dY, torch::Tensor X, torch::Tensor o, torch::
 void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t n);
 void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
+// attention.cu
+void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
+              int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
+              torch::Tensor o_c, torch::Tensor out, torch::Tensor lse, torch::Tensor max_logit, torch::Tensor err);
+void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
+              int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
+              torch::Tensor o_c, torch::Tensor lse, torch::Tensor dout, torch::Tensor dq, torch::Tensor dk,
+              torch::Tensor dv, torch::Tensor dkv, torch::Tensor dsink, torch::Tensor err);
+void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel);
 // data.cpp
 void bind_data(pybind11::module_& m);
 }  // namespace sv4
@@ -61,6 +70,9 @@ void bind_data(pybind11::module_& m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "saint_llm_b200 sm_100a kernels";
   sv4::bind_data(m);
+  m.def("attn_fwd", &sv4::attn_fwd);
+  m.def("attn_bwd", &sv4::attn_bwd);
+  m.def("csa_select_mask", &sv4::csa_select_mask);
   m.def("gemm", &sv4::gemm);
   m.def("grouped_gemm", &sv4::grouped_gemm);
   m.def("build_moe_problems", &sv4::build_moe_problems);

@@ -48,6 +48,30 @@ CUtensorMap make_map_3d(const void* base, CUtensorMapDataType dt, int elem_bytes
   return m;
 }
 
+// Generic tiled map (rank 2..5): dims inner-first, strides in bytes for dims 1..rank-1.
+CUtensorMap make_map_nd(const void* base, CUtensorMapDataType dt, int rank, const uint64_t* dims,
+                        const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  TORCH_CHECK(rank >= 2 && rank <= 5, "tensor map rank");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base address must be 16-byte aligned");
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) {
+    TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
+    st[i] = strides_bytes[i];
+  }
+  CUtensorMap m;
+  CUresult r = encode_fn()(&m, dt, rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  return m;
+}
+
 // An operand view as (batch, outer, inner) with unit inner stride.
 struct OperandView {
   const void* ptr;

@@ -9,10 +9,11 @@ SWA/HCA rope then norm).
 The lightning indexer (no gradient flows through its integer output) streams token
 chunks: scores = relu(q_h . k_s) weighted over heads, strict block-causal mask, top-k.
 
-Attention itself uses a memory-bounded formulation: the sliding window is computed per
-block of queries against its own and the previous key block (never a T x T score
-tensor), and the CSA sparse branch is evaluated as a masked softmax over the (short)
-compressed table -- exact, because the top-k picks are a subset of that table.
+Attention itself is one fused tcgen05 kernel per direction (``csrc/attention.cu``): the
+sliding-window branch (sink, softcap, max-logit telemetry) and the compressed branch
+(HCA block-causal + sink, or CSA over the indexer's picks given as a bitmask -- exact,
+because the top-k picks are a subset of the compressed table) run as two online
+softmaxes whose outputs are summed; no score tensor ever reaches HBM.
 """
 
 from __future__ import annotations
@@ -23,7 +24,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-from saint_llm_b200.ops import gemm
+from saint_llm_b200.ops import backend, gemm
 from saint_llm_b200.ops import linear as lin
 from saint_llm_b200.ops.norm import rms_norm, rope_norm
 
@@ -79,50 +80,74 @@ def _pool(c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int) -> Tensor:
     return (torch.softmax(z, dim=-2) * c_b[:, : n * m].float().reshape(b, n, m, c)).sum(-2)
 
 
-def _sw_attention(q: Tensor, k: Tensor, v: Tensor, window: int, sink: Tensor | None,
-                  softcap: float | None, layer: nn.Module) -> Tensor:
-    """q (B,H,T,d), k/v (B,T,d): causal sliding window with per-head sink, blocked by `window`."""
-    b, h, t, d = q.shape
-    bq = max(16, window)
-    nb = (t + bq - 1) // bq
-    tp = nb * bq
-    qp = F.pad(q, (0, 0, 0, tp - t)).view(b, h, nb, bq, d)
-    kp = F.pad(k, (0, 0, bq, tp - t))  # one leading block of zeros
-    vp = F.pad(v, (0, 0, bq, tp - t))
-    kb = kp.unfold(1, 2 * bq, bq).transpose(-1, -2)  # (B, nb, 2bq, d)
-    vb = vp.unfold(1, 2 * bq, bq).transpose(-1, -2)
-    s = torch.matmul(qp, kb.unsqueeze(1).transpose(-1, -2)) / math.sqrt(d)  # (B,H,nb,bq,2bq)
-    qpos = torch.arange(tp, device=q.device).view(nb, bq, 1)
-    kpos = ((torch.arange(nb, device=q.device).view(nb, 1, 1) - 1) * bq
-            + torch.arange(2 * bq, device=q.device).view(1, 1, 2 * bq))
-    vis = (kpos <= qpos) & (qpos - kpos < window) & (kpos >= 0)
-    with torch.no_grad():
-        layer.max_attn_logit.copy_(s.detach().masked_fill(~vis, 0).abs().amax().float())
-    if softcap is not None:
-        s = softcap * torch.tanh(s / softcap)
-    s = s.float().masked_fill(~vis, float("-inf"))
-    if sink is not None:
-        sk = sink.float().view(1, h, 1, 1, 1).expand(b, h, nb, bq, 1)
-        p = torch.softmax(torch.cat([s, sk], -1), -1)[..., :-1]
-    else:
-        p = torch.softmax(s, -1)
-    out = torch.matmul(p.to(vb.dtype), vb.unsqueeze(1))  # (B,H,nb,bq,d)
-    return out.reshape(b, h, tp, d)[:, :, :t]
+def _pad_head(t: Tensor, hd: int) -> Tensor:
+    return t if t.shape[-1] == hd else F.pad(t, (0, hd - t.shape[-1]))
 
 
-def _masked_compressed_attention(q: Tensor, kv: Tensor, mask: Tensor, sink: Tensor | None) -> Tensor:
-    """q (B,H,T,d), kv (B,n,d) (K = V), mask (B|1, T, n).  Rows with nothing visible give 0."""
-    d = q.shape[-1]
-    s = torch.matmul(q, kv.unsqueeze(1).transpose(-1, -2)).float() / math.sqrt(d)  # (B,H,T,n)
-    s = s.masked_fill(~mask.unsqueeze(1), float("-inf"))
-    if sink is not None:
-        sk = sink.float().view(1, -1, 1, 1).expand(*s.shape[:-1], 1)
-        p = torch.softmax(torch.cat([s, sk], -1), -1)[..., :-1]
-    else:
-        any_vis = mask.any(-1).unsqueeze(1).unsqueeze(-1)
-        p = torch.softmax(torch.where(any_vis, s, torch.zeros_like(s)), -1)
-        p = torch.where(any_vis, p, torch.zeros_like(p))
-    return torch.matmul(p.to(kv.dtype), kv.unsqueeze(1))
+class _FusedAttnFn(torch.autograd.Function):
+    """Window branch (+ sink, softcap) and optional compressed branch in one tcgen05 kernel.
+
+    q (B, T, H, d), k/v (B, T, d), kv (B, n, d) (K = V, already k-normed), sink (H) or None,
+    sel: CSA selection bits (B, T, words) or None.  Returns (B, T, H, d) = o_window + o_comp.
+    """
+
+    @staticmethod
+    def forward(ctx, q, k, v, kv, sink, sel, mode, m, window, softcap, maxlogit):  # type: ignore[override]
+        d = q.shape[-1]
+        hd = 64 if d <= 64 else 128
+        if d > 128:
+            raise ValueError("fused attention supports head_dim <= 128")
+        qb, kb_, vb = (_pad_head(_bf16(t), hd).contiguous() for t in (q, k, v))
+        kvb = _pad_head(_bf16(kv), hd).contiguous() if mode else qb.new_empty(0)
+        b, t, h = q.shape[:3]
+        ext = backend.ext()
+        o_sw = torch.empty(b, t, h, hd, dtype=torch.bfloat16, device=q.device)
+        o_c = torch.empty_like(o_sw) if mode else o_sw.new_empty(0)
+        out = torch.empty_like(o_sw) if mode else o_sw
+        lse = torch.empty(2, b, h, t, dtype=torch.float32, device=q.device)
+        sink_f = sink.float().contiguous() if sink is not None else lse.new_empty(0)
+        sel_t = sel if sel is not None else torch.empty(0, dtype=torch.int32, device=q.device)
+        # the kernel max-reduces |logit| into an fp32 scalar
+        ml = None
+        if maxlogit is not None:
+            ml = maxlogit if maxlogit.dtype == torch.float32 and maxlogit.numel() == 1 else \
+                torch.zeros((), dtype=torch.float32, device=q.device)
+            ml.zero_()
+        ext.attn_fwd(qb, kb_, vb, kvb, sel_t, mode, m, window, sink_f, float(softcap or 0.0), 1.0 / math.sqrt(d),
+                     o_sw, o_c, out, lse, ml if ml is not None else lse.new_empty(0), gemm.error_word(q.device))
+        if ml is not None and ml is not maxlogit:
+            maxlogit.copy_(ml)
+        ctx.save_for_backward(qb, kb_, vb, kvb, sink_f, sel_t, o_sw, o_c, lse)
+        ctx.meta = (mode, m, window, float(softcap or 0.0), d, sink is not None,
+                    sink.dtype if sink is not None else None, kv.dtype if mode else None)
+        return out[..., :d]
+
+    @staticmethod
+    def backward(ctx, dout):  # type: ignore[override]
+        qb, kb_, vb, kvb, sink_f, sel_t, o_sw, o_c, lse = ctx.saved_tensors
+        mode, m, window, softcap, d, has_sink, sink_dtype, kv_dtype = ctx.meta
+        hd = qb.shape[-1]
+        dob = _pad_head(_bf16(dout), hd).contiguous()
+        dq = torch.empty_like(qb)
+        dk = torch.zeros(kb_.shape, dtype=torch.float32, device=qb.device)
+        dv = torch.zeros_like(dk)
+        dkv = torch.zeros(kvb.shape, dtype=torch.float32, device=qb.device) if mode else dk.new_empty(0)
+        dsink = torch.zeros_like(sink_f)
+        backend.ext().attn_bwd(qb, kb_, vb, kvb, sel_t, mode, m, window, sink_f, softcap, 1.0 / math.sqrt(d), o_sw,
+                               o_c, lse, dob, dq, dk, dv, dkv, dsink, gemm.error_word(qb.device))
+        gkv = dkv[..., :d].to(kv_dtype) if mode else None
+        gs = dsink.to(sink_dtype) if has_sink else None
+        return (dq[..., :d], dk[..., :d].to(torch.bfloat16), dv[..., :d].to(torch.bfloat16), gkv, gs,
+                None, None, None, None, None, None)
+
+
+def fused_attention(q: Tensor, k: Tensor, v: Tensor, *, window: int, sink: Tensor | None, softcap: float | None,
+                    kv: Tensor | None = None, mode: int = 0, m: int = 1, sel: Tensor | None = None,
+                    maxlogit: Tensor | None = None) -> Tensor:
+    """Sliding-window attention (+ compressed branch) on the native kernel; see ``_FusedAttnFn``."""
+    if mode and (kv is None or kv.shape[1] == 0):
+        mode, kv = 0, None
+    return _FusedAttnFn.apply(q, k, v, kv if mode else q.new_empty(0), sink, sel, mode, m, window, softcap, maxlogit)
 
 
 @torch.no_grad()
@@ -180,12 +205,11 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
     cos, sin = rope_tables(t, rd, cfg.rope_theta, h.device)
     cos_b, sin_b = cos.repeat(b, 1), sin.repeat(b, 1)
     q = lin.linear(c_q, layer.q_up.weight).reshape(b * t, H, d)
-    q = rope_norm(q, layer.q_norm.weight, cos_b, sin_b, rd, norm_first=False,
-                  eps=layer.q_norm.eps).view(b, t, H, d).transpose(1, 2)
+    q = rope_norm(q, layer.q_norm.weight, cos_b, sin_b, rd, norm_first=False, eps=layer.q_norm.eps)
     k = rope_norm(k.reshape(b * t, 1, d), layer.k_norm.weight, cos_b, sin_b, rd,
                   norm_first=(kind == "csa"), eps=layer.k_norm.eps).view(b, t, d)
-    v = v.contiguous()
-    out = _sw_attention(q, k, v, cfg.sliding_window_size, layer.sink_logit, cfg.logit_softcap, layer)
+    q = q.view(b, t, H, d)
+    mode, m, kvn, sel = 0, 1, None, None
     if kind in ("csa", "hca"):
         m = layer.csa_cfg.compression_rate if kind == "csa" else layer.hca_cfg.compression_rate
         comp = _pool(parts[3], parts[4], layer.kv_compressor.bias_b, m)
@@ -195,14 +219,15 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
             if kind == "csa":
                 top = indexer_topk(layer.indexer, hb, is_visual)
                 if top.shape[-1] > 0:
-                    sel = torch.zeros(b, t, n_blocks + 1, dtype=torch.bool, device=h.device)
-                    sel.scatter_(2, torch.where(top >= 0, top, torch.full_like(top, n_blocks)), True)
-                    out = out + _masked_compressed_attention(q, kvn, sel[..., :n_blocks], None).to(out.dtype)
+                    sel = torch.empty(b, t, (n_blocks + 31) // 32, dtype=torch.int32, device=h.device)
+                    backend.ext().csa_select_mask(top.contiguous(), n_blocks, sel)
+                    mode = 2
             else:
-                qpos = torch.arange(t, device=h.device).view(-1, 1)
-                valid = (torch.arange(n_blocks, device=h.device).view(1, -1) * m + (m - 1) < qpos).unsqueeze(0)
-                out = out + _masked_compressed_attention(q, kvn, valid, layer.sink_logit).to(out.dtype)
-    flat = out.transpose(1, 2).reshape(b, t, H * d)
+                mode = 1
+    out = fused_attention(q, k, v.contiguous(), window=cfg.sliding_window_size, sink=layer.sink_logit,
+                          softcap=cfg.logit_softcap, kv=kvn, mode=mode, m=m, sel=sel,
+                          maxlogit=layer.max_attn_logit)
+    flat = out.reshape(b, t, H * d)
     return layer.output.forward_flat(flat)
 
 

@@ -1,0 +1,106 @@
+"""Fused tcgen05 attention (window + sink + softcap, HCA / CSA compressed branch) against a
+plain fp32 PyTorch reference of the same math, forward and backward."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, k, v, kv, sink, sel, mode, m, window, softcap):
+    b, t, h, d = q.shape
+    q, k, v = q.float(), k.float(), v.float()
+    s = torch.einsum("bthd,bsd->bhts", q, k) / math.sqrt(d)
+    qpos = torch.arange(t, device=q.device).view(-1, 1)
+    kpos = torch.arange(t, device=q.device).view(1, -1)
+    vis = (kpos <= qpos) & (qpos - kpos < window)
+    amax = s.detach().abs().masked_fill(~vis, 0).amax()
+    if softcap:
+        s = softcap * torch.tanh(s / softcap)
+    s = s.masked_fill(~vis, float("-inf"))
+    if sink is not None:
+        s = torch.cat([s, sink.float().view(1, h, 1, 1).expand(b, h, t, 1)], -1)
+    p = torch.softmax(s, -1)
+    if sink is not None:
+        p = p[..., :-1]
+    o = torch.einsum("bhts,bsd->bthd", p, v)
+    if mode:
+        kvf = kv.float()
+        n = kvf.shape[1]
+        sc = torch.einsum("bthd,bnd->bhtn", q, kvf) / math.sqrt(d)
+        if mode == 1:
+            visc = ((torch.arange(n, device=q.device) * m + m - 1).view(1, -1) < qpos).view(1, 1, t, n)
+        else:
+            visc = sel.view(b, 1, t, n)
+        sc = sc.masked_fill(~visc, float("-inf"))
+        if mode == 1 and sink is not None:
+            sc = torch.cat([sc, sink.float().view(1, h, 1, 1).expand(b, h, t, 1)], -1)
+            pc = torch.softmax(sc, -1)[..., :-1]
+        else:
+            pc = torch.nan_to_num(torch.softmax(sc, -1), nan=0.0)
+        o = o + torch.einsum("bhtn,bnd->bthd", pc, kvf)
+    return o, amax
+
+
+def _close(x, y, tol):
+    err = (x.float() - y.float()).abs().max().item()
+    scale = y.float().abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err} vs scale {scale}"
+
+
+CASES = [
+    # (B, T, H, d, window, mode, m, sink, softcap)
+    (1, 256, 2, 128, 128, 0, 1, True, None),
+    (2, 300, 3, 128, 64, 0, 1, False, 30.0),
+    (1, 384, 2, 64, 200, 1, 8, True, None),
+    (2, 260, 2, 128, 128, 2, 4, False, None),
+    (1, 200, 2, 32, 16, 1, 16, True, 20.0),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fused_attention_matches_reference(cuda, case):
+    from saint_llm_b200.ops import gemm
+    from saint_llm_b200.ops.attention import fused_attention
+
+    b, t, h, d, window, mode, m, with_sink, softcap = case
+    g = torch.Generator(device="cuda").manual_seed(0)
+    mk = lambda *s: (torch.randn(*s, device=cuda, generator=g) * 1.5).to(torch.bfloat16)  # noqa: E731
+    q, k, v = mk(b, t, h, d), mk(b, t, d), mk(b, t, d)
+    n = t // m if mode else 0
+    kv = mk(b, n, d) if mode else None
+    sink = (torch.randn(h, device=cuda, generator=g)).to(torch.bfloat16) if with_sink else None
+    sel_bool, sel = None, None
+    if mode == 2:
+        qpos = torch.arange(t, device=cuda).view(-1, 1)
+        causal = (torch.arange(n, device=cuda) * m + m - 1).view(1, -1) < qpos
+        sel_bool = (torch.rand(b, t, n, device=cuda, generator=g) < 0.5) & causal
+        top = torch.where(sel_bool, torch.arange(n, device=cuda).expand(b, t, n), torch.full_like(sel_bool, -1,
+                                                                                                dtype=torch.long))
+        sel = torch.empty(b, t, (n + 31) // 32, dtype=torch.int32, device=cuda)
+        from saint_llm_b200.ops import backend
+
+        backend.ext().csa_select_mask(top.contiguous(), n, sel)
+    leaves = [x.detach().clone().requires_grad_(True) if x is not None else None for x in (q, k, v, kv, sink)]
+    ml = torch.zeros((), device=cuda)
+    out = fused_attention(leaves[0], leaves[1], leaves[2], window=window, sink=leaves[4], softcap=softcap,
+                          kv=leaves[3], mode=mode, m=m, sel=sel, maxlogit=ml)
+    ref_leaves = [x.detach().clone().float().requires_grad_(True) if x is not None else None
+                  for x in (q, k, v, kv, sink)]
+    ref, amax = _ref(ref_leaves[0], ref_leaves[1], ref_leaves[2], ref_leaves[3], ref_leaves[4], sel_bool, mode, m,
+                     window, softcap)
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    _close(out, ref, 2e-2)
+    assert abs(float(ml) - float(amax)) <= 1e-2 * float(amax) + 1e-3
+    dout = torch.randn(out.shape, device=cuda, generator=g).to(torch.bfloat16)
+    out.backward(dout)
+    ref.backward(dout.float())
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    for name, a_, r_ in zip(("q", "k", "v", "kv", "sink"), leaves, ref_leaves, strict=True):
+        if a_ is None:
+            continue
+        _close(a_.grad, r_.grad, 3e-2 if name != "sink" else 5e-2)

@@ -131,18 +131,21 @@ __device__ __forceinline__ bool branch_has_sink(const AttnParams& P, int br) {
 
 // ====================================================================== forward
 template <int HD>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                 const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mkv,
                 const AttnParams P) {
   constexpr int A = HD / 64;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // P aliases the K buffer: K is dead once S = Q K^T has completed, and the next K is
+  // loaded only after P V has completed.  96 KB per CTA -> two CTAs per SM (d = 128).
+  constexpr int KA = A > 2 ? A : 2;
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + A * kAtom;
-  uint8_t* sV = sK + A * kAtom;
-  uint8_t* sP = sV + A * kAtom;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + 2 * kAtom);  // 0 q, 1 kv, 2 s, 3 o
+  uint8_t* sV = sK + KA * kAtom;
+  uint8_t* sP = sK;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + A * kAtom);  // 0 q, 1 kv, 2 s, 3 o
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   __shared__ float red[4];
 
@@ -194,9 +197,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
             tma_load_3d(sK + a * kAtom, &mk, &bar[1], a * 64, kb * 128, b);
             tma_load_3d(sV + a * kAtom, &mv, &bar[1], a * 64, kb * 128, b);
           }
-        } else {
+        } else {  // K = V = kv: kept in the V buffer (the K buffer holds P)
           mbar_arrive_expect_tx(&bar[1], A * kAtom);
-          for (int a = 0; a < A; ++a) tma_load_3d(sK + a * kAtom, &mkv, &bar[1], a * 64, kb * 128, b);
+          for (int a = 0; a < A; ++a) tma_load_3d(sV + a * kAtom, &mkv, &bar[1], a * 64, kb * 128, b);
         }
         mbar_wait(&bar[1], n_kv & 1, P.err, kErrTimeoutFull);
         if (q_wait) {
@@ -204,7 +207,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           q_wait = false;
         }
         tc_fence_after();
-        const uint32_t aq = smem_u32(sQ), ak = smem_u32(sK);
+        const uint32_t aq = smem_u32(sQ), ak = smem_u32(br == 0 ? sK : sV);
 #pragma unroll
         for (int s = 0; s < HD / 16; ++s) mma_bf16(tbase, desc_k(aq, s), desc_k(ak, s), kIdS, s > 0 ? 1u : 0u);
         mma_commit(&bar[2]);
@@ -292,7 +295,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
       __syncthreads();
       if (leader) {
         tc_fence_after();
-        const uint32_t ap = smem_u32(sP), av = smem_u32(br == 0 ? sV : sK);
+        const uint32_t ap = smem_u32(sP), av = smem_u32(sV);
 #pragma unroll
         for (int s = 0; s < 8; ++s)
           mma_bf16(tbase + 128, desc_k(ap, s), desc_mn(av, s), kIdO, (n_o > o_before || s > 0) ? 1u : 0u);
@@ -657,7 +660,7 @@ static void check_inputs(const torch::Tensor& q, const torch::Tensor& k, const t
                         "kv: (B, n, HD)");
 }
 
-static int fwd_smem(int hd) { return 3 * (hd / 64) * kAtom + 2 * kAtom + 64 + 1024; }
+static int fwd_smem(int hd) { return 2 * (hd / 64) * kAtom + std::max(hd / 64, 2) * kAtom + 64 + 1024; }
 static int bwd_smem(int hd) { return 4 * (hd / 64) * kAtom + 4 * kAtom + 4 * 4096 + 64 + 1024; }
 
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,

@@ -63,6 +63,10 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor k
               torch::Tensor o_c, torch::Tensor lse, torch::Tensor dout, torch::Tensor dq, torch::Tensor dk,
               torch::Tensor dv, torch::Tensor dkv, torch::Tensor dsink, torch::Tensor err);
 void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel);
+// ce.cu
+void ce_fwd(torch::Tensor z, torch::Tensor target, double softcap, torch::Tensor lse, torch::Tensor nll);
+void ce_bwd(torch::Tensor z, torch::Tensor target, torch::Tensor lse, double softcap, torch::Tensor scale,
+            torch::Tensor dz);
 // data.cpp
 void bind_data(pybind11::module_& m);
 }  // namespace sv4
@@ -73,6 +77,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &sv4::attn_fwd);
   m.def("attn_bwd", &sv4::attn_bwd);
   m.def("csa_select_mask", &sv4::csa_select_mask);
+  m.def("ce_fwd", &sv4::ce_fwd);
+  m.def("ce_bwd", &sv4::ce_bwd);
   m.def("gemm", &sv4::gemm);
   m.def("grouped_gemm", &sv4::grouped_gemm);
   m.def("build_moe_problems", &sv4::build_moe_problems);

@@ -66,20 +66,20 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const fl
 }
 
 // dx = r * (w*dy - x * r^2 * mean(w*dy*x)); dw partials per CTA (rows_per_cta rows).
+// Phase 1: one warp per row computes mean(w*dy*x).  Phase 2: thread t owns columns
+// [8t, 8t+8) (+ 8*blockDim strides): coalesced 16-byte row reads, dx writes, and dw
+// accumulated in registers (no shared-memory atomics).
+constexpr int kNormRowsPerCta = 16;
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const float* __restrict__ w, const float* __restrict__ rstd,
-                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int rows, int D,
-                                   int rows_per_cta) {
-  extern __shared__ float sdw[];  // D floats
-  for (int d = threadIdx.x; d < D; d += blockDim.x) sdw[d] = 0.f;
-  __syncthreads();
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int rows, int D) {
+  __shared__ float sdot[kNormRowsPerCta];
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * rows_per_cta;
-  for (int rr = threadIdx.x >> 5; rr < rows_per_cta; rr += warps) {
+  const int row0 = blockIdx.x * kNormRowsPerCta;
+  const int nrows = min(kNormRowsPerCta, rows - row0);
+  for (int rr = threadIdx.x >> 5; rr < nrows; rr += warps) {
     const int row = row0 + rr;
-    if (row >= rows) break;
-    const float r = rstd[row];
     const __nv_bfloat16* xr = x + static_cast<int64_t>(row) * D;
     const __nv_bfloat16* gr = dy + static_cast<int64_t>(row) * D;
     float dot = 0.f;
@@ -88,24 +88,58 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
       load8(xr + d, fx);
       load8(gr + d, fg);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        dot += w[d + q] * fg[q] * fx[q];
-        atomicAdd(&sdw[d + q], fg[q] * fx[q] * r);
-      }
+      for (int q = 0; q < 8; ++q) dot += w[d + q] * fg[q] * fx[q];
     }
-    dot = warp_sum(dot) / D;
-    __nv_bfloat16* dr = dx + static_cast<int64_t>(row) * D;
-    for (int d = lane * 8; d < D; d += 256) {
-      float fx[8], fg[8], o[8];
-      load8(xr + d, fx);
-      load8(gr + d, fg);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = r * (w[d + q] * fg[q] - fx[q] * r * r * dot);
-      store8(dr + d, o);
-    }
+    dot = warp_sum(dot);
+    if (lane == 0) sdot[rr] = dot / D;
   }
   __syncthreads();
-  for (int d = threadIdx.x; d < D; d += blockDim.x) dw_part[static_cast<int64_t>(blockIdx.x) * D + d] = sdw[d];
+  for (int d0 = threadIdx.x * 8; d0 < D; d0 += blockDim.x * 8) {
+    float wv[8], acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      wv[q] = w[d0 + q];
+      acc[q] = 0.f;
+    }
+    for (int rr = 0; rr < nrows; rr += 4) {
+      uint4 xv[4], gv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // issue all loads of four rows first
+        const int64_t off = static_cast<int64_t>(row0 + min(rr + u, nrows - 1)) * D + d0;
+        xv[u] = *reinterpret_cast<const uint4*>(x + off);
+        gv[u] = *reinterpret_cast<const uint4*>(dy + off);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (rr + u >= nrows) break;
+        const int64_t off = static_cast<int64_t>(row0 + rr + u) * D + d0;
+        const float r = rstd[row0 + rr + u];
+        const float c = r * r * sdot[rr + u];
+        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv[u]);
+        float o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fx = __bfloat1622float2(xh[q]), fg = __bfloat1622float2(gh[q]);
+          acc[2 * q] += fg.x * fx.x * r;
+          acc[2 * q + 1] += fg.y * fx.y * r;
+          o[2 * q] = r * (wv[2 * q] * fg.x - fx.x * c);
+          o[2 * q + 1] = r * (wv[2 * q + 1] * fg.y - fx.y * c);
+        }
+        store8(dx + off, o);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) dw_part[static_cast<int64_t>(blockIdx.x) * D + d0 + q] = acc[q];
+  }
+}
+
+__global__ void column_sum_kernel(const float* __restrict__ part, int n, int D, float* __restrict__ out) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = 0.f;
+  for (int i = 0; i < n; ++i) s += part[static_cast<int64_t>(i) * D + d];
+  out[d] = s;
 }
 
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor rstd, double eps) {
@@ -125,17 +159,20 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   c10::cuda::CUDAGuard guard(x.device());
   const int D = x.size(-1);
   const int rows = x.numel() / D;
-  const int rpc = 16;
-  const int ctas = std::max(1, (rows + rpc - 1) / rpc);
-  auto part = torch::zeros({ctas, D}, x.options().dtype(at::kFloat));
-  if (rows > 0) {
-    rmsnorm_bwd_kernel<<<ctas, 256, D * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-        w.data_ptr<float>(), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()),
-        part.data_ptr<float>(), rows, D, rpc);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
-  return part.sum(0);
+  TORCH_CHECK(D % 8 == 0, "rmsnorm_bwd: D % 8 == 0");
+  const int ctas = std::max(1, (rows + kNormRowsPerCta - 1) / kNormRowsPerCta);
+  auto part = torch::empty({ctas, D}, x.options().dtype(at::kFloat));
+  auto dw = torch::empty({D}, x.options().dtype(at::kFloat));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (rows == 0) return dw.zero_();
+  rmsnorm_bwd_kernel<<<ctas, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      w.data_ptr<float>(), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()),
+      part.data_ptr<float>(), rows, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  column_sum_kernel<<<(D + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), ctas, D, dw.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dw;
 }
 
 // ------------------------------------------------------------ RoPE + RMSNorm
@@ -275,7 +312,7 @@ torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 // Stream X: (T, F) with F = n*D.  W: (P, F) gate projections with the RMSNorm weight folded
 // in (P = 2n + n^2).  The raw dots q = X W^T come from the GEMM, the row sums of squares from
 // row_sumsq; the gates kernel turns them into r = 1/rms and p = r q.
-constexpr int kMhcTok = 32;    // tokens per CTA (backward kernels)
+constexpr int kMhcTok = 128;   // tokens per CTA of the split backward (amortises the W slice)
 // ssq[t] = sum_k X[t, k]^2 (bf16 rows, fp32 result): one warp per row, 16-byte loads.
 // The mHC projection itself (X W^T, skinny N) runs on the tcgen05 GEMM with split-K.
 __global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ X, float* __restrict__ ssq, int T, int F) {
@@ -680,21 +717,26 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
   const int F = N * D;
   __shared__ float sdp[kMhcTok][P];
   __shared__ float scoef[kMhcTok][2];
+  __shared__ float sa[kMhcTok][N];
   const int t0 = blockIdx.x * kMhcTok;
   for (int i = threadIdx.x; i < kMhcTok * P; i += blockDim.x) {
     const int tt = i / P, j = i % P;
     sdp[tt][j] = (t0 + tt < T) ? dp[static_cast<int64_t>(t0 + tt) * P + j] : 0.f;
   }
+  for (int i = threadIdx.x; i < kMhcTok * N; i += blockDim.x) {
+    const int tt = i / N;
+    sa[tt][i % N] = (t0 + tt < T) ? a[static_cast<int64_t>(t0 + tt) * N + i % N] : 0.f;
+  }
   __syncthreads();
-  if (threadIdx.x < kMhcTok) {
-    const int t = t0 + threadIdx.x;
+  for (int tt0 = threadIdx.x; tt0 < kMhcTok; tt0 += blockDim.x) {
+    const int t = t0 + tt0;
     float rr = 0.f, s = 0.f;
     if (t < T) {
       rr = r[t];
-      for (int j = 0; j < P; ++j) s += sdp[threadIdx.x][j] * p[static_cast<int64_t>(t) * P + j] / rr;
+      for (int j = 0; j < P; ++j) s += sdp[tt0][j] * p[static_cast<int64_t>(t) * P + j] / rr;
     }
-    scoef[threadIdx.x][0] = rr;
-    scoef[threadIdx.x][1] = rr * rr * rr / F * s;
+    scoef[tt0][0] = rr;
+    scoef[tt0][1] = rr * rr * rr / F * s;
   }
   __syncthreads();
   for (int f0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; f0 < F; f0 += gridDim.y * blockDim.x * 4) {
@@ -706,36 +748,45 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
     }
     const int h = f0 / D, d = f0 % D;
     const int n_tok = min(kMhcTok, T - t0);
-#pragma unroll 4
-    for (int tt = 0; tt < n_tok; ++tt) {
-      const int t = t0 + tt;
-      const int64_t off = static_cast<int64_t>(t) * F + f0;
-      const uint2 xv = *reinterpret_cast<const uint2*>(X + off);
-      const uint2 gv = *reinterpret_cast<const uint2*>(din + static_cast<int64_t>(t) * D + d);
-      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv);
-      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv);
-      float x[4], acc[4] = {0.f, 0.f, 0.f, 0.f}, g[4];
+    // four tokens per step: all eight loads are issued before any math (memory parallelism)
+    for (int tt = 0; tt < n_tok; tt += 4) {
+      uint2 xv[4], gv[4];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const float2 a2 = __bfloat1622float2(xh[q]);
-        const float2 c2 = __bfloat1622float2(gh[q]);
-        x[2 * q] = a2.x; x[2 * q + 1] = a2.y;
-        g[2 * q] = c2.x; g[2 * q + 1] = c2.y;
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + min(tt + u, n_tok - 1);
+        xv[u] = *reinterpret_cast<const uint2*>(X + static_cast<int64_t>(t) * F + f0);
+        gv[u] = *reinterpret_cast<const uint2*>(din + static_cast<int64_t>(t) * D + d);
       }
-      const float ah = a[t * N + h];
-      const float rr = scoef[tt][0], cc = scoef[tt][1];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float s = 0.f;
+      for (int u = 0; u < 4; ++u) {
+        if (tt + u >= n_tok) break;
+        const int ti = tt + u;
+        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv[u]);
+        float x[4], g[4];
 #pragma unroll
-        for (int j = 0; j < P; ++j) s += sdp[tt][j] * wv[j][q];
-        acc[q] += ah * g[q] + rr * s - cc * x[q];
+        for (int q = 0; q < 2; ++q) {
+          const float2 a2 = __bfloat1622float2(xh[q]);
+          const float2 c2 = __bfloat1622float2(gh[q]);
+          x[2 * q] = a2.x; x[2 * q + 1] = a2.y;
+          g[2 * q] = c2.x; g[2 * q + 1] = c2.y;
+        }
+        const float ah = sa[ti][h];
+        const float rr = scoef[ti][0], cc = scoef[ti][1];
+        float acc[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < P; ++j) sum += sdp[ti][j] * wv[j][q];
+          acc[q] = ah * g[q] + rr * sum - cc * x[q];
+        }
+        uint2 ov;
+        __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
+        oh[0] = __floats2bfloat162_rn(acc[0], acc[1]);
+        oh[1] = __floats2bfloat162_rn(acc[2], acc[3]);
+        *reinterpret_cast<uint2*>(dX + static_cast<int64_t>(t0 + ti) * F + f0) = ov;
       }
-      uint2 ov;
-      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
-      oh[0] = __floats2bfloat162_rn(acc[0], acc[1]);
-      oh[1] = __floats2bfloat162_rn(acc[2], acc[3]);
-      *reinterpret_cast<uint2*>(dX + off) = ov;
     }
   }
 }

@@ -177,9 +177,10 @@ def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None, chunk: int
             t1 = min(t, t0 + chunk)
             qc = q[bi, t0:t1].reshape((t1 - t0) * nh, c)
             s = gemm.gemm_nt(qc, keys_b[bi], out_dtype=torch.float32).view(t1 - t0, nh, n_blocks).clamp_(min=0.0)
-            if vis_bias is not None:
-                s += vis_bias[bi].view(1, 1, n_blocks) * 0.5
-            sc = torch.einsum("thn,th->tn", s, w[bi, t0:t1].float())
+            wc = w[bi, t0:t1].float()
+            sc = torch.bmm(wc.unsqueeze(1), s).squeeze(1)  # sum_h w_h relu(q_h . k)
+            if vis_bias is not None:  # sum_h w_h (relu(.) + b/2) = ... + (b/2) sum_h w_h
+                sc += 0.5 * vis_bias[bi].view(1, n_blocks) * wc.sum(-1, keepdim=True)
             qpos = torch.arange(t0, t1, device=h.device).view(-1, 1)
             sc.masked_fill_(~(block_end.view(1, -1) < qpos), float("-inf"))
             vals, ids = sc.topk(k_eff, dim=-1)

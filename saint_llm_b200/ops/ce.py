@@ -1,11 +1,11 @@
 """Fused LM-head + (softcap) + cross-entropy without materialising (B, T, V) logits.
 
 Token rows are processed in chunks: logits_chunk = h_chunk W^T on the native GEMM (fp32
-output), optional Gemma softcap ``c * tanh(z / c)``, log-sum-exp and the target logit.
-Backward recomputes each chunk's logits and forms ``dz = softmax - onehot`` (times the
-softcap derivative) before two native GEMMs: ``dh = dz W`` and ``dW += dz^T h`` (into
-``W.main_grad`` when present).  Value and gradients equal ``F.cross_entropy`` on the
-full logits (mean over rows).  ``token_logprobs`` serves GRPO-style log-probabilities.
+output), then one native kernel per row computes the (softcapped) log-sum-exp and the
+target logit.  Backward recomputes each chunk's logits; a native kernel forms
+``dz = scale * (softmax - onehot) * softcap'`` directly in bf16 before two native GEMMs:
+``dh = dz W`` and ``dW += dz^T h`` (into ``W.main_grad`` when present).  Value and
+gradients equal ``F.cross_entropy`` on the full logits (mean over rows).  ``token_logprobs`` serves GRPO-style log-probabilities.
 """
 
 from __future__ import annotations
@@ -14,7 +14,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
-from saint_llm_b200.ops import gemm
+from saint_llm_b200.ops import backend, gemm
 
 CHUNK_ROWS = 4096
 
@@ -23,64 +23,48 @@ def _bf16(t: Tensor) -> Tensor:
     return t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)
 
 
-def _logits(hc: Tensor, wb: Tensor, softcap: float | None) -> Tensor:
-    z = gemm.gemm_nt(hc, wb, out_dtype=torch.float32)
-    if softcap is not None:
-        z = softcap * torch.tanh(z / softcap)
-    return z
-
-
 class _LMHeadCEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h: Tensor, weight: Tensor, target: Tensor, softcap: float | None) -> Tensor:  # type: ignore[override]
         d = h.shape[-1]
         h2 = _bf16(h.reshape(-1, d)).contiguous()
-        t2 = target.reshape(-1)
+        t2 = target.reshape(-1).contiguous()
         n = h2.shape[0]
         # pad rows to a multiple of 64 once so the weight-gradient GEMM (K = rows) needs no copy
         n_pad = (n + 63) // 64 * 64
         if n_pad != n:
             h2 = F.pad(h2, (0, 0, 0, n_pad - n))
         wb = _bf16(weight)
-        total = torch.zeros((), dtype=torch.float32, device=h.device)
+        ext = backend.ext()
+        cap = float(softcap or 0.0)
         lse_all = torch.empty(n, dtype=torch.float32, device=h.device)
+        nll = torch.empty(n, dtype=torch.float32, device=h.device)
         for r0 in range(0, n, CHUNK_ROWS):
             r1 = min(n, r0 + CHUNK_ROWS)
-            z = _logits(h2[r0:r1], wb, softcap)
-            lse = torch.logsumexp(z, dim=-1)
-            lse_all[r0:r1] = lse
-            total += (lse - z.gather(1, t2[r0:r1, None]).squeeze(1)).sum()
+            z = gemm.gemm_nt(h2[r0:r1], wb, out_dtype=torch.float32)
+            ext.ce_fwd(z, t2[r0:r1], cap, lse_all[r0:r1], nll[r0:r1])
         ctx.save_for_backward(h2, weight, t2, lse_all)
-        ctx.softcap = softcap
+        ctx.softcap = cap
         ctx.hshape = h.shape
         ctx.n = n
-        return total / max(n, 1)
+        return nll.sum() / max(n, 1)
 
     @staticmethod
     def backward(ctx, g: Tensor):  # type: ignore[override]
         h2, weight, t2, lse_all = ctx.saved_tensors
-        softcap, n = ctx.softcap, ctx.n
+        cap, n = ctx.softcap, ctx.n
         wb = _bf16(weight)
-        scale = g.float() / max(n, 1)
+        ext = backend.ext()
+        scale = (g.float() / max(n, 1)).reshape(1).contiguous()
         dh = torch.empty(n, h2.shape[1], dtype=torch.bfloat16, device=h2.device)
         mg = getattr(weight, "main_grad", None)
         dw = mg if mg is not None else torch.zeros(weight.shape, dtype=torch.float32, device=h2.device)
         for r0 in range(0, n, CHUNK_ROWS):
             r1 = min(n, r0 + CHUNK_ROWS)
             rp = min(h2.shape[0], (r1 + 63) // 64 * 64) if r1 == n else r1
-            raw = gemm.gemm_nt(h2[r0:rp], wb, out_dtype=torch.float32)
-            if softcap is not None:
-                th = torch.tanh(raw / softcap)
-                z = softcap * th
-            else:
-                z = raw
-            p = torch.exp(z[: r1 - r0] - lse_all[r0:r1, None])
-            p[torch.arange(r1 - r0, device=p.device), t2[r0:r1]] -= 1.0
-            p *= scale
-            if softcap is not None:
-                p *= 1.0 - th[: r1 - r0] * th[: r1 - r0]
-            pb = torch.zeros(rp - r0, p.shape[1], dtype=torch.bfloat16, device=p.device)
-            pb[: r1 - r0] = p
+            raw = gemm.gemm_nt(h2[r0:r1], wb, out_dtype=torch.float32)
+            pb = torch.empty(rp - r0, raw.shape[1], dtype=torch.bfloat16, device=h2.device)
+            ext.ce_bwd(raw, t2[r0:r1], lse_all[r0:r1], cap, scale, pb)  # rows past r1 are zero
             gemm.gemm_nt(pb[: r1 - r0], wb.t(), out=dh[r0:r1])
             gemm.gemm_nt(pb.t(), h2[r0:rp].t(), out=dw, accumulate=True)
         dweight = None if mg is not None else dw.to(weight.dtype)
@@ -96,15 +80,17 @@ def lm_head_cross_entropy(h: Tensor, weight: Tensor, target: Tensor, *, softcap:
 def token_logprobs(h: Tensor, weight: Tensor, target: Tensor, *, softcap: float | None = None) -> Tensor:
     """log p(target) per row without materialising all logits at once (no grad)."""
     d = h.shape[-1]
-    h2 = _bf16(h.reshape(-1, d))
-    t2 = target.reshape(-1)
+    h2 = _bf16(h.reshape(-1, d)).contiguous()
+    t2 = target.reshape(-1).contiguous()
     wb = _bf16(weight)
-    out = torch.empty(h2.shape[0], dtype=torch.float32, device=h.device)
-    for r0 in range(0, h2.shape[0], CHUNK_ROWS):
-        r1 = min(h2.shape[0], r0 + CHUNK_ROWS)
-        z = _logits(h2[r0:r1], wb, softcap)
-        out[r0:r1] = z.gather(1, t2[r0:r1, None]).squeeze(1) - torch.logsumexp(z, -1)
-    return out.view(target.shape)
+    n = h2.shape[0]
+    lse = torch.empty(n, dtype=torch.float32, device=h.device)
+    nll = torch.empty(n, dtype=torch.float32, device=h.device)
+    for r0 in range(0, n, CHUNK_ROWS):
+        r1 = min(n, r0 + CHUNK_ROWS)
+        z = gemm.gemm_nt(h2[r0:r1], wb, out_dtype=torch.float32)
+        backend.ext().ce_fwd(z, t2[r0:r1], float(softcap or 0.0), lse[r0:r1], nll[r0:r1])
+    return (-nll).view(target.shape)
 
 
 __all__ = ["lm_head_cross_entropy", "token_logprobs"]

@@ -128,11 +128,12 @@ static int num_sms(int dev) {
 
 // Kernel instantiations live in gemm_inst_*.cu (compiled in parallel).
 void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
-                         const CUtensorMap& md, const GemmParams& p, int grid, cudaStream_t stream);
+                         const CUtensorMap& md, const CUtensorMap& mx, const GemmParams& p, int grid,
+                         cudaStream_t stream);
 
 static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap& ma, const CUtensorMap& mb0,
                      const CUtensorMap& mb1, const CUtensorMap& md, const GemmParams& p, int grid,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, const CUtensorMap* mx = nullptr) {
   struct V { bool a, b; int bm, ep; };
   static const V table[] = {
       {false, false, kBSingle, kEpiBF16},
@@ -156,7 +157,7 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
   for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
     const V& v = table[i];
     if (v.a == a_mn && v.b == b_mn && v.bm == bmode && v.ep == epi) {
-      gemm_launch_variant(i, ma, mb0, mb1, md, p, grid, stream);
+      gemm_launch_variant(i, ma, mb0, mb1, md, mx ? *mx : md, p, grid, stream);
       return;
     }
   }
@@ -306,15 +307,20 @@ void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   // D as one (rows, cols) row-major buffer; problems address it by row (d_off is a multiple of d_ld).
   CUtensorMap md = map_for(va, 128);  // placeholder when D is not TMA-addressable
-  if (mode != 0 && out.is_contiguous() && out.numel() > 0) {
+  CUtensorMap mx = md;
+  if (out.is_contiguous() && out.numel() > 0) {
     const int64_t cols = out.size(-1);
-    p.tma_d = map_d_for(out.data_ptr(), out.scalar_type() == at::kFloat, cols, out.numel() / cols, 1, cols, 0, md)
-                  ? 1 : 0;
+    bool ok = map_d_for(out.data_ptr(), out.scalar_type() == at::kFloat, cols, out.numel() / cols, 1, cols, 0, md);
+    if (mode == 0) {  // SwiGLU: pre-activations (rows, 2I) through a second map
+      const int64_t ac = aux.size(-1);
+      ok = ok && aux.is_contiguous() && map_d_for(aux.data_ptr(), false, ac, aux.numel() / ac, 1, ac, 0, mx);
+    }
+    p.tma_d = ok ? 1 : 0;
   }
   switch (mode) {
     case 0: {
       CUtensorMap ma = map_for(va, 128), m0 = map_for(vb0, 128), m1 = map_for(vb1, 128);
-      dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, md, p, grid, stream);
+      dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, md, p, grid, stream, &mx);
       break;
     }
     case 1: {
@@ -360,8 +366,11 @@ void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Te
   p.err = err.data_ptr<int>();
   const int tiles = ((M + 127) / 128) * ((I + 127) / 128);
   if (tiles == 0) return;
-  dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, ma, p, std::min<int>(tiles, num_sms(x.get_device())),
-           at::cuda::getCurrentCUDAStream());
+  CUtensorMap md = ma, mx = ma;
+  p.tma_d = (map_d_for(act.data_ptr(), false, I, M, 1, s.d_ld, 0, md) &&
+             map_d_for(pre.data_ptr(), false, 2 * I, M, 1, s.aux_ld, 0, mx)) ? 1 : 0;
+  dispatch(false, false, kBSplitN, kEpiSwiGLU, ma, m0, m1, md, p, std::min<int>(tiles, num_sms(x.get_device())),
+           at::cuda::getCurrentCUDAStream(), &mx);
 }
 
 // dx = dpre[:, :I] Wg + dpre[:, I:] Wu   (B split along K between the two weights)
@@ -452,32 +461,33 @@ void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t
 int64_t problem_bytes() { return sizeof(GemmProblem); }
 
 bool gemm_launch_group0(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group1(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group2(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group3(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group4(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group5(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group6(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 bool gemm_launch_group7(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
-                        const GemmParams&, int, cudaStream_t);
+                        const CUtensorMap&, const GemmParams&, int, cudaStream_t);
 
 void gemm_launch_variant(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
-                         const CUtensorMap& md, const GemmParams& p, int grid, cudaStream_t stream) {
-  const bool ok = gemm_launch_group0(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group1(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group2(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group3(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group4(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group5(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group6(variant, ma, mb0, mb1, md, p, grid, stream) ||
-                  gemm_launch_group7(variant, ma, mb0, mb1, md, p, grid, stream);
+                         const CUtensorMap& md, const CUtensorMap& mx, const GemmParams& p, int grid,
+                         cudaStream_t stream) {
+  const bool ok = gemm_launch_group0(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group1(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group2(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group3(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group4(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group5(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group6(variant, ma, mb0, mb1, md, mx, p, grid, stream) ||
+                  gemm_launch_group7(variant, ma, mb0, mb1, md, mx, p, grid, stream);
   TORCH_CHECK(ok, "GEMM variant not instantiated");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

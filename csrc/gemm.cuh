@@ -61,9 +61,11 @@ struct GemmParams {
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // bf16: 64 elements = 128 bytes = one swizzle row
 
-// Epilogue staging: one 32-row x 128-byte buffer per epilogue warp (128B-swizzled, the
-// layout of a D tensor-map box), written by the warp and drained by a TMA store/reduce.
+// Epilogue staging: two 32-row x 128-byte buffers per epilogue warp (128B-swizzled, the
+// layout of a D tensor-map box), written by the warp and drained by TMA stores/reduces;
+// the warp fills one buffer while the previous store still reads the other.
 constexpr int kEpiStageBytes = 32 * 128;
+constexpr int kEpiBufs = 2;
 
 template <int BN>
 struct GemmSmem {
@@ -72,9 +74,42 @@ struct GemmSmem {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = kStages * kStageBytes;          // 1024-aligned
-  static constexpr int kBarOffset = kEpiOffset + 4 * kEpiStageBytes;
+  static constexpr int kBarOffset = kEpiOffset + 4 * kEpiBufs * kEpiStageBytes;
   static constexpr int kTotal = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
+
+// Write this warp's 32 rows x 128 B (row = lane) into the next staging buffer, 128B-swizzled,
+// then (lane 0, if `issue`) store or reduce-add it to `map` at (c0, c1, c2).  `pack(q)` returns
+// the q-th 16-byte chunk of the calling lane's row.
+template <typename Pack>
+__device__ __forceinline__ void stage_store(uint8_t* stg_warp, int& buf, int lane, Pack pack, const CUtensorMap* map,
+                                            bool reduce, int c0, int c1, int c2, bool issue) {
+  uint8_t* b = stg_warp + buf * kEpiStageBytes;
+  if (lane == 0) bulk_wait_read<kEpiBufs - 1>();  // the store that last used this buffer has read it
+  __syncwarp();
+  uint8_t* myrow = b + lane * 128;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pack(q);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && issue) {
+    if (reduce) tma_reduce_add_3d(map, b, c0, c1, c2);
+    else tma_store_3d(map, b, c0, c1, c2);
+    bulk_commit_group();
+  }
+  // Only a buffer that a committed store reads moves the rotation: with an un-issued chunk the
+  // next write may reuse this buffer, and wait_read<kEpiBufs - 1> keeps its meaning.
+  if (issue) buf = (buf + 1) % kEpiBufs;
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+  __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]);
+  __nv_bfloat162 h3 = __floats2bfloat162_rn(v[6], v[7]);
+  return make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                    *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+}
 
 __device__ __forceinline__ int tiles_m(const GemmProblem& p) { return (p.m + kBM - 1) / kBM; }
 
@@ -115,7 +150,7 @@ template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
 __global__ void __launch_bounds__(192, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
                  const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_d,
-                 const GemmParams P) {
+                 const __grid_constant__ CUtensorMap map_aux, const GemmParams P) {
   using S = GemmSmem<BN>;
   constexpr int kStages = S::kStages;
   constexpr uint32_t kIdesc = make_idesc_f16(kBM, BN, 1, 1, A_MN, B_MN);
@@ -151,6 +186,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     tma_prefetch_desc(&map_b0);
     if (BMODE != kBSingle) tma_prefetch_desc(&map_b1);
     if (P.tma_d) tma_prefetch_desc(&map_d);
+    if (P.tma_d && EPI == kEpiSwiGLU) tma_prefetch_desc(&map_aux);
   }
   tc_fence_before();
   __syncthreads();
@@ -260,6 +296,8 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    uint8_t* stg = smem + S::kEpiOffset + quarter * kEpiBufs * kEpiStageBytes;
+    int sbuf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     int hint = 0;
@@ -275,7 +313,50 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       if (split) bt = 0;  // every K-slice reduces into the same D
       const long long dbase = pr.d_off + static_cast<long long>(bt) * pr.d_bstride + row * pr.d_ld;
-      if constexpr (EPI == kEpiSwiGLU) {
+      if (EPI == kEpiSwiGLU && P.tma_d && (P.probs == nullptr || mt * kBM + kBM <= pr.m)) {
+        // act -> map_d, gate / up pre-activations -> map_aux columns [0, n) / [n, 2n)
+        const int half = BN / 2;
+        const int drow = static_cast<int>(pr.d_off / pr.d_ld) + mt * kBM + quarter * 32;
+        const int arow = static_cast<int>(pr.aux_off / pr.aux_ld) + mt * kBM + quarter * 32;
+        const bool rows_in = mt * kBM + quarter * 32 < pr.m;
+#pragma unroll 1
+        for (int c = 0; c < half; c += 64) {
+          uint32_t g[64], u[64];
+          tmem_ld32(t_row + c, *reinterpret_cast<uint32_t(*)[32]>(g));
+          tmem_ld32(t_row + c + 32, *reinterpret_cast<uint32_t(*)[32]>(g + 32));
+          tmem_ld32(t_row + half + c, *reinterpret_cast<uint32_t(*)[32]>(u));
+          tmem_ld32(t_row + half + c + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+          tmem_ld_wait();
+          if (zero_k) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) g[j] = u[j] = 0u;
+          }
+          const int col0 = nt * half + c;
+          const bool issue = rows_in && col0 < pr.n;
+          const float gmax = P.gate_max, lo = P.lin_lo, hi = P.lin_hi;
+          stage_store(stg, sbuf, lane, [&](int q) {
+            float a8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float gv = __uint_as_float(g[8 * q + e]), uv = __uint_as_float(u[8 * q + e]);
+              a8[e] = silu_f(fminf(gv, gmax)) * fminf(fmaxf(uv, lo), hi);
+            }
+            return pack_bf16x8(a8);
+          }, &map_d, false, col0, drow, 0, issue);
+          stage_store(stg, sbuf, lane, [&](int q) {
+            float g8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g8[e] = __uint_as_float(g[8 * q + e]);
+            return pack_bf16x8(g8);
+          }, &map_aux, false, col0, arow, 0, issue);
+          stage_store(stg, sbuf, lane, [&](int q) {
+            float u8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) u8[e] = __uint_as_float(u[8 * q + e]);
+            return pack_bf16x8(u8);
+          }, &map_aux, false, pr.n + col0, arow, 0, issue);
+        }
+      } else if constexpr (EPI == kEpiSwiGLU) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d);
         __nv_bfloat16* pre = reinterpret_cast<__nv_bfloat16*>(P.aux);
         const int half = BN / 2;
@@ -338,7 +419,6 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // (single mode: per batch, 3-D map); table-mode tiles are whole 128-row tiles.
         constexpr bool kF32 = (EPI == kEpiF32 || EPI == kEpiF32Acc);
         constexpr int kCW = kF32 ? 32 : 64;  // columns per 128-byte row chunk
-        uint8_t* stg = smem + S::kEpiOffset + quarter * kEpiStageBytes;
         const float rs = (EPI == kEpiRowScaleBF16 && row_ok) ? P.rowscale[pr.aux_off + row] : 1.0f;
         const int drow = static_cast<int>(pr.d_off / pr.d_ld) + mt * kBM + quarter * 32;
 #pragma unroll 1
@@ -356,37 +436,34 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           if constexpr (EPI == kEpiAxpbyBF16) {
             if (row_ok) {
               const __nv_bfloat16* cin = reinterpret_cast<const __nv_bfloat16*>(P.aux) + dbase + col0;
-              for (int j = 0; j < kCW; ++j)
-                if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
-            }
-          }
-          if (lane == 0) bulk_wait_read_all();  // previous chunk's store has left the buffer
-          __syncwarp();
-          uint8_t* myrow = stg + lane * 128;
+              if (col0 + kCW <= pr.n && (reinterpret_cast<uintptr_t>(cin) & 15) == 0) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {  // 16-byte chunk q of this row, 128B-swizzled
-            uint4 pk;
-            if constexpr (kF32) {
-              pk = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
-                              __float_as_uint(v[4 * q + 3]));
-            } else {
-              __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q], v[8 * q + 1]);
-              __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
-              __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
-              pk = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                              *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+                for (int j = 0; j < kCW; j += 8) {  // 16-byte loads of C
+                  const uint4 cv = *reinterpret_cast<const uint4*>(cin + j);
+                  const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&cv);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float2 f = __bfloat1622float2(ch[q]);
+                    v[j + 2 * q] += P.beta * f.x;
+                    v[j + 2 * q + 1] += P.beta * f.y;
+                  }
+                }
+              } else {
+                for (int j = 0; j < kCW; ++j)
+                  if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
+              }
             }
-            *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pk;
           }
-          fence_proxy_async_smem();
-          __syncwarp();
           // Boxes starting past the problem are skipped (never issue a fully clipped store).
-          if (lane == 0 && col0 < pr.n && mt * kBM + quarter * 32 < pr.m) {
-            if (EPI == kEpiF32Acc) tma_reduce_add_3d(&map_d, stg, col0, drow, bt);
-            else tma_store_3d(&map_d, stg, col0, drow, bt);
-            bulk_commit_group();
-          }
+          const bool issue = col0 < pr.n && mt * kBM + quarter * 32 < pr.m;
+          stage_store(stg, sbuf, lane, [&](int q) {
+            if constexpr (kF32) {
+              return make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                                __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+            } else {
+              return pack_bf16x8(v + 8 * q);
+            }
+          }, &map_d, EPI == kEpiF32Acc, col0, drow, bt, issue);
         }
       } else {
         const float rs = (EPI == kEpiRowScaleBF16 && row_ok) ? P.rowscale[pr.aux_off + row] : 1.0f;

@@ -5,19 +5,20 @@ namespace sv4 {
 
 template <int BN, bool A_MN, bool B_MN, int BMODE, int EPI>
 static void launch_one(const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1, const CUtensorMap& md,
-                       const GemmParams& p, int grid, cudaStream_t stream) {
+                       const CUtensorMap& mx, const GemmParams& p, int grid, cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, BMODE, EPI>;
   constexpr int smem = GemmSmem<BN>::kTotal;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  kern<<<grid, 192, smem, stream>>>(ma, mb0, mb1, md, p);
+  kern<<<grid, 192, smem, stream>>>(ma, mb0, mb1, md, mx, p);
 }
 
 bool gemm_launch_group6(int variant, const CUtensorMap& ma, const CUtensorMap& mb0, const CUtensorMap& mb1,
-                         const CUtensorMap& md, const GemmParams& p, int grid, cudaStream_t stream) {
+                         const CUtensorMap& md, const CUtensorMap& mx, const GemmParams& p, int grid,
+                         cudaStream_t stream) {
   switch (variant) {
-    case 11: launch_one<256, true, false, kBSingle, kEpiBF16>(ma, mb0, mb1, md, p, grid, stream); return true;
-    case 12: launch_one<256, true, false, kBSingle, kEpiF32>(ma, mb0, mb1, md, p, grid, stream); return true;
-    case 13: launch_one<256, true, false, kBSingle, kEpiF32Acc>(ma, mb0, mb1, md, p, grid, stream); return true;
+    case 11: launch_one<256, true, false, kBSingle, kEpiBF16>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
+    case 12: launch_one<256, true, false, kBSingle, kEpiF32>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
+    case 13: launch_one<256, true, false, kBSingle, kEpiF32Acc>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
     default: return false;
   }
 }

@@ -312,7 +312,7 @@ torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 // Stream X: (T, F) with F = n*D.  W: (P, F) gate projections with the RMSNorm weight folded
 // in (P = 2n + n^2).  The raw dots q = X W^T come from the GEMM, the row sums of squares from
 // row_sumsq; the gates kernel turns them into r = 1/rms and p = r q.
-constexpr int kMhcTok = 128;   // tokens per CTA of the split backward (amortises the W slice)
+constexpr int kMhcTok = 32;    // tokens per CTA of the split backward
 // ssq[t] = sum_k X[t, k]^2 (bf16 rows, fp32 result): one warp per row, 16-byte loads.
 // The mHC projection itself (X W^T, skinny N) runs on the tcgen05 GEMM with split-K.
 __global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ X, float* __restrict__ ssq, int T, int F) {

@@ -80,7 +80,8 @@ __global__ void ce_fwd_kernel(const float* __restrict__ z, const int64_t* __rest
 
 __global__ void ce_bwd_kernel(const float* __restrict__ z, const int64_t* __restrict__ target,
                               const float* __restrict__ lse, int rows, int rows_out, int V, int ld, float softcap,
-                              const float* __restrict__ scale_ptr, __nv_bfloat16* __restrict__ dz) {
+                              const float* __restrict__ scale_ptr, int scale_per_row,
+                              __nv_bfloat16* __restrict__ dz) {
   const int r = blockIdx.x;
   __nv_bfloat16* out = dz + static_cast<int64_t>(r) * V;
   if (r >= rows) {  // padding rows of the weight-gradient GEMM operand
@@ -90,7 +91,7 @@ __global__ void ce_bwd_kernel(const float* __restrict__ z, const int64_t* __rest
   const float* zr = z + static_cast<int64_t>(r) * ld;
   const float l = lse[r];
   const int64_t t = target[r];
-  const float scale = *scale_ptr;
+  const float scale = scale_ptr[scale_per_row ? r : 0];
   auto grad = [&](int v) {
     float zz = zr[v], d = 1.f;
     if (softcap > 0.f) {
@@ -143,16 +144,19 @@ void ce_fwd(torch::Tensor z, torch::Tensor target, double softcap, torch::Tensor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// dz: (rows_out >= rows, V) bf16; rows past `rows` are zero-filled.  scale: device scalar.
+// dz: (rows_out >= rows, V) bf16; rows past `rows` are zero-filled.  scale: one device
+// scalar for every row, or one value per row (per-token weights, e.g. policy gradients).
 void ce_bwd(torch::Tensor z, torch::Tensor target, torch::Tensor lse, double softcap, torch::Tensor scale,
             torch::Tensor dz) {
   c10::cuda::CUDAGuard guard(z.device());
   const int rows = z.size(0), V = z.size(1), ld = z.stride(0), rows_out = dz.size(0);
   TORCH_CHECK(z.stride(1) == 1 && dz.is_contiguous() && dz.size(1) == V, "ce_bwd shapes");
+  TORCH_CHECK(scale.numel() == 1 || scale.numel() == rows, "ce_bwd: scale must have 1 or `rows` values");
   if (rows_out == 0) return;
   ce_bwd_kernel<<<rows_out, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       z.data_ptr<float>(), target.data_ptr<int64_t>(), lse.data_ptr<float>(), rows, rows_out, V, ld,
-      static_cast<float>(softcap), scale.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dz.data_ptr()));
+      static_cast<float>(softcap), scale.data_ptr<float>(), scale.numel() == rows && rows > 1 ? 1 : 0,
+      reinterpret_cast<__nv_bfloat16*>(dz.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -40,6 +40,15 @@ def _grad(p: Tensor) -> Tensor | None:
     return mg if mg is not None else p.grad
 
 
+def _active_grad(opt: torch.optim.Optimizer, p: Tensor) -> Tensor | None:
+    """The gradient to step with, or None when the parameter is skipped this step (no gradient,
+    or a ``param_filter`` -- e.g. ZeRO ownership -- excludes it)."""
+    flt = getattr(opt, "param_filter", None)
+    if flt is not None and not flt(p):
+        return None
+    return _grad(p)
+
+
 @runtime_checkable
 class _QKClippable(Protocol):
     _last_max_attn_logit: float
@@ -135,7 +144,7 @@ def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: st
     lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
     by_shape: dict[tuple[Any, ...], list[Tensor]] = {}
     for p in group["params"]:
-        g = _grad(p)
+        g = _active_grad(opt, p)
         if g is None:
             continue
         if p.dim() != 2 and (strict_2d or p.dim() != 3):
@@ -231,6 +240,7 @@ class Muon(_QKClipMixin, torch.optim.Optimizer):
                                                 ns_iter_stage2, ns_coeffs_stage1, ns_coeffs_stage2))
         self._init_qk_clip(qk_clip_enabled, qk_clip_tau, qk_clip_layers)
         self.ns_impl = ns_impl
+        self.param_filter: Callable[[Tensor], bool] | None = None
         self.strict_2d = strict_2d
 
     @torch.no_grad()
@@ -266,6 +276,7 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
         super().__init__([g for g in groups if g["params"]], {})
         self._init_qk_clip(qk_clip_enabled, qk_clip_tau, qk_clip_layers)
         self.ns_impl = ns_impl
+        self.param_filter: Callable[[Tensor], bool] | None = None
 
     @torch.no_grad()
     def step(self, closure: Callable[[], Tensor] | None = None) -> Tensor | None:
@@ -284,7 +295,7 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
 
     @torch.no_grad()
     def _adamw_group_step(self, group: dict[str, Any]) -> None:
-        params = [p for p in group["params"] if _grad(p) is not None]
+        params = [p for p in group["params"] if _active_grad(self, p) is not None]
         if not params:
             return
         b1, b2 = group["betas"]

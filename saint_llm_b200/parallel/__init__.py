@@ -1,12 +1,52 @@
 """Parallelism: expert parallelism (dispatch/combine), data-parallel gradient sync, and
 the distributed-training building blocks of the reference (ZeRO planner, DiLoCo/NoLoCo,
-gradient compression, verification, reputation, decentralised rounds)."""
+gradient compression, verification, reputation, decentralised rounds, miner/validator
+protocol, FSDP2 wrapping)."""
 
+from saint_llm_b200.parallel.compression import (
+    CompressedGradient,
+    SparseLoCoBloom,
+    TopKWithResidualCompressor,
+    bloom_size_for,
+    decompress,
+    sparse_loco_compress,
+    top_k_compression,
+)
 from saint_llm_b200.parallel.ep import (
     DispatchPlan,
     combine_outputs_by_expert,
     dispatch_tokens_by_expert,
     setup_expert_parallel,
 )
+from saint_llm_b200.parallel.local_sgd import (
+    AllReduceReducer,
+    DiLoCo,
+    DiLoCoConfig,
+    IdentityReducer,
+    NoLoCo,
+    NoLoCoConfig,
+    RingAllReduceSimulator,
+    ring_all_reduce,
+)
+from saint_llm_b200.parallel.trust import (
+    DecentralizedTrainingRound,
+    GradientVerifier,
+    PeerReputationConfig,
+    PeerReputationTracker,
+    PeerSubmission,
+    reputation_weighted_reduce,
+)
+from saint_llm_b200.parallel.zero import (
+    BucketAssignment,
+    ZeroOptimizerSync,
+    hybrid_zero_assign,
+    pack_buckets_by_cost,
+)
 
-__all__ = ["DispatchPlan", "combine_outputs_by_expert", "dispatch_tokens_by_expert", "setup_expert_parallel"]
+__all__ = ["AllReduceReducer", "BucketAssignment", "CompressedGradient", "DecentralizedTrainingRound", "DiLoCo",
+           "DiLoCoConfig", "DispatchPlan", "GradientVerifier", "IdentityReducer", "NoLoCo", "NoLoCoConfig",
+           "PeerReputationConfig", "PeerReputationTracker", "PeerSubmission", "RingAllReduceSimulator",
+           "SparseLoCoBloom", "TopKWithResidualCompressor", "ZeroOptimizerSync", "bloom_size_for",
+           "combine_outputs_by_expert", "decompress", "dispatch_tokens_by_expert", "hybrid_zero_assign",
+           "pack_buckets_by_cost", "reputation_weighted_reduce", "ring_all_reduce", "setup_expert_parallel",
+           "sparse_loco_compress", "top_k_compression"]

@@ -33,6 +33,11 @@ class CSAConfig(_Frozen):
     attention_top_k: int = 512
 
 
+class NSAConfig(_Frozen):
+    compression_rate: int = 32
+    selection_k: int = 16
+
+
 class HCAConfig(_Frozen):
     """Heavily compressed attention: compression rate m'."""
 
@@ -117,10 +122,12 @@ class ModelConfig(_Frozen):
     vocab_size: int = 131072
 
     first_dense_swa_layers: int = 2
-    attention_pattern: Literal["csa_hca_interleaved"] = "csa_hca_interleaved"
+    # "nsa" (an extension): every layer after the dense SWA layers is NSA
+    attention_pattern: Literal["csa_hca_interleaved", "nsa"] = "csa_hca_interleaved"
 
     csa: CSAConfig = Field(default_factory=CSAConfig)
     hca: HCAConfig = Field(default_factory=HCAConfig)
+    nsa: NSAConfig = Field(default_factory=NSAConfig)
     attention: AttentionConfig = Field(default_factory=AttentionConfig)
     moe: MoEConfig = Field(default_factory=MoEConfig)
     mhc: MHCConfig = Field(default_factory=MHCConfig)
@@ -142,10 +149,12 @@ class ModelConfig(_Frozen):
     activation_checkpointing: bool = False
 
     # ---- helpers -------------------------------------------------------------------
-    def layer_kind(self, layer_idx: int) -> Literal["swa", "csa", "hca"]:
+    def layer_kind(self, layer_idx: int) -> Literal["swa", "csa", "hca", "nsa"]:
         """Attention type of block ``layer_idx`` (SWA first, then CSA/HCA alternating)."""
         if layer_idx < self.first_dense_swa_layers:
             return "swa"
+        if self.attention_pattern == "nsa":
+            return "nsa"
         return "csa" if (layer_idx - self.first_dense_swa_layers) % 2 == 0 else "hca"
 
     def to_json(self) -> str:
@@ -338,6 +347,7 @@ __all__ = [
     "AttentionConfig",
     "CSAConfig",
     "HCAConfig",
+    "NSAConfig",
     "MHCConfig",
     "MTPConfig",
     "MoEConfig",

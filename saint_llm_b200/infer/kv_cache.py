@@ -239,7 +239,7 @@ class KVCacheBundle:
                   device: torch.device | str | None = None, dtype: torch.dtype | None = None,
                   keep_history: bool = False) -> KVCacheBundle:
         """One cache per block by attention type; dtype/device default to the model's."""
-        from saint_llm_b200.models.attention import CSA, HCA, SWAttention
+        from saint_llm_b200.models.attention import CSA, HCA, NSAttention, SWAttention
 
         cfg = model.cfg  # type: ignore[attr-defined]
         p = next(model.parameters())  # type: ignore[attr-defined]
@@ -256,7 +256,7 @@ class KVCacheBundle:
                                               **ckw))
             elif isinstance(a, HCA):
                 layers.append(HCAKVCacheLayer(max_seq_len, d, hd, cfg.hca.compression_rate, **ckw))
-            elif isinstance(a, SWAttention):
+            elif isinstance(a, (SWAttention, NSAttention)):
                 layers.append(SWAKVCacheLayer(max_seq_len, hd, **kw))
             else:
                 layers.append(None)

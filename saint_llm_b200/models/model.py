@@ -25,7 +25,7 @@ from torch import Tensor, nn
 from torch.utils.checkpoint import checkpoint
 
 from saint_llm_b200.config import ModelConfig
-from saint_llm_b200.models.attention import CSA, HCA, RMSNorm, SWAttention
+from saint_llm_b200.models.attention import CSA, HCA, NSAttention, RMSNorm, SWAttention
 from saint_llm_b200.models.init import normal_init, umup_init
 from saint_llm_b200.models.linear import LinearFactory, make_linear_factory
 from saint_llm_b200.models.mhc import MHC
@@ -55,6 +55,9 @@ class TransformerBlock(nn.Module):
             self.attention = SWAttention(cfg.hidden_dim, cfg.attention, linear_factory=linear_factory)
         elif kind == "csa":
             self.attention = CSA(cfg.hidden_dim, cfg.attention, cfg.csa, linear_factory=linear_factory)
+        elif kind == "nsa":
+            self.attention = NSAttention(cfg.hidden_dim, cfg.attention, compression_rate=cfg.nsa.compression_rate,
+                                         selection_k=cfg.nsa.selection_k, linear_factory=linear_factory)
         else:
             self.attention = HCA(cfg.hidden_dim, cfg.attention, cfg.hca, linear_factory=linear_factory)
         self.attn_mhc = MHC(cfg.hidden_dim, cfg.mhc, rms_norm_eps=cfg.rms_norm_eps)

@@ -28,6 +28,9 @@ import subprocess
 import sys
 import time
 
+# fewer fragmentation stalls near the 180 GB ceiling (must be set before CUDA initialises)
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -123,7 +126,8 @@ def build_ours(args, device, world):
     if world > 1:
         from saint_llm_b200.parallel import ep as ep_mod
 
-        grad_sync = ep_mod.setup_expert_parallel(model)
+        grad_sync = ep_mod.setup_expert_parallel(model, transport=args.ep_transport,
+                                                 capacity_factor=args.ep_capacity)
         torch.cuda.empty_cache()
     params = attach_main_grads(model)
     muon, adamw = split_for_muon_adamw(model)
@@ -195,6 +199,7 @@ def run_ours(args) -> dict:
         "config": {"model": MODEL_DESC, "n_layers": cfg.n_layers, "global_batch": world * args.seqs_per_gpu,
                    "seq_len": args.seq_len, "micro_batch": args.micro_batch,
                    "parallelism": f"ep{world}+dp{world}" if world > 1 else "single-gpu",
+                   "ep_transport": args.ep_transport if world > 1 else None,
                    "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
                    "l2": "inputs larger than L2 (the weights stream through HBM every step)",
                    "final_loss": final_loss,
@@ -222,7 +227,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seqs-per-gpu", type=int, default=32)
-    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--micro-batch", type=int, default=2)
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
+    ap.add_argument("--ep-capacity", type=float, default=2.0,
+                    help="receive capacity per rank in units of its own (token, slot) pairs; an overflow raises")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--linear-quant", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--ckpt", action="store_true", help="activation checkpointing per block")

@@ -69,6 +69,28 @@ void ce_bwd(torch::Tensor z, torch::Tensor target, torch::Tensor lse, double sof
             torch::Tensor dz);
 // data.cpp
 void bind_data(pybind11::module_& m);
+// ep.cu
+void ep_signal(std::vector<int64_t> flag_ptrs, int64_t phase, int64_t rank, int64_t epoch);
+void ep_post_counts(torch::Tensor counts, std::vector<int64_t> cnt_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                    int64_t slot, int64_t epoch);
+void ep_plan(torch::Tensor idx, torch::Tensor pos_local, torch::Tensor seg_start_local, torch::Tensor my_cnt,
+             torch::Tensor my_flags, int64_t slot, int64_t epoch, int64_t rank, int64_t ws, int64_t C,
+             torch::Tensor gpos, torch::Tensor seg_start_dst, torch::Tensor seg_rows_dst, torch::Tensor seg_pad_dst,
+             int64_t timeout_ns, torch::Tensor err);
+void ep_dispatch(torch::Tensor h, torch::Tensor gpos, int64_t C, std::vector<int64_t> x_ptrs);
+void ep_wait_zero(torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch, torch::Tensor buf,
+                  torch::Tensor seg_start, torch::Tensor seg_rows, int64_t timeout_ns, torch::Tensor err);
+void ep_combine(std::vector<int64_t> y_ptrs, torch::Tensor gpos, torch::Tensor gate, int64_t C, torch::Tensor out,
+                c10::optional<torch::Tensor> ypair, torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch,
+                int64_t timeout_ns, torch::Tensor err);
+void ep_combine_bwd(torch::Tensor dout, torch::Tensor ypair, torch::Tensor gate, torch::Tensor gpos, int64_t C,
+                    std::vector<int64_t> dy_ptrs, torch::Tensor dgate);
+void ep_dispatch_bwd(std::vector<int64_t> dx_ptrs, torch::Tensor gpos, int64_t C, torch::Tensor dh,
+                     torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch, int64_t timeout_ns,
+                     torch::Tensor err);
+std::tuple<torch::Tensor, std::string> symm_alloc(int64_t nbytes, int64_t device);
+int64_t symm_open(const std::string& handle, int64_t device);
+void symm_close(int64_t ptr, int64_t device);
 }  // namespace sv4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -100,6 +122,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_norm_fwd", &sv4::rope_norm_fwd);
   m.def("rope_norm_bwd", &sv4::rope_norm_bwd);
   m.def("row_sumsq", &sv4::row_sumsq);
+  m.def("ep_signal", &sv4::ep_signal);
+  m.def("ep_post_counts", &sv4::ep_post_counts);
+  m.def("ep_plan", &sv4::ep_plan);
+  m.def("ep_dispatch", &sv4::ep_dispatch);
+  m.def("ep_wait_zero", &sv4::ep_wait_zero);
+  m.def("ep_combine", &sv4::ep_combine);
+  m.def("ep_combine_bwd", &sv4::ep_combine_bwd);
+  m.def("ep_dispatch_bwd", &sv4::ep_dispatch_bwd);
+  m.def("symm_alloc", [](int64_t n, int64_t dev) {
+    auto r = sv4::symm_alloc(n, dev);
+    return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));
+  });
+  m.def("symm_open", [](pybind11::bytes h, int64_t dev) { return sv4::symm_open(std::string(h), dev); });
+  m.def("symm_close", &sv4::symm_close);
   m.def("mhc_gates_fwd", &sv4::mhc_gates_fwd);
   m.def("mhc_gates_bwd", &sv4::mhc_gates_bwd);
   m.def("mhc_premix", &sv4::mhc_premix);

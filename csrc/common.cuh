@@ -23,6 +23,7 @@ enum ErrorCode : int {
   kErrBadShape = 4,
   kErrPeerTimeout = 5,      // cross-GPU flag never arrived
   kErrBounds = 6,           // gathered index out of range (bounds-check mode)
+  kErrCapacity = 7,         // expert-parallel receive layout exceeded the buffer capacity
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {

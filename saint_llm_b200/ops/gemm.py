@@ -33,7 +33,7 @@ def error_word(device: torch.device) -> Tensor:
 
 ERROR_NAMES = {1: "timeout waiting for a TMA stage", 2: "timeout waiting for a free stage",
                3: "timeout waiting for a TMEM accumulator", 4: "bad shape", 5: "peer timeout",
-               6: "index out of bounds"}
+               6: "index out of bounds", 7: "expert-parallel receive capacity exceeded"}
 
 
 def check_errors(device: torch.device | None = None) -> None:

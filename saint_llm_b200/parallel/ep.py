@@ -110,6 +110,11 @@ def moe_forward_ep(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vis
     """``DeepSeekMoE`` forward with the routed experts sharded over the EP group."""
     from saint_llm_b200.ops import backend
 
+    if getattr(layer, "ep_comm", None) is not None and backend.native_for(x):
+        from saint_llm_b200.parallel.ep_p2p import moe_forward_p2p
+
+        return moe_forward_p2p(layer, x, token_ids, is_visual)
+
     b, t, d = x.shape
     h = layer.norm(x)
     idx, gate, aux = layer.route(h, token_ids, is_visual)
@@ -210,10 +215,25 @@ def make_grad_sync(expert_params: list[Tensor], group: dist.ProcessGroup | None,
     return sync
 
 
-def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None) -> Callable[[list[Tensor]], None]:
+def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",
+                          capacity_factor: float | None = None) -> Callable[[list[Tensor]], None]:
+    """Shard the experts over ``group`` and return the gradient synchroniser.
+
+    ``transport``: "p2p" moves tokens with the peer-memory kernels of ``parallel.ep_p2p``
+    (CUDA only), "nccl" with ``all_to_all_single``; "auto" picks p2p on CUDA."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
-    return make_grad_sync(shard_grouped_experts(model, rank, ws, group), group)
+    sync = make_grad_sync(shard_grouped_experts(model, rank, ws, group), group)
+    dev = next(model.parameters()).device
+    if transport not in ("auto", "p2p", "nccl"):
+        raise ValueError(f"unknown transport {transport!r}")
+    if transport == "p2p" or (transport == "auto" and dev.type == "cuda"):
+        if dev.type != "cuda":
+            raise ValueError("the p2p transport needs CUDA parameters")
+        from saint_llm_b200.parallel.ep_p2p import attach_p2p_comm
+
+        attach_p2p_comm(model, group, dev, capacity_factor=capacity_factor)
+    return sync
 
 
 __all__ = [

@@ -1,7 +1,9 @@
-"""Parallelism: expert parallelism (dispatch/combine), data-parallel gradient sync, and
-the distributed-training building blocks of the reference (ZeRO planner, DiLoCo/NoLoCo,
-gradient compression, verification, reputation, decentralised rounds, miner/validator
-protocol, FSDP2 wrapping)."""
+"""Parallelism: expert parallelism (NCCL baseline and the peer-memory kernels of
+``ep_p2p``), data-parallel gradient sync, tensor parallelism for attention (``tp``),
+two-stage context parallelism (``cp``), 1F1B pipeline parallelism (``pipeline``), and
+the distributed-training building blocks of the reference (ZeRO planner and runtime,
+DiLoCo/NoLoCo, gradient compression, verification, reputation, decentralised rounds,
+miner/validator protocol, FSDP2 wrapping)."""
 
 from saint_llm_b200.parallel.compression import (
     CompressedGradient,

@@ -1,0 +1,151 @@
+"""Two-stage context parallelism for the CSA / HCA / SWA / NSA stack (absent in the
+reference; planned there).  The sequence is split into contiguous shards, rank r of a
+CP group of size c holds tokens ``[r*Tl, (r+1)*Tl)``; everything except attention is
+per token, so only attention exchanges data:
+
+* stage 1 — compressed entries: each rank compresses its own blocks (shards are
+  block-aligned) and the entries of all ranks are all-gathered (HCA's dense compressed
+  branch, CSA's top-k sparse branch and its lightning-indexer keys all index global
+  block numbers); the all-gather's backward sums the gradients back to their owners;
+* stage 2 — the sliding-window halo: the last ``w`` post-RoPE K/V rows of rank r-1
+  reach rank r, and their gradients travel back.
+
+Both stages share one all-gather per layer (tails and compressed entries packed in one
+buffer; with one MQA K/V head a tail is ``w x 2 x head_dim`` values), so every rank
+issues the same collectives in the same order in forward and backward — two separate
+exchanges per layer could be reordered by the autograd engine on one rank and not on
+another.
+
+The attention modules are run unchanged through their KV-cache entry point: a
+``CPLayerView`` presents "the context before this shard" exactly as a cache would
+(``length`` = the shard's start, so RoPE and every block-causal / window mask use
+global positions).  The window K/V are presented at full length with zeros before the
+halo (outside every query's window, so never attended); with the MQA layout (one K/V
+head) that costs two (B, T, head_dim) buffers per layer.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+
+class _GatherStack(torch.autograd.Function):
+    """(ws, *x.shape) = every rank's ``x``; the backward sums the gradient over ranks and
+    keeps this rank's slice."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, group: object) -> Tensor:  # type: ignore[override]
+        ctx.group = group
+        parts = [torch.empty_like(x) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        return torch.stack(parts)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):  # type: ignore[override]
+        g = g.contiguous().clone()
+        dist.all_reduce(g, group=ctx.group)
+        return g[dist.get_rank(ctx.group)], None
+
+
+def gather_stack(x: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+    return _GatherStack.apply(x, group)
+
+
+class CPLayerView:
+    """Cache-shaped view of the context before this rank's shard, for one layer.
+
+    One collective per layer and direction: every rank contributes its window tail
+    (the last ``w`` K/V rows) and its compressed entries packed in one buffer; the
+    all-gather gives each rank the previous rank's tail (the halo) and every rank's
+    compressed entries in global block order."""
+
+    def __init__(self, group: dist.ProcessGroup | None, shard_len: int, window: int) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.ws = dist.get_world_size(group)
+        self.length = self.rank * shard_len
+        self.window = min(window, shard_len)
+
+    def append(self, *args: Tensor, compressor=None, indexer_compressor=None):  # noqa: ANN001, ANN201
+        if compressor is None:  # SWA / NSA: (k, v)
+            h, (k, v) = None, args
+        else:
+            h, k, v = args
+        b, d, w = k.shape[0], k.shape[-1], self.window
+        parts = [torch.cat([k[:, -w:], v[:, -w:]], -1)]
+        if compressor is not None:
+            parts.append(compressor(h))
+            if indexer_compressor is not None:
+                parts.append(indexer_compressor(h))
+        sizes = [p.shape[1:] for p in parts]
+        g = gather_stack(torch.cat([p.reshape(b, -1) for p in parts], 1), self.group)  # (ws, B, L)
+        outs, off = [], 0
+        for shp in sizes:
+            n = shp.numel()
+            outs.append(g[:, :, off:off + n].reshape(self.ws, b, *shp))
+            off += n
+        if self.rank == 0:  # no halo; the empty slice keeps the gather in the graph on every rank
+            empty = outs[0][0][:, :0]
+            k_all, v_all = torch.cat([empty[..., :d], k], 1), torch.cat([empty[..., d:], v], 1)
+        else:
+            halo = outs[0][self.rank - 1]
+            z = k.new_zeros(b, self.length - w, d)
+            k_all = torch.cat([z, halo[..., :d], k], 1)
+            v_all = torch.cat([z, halo[..., d:], v], 1)
+        if compressor is None:
+            return k_all, v_all
+        comp = [o.transpose(0, 1).reshape(b, -1, o.shape[-1]) for o in outs[1:]]
+        if indexer_compressor is None:  # HCA
+            return comp[0], k_all, v_all
+        return comp[0], comp[1], k_all, v_all
+
+
+class CPBundle:
+    """Per-layer CP views for ``model.backbone(..., kv_cache_bundle=CPBundle(...))``."""
+
+    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None, shard_len: int) -> None:
+        cfg = model.cfg  # type: ignore[attr-defined]
+        if cfg.n_sink_tokens:
+            raise ValueError("context parallelism does not support prepended sink tokens")
+        rates = {"csa": cfg.csa.compression_rate, "hca": cfg.hca.compression_rate, "nsa": cfg.nsa.compression_rate}
+        kinds = {cfg.layer_kind(i) for i in range(len(model.blocks))}  # type: ignore[arg-type]
+        for m in (rates[k] for k in kinds if k in rates):
+            if shard_len % m:
+                raise ValueError(f"shard length {shard_len} must be a multiple of every compression rate ({m})")
+        if shard_len < cfg.attention.sliding_window_size:
+            raise ValueError("shard length must be at least the sliding window")
+        self.views = [CPLayerView(group, shard_len, cfg.attention.sliding_window_size)
+                      for _ in model.blocks]  # type: ignore[attr-defined]
+        self.length = self.views[0].length
+
+    def for_layer(self, i: int) -> CPLayerView:
+        return self.views[i]
+
+
+def cp_shard(ids: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+    """This rank's contiguous slice of (B, T) token ids."""
+    r, ws = dist.get_rank(group), dist.get_world_size(group)
+    t = ids.shape[1] // ws
+    return ids[:, r * t:(r + 1) * t]
+
+
+def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+    """Next-token cross-entropy of the full sequence ``ids`` (B, T) computed with its tokens
+    sharded over ``group``; returns this rank's share of the global mean (the sum over
+    ranks is the loss)."""
+    r, ws = dist.get_rank(group), dist.get_world_size(group)
+    b, t = ids.shape
+    tl = t // ws
+    local = ids[:, r * tl:(r + 1) * tl]
+    h, _ = model.backbone(local, kv_cache_bundle=CPBundle(model, group, tl))  # type: ignore[attr-defined]
+    logits = model.logits(h).float()  # type: ignore[attr-defined]
+    tgt = ids[:, r * tl + 1:(r + 1) * tl + 1]
+    n = tgt.shape[1]
+    loss = torch.nn.functional.cross_entropy(logits[:, :n].reshape(-1, logits.shape[-1]), tgt.reshape(-1),
+                                             reduction="sum")
+    return loss / (b * (t - 1))
+
+
+__all__ = ["CPBundle", "CPLayerView", "cp_lm_loss", "cp_shard", "gather_stack"]

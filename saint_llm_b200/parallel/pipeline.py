@@ -1,0 +1,179 @@
+"""Pipeline parallelism: the block stack split into contiguous stages, one per rank,
+driven by a 1F1B schedule with point-to-point send/recv of the mHC residual stream
+(absent in the reference, which plans DualPipe; the build plan keeps pipeline traffic
+on NCCL p2p, overlapped with compute).
+
+Stage ``s`` of ``S`` owns blocks ``[s*L/S, (s+1)*L/S)``; stage 0 also owns the input
+embedding, the last stage the final norm, LM head, MTP heads and the loss.  Between
+stages travels ``x`` of shape (micro-batch, T, n_hc, D) forward and its gradient
+backward.  Every stage gets the micro-batch's token ids (the hash router and the MTP
+targets need them; ids are tiny next to activations).
+
+1F1B: stage ``s`` runs ``min(S-s-1, M)`` warm-up forwards, then alternates one
+forward and one backward, then drains the remaining backwards; at most ``S - s``
+micro-batches of activations are alive on stage s.  Sends are non-blocking
+(``isend``), receives blocking; every stage issues its sends and receives in schedule
+order, so matching pairs always meet.
+
+With tied embeddings the first and last stages both hold the embedding matrix;
+``sync_tied_embedding`` sums its gradient over the two after the schedule.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from saint_llm_b200.models.mhc import MHC
+
+
+def stage_bounds(n_layers: int, n_stages: int, stage: int) -> tuple[int, int]:
+    base, extra = divmod(n_layers, n_stages)
+    start = stage * base + min(stage, extra)
+    return start, start + base + (1 if stage < extra else 0)
+
+
+class PipelineStage:
+    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None = None, *, prune: bool = False) -> None:
+        self.model, self.group = model, group
+        self.stage = dist.get_rank(group)
+        self.n_stages = dist.get_world_size(group)
+        self.first, self.last = self.stage == 0, self.stage == self.n_stages - 1
+        self.lo, self.hi = stage_bounds(len(model.blocks), self.n_stages, self.stage)  # type: ignore[arg-type]
+        if prune:
+            for i in range(len(model.blocks)):  # type: ignore[arg-type]
+                if not self.lo <= i < self.hi:
+                    model.blocks[i] = nn.Identity()  # type: ignore[index]
+
+    def _peer(self, s: int) -> int:
+        return dist.get_global_rank(self.group, s) if self.group is not None else s
+
+    def forward(self, ids: Tensor, x_in: Tensor | None) -> Tensor:
+        m = self.model
+        if self.first:
+            x = MHC.expand(m._embed_inputs(ids, None, None), m.cfg.mhc.expansion_factor)  # type: ignore[attr-defined]
+        else:
+            assert x_in is not None
+            x = x_in
+        vis = ids == m.cfg.tokenizer_slots.image_pad  # type: ignore[attr-defined]
+        for i in range(self.lo, self.hi):
+            x = m.blocks[i](x, token_ids=ids, is_visual=vis)  # type: ignore[index]
+        return x
+
+    def loss(self, ids: Tensor, x: Tensor, loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor]) -> Tensor:
+        """Last stage: ``loss_fn(model, final-normed hidden, ids)``."""
+        h = self.model.final_norm(MHC.collapse(x))  # type: ignore[attr-defined]
+        return loss_fn(self.model, h, ids)
+
+
+def aux_losses(model: nn.Module, lo: int, hi: int) -> Tensor | None:
+    total = None
+    for i in range(lo, hi):
+        a = getattr(model.blocks[i].moe, "_last_aux_loss", None)  # type: ignore[index]
+        if isinstance(a, Tensor) and a.requires_grad:
+            total = a if total is None else total + a
+    return total
+
+
+def default_lm_loss(model: nn.Module, h: Tensor, ids: Tensor) -> Tensor:
+    """Main next-token CE (mean over the micro-batch's positions)."""
+    logits = model.logits(h[:, :-1]).float()  # type: ignore[attr-defined]
+    return torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
+
+
+def run_1f1b(stage: PipelineStage, micro_ids: list[Tensor], *,
+             loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor] = default_lm_loss,
+             aux_weight: float = 0.0) -> Tensor | None:
+    """One pipelined forward+backward over ``micro_ids``; gradients accumulate in the
+    stage's parameters (each micro-batch's loss is divided by M).  Returns the mean loss
+    on the last stage, None elsewhere."""
+    m = stage.model
+    M = len(micro_ids)
+    cfg = m.cfg  # type: ignore[attr-defined]
+    dtype = next(m.parameters()).dtype
+    dev = micro_ids[0].device
+    n_warm = min(stage.n_stages - stage.stage - 1, M)
+    saved: dict[int, tuple[Tensor | None, Tensor]] = {}
+    pending: list = []
+    losses: list[Tensor] = []
+
+    def shape(ids: Tensor) -> tuple[int, ...]:
+        return (ids.shape[0], ids.shape[1], cfg.mhc.expansion_factor, cfg.hidden_dim)
+
+    def fwd(i: int) -> None:
+        ids = micro_ids[i]
+        x_in = None
+        if not stage.first:
+            x_in = torch.empty(shape(ids), dtype=dtype, device=dev)
+            dist.recv(x_in, stage._peer(stage.stage - 1), group=stage.group)
+            x_in.requires_grad_(True)
+        out = stage.forward(ids, x_in)
+        aux = aux_losses(m, stage.lo, stage.hi)
+        if stage.last:
+            loss = stage.loss(ids, out, loss_fn)
+            losses.append(loss.detach())
+            out = loss / M
+        if aux is not None and aux_weight:
+            out = (out, aux * (aux_weight / M))  # type: ignore[assignment]
+        saved[i] = (x_in, out)  # type: ignore[assignment]
+        if not stage.last:
+            y = out[0] if isinstance(out, tuple) else out
+            pending.append(dist.isend(y.detach().contiguous(), stage._peer(stage.stage + 1), group=stage.group))
+
+    def bwd(i: int) -> None:
+        x_in, out = saved.pop(i)
+        outs, grads = [], []
+        y, aux = (out if isinstance(out, tuple) else (out, None))
+        if stage.last:
+            outs.append(y)
+            grads.append(None)
+        else:
+            g = torch.empty_like(y)
+            dist.recv(g, stage._peer(stage.stage + 1), group=stage.group)
+            outs.append(y)
+            grads.append(g)
+        if aux is not None:
+            outs.append(aux)
+            grads.append(None)
+        torch.autograd.backward(outs, grads)
+        if not stage.first:
+            assert x_in is not None
+            pending.append(dist.isend(x_in.grad.contiguous(), stage._peer(stage.stage - 1), group=stage.group))
+
+    for i in range(n_warm):
+        fwd(i)
+    for i in range(M - n_warm):
+        fwd(n_warm + i)
+        bwd(i)
+    for i in range(M - n_warm, M):
+        bwd(i)
+    for req in pending:
+        req.wait()
+    return torch.stack(losses).mean() if losses else None
+
+
+def sync_tied_embedding(stage: PipelineStage) -> None:
+    """Sum the tied embedding / LM-head gradient over the first and last stages (a P2P
+    exchange between the two; the middle stages do nothing)."""
+    m = stage.model
+    if stage.n_stages == 1 or not (stage.first or stage.last) or not m.cfg.tie_word_embeddings:  # type: ignore[attr-defined]
+        return
+    w = m.embed.weight  # type: ignore[attr-defined]
+    g = getattr(w, "main_grad", None)
+    if g is None:
+        if w.grad is None:
+            w.grad = torch.zeros_like(w)
+        g = w.grad
+    peer = stage._peer(stage.n_stages - 1 if stage.first else 0)
+    mine = g.detach().float().contiguous().clone()
+    other = torch.empty_like(mine)
+    for r in dist.batch_isend_irecv([dist.P2POp(dist.isend, mine, peer, stage.group),
+                                     dist.P2POp(dist.irecv, other, peer, stage.group)]):
+        r.wait()
+    g.copy_(mine + other)
+
+
+__all__ = ["PipelineStage", "aux_losses", "default_lm_loss", "run_1f1b", "stage_bounds", "sync_tied_embedding"]

@@ -1,0 +1,170 @@
+"""Tensor, context and pipeline parallelism on 2 gloo CPU ranks against the same model
+run in one process (fp32)."""
+
+import copy
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.distributed
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(fn, ws=2):
+    ctx = mp.get_context("spawn")
+    q, port = ctx.Queue(), _port()
+    ps = [ctx.Process(target=_entry, args=(fn, r, ws, port, q)) for r in range(ws)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(ws)]
+    for p in ps:
+        p.join(timeout=60)
+    return res
+
+
+def _entry(fn, rank, ws, port, q):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        q.put(fn(rank, ws))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _model(**upd):
+    from saint_llm_b200.config import ModelConfig
+    from saint_llm_b200.models import SaintLLM
+
+    cfg = ModelConfig.tiny().model_copy(update=upd)
+    torch.manual_seed(0)
+    return SaintLLM(cfg)
+
+
+def _close(a, b, tol=2e-4):
+    return bool(torch.allclose(a, b, atol=tol, rtol=1e-3))
+
+
+# ------------------------------------------------------------------ TP
+def _tp(rank, ws):
+    from saint_llm_b200.parallel.tp import apply_tensor_parallel
+
+    full = _model()
+    tp = copy.deepcopy(full)
+    sync = apply_tensor_parallel(tp)
+    torch.manual_seed(5)
+    ids = torch.randint(0, full.cfg.vocab_size, (2, 24))
+    lf = full(ids)["logits"]
+    lf.square().mean().backward()
+    lt = tp(ids)["logits"]
+    lt.square().mean().backward()
+    sync()
+    ok = [_close(lt, lf)]
+    fp = dict(full.named_parameters())
+    per = full.cfg.attention.output_proj_groups // ws
+    for n, p in tp.named_parameters():
+        if ".group_projs." in n:  # local group i is global group rank * per + i
+            head, tail = n.split(".group_projs.")
+            i, rest = tail.split(".", 1)
+            n = f"{head}.group_projs.{rank * per + int(i)}.{rest}"
+        g_full = fp[n].grad
+        if p.grad is None or g_full is None:
+            continue
+        if p.shape == g_full.shape:
+            ok.append(_close(p.grad, g_full))
+        elif n.endswith("q_up.weight"):
+            r = p.shape[0]
+            ok.append(_close(p.grad, g_full[rank * r:(rank + 1) * r]))
+    return rank, all(ok), len(ok)
+
+
+def test_tensor_parallel_attention_two_ranks():
+    res = _run(_tp)
+    for r in res:
+        assert r[1] is True and r[2] > 20, r
+
+
+# ------------------------------------------------------------------ CP
+def _cp(rank, ws):
+    from saint_llm_b200.parallel.cp import cp_lm_loss
+
+    for pattern in ("csa_hca_interleaved", "nsa"):
+        upd = {"attention_pattern": pattern}
+        if pattern == "nsa":
+            from saint_llm_b200.config import NSAConfig
+
+            upd["nsa"] = NSAConfig(compression_rate=8, selection_k=2)
+        full = _model(**upd)
+        cp = copy.deepcopy(full)
+        torch.manual_seed(7)
+        ids = torch.randint(0, full.cfg.vocab_size, (2, 64))
+        h, _ = full.backbone(ids)
+        logits = full.logits(h).float()
+        ref = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
+        ref.backward()
+        loss = cp_lm_loss(cp, ids)
+        loss.backward()
+        tot = loss.detach().clone()
+        dist.all_reduce(tot)
+        if not _close(tot, ref.detach(), 1e-5):
+            return rank, f"{pattern}: loss {tot.item()} vs {ref.item()}"
+        fp = dict(full.named_parameters())
+        for n, p in cp.named_parameters():
+            g = p.grad if p.grad is not None else torch.zeros_like(p)
+            dist.all_reduce(g)
+            ref_g = fp[n].grad if fp[n].grad is not None else torch.zeros_like(p)
+            if not _close(g, ref_g):
+                return rank, f"{pattern}: grad {n} max err {(g - ref_g).abs().max().item()}"
+    return rank, True
+
+
+def test_context_parallel_two_ranks():
+    res = _run(_cp)
+    for r in res:
+        assert r[1] is True, r
+
+
+# ------------------------------------------------------------------ PP
+def _pp(rank, ws):
+    from saint_llm_b200.parallel.pipeline import PipelineStage, default_lm_loss, run_1f1b, sync_tied_embedding
+
+    full = _model()
+    pp = copy.deepcopy(full)
+    torch.manual_seed(9)
+    micro = [torch.randint(0, full.cfg.vocab_size, (1, 16)) for _ in range(4)]
+    ref_losses = []
+    for ids in micro:
+        h, _ = full.backbone(ids)
+        loss = default_lm_loss(full, h, ids)
+        (loss / len(micro)).backward()
+        ref_losses.append(loss.detach())
+    stage = PipelineStage(pp)
+    out = run_1f1b(stage, micro)
+    sync_tied_embedding(stage)
+    ok = []
+    if stage.last:
+        ok.append(_close(out, torch.stack(ref_losses).mean(), 1e-5))
+    fp = dict(full.named_parameters())
+    own = [f"blocks.{i}." for i in range(stage.lo, stage.hi)]
+    for n, p in pp.named_parameters():
+        mine = any(n.startswith(o) for o in own) or (n.startswith("embed.") and (stage.first or stage.last)) or \
+            (n.startswith("final_norm.") and stage.last)
+        if mine and fp[n].grad is not None:
+            ok.append(_close(p.grad, fp[n].grad))
+    return rank, all(ok), len(ok)
+
+
+def test_pipeline_1f1b_two_stages():
+    res = _run(_pp)
+    for r in res:
+        assert r[1] is True and r[2] > 5, r

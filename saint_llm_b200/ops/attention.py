@@ -6,8 +6,9 @@ fused into one GEMM (``[q_compressor; k_proj; v_proj; w_b_kv; w_b_z]`` for atten
 kernel per tensor in the reference's order (Q: rope then norm; K: CSA norm then rope,
 SWA/HCA rope then norm).
 
-The lightning indexer (no gradient flows through its integer output) streams token
-chunks: scores = relu(q_h . k_s) weighted over heads, strict block-causal mask, top-k.
+The lightning indexer (no gradient flows through its integer output) is one fused
+tcgen05 kernel (``csrc/indexer.cu``): scores = sum_h w_h relu(q_h . k_s) with the
+strict block-causal mask, written once as (B, T, blocks); then top-k.
 
 Attention itself is one fused tcgen05 kernel per direction (``csrc/attention.cu``): the
 sliding-window branch (sink, softcap, max-logit telemetry) and the compressed branch
@@ -151,8 +152,10 @@ def fused_attention(q: Tensor, k: Tensor, v: Tensor, *, window: int, sink: Tenso
 
 
 @torch.no_grad()
-def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None, chunk: int = 512) -> Tensor:
-    """Lightning-indexer top-k block ids (B, T, k) with -1 for invalid picks."""
+def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
+    """Lightning-indexer top-k block ids (B, T, k) with -1 for invalid picks.  The scores
+    (sum over heads of the weighted ReLU'd dot products, masked block-causally) come from
+    the fused ``indexer_scores`` kernel in one pass; only (B, T, blocks) is written."""
     b, t, _ = h.shape
     comp = idx.compressor
     y = lin.linear(h, torch.cat([_bf16(idx.w_dq.weight), _bf16(idx.w_w.weight), _bf16(comp.w_b_kv.weight),
@@ -169,23 +172,12 @@ def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None, chunk: int
     if is_visual is not None:
         vis_bias = is_visual[:, : n_blocks * m_eff].reshape(b, n_blocks, m_eff).float().mean(-1)
     q = lin.linear(c_dq, idx.w_iuq.weight)  # (B, T, nh*c)
-    keys_b = _bf16(keys)
-    out = torch.empty(b, t, k_eff, dtype=torch.long, device=h.device)
-    block_end = torch.arange(n_blocks, device=h.device) * m_eff + (m_eff - 1)
-    for bi in range(b):
-        for t0 in range(0, t, chunk):
-            t1 = min(t, t0 + chunk)
-            qc = q[bi, t0:t1].reshape((t1 - t0) * nh, c)
-            s = gemm.gemm_nt(qc, keys_b[bi], out_dtype=torch.float32).view(t1 - t0, nh, n_blocks).clamp_(min=0.0)
-            wc = w[bi, t0:t1].float()
-            sc = torch.bmm(wc.unsqueeze(1), s).squeeze(1)  # sum_h w_h relu(q_h . k)
-            if vis_bias is not None:  # sum_h w_h (relu(.) + b/2) = ... + (b/2) sum_h w_h
-                sc += 0.5 * vis_bias[bi].view(1, n_blocks) * wc.sum(-1, keepdim=True)
-            qpos = torch.arange(t0, t1, device=h.device).view(-1, 1)
-            sc.masked_fill_(~(block_end.view(1, -1) < qpos), float("-inf"))
-            vals, ids = sc.topk(k_eff, dim=-1)
-            out[bi, t0:t1] = torch.where(torch.isfinite(vals), ids, torch.full_like(ids, -1))
-    return out
+    scores = torch.empty(b, t, n_blocks, dtype=torch.float32, device=h.device)
+    backend.ext().indexer_scores(q.contiguous(), _bf16(keys).contiguous(), w.float().contiguous(),
+                                 None if vis_bias is None else vis_bias.contiguous(), m_eff, 0, scores,
+                                 gemm.error_word(h.device))
+    vals, ids = scores.topk(k_eff, dim=-1)
+    return torch.where(torch.isfinite(vals), ids, torch.full_like(ids, -1))
 
 
 def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor | None) -> Tensor:

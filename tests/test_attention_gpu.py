@@ -104,3 +104,34 @@ def test_fused_attention_matches_reference(cuda, case):
         if a_ is None:
             continue
         _close(a_.grad, r_.grad, 3e-2 if name != "sink" else 5e-2)
+
+
+@pytest.mark.parametrize("B,T,nb,nh,c,m,q_start,vis", [(1, 300, 75, 8, 128, 4, 0, False),
+                                                      (2, 512, 256, 64, 128, 2, 0, True),
+                                                      (1, 200, 130, 5, 64, 1, 37, False)])
+def test_indexer_scores_kernel(cuda, B, T, nb, nh, c, m, q_start, vis):
+    """Fused indexer scores vs the fp32 oracle sum_h w_h relu(q_h . k_s), block-causal."""
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.gemm import check_errors, error_word
+
+    torch.manual_seed(0)
+    q = torch.randn(B, T, nh * c, device=cuda).to(torch.bfloat16)
+    keys = torch.randn(B, nb, c, device=cuda).to(torch.bfloat16)
+    w = torch.randn(B, T, nh, device=cuda)
+    vb = torch.rand(B, nb, device=cuda) if vis else None
+    out = torch.empty(B, T, nb, device=cuda)
+    backend.ext().indexer_scores(q, keys, w, vb, m, q_start, out, error_word(cuda))
+    torch.cuda.synchronize()
+    check_errors(cuda)
+    qf = q.float().view(B, T, nh, c)
+    head = torch.einsum("bthc,bnc->bthn", qf, keys.float()).clamp(min=0)
+    ref = (w.unsqueeze(-1) * head).sum(2)
+    if vis:
+        ref = ref + 0.5 * vb[:, None, :] * w.sum(-1, keepdim=True)
+    qpos = torch.arange(q_start, q_start + T, device=cuda)[:, None]
+    ok = torch.arange(nb, device=cuda)[None, :] * m + m - 1 < qpos
+    ref = ref.masked_fill(~ok, float("-inf"))
+    assert torch.equal(torch.isinf(out), torch.isinf(ref))
+    fin = torch.isfinite(ref)
+    err = (out[fin] - ref[fin]).abs().max().item()
+    assert err <= 1e-3 * ref[fin].abs().max().item() + 1e-3, err

@@ -210,6 +210,9 @@ def run_ours(args) -> dict:
         "gpu_launches": launches,
     }
     if world > 1:
+        comm = getattr(model, "ep_comm", None)
+        if comm is not None:
+            comm.close()  # collective: peers stop touching each other's buffers first
         torch.distributed.destroy_process_group()
     return result if rank == 0 else {}
 

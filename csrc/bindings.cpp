@@ -94,6 +94,7 @@ void indexer_scores(torch::Tensor q, torch::Tensor keys, torch::Tensor w, c10::o
                     int64_t m, int64_t q_start, torch::Tensor out, torch::Tensor err);
 int64_t symm_open(const std::string& handle, int64_t device);
 void symm_close(int64_t ptr, int64_t device);
+void symm_free(int64_t ptr, int64_t device);
 }  // namespace sv4
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -140,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("symm_open", [](pybind11::bytes h, int64_t dev) { return sv4::symm_open(std::string(h), dev); });
   m.def("symm_close", &sv4::symm_close);
+  m.def("symm_free", &sv4::symm_free);
   m.def("mhc_gates_fwd", &sv4::mhc_gates_fwd);
   m.def("mhc_gates_bwd", &sv4::mhc_gates_bwd);
   m.def("mhc_premix", &sv4::mhc_premix);

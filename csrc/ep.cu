@@ -463,7 +463,10 @@ void ep_dispatch_bwd(std::vector<int64_t> dx_ptrs, torch::Tensor gpos, int64_t C
 
 // ------------------------------------------------------------- symmetric buffers
 // cudaMalloc'd (outside the caching allocator, so the IPC handle covers exactly this
-// buffer) and zero-filled.  The returned tensor owns the memory.
+// buffer) and zero-filled.  The returned tensor does NOT own the memory: peers map it,
+// so it may only be released by symm_free once every peer has stopped using it (the
+// Python heap does that behind a barrier); a buffer never released lives until the
+// process exits.
 std::tuple<torch::Tensor, std::string> symm_alloc(int64_t nbytes, int64_t device) {
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   void* ptr = nullptr;
@@ -472,8 +475,13 @@ std::tuple<torch::Tensor, std::string> symm_alloc(int64_t nbytes, int64_t device
   cudaIpcMemHandle_t h;
   C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, ptr));
   auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
-  torch::Tensor t = torch::from_blob(ptr, {nbytes}, [](void* p) { cudaFree(p); }, opts);
+  torch::Tensor t = torch::from_blob(ptr, {nbytes}, [](void*) {}, opts);
   return {t, std::string(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+
+void symm_free(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr)));
 }
 
 int64_t symm_open(const std::string& handle, int64_t device) {

@@ -77,12 +77,17 @@ class SymmetricHeap:
             raise ValueError(f"peer-memory expert parallelism supports up to {MAX_RANKS} ranks (one node)")
         self.device = device
         self._opened: list[int] = []
+        self._owned: list[int] = []
         self.bytes = 0
+        self.closed = False
 
     def alloc(self, nbytes: int) -> SymmetricBuffer:
         nbytes = (nbytes + 255) // 256 * 256
         ext = backend.ext()
+        if self.closed:
+            raise RuntimeError("symmetric heap is closed")
         t, h = ext.symm_alloc(nbytes, self.device.index)
+        self._owned.append(t.data_ptr())
         handles: list = [None] * self.ws
         dist.all_gather_object(handles, h, group=self.group)
         ptrs = []
@@ -97,11 +102,22 @@ class SymmetricHeap:
         return SymmetricBuffer(t, ptrs)
 
     def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's, after every rank's
+        device has finished all work that touches them.  Tensors handed out by ``alloc``
+        must not be used afterwards."""
+        if self.closed:
+            return
         ext = backend.ext()
         torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every peer is done with our memory
         for p in self._opened:
             ext.symm_close(p, self.device.index)
         self._opened.clear()
+        dist.barrier(group=self.group)  # every peer has unmapped our memory
+        for p in self._owned:
+            ext.symm_free(p, self.device.index)
+        self._owned.clear()
+        self.closed = True
 
 
 class EmulatedHeap:
@@ -174,6 +190,12 @@ class P2PExpertComm:
         row_bytes = self.C * self.D * 2
         self.y, self.dy, self.dx = (self.heap.alloc(row_bytes) for _ in range(3))
         self.x = {}
+
+    def close(self) -> None:
+        """Collective release of every buffer (see ``SymmetricHeap.close``)."""
+        self.y = self.dy = self.dx = None
+        self.x = {}
+        self.heap.close()
 
     def x_buffer(self, layer_key: int) -> SymmetricBuffer:
         buf = self.x.get(layer_key)
@@ -393,6 +415,7 @@ def attach_p2p_comm(model: nn.Module, group: dist.ProcessGroup | None, device: t
                          capacity_factor=capacity_factor, timeout_s=timeout_s)
     for m in layers:
         m.ep_comm = comm
+    model.ep_comm = comm  # callers release it with model.ep_comm.close() (collective)
     return comm
 
 

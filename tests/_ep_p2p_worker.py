@@ -4,6 +4,7 @@ the peer-memory transport and with the NCCL transport.  Rank 0 prints one JSON l
 
 import copy
 import datetime
+import faulthandler
 import json
 import os
 import sys
@@ -19,6 +20,7 @@ def _rel(x, y):
 
 
 def main() -> None:
+    faulthandler.enable()
     rank, ws = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     torch.cuda.set_device(dev)
@@ -59,6 +61,8 @@ def main() -> None:
             y.backward(g)
         torch.cuda.synchronize()
         check_errors(dev)
+        if transport == "p2p":
+            m.ep_comm.close()  # collective; no rank frees memory a peer may still read
         ge = m.grouped_experts
         res[transport] = {
             "out": _rel(y, y_ref), "dx": _rel(xe.grad, xr.grad),

@@ -4,12 +4,29 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
 #include "gemm.cuh"
 
 namespace sv4 {
+
+static bool host_trace() {
+  static const bool on = [] {
+    const char* e = getenv("SV4_TRACE_HOST");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+#define SV4_TRACE(...)                      \
+  do {                                      \
+    if (host_trace()) {                     \
+      fprintf(stderr, "[sv4] " __VA_ARGS__); \
+      fprintf(stderr, "\n");                \
+      fflush(stderr);                       \
+    }                                       \
+  } while (0)
 
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -29,6 +46,26 @@ static EncodeFn encode_fn() {
   return fn;
 }
 
+// cuTensorMapEncodeTiled is a driver call that needs a current context in the calling
+// thread.  Autograd runs backward passes on its own device threads, where no runtime call
+// may have made the primary context current yet (a device guard does not), so every
+// encode first makes the current device's primary context current in this thread.
+static void ensure_context() {
+  static thread_local int ready = -1;
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev != ready) {
+    C10_CUDA_CHECK(cudaSetDevice(dev));
+    ready = dev;
+  }
+}
+
+static CUtensorMap* encode_scratch() {
+  ensure_context();
+  alignas(128) static thread_local CUtensorMap scratch;
+  return &scratch;
+}
+
 // 3-D tiled map: dims/strides given inner-first; strides in bytes for dims 1 and 2.
 CUtensorMap make_map_3d(const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0, uint64_t d1,
                         uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1,
@@ -41,10 +78,15 @@ CUtensorMap make_map_3d(const void* base, CUtensorMapDataType dt, int elem_bytes
   cuuint64_t strides[2] = {s1_bytes, s2_bytes};
   cuuint32_t box[3] = {b0, b1, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+  CUtensorMap* tmp = encode_scratch();
+  SV4_TRACE("map3d base=%p d=%llu,%llu,%llu s=%llu,%llu box=%u,%u local=%p scratch=%p", base,
+            (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, (unsigned long long)s1_bytes,
+            (unsigned long long)s2_bytes, b0, b1, (void*)&m, (void*)tmp);
+  CUresult r = encode_fn()(tmp, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  memcpy(&m, tmp, sizeof(CUtensorMap));
   return m;
 }
 
@@ -66,9 +108,11 @@ CUtensorMap make_map_nd(const void* base, CUtensorMapDataType dt, int rank, cons
     st[i] = strides_bytes[i];
   }
   CUtensorMap m;
-  CUresult r = encode_fn()(&m, dt, rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+  CUtensorMap* tmp = encode_scratch();
+  CUresult r = encode_fn()(tmp, dt, rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  memcpy(&m, tmp, sizeof(CUtensorMap));
   return m;
 }
 
@@ -157,7 +201,10 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
   for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
     const V& v = table[i];
     if (v.a == a_mn && v.b == b_mn && v.bm == bmode && v.ep == epi) {
+      SV4_TRACE("launch variant %d grid %d m=%d n=%d k=%d tma_d=%d", i, grid, p.single.m, p.single.n, p.single.k,
+                p.tma_d);
       gemm_launch_variant(i, ma, mb0, mb1, md, mx ? *mx : md, p, grid, stream);
+      SV4_TRACE("launched variant %d", i);
       return;
     }
   }
@@ -171,6 +218,7 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
 //   out: (.., M, N) bf16 or fp32 with unit inner stride.
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate,
           double alpha, torch::Tensor err) {
+  SV4_TRACE("gemm a=%p b=%p out=%p a_mn=%d b_mn=%d", a.data_ptr(), b.data_ptr(), out.data_ptr(), a_mn, b_mn);
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "bf16 operands required");
   TORCH_CHECK(out.stride(-1) == 1, "output needs unit inner stride");
   c10::cuda::CUDAGuard guard(a.device());

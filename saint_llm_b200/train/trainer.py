@@ -13,6 +13,7 @@ region has no per-micro-step host sync; this class keeps the reference's contrac
 from __future__ import annotations
 
 import math
+import time
 from collections import deque
 from collections.abc import Callable, Iterable
 from pathlib import Path
@@ -59,6 +60,7 @@ class Trainer:
         self.lr_scheduler = lr_scheduler
         self.grad_clip_norm = grad_clip_norm
         self.metrics_callback = metrics_callback
+        self._t_last, self._tokens_since = time.perf_counter(), 0  # perf/ metrics
         self.skip_nonfinite_loss = skip_nonfinite_loss
         self.loss_spike_factor = loss_spike_factor
         self.gradient_accumulation_steps = gradient_accumulation_steps
@@ -99,11 +101,19 @@ class Trainer:
         if skip_reason is not None:
             m["skipped"] = 1.0
             m[f"skip_reason_{skip_reason}"] = 1.0
+        else:
+            now = time.perf_counter()
+            dt = now - self._t_last
+            if dt > 0 and self._tokens_since:
+                m["perf/step_s"] = dt
+                m["perf/tokens_per_s"] = self._tokens_since / dt
+            self._t_last, self._tokens_since = now, 0
         self.metrics_callback(self.step, m)
 
     def train_step(self, batch: Tensor) -> float:
         self.model.train()
         batch = batch.to(self.device, non_blocking=True)
+        self._tokens_since += batch.numel()
         loss = self._forward(batch)
         value = float(loss.detach().item())
         reason = None

@@ -127,11 +127,13 @@ def build_ours(args, device, world):
         from saint_llm_b200.parallel import ep as ep_mod
 
         grad_sync = ep_mod.setup_expert_parallel(model, transport=args.ep_transport,
-                                                 capacity_factor=args.ep_capacity)
+                                                 capacity_factor=args.ep_capacity, zero=not args.no_zero)
         torch.cuda.empty_cache()
     params = attach_main_grads(model)
     muon, adamw = split_for_muon_adamw(model)
     opt = MuonAdamW(muon, adamw, lr=2.7e-4, qk_clip_layers=model.attention_layers())
+    if grad_sync is not None:
+        grad_sync.configure_optimizer(opt)
     step = TrainStep(model, opt, micro_batches=args.seqs_per_gpu // args.micro_batch, params=params,
                      grad_sync=grad_sync)
     return cfg, model, step
@@ -198,7 +200,8 @@ def run_ours(args) -> dict:
         "data": "synthetic uniform-random tokens; random-init weights N(0,0.02)",
         "config": {"model": MODEL_DESC, "n_layers": cfg.n_layers, "global_batch": world * args.seqs_per_gpu,
                    "seq_len": args.seq_len, "micro_batch": args.micro_batch,
-                   "parallelism": f"ep{world}+dp{world}" if world > 1 else "single-gpu",
+                   "parallelism": (f"ep{world}+dp{world}" + ("" if args.no_zero else "+zero")) if world > 1
+                   else "single-gpu",
                    "ep_transport": args.ep_transport if world > 1 else None,
                    "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
                    "l2": "inputs larger than L2 (the weights stream through HBM every step)",
@@ -233,6 +236,8 @@ def main() -> None:
     ap.add_argument("--micro-batch", type=int, default=2)
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
+    ap.add_argument("--no-zero", action="store_true",
+                    help="N > 1: all-reduce replicated gradients and update them on every rank (no hybrid ZeRO)")
     ap.add_argument("--ep-capacity", type=float, default=2.0,
                     help="receive capacity per rank in units of its own (token, slot) pairs; an overflow raises")
     ap.add_argument("--seq-len", type=int, default=4096)

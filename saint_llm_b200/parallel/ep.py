@@ -215,15 +215,84 @@ def make_grad_sync(expert_params: list[Tensor], group: dist.ProcessGroup | None,
     return sync
 
 
+def _sync_attention_logits(model: nn.Module, group: dist.ProcessGroup | None) -> None:
+    """Global (MAX over ranks) attention-logit telemetry, so MuonClip makes the same
+    decision for the replicated ``q_up`` / ``k_proj`` on every rank."""
+    bufs = [m.max_attn_logit for m in model.modules() if isinstance(getattr(m, "max_attn_logit", None), Tensor)]
+    if bufs:
+        flat = torch.stack([b.float() for b in bufs])
+        dist.all_reduce(flat, op=dist.ReduceOp.MAX, group=group)
+        for b, v in zip(bufs, flat, strict=True):
+            b.copy_(v)
+
+
+class ParallelSync:
+    """Gradient synchroniser returned by ``setup_expert_parallel`` (callable as
+    ``sync(params)`` after the backward); ``post_step()`` runs after the optimizer.
+
+    Plain mode: replicated gradients are all-reduced and every rank updates every
+    replicated parameter.  ZeRO mode (hybrid ZeRO, reference planner
+    ``distributed/zero.py:47-216`` with a runtime): each replicated parameter has one
+    owner chosen by the LPT planner over Muon / AdamW costs; gradients are reduced to the
+    owner only, only the owner runs the optimizer on it (``optimizer.param_filter``), and
+    the updated parameters are broadcast from their owners.  Expert parameters are local
+    to their rank in both modes (their gradients are divided by the world size so the
+    loss is the global mean)."""
+
+    def __init__(self, model: nn.Module, expert_params: list[Tensor], group: dist.ProcessGroup | None,
+                 *, zero: bool) -> None:
+        self.model, self.group = model, group
+        self.ws = dist.get_world_size(group)
+        self.expert_ids = {id(p) for p in expert_params}
+        self.expert_params = expert_params
+        self.zero = None
+        self._plain = None
+        if zero:
+            from saint_llm_b200.optim import split_for_muon_adamw
+            from saint_llm_b200.parallel.zero import ZeroOptimizerSync
+
+            muon, adamw = split_for_muon_adamw(model)
+            kinds = {id(p): "muon" for p in muon} | {id(p): "adamw" for p in adamw}
+            rep = [p for p in model.parameters() if id(p) not in self.expert_ids and p.requires_grad]
+            self.zero = ZeroOptimizerSync(rep, [kinds.get(id(p), "adamw") for p in rep], group=group)
+        else:
+            self._plain = make_grad_sync(expert_params, group)
+
+    def is_updated_here(self, p: Tensor) -> bool:
+        return self.zero is None or id(p) in self.expert_ids or self.zero.is_owned(p)
+
+    def configure_optimizer(self, optimizer: torch.optim.Optimizer) -> None:
+        if self.zero is not None:
+            optimizer.param_filter = self.is_updated_here  # type: ignore[attr-defined]
+
+    @torch.no_grad()
+    def __call__(self, params: list[Tensor]) -> None:
+        _sync_attention_logits(self.model, self.group)
+        if self._plain is not None:
+            self._plain(params)
+            return
+        self.zero.reduce_grads()
+        for p in self.expert_params:
+            g = getattr(p, "main_grad", None)
+            (g if g is not None else p.grad).div_(self.ws)
+
+    @torch.no_grad()
+    def post_step(self) -> None:
+        if self.zero is not None:
+            self.zero.broadcast_params()
+
+
 def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",
-                          capacity_factor: float | None = None) -> Callable[[list[Tensor]], None]:
+                          capacity_factor: float | None = None, zero: bool = False) -> ParallelSync:
     """Shard the experts over ``group`` and return the gradient synchroniser.
 
     ``transport``: "p2p" moves tokens with the peer-memory kernels of ``parallel.ep_p2p``
-    (CUDA only), "nccl" with ``all_to_all_single``; "auto" picks p2p on CUDA."""
+    (CUDA only), "nccl" with ``all_to_all_single``; "auto" picks p2p on CUDA.
+    ``zero``: hybrid ZeRO for the replicated parameters (see ``ParallelSync``); call
+    ``sync.configure_optimizer(opt)`` once and ``sync.post_step()`` after every step."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
-    sync = make_grad_sync(shard_grouped_experts(model, rank, ws, group), group)
+    sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero)
     dev = next(model.parameters()).device
     if transport not in ("auto", "p2p", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")
@@ -238,6 +307,7 @@ def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
 
 __all__ = [
     "DispatchPlan",
+    "ParallelSync",
     "combine_outputs_by_expert",
     "dispatch_tokens_by_expert",
     "make_grad_sync",

@@ -43,6 +43,9 @@ class TrainStep:
         if self.grad_sync is not None:
             self.grad_sync(self.params)
         self.optimizer.step()
+        post = getattr(self.grad_sync, "post_step", None)
+        if post is not None:
+            post()
         zero_main_grads(self.params)
         return total
 

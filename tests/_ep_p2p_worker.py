@@ -34,6 +34,7 @@ def main() -> None:
                     expert_intermediate_dim=256)
     torch.manual_seed(0)
     full = DeepSeekMoE(512, cfg, layer_idx=3, use_grouped_gemm=True).to(dev).to(torch.bfloat16)
+    copies = {t: copy.deepcopy(full) for t in ("p2p", "nccl")}  # before any forward (non-leaf attributes)
     torch.manual_seed(1 + rank)
     x = torch.randn(2, 192, 512, device=dev, dtype=torch.bfloat16)
     g = torch.randn_like(x)
@@ -47,7 +48,7 @@ def main() -> None:
         dist.all_reduce(w)
     el = cfg.routed_experts // ws
     for transport in ("p2p", "nccl"):
-        m = copy.deepcopy(full)
+        m = copies[transport]
         m.zero_grad()
         ep.shard_grouped_experts(m, rank, ws, None)
         if transport == "p2p":

@@ -115,15 +115,27 @@ def scaled_dot_product(
     score_observer: Callable[[Tensor], None] | None = None,
     logit_softcap: float | None = None,
 ) -> Tensor:
-    """Dense attention oracle. q (B,H,Tq,d); k, v (B,H|1,Tk,d)."""
-    scores = torch.matmul(q, k.transpose(-1, -2)) / math.sqrt(q.shape[-1])
+    """Dense attention oracle. q (B,H,Tq,d); k, v (B,H|1,Tk,d).
+
+    With one K/V head (MQA) the heads are folded into the query rows, (B, H*Tq, d) x
+    (B, d, Tk), so the shared K/V are never broadcast-copied per head."""
+    b, h, tq, d = q.shape
+    mqa = k.shape[1] == 1 and h > 1 and k.shape[0] == b and v.shape[0] == b
+    if mqa:
+        scores = torch.bmm(q.reshape(b, h * tq, d), k[:, 0].transpose(-1, -2)).view(b, h, tq, -1)
+        scores = scores / math.sqrt(d)
+    else:
+        scores = torch.matmul(q, k.transpose(-1, -2)) / math.sqrt(q.shape[-1])
     if score_observer is not None:
         score_observer(scores)
     if logit_softcap is not None:
         scores = logit_softcap * torch.tanh(scores / logit_softcap)
     if mask is not None:
         scores = scores.masked_fill(~mask, float("-inf"))
-    return torch.matmul(softmax_with_sink(scores, sink_logit), v)
+    p = softmax_with_sink(scores, sink_logit)
+    if mqa:
+        return torch.bmm(p.reshape(b, h * tq, -1).to(v.dtype), v[:, 0]).view(b, h, tq, v.shape[-1])
+    return torch.matmul(p, v)
 
 
 attend = scaled_dot_product

@@ -207,7 +207,10 @@ class _AttentionBase(nn.Module):
     def _sw_branch(self, q: Tensor, k: Tensor, v: Tensor, q_start: int) -> Tensor:
         cfg = self.attn_cfg
         b, n_heads, t, d = q.shape
-        mask = window_mask_at(q_start, t, k.shape[1], cfg.sliding_window_size, q.device)
+        # with a cache only the last `window` keys before the first query can be visible
+        lo = max(0, q_start - cfg.sliding_window_size + 1) if k.shape[1] > t else 0
+        k, v = k[:, lo:], v[:, lo:]
+        mask = window_mask_at(q_start - lo, t, k.shape[1], cfg.sliding_window_size, q.device)
         return scaled_dot_product(
             q, k.unsqueeze(1), v.unsqueeze(1), mask=mask, sink_logit=self.sink_logit,
             score_observer=self._observe, logit_softcap=cfg.logit_softcap,

@@ -115,9 +115,11 @@ class NSAttention(_AttentionBase):
         comp = self.compressed_branch(q, k, v, off)
         sel = selective_attention(q, k, v, block_size=self.compression_rate, top_k=self.selection_k, q_start=off,
                                   logit_softcap=cfg.logit_softcap)
-        mask = window_mask_at(off, q.shape[2], k.shape[1], cfg.sliding_window_size, q.device)
-        sw = scaled_dot_product(q, k.unsqueeze(1), v.unsqueeze(1), mask=mask, sink_logit=self.sink_logit,
-                                score_observer=self._observe, logit_softcap=cfg.logit_softcap)
+        lo = max(0, off - cfg.sliding_window_size + 1) if k.shape[1] > q.shape[2] else 0
+        mask = window_mask_at(off - lo, q.shape[2], k.shape[1] - lo, cfg.sliding_window_size, q.device)
+        sw = scaled_dot_product(q, k[:, lo:].unsqueeze(1), v[:, lo:].unsqueeze(1), mask=mask,
+                                sink_logit=self.sink_logit, score_observer=self._observe,
+                                logit_softcap=cfg.logit_softcap)
         g = torch.sigmoid(self.branch_gate(q))
         g = g / g.sum(-1, keepdim=True).clamp(min=1.0e-6)
         return self.output(g[..., 0:1] * comp + g[..., 1:2] * sel + g[..., 2:3] * sw)

@@ -5,9 +5,10 @@ prompts, 512 greedy steps; random-init bf16 weights).
     python -m saint_llm_b200.bench.decode [--batch 64] [--prompt 4096] [--steps 512]
 
 The prompt is prefilled in chunks through the cached forward (every layer's window K/V,
-compressed blocks and indexer keys go into the cache); then each decode step feeds the
-batch's last tokens through the cached forward and takes the argmax of the last-position
-logits on the device.  Prefill and decode are timed separately with CUDA events after a
+compressed blocks and indexer keys go into the cache).  Decoding (default) imports the
+cache into ``infer.static_decode.StaticDecoder`` and replays one CUDA graph per token
+(all 28 layers, LM head and argmax, position on the device); ``--engine cached`` feeds
+each token through the eager cached forward instead.  Prefill and decode are timed separately with CUDA events after a
 synchronize on both sides.  Prints one JSON line.
 """
 
@@ -30,6 +31,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=512)
     ap.add_argument("--chunk", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="(development only) override n_layers")
+    ap.add_argument("--engine", choices=["graph", "cached"], default="graph",
+                    help="graph: static-shape step captured in a CUDA graph; cached: the eager cached path")
     args = ap.parse_args()
     if ROOT not in sys.path:
         sys.path.insert(0, ROOT)
@@ -67,21 +70,36 @@ def main() -> None:
         for c in range(0, P, args.chunk):
             logits = last_logits(model, ids[:, c:c + args.chunk], bundle=bundle)
         s1.record()
-        tok = logits.argmax(-1, keepdim=True)
-        for i in range(S):
-            out[:, i:i + 1] = tok
-            tok = last_logits(model, tok, bundle=bundle).argmax(-1, keepdim=True)
-        s2.record()
+        torch.cuda.synchronize()
+        prefill_ms = s0.elapsed_time(s1)
+        kv_gb = bundle.nbytes() / 1e9
+        if args.engine == "cached":
+            tok = logits.argmax(-1, keepdim=True)
+            for i in range(S):
+                out[:, i:i + 1] = tok
+                tok = last_logits(model, tok, bundle=bundle).argmax(-1, keepdim=True)
+            s2.record()
+        else:
+            from saint_llm_b200.infer.static_decode import StaticDecoder
+
+            dec = StaticDecoder(model, B, P + S)
+            dec.load(bundle, logits)
+            del bundle
+            dec.capture()  # capture cost is outside the timed decode
+            torch.cuda.synchronize()
+            s1.record()
+            dec.generate(S, out)
+            s2.record()
         torch.cuda.synchronize()
     check_errors(dev)
-    prefill_ms, decode_ms = s0.elapsed_time(s1), s1.elapsed_time(s2)
+    decode_ms = s1.elapsed_time(s2)
     print(json.dumps({
         "bench": "decode", "metric": "decode tok/s", "value": B * S / (decode_ms / 1000.0), "unit": "tokens/s",
         "prefill_tokens_per_s": B * P / (prefill_ms / 1000.0), "decode_ms_per_step": decode_ms / S,
         "n_gpus": 1, "dtype": "bf16", "data": "synthetic uniform-random prompts; random-init weights",
         "config": {"model": "config-3 architecture (d2048 L%d, 64 routed top-6)" % cfg.n_layers, "batch": B,
                    "prompt": P, "decode_steps": S, "prefill_chunk": args.chunk,
-                   "kv_cache_gb": round(bundle.nbytes() / 1e9, 2),
+                   "kv_cache_gb": round(kv_gb, 2), "engine": args.engine,
                    "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1)},
     }), flush=True)
 

@@ -5,6 +5,7 @@
     python -m saint_llm_b200.bench.kernels moe --tokens 4096 --dim 2048 --inter 1408 --experts 64 --topk 6
     python -m saint_llm_b200.bench.kernels rmsnorm --rows 4096 --dim 2048
     python -m saint_llm_b200.bench.kernels mhc --tokens 4096 --dim 2048 --hc 4
+    python -m saint_llm_b200.bench.kernels indexer --t 4096 --index-heads 64 --index-dim 128 --index-m 4
 
 Timing: CUDA events on the launching stream around ``--iters`` launches after
 ``--warmup`` launches, with an L2 flush (a write larger than the 126 MB L2) before every
@@ -189,9 +190,30 @@ def bench_mhc(args: argparse.Namespace) -> None:
                  bytes_=bytes_)
 
 
+def bench_indexer(args: argparse.Namespace) -> None:
+    """Lightning-indexer scores: FLOPs of the visible (block-causal) tiles only."""
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.gemm import error_word
+
+    torch.manual_seed(0)
+    T, nh, c, m = args.t, args.index_heads, args.index_dim, args.index_m
+    nb = T // m
+    q = torch.randn(1, T, nh * c, device="cuda", dtype=torch.bfloat16)
+    keys = torch.randn(1, nb, c, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(1, T, nh, device="cuda")
+    out = torch.empty(1, T, nb, device="cuda")
+    err = error_word(torch.device("cuda"))
+    vis_tiles = sum(1 for qt in range(0, T, 128) for bt in range(0, nb, 128)
+                    if bt * m + m - 1 < min(T, qt + 128) - 1)
+    flops = 2.0 * vis_tiles * 128 * 128 * nh * c
+    bytes_ = 2.0 * (T * nh * c + nb * c) + 4.0 * (T * nh + T * nb)
+    _run(args, f"indexer_scores T={T} heads={nh} c={c} blocks={nb}",
+         lambda: backend.ext().indexer_scores(q, keys, w, None, m, 0, out, err), flops=flops, bytes_=bytes_)
+
+
 def main(argv: list[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["gemm", "attention", "moe", "rmsnorm", "mhc"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "moe", "rmsnorm", "mhc", "indexer"])
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--launches", type=int, default=0, help="run N launches and exit (profiler captures)")
@@ -211,9 +233,12 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--topk", type=int, default=6)
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--hc", type=int, default=4, help="mHC expansion factor")
+    ap.add_argument("--index-heads", type=int, default=64)
+    ap.add_argument("--index-dim", type=int, default=128)
+    ap.add_argument("--index-m", type=int, default=4)
     args = ap.parse_args(argv)
     {"gemm": bench_gemm, "attention": bench_attention, "moe": bench_moe, "rmsnorm": bench_rmsnorm,
-     "mhc": bench_mhc}[args.kernel](args)
+     "mhc": bench_mhc, "indexer": bench_indexer}[args.kernel](args)
 
 
 if __name__ == "__main__":

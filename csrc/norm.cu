@@ -313,6 +313,7 @@ torch::Tensor rope_norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 // in (P = 2n + n^2).  The raw dots q = X W^T come from the GEMM, the row sums of squares from
 // row_sumsq; the gates kernel turns them into r = 1/rms and p = r q.
 constexpr int kMhcTok = 32;    // tokens per CTA of the split backward
+constexpr int kMhcStep = 8;    // tokens whose loads are in flight together (160 registers, 3 CTAs / SM)
 // ssq[t] = sum_k X[t, k]^2 (bf16 rows, fp32 result): one warp per row, 16-byte loads.
 // The mHC projection itself (X W^T, skinny N) runs on the tcgen05 GEMM with split-K.
 __global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ X, float* __restrict__ ssq, int T, int F) {
@@ -748,17 +749,17 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
     }
     const int h = f0 / D, d = f0 % D;
     const int n_tok = min(kMhcTok, T - t0);
-    // four tokens per step: all eight loads are issued before any math (memory parallelism)
-    for (int tt = 0; tt < n_tok; tt += 4) {
-      uint2 xv[4], gv[4];
+    // kMhcStep tokens per step: all 2*kMhcStep loads are issued before any math (memory parallelism)
+    for (int tt = 0; tt < n_tok; tt += kMhcStep) {
+      uint2 xv[kMhcStep], gv[kMhcStep];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kMhcStep; ++u) {
         const int t = t0 + min(tt + u, n_tok - 1);
-        xv[u] = *reinterpret_cast<const uint2*>(X + static_cast<int64_t>(t) * F + f0);
+        xv[u] = __ldcs(reinterpret_cast<const uint2*>(X + static_cast<int64_t>(t) * F + f0));
         gv[u] = *reinterpret_cast<const uint2*>(din + static_cast<int64_t>(t) * D + d);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kMhcStep; ++u) {
         if (tt + u >= n_tok) break;
         const int ti = tt + u;
         const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
@@ -785,7 +786,7 @@ __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_
         __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
         oh[0] = __floats2bfloat162_rn(acc[0], acc[1]);
         oh[1] = __floats2bfloat162_rn(acc[2], acc[3]);
-        *reinterpret_cast<uint2*>(dX + static_cast<int64_t>(t0 + ti) * F + f0) = ov;
+        __stcs(reinterpret_cast<uint2*>(dX + static_cast<int64_t>(t0 + ti) * F + f0), ov);
       }
     }
   }

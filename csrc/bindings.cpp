@@ -4,7 +4,8 @@
 namespace sv4 {
 // gemm.cu
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate,
-          double alpha, torch::Tensor err);
+          double alpha, torch::Tensor err, bool symmetric);
+void sym_mirror(torch::Tensor d);
 void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor b1, torch::Tensor out,
                   torch::Tensor aux, torch::Tensor rowscale, torch::Tensor probs, torch::Tensor total_tiles,
                   int64_t n_probs, double gate_max, double lin_lo, double lin_hi, int64_t ksplit,
@@ -13,7 +14,7 @@ void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t
                         torch::Tensor probs, torch::Tensor total);
 int64_t problem_bytes();
 void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor out, bool a_mn, bool b_mn,
-                double alpha, double beta, torch::Tensor err);
+                double alpha, double beta, torch::Tensor err, bool symmetric);
 // optim.cu
 void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_t slice, double mu);
 void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
@@ -110,6 +111,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("build_moe_problems", &sv4::build_moe_problems);
   m.def("problem_bytes", &sv4::problem_bytes);
   m.def("gemm_axpby", &sv4::gemm_axpby);
+  m.def("sym_mirror", &sv4::sym_mirror);
   m.def("muon_momentum", &sv4::muon_momentum);
   m.def("muon_normalize", &sv4::muon_normalize);
   m.def("muon_apply", &sv4::muon_apply);

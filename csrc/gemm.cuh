@@ -55,6 +55,7 @@ struct GemmParams {
   int tma_d;                  // 1: D is written through map_d (TMA store / reduce-add) where possible
   int splitk;                 // single mode: > 1 splits K into `splitk` slices of `kc` (reduce-add into D)
   int kc;
+  int sym;                    // single mode: D is symmetric; tiles strictly below the diagonal are skipped
   int* err;
 };
 
@@ -133,7 +134,8 @@ __device__ __forceinline__ bool locate_tile(const GemmParams& P, int t, int& hin
     const int local = t - bt * per;
     mt = local / tiles_n<BN, BMODE>(pr);
     nt = local % tiles_n<BN, BMODE>(pr);
-    return true;
+    // symmetric output: a tile whose every column is left of its first row is mirrored later
+    return !(P.sym && nt * BN + BN - 1 < mt * kBM);
   }
   while (hint + 1 < P.n_probs && P.probs[hint + 1].tile_begin <= t) ++hint;
   pr = P.probs[hint];

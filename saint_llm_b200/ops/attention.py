@@ -172,8 +172,15 @@ def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
     if is_visual is not None:
         vis_bias = is_visual[:, : n_blocks * m_eff].reshape(b, n_blocks, m_eff).float().mean(-1)
     q = lin.linear(c_dq, idx.w_iuq.weight)  # (B, T, nh*c)
+    keys_b = _bf16(keys)
+    cp = 64 if c <= 64 else 128
+    if c > 128:
+        raise ValueError("indexer head dim above 128 is not supported by the fused indexer kernel")
+    if cp != c:  # zero-padding the head dim leaves every dot product unchanged
+        q = F.pad(q.view(b, t, nh, c), (0, cp - c)).view(b, t, nh * cp)
+        keys_b = F.pad(keys_b, (0, cp - c))
     scores = torch.empty(b, t, n_blocks, dtype=torch.float32, device=h.device)
-    backend.ext().indexer_scores(q.contiguous(), _bf16(keys).contiguous(), w.float().contiguous(),
+    backend.ext().indexer_scores(q.contiguous(), keys_b.contiguous(), w.float().contiguous(),
                                  None if vis_bias is None else vis_bias.contiguous(), m_eff, 0, scores,
                                  gemm.error_word(h.device))
     vals, ids = scores.topk(k_eff, dim=-1)

@@ -66,7 +66,9 @@ def _as_operand(x: Tensor) -> tuple[Tensor, bool]:
 
 
 def gemm_nt(a: Tensor, b: Tensor, *, out: Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-            accumulate: bool = False, alpha: float = 1.0) -> Tensor:
+            accumulate: bool = False, alpha: float = 1.0, symmetric: bool = False) -> Tensor:
+    """``symmetric=True``: the caller guarantees ``a @ b^T`` is symmetric (e.g. ``b is a``);
+    only tiles on or above the diagonal are computed and the rest is mirrored."""
     if a.dtype != torch.bfloat16:
         a = a.to(torch.bfloat16)
     if b.dtype != torch.bfloat16:
@@ -97,13 +99,18 @@ def gemm_nt(a: Tensor, b: Tensor, *, out: Tensor | None = None, out_dtype: torch
     bv, b_mn = _as_operand(b)
     if av.dim() == 2 and a.dim() == 2:
         squeeze = False
-    backend.ext().gemm(av, bv, out, a_mn, b_mn, accumulate, float(alpha), error_word(a.device))
+    sym = symmetric and not accumulate
+    backend.ext().gemm(av, bv, out, a_mn, b_mn, accumulate, float(alpha), error_word(a.device), sym)
+    if sym:
+        backend.ext().sym_mirror(out)
     del squeeze
     return out
 
 
-def gemm_axpby(a: Tensor, b: Tensor, c: Tensor, *, alpha: float = 1.0, beta: float = 1.0) -> Tensor:
-    """``alpha * a @ b^T + beta * c`` in one GEMM pass (bf16 in/out, fp32 accumulation)."""
+def gemm_axpby(a: Tensor, b: Tensor, c: Tensor, *, alpha: float = 1.0, beta: float = 1.0,
+               symmetric: bool = False) -> Tensor:
+    """``alpha * a @ b^T + beta * c`` in one GEMM pass (bf16 in/out, fp32 accumulation);
+    ``symmetric=True`` when the result is symmetric (see ``gemm_nt``)."""
     a, b = a.to(torch.bfloat16), b.to(torch.bfloat16)
     k = a.shape[-1]
     if k % 64:
@@ -113,7 +120,9 @@ def gemm_axpby(a: Tensor, b: Tensor, c: Tensor, *, alpha: float = 1.0, beta: flo
     out = torch.empty_like(c)
     av, a_mn = _as_operand(a)
     bv, b_mn = _as_operand(b)
-    backend.ext().gemm_axpby(av, bv, c, out, a_mn, b_mn, float(alpha), float(beta), error_word(a.device))
+    backend.ext().gemm_axpby(av, bv, c, out, a_mn, b_mn, float(alpha), float(beta), error_word(a.device), symmetric)
+    if symmetric:
+        backend.ext().sym_mirror(out)
     return out
 
 

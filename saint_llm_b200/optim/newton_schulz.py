@@ -90,6 +90,8 @@ def native_newton_schulz(y: Tensor, n_iter_stage1: int = 8, n_iter_stage2: int =
     Tall (r > c):   G = Y^T Y ;  P = c G G + b G ;  Y <- Y P + a Y
     The "+ b G" and "+ a Y" terms ride in the GEMM epilogue (no element-wise passes),
     and neither orientation needs a transpose copy: the tensor cores read Y^T directly.
+    G and P are symmetric: their GEMMs skip the tiles below the diagonal (~40 % of the
+    tiles of a 1408 x 1408 Gram) and a transpose kernel mirrors them.
     """
     from saint_llm_b200.ops import gemm
 
@@ -97,13 +99,13 @@ def native_newton_schulz(y: Tensor, n_iter_stage1: int = 8, n_iter_stage2: int =
     for steps, (a, b, c) in ((n_iter_stage1, coeffs_stage1), (n_iter_stage2, coeffs_stage2)):
         for _ in range(steps):
             if wide:
-                g = gemm.gemm_nt(y, y)
-                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b)
+                g = gemm.gemm_nt(y, y, symmetric=True)
+                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b, symmetric=True)
                 y = gemm.gemm_axpby(p, y.transpose(-1, -2), y, alpha=1.0, beta=a)
             else:
                 yt = y.transpose(-1, -2)
-                g = gemm.gemm_nt(yt, yt)
-                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b)
+                g = gemm.gemm_nt(yt, yt, symmetric=True)
+                p = gemm.gemm_axpby(g, g, g, alpha=c, beta=b, symmetric=True)
                 y = gemm.gemm_axpby(y, p, y, alpha=1.0, beta=a)
     return y
 

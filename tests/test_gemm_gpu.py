@@ -82,3 +82,20 @@ def test_gemm_bf16_output_view_with_row_stride(cuda):
     torch.cuda.synchronize()
     _close(wide[:, 8:208], _ref(a, b))
     assert wide[:, :8].abs().sum() == 0 and wide[:, 208:].abs().sum() == 0
+
+
+@pytest.mark.parametrize("batch,r,k", [(3, 1408, 2048), (2, 200, 256), (1, 520, 64)])
+def test_symmetric_gemm_and_axpby(cuda, batch, r, k):
+    """Symmetric outputs computed on the upper tiles only and mirrored."""
+    from saint_llm_b200.ops.gemm import gemm_axpby, gemm_nt
+
+    torch.manual_seed(0)
+    y = (torch.randn(batch, r, k, device=cuda) / k ** 0.5).to(torch.bfloat16)
+    g = gemm_nt(y, y, symmetric=True)
+    ref = y.float() @ y.float().transpose(-1, -2)
+    assert torch.equal(g, g.transpose(-1, -2))
+    assert ((g.float() - ref).norm() / ref.norm()).item() < 1e-2
+    p = gemm_axpby(g, g, g, alpha=-1.5, beta=0.5, symmetric=True)
+    pref = -1.5 * g.float() @ g.float() + 0.5 * g.float()
+    assert torch.equal(p, p.transpose(-1, -2))
+    assert ((p.float() - pref).norm() / pref.norm()).item() < 1e-2

@@ -26,6 +26,15 @@
 
 namespace sv4 {
 
+#ifdef SV4_ATTN_TRACE
+__device__ long long g_attn_trace[128];
+#define ATR(i) do { if (trace_cta && tid == 0 && (i) < 128) g_attn_trace[(i)] = clock64(); } while (0)
+#define ATRN() do { if (trace_cta && tid == 0 && tr < 128) g_attn_trace[tr] = clock64(); ++tr; } while (0)
+#else
+#define ATR(i) do { } while (0)
+#define ATRN() do { } while (0)
+#endif
+
 CUtensorMap make_map_nd(const void* base, CUtensorMapDataType dt, int rank, const uint64_t* dims,
                         const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
 
@@ -117,14 +126,6 @@ __device__ __forceinline__ void key_blocks(const AttnParams& P, int br, int t0, 
   }
 }
 
-// Visibility of key `key` to query `qpos` in branch `br`; `word` = the CSA mask word of the key.
-__device__ __forceinline__ bool visible(const AttnParams& P, int br, int key, int qpos, uint32_t word) {
-  if (br == 0) return key <= qpos && qpos - key < P.window;
-  if (key >= P.n) return false;
-  if (P.mode == 1) return key * P.m + P.m - 1 < qpos;
-  return (word >> (key & 31)) & 1u;
-}
-
 __device__ __forceinline__ bool branch_has_sink(const AttnParams& P, int br) {
   return P.sink != nullptr && (br == 0 || P.mode == 1);
 }
@@ -135,6 +136,10 @@ __global__ void __launch_bounds__(128, 2)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                 const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mkv,
                 const AttnParams P) {
+#ifdef SV4_ATTN_TRACE
+  const bool trace_cta = blockIdx.x == gridDim.x / 2 && blockIdx.y == 0 && blockIdx.z == 0;
+  int tr = 2;
+#endif
   constexpr int A = HD / 64;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -154,6 +159,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
   const int qpos = t0 + tid;
   const bool row_ok = qpos < P.T;
   const bool leader = tid == 0;
+  const float scale = P.scale, softcap = P.softcap;
+  const int window = P.window, mode = P.mode, cm = P.m, cn = P.n;
   if (leader) {
     for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
     fence_barrier_init();
@@ -170,6 +177,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
   const uint32_t tS = tbase + lane_off, tO = tbase + 128 + lane_off;
   constexpr uint32_t kIdS = make_idesc_f16(128, 128, 1, 1, false, false);
   constexpr uint32_t kIdO = make_idesc_f16(128, HD, 1, 1, false, true);
+  ATR(0);
 
   if (leader) {
     mbar_arrive_expect_tx(&bar[0], A * kAtom);
@@ -201,7 +209,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           mbar_arrive_expect_tx(&bar[1], A * kAtom);
           for (int a = 0; a < A; ++a) tma_load_3d(sV + a * kAtom, &mkv, &bar[1], a * 64, kb * 128, b);
         }
+        ATRN();
         mbar_wait(&bar[1], n_kv & 1, P.err, kErrTimeoutFull);
+        ATRN();
         if (q_wait) {
           mbar_wait(&bar[0], 0, P.err, kErrTimeoutFull);
           q_wait = false;
@@ -215,6 +225,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
       __syncwarp();
       ++n_kv;
       mbar_wait(&bar[2], n_s & 1, P.err, kErrTimeoutAccum);
+      ATRN();
       __syncwarp();  // reconverge before warp-collective tcgen05.ld
       ++n_s;
       tc_fence_after();
@@ -224,27 +235,45 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < 4; ++c) wmask[c] = kb * 4 + c < P.mask_words ? srow[kb * 4 + c] : 0u;
       }
-      // pass 1: row max of the visible logits
+      // visible keys of this row: [klo, khi], and for CSA the indexer's bitmask
+      int klo = 1, khi = 0;
+      if (row_ok) {
+        if (br == 0) {
+          klo = qpos - window + 1;
+          khi = qpos;
+        } else if (mode == 1) {
+          klo = 0;
+          khi = qpos >= cm ? min(cn - 1, (qpos - cm) / cm) : -1;
+        } else {
+          klo = 0;
+          khi = cn - 1;
+        }
+      }
+      const bool bits = br == 1 && mode == 2;
+      const bool cap = br == 0 && softcap > 0.f;
+      // pass 1: row max of the visible logits (branch-free per element)
       float rmax = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         tmem_ld32(tS + c * 32, r);
+        const uint32_t word = !bits ? 0xffffffffu : (c == 0 ? wmask[0] : c == 1 ? wmask[1] : c == 2 ? wmask[2] : wmask[3]);
+        const int base = kb * 128 + c * 32;
         tmem_ld_wait();
+        if (c == 0) ATRN();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int key = kb * 128 + c * 32 + j;
-          if (row_ok && visible(P, br, key, qpos, wmask[c])) {
-            float s = __uint_as_float(r[j]) * P.scale;
-            if (br == 0) {
-              amax = fmaxf(amax, fabsf(s));
-              if (P.softcap > 0.f) s = P.softcap * tanhf(s / P.softcap);
-            }
-            rmax = fmaxf(rmax, s);
-          }
+          const int key = base + j;
+          const bool vis = key >= klo && key <= khi && ((word >> j) & 1u);
+          float sv = __uint_as_float(r[j]) * scale;
+          if (br == 0) amax = fmaxf(amax, vis ? fabsf(sv) : 0.f);
+          if (cap) sv = softcap * tanhf(sv / softcap);
+          rmax = fmaxf(rmax, vis ? sv : -INFINITY);
         }
+        if (c == 0) ATRN();
       }
       const float m_new = fmaxf(m_run, rmax);
+      ATRN();
       if (n_o > o_before) {  // previous PV of this branch must finish before P / O are touched
         mbar_wait(&bar[3], (n_o - 1) & 1, P.err, kErrTimeoutAccum);
         __syncwarp();  // reconverge before warp-collective tcgen05.ld
@@ -269,30 +298,36 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
         l_run *= __expf(m_run - m_new);  // only the sink contributed so far
       }
       m_run = m_new;
+      ATRN();
       // pass 2: probabilities -> bf16 P tile
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
         tmem_ld32(tS + c * 32, r);
+        const uint32_t word = !bits ? 0xffffffffu : (c == 0 ? wmask[0] : c == 1 ? wmask[1] : c == 2 ? wmask[2] : wmask[3]);
+        const int base = kb * 128 + c * 32;
         tmem_ld_wait();
         float pv[32];
+        float lp[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums (no 32-long add chain)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int key = kb * 128 + c * 32 + j;
-          float p = 0.f;
-          if (row_ok && visible(P, br, key, qpos, wmask[c])) {
-            float s = __uint_as_float(r[j]) * P.scale;
-            if (br == 0 && P.softcap > 0.f) s = P.softcap * tanhf(s / P.softcap);
-            p = __expf(s - m_run);
-          }
-          l_run += p;
-          pv[j] = p;
+          const int key = base + j;
+          const bool vis = key >= klo && key <= khi && ((word >> j) & 1u);
+          float sv = __uint_as_float(r[j]) * scale;
+          if (cap) sv = softcap * tanhf(sv / softcap);
+          const float pr = vis ? __expf(sv - m_run) : 0.f;
+          lp[j & 3] += pr;
+          pv[j] = pr;
         }
+        l_run += (lp[0] + lp[1]) + (lp[2] + lp[3]);
         put_row32(sP, tid, c * 32, pv);
+        if (c == 0) ATRN();
       }
+      ATRN();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
+      ATRN();
       if (leader) {
         tc_fence_after();
         const uint32_t ap = smem_u32(sP), av = smem_u32(sV);
@@ -301,6 +336,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           mma_bf16(tbase + 128, desc_k(ap, s), desc_mn(av, s), kIdO, (n_o > o_before || s > 0) ? 1u : 0u);
         mma_commit(&bar[3]);
       }
+      ATRN();
       __syncwarp();
       ++n_o;
     }
@@ -344,6 +380,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
     tc_fence_after();
   }
 
+  ATR(1);
   if (P.max_logit != nullptr) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -481,30 +518,45 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < 4; ++c) wmask[c] = kb * 4 + c < P.mask_words ? srow[kb * 4 + c] : 0u;
       }
+      int klo = 1, khi = 0;
+      if (row_ok) {
+        if (br == 0) {
+          klo = qpos - P.window + 1;
+          khi = qpos;
+        } else if (P.mode == 1) {
+          klo = 0;
+          khi = qpos >= P.m ? min(P.n - 1, (qpos - P.m) / P.m) : -1;
+        } else {
+          klo = 0;
+          khi = P.n - 1;
+        }
+      }
+      const bool bits = br == 1 && P.mode == 2;
+      const bool cap = br == 0 && P.softcap > 0.f;
+      const float scale = P.scale, softcap = P.softcap, lse_b = lse[br], dv_b = Dv[br];
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t rs[32], rp[32];
         tmem_ld32(tS + lane_off + c * 32, rs);
         tmem_ld32(tdP + lane_off + c * 32, rp);
+        const uint32_t word = !bits ? 0xffffffffu : (c == 0 ? wmask[0] : c == 1 ? wmask[1] : c == 2 ? wmask[2] : wmask[3]);
+        const int base = kb * 128 + c * 32;
         tmem_ld_wait();
         float pv[32], dv[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int key = kb * 128 + c * 32 + j;
-          float p = 0.f, ds = 0.f;
-          if (row_ok && visible(P, br, key, qpos, wmask[c])) {
-            const float raw = __uint_as_float(rs[j]) * P.scale;
-            float s = raw, dcap = 1.f;
-            if (br == 0 && P.softcap > 0.f) {
-              const float th = tanhf(raw / P.softcap);
-              s = P.softcap * th;
-              dcap = 1.f - th * th;
-            }
-            p = __expf(s - lse[br]);
-            ds = p * (__uint_as_float(rp[j]) - Dv[br]) * dcap * P.scale;
+          const int key = base + j;
+          const bool vis = key >= klo && key <= khi && ((word >> j) & 1u);
+          const float raw = __uint_as_float(rs[j]) * scale;
+          float sv = raw, dcap = 1.f;
+          if (cap) {
+            const float th = tanhf(raw / softcap);
+            sv = softcap * th;
+            dcap = 1.f - th * th;
           }
-          pv[j] = p;
-          dv[j] = ds;
+          const float pr = vis ? __expf(sv - lse_b) : 0.f;
+          pv[j] = pr;
+          dv[j] = pr * (__uint_as_float(rp[j]) - dv_b) * dcap * scale;
         }
         put_row32(sP, tid, c * 32, pv);
         put_row32(sdS, tid, c * 32, dv);
@@ -662,6 +714,16 @@ static void check_inputs(const torch::Tensor& q, const torch::Tensor& k, const t
 
 static int fwd_smem(int hd) { return 2 * (hd / 64) * kAtom + std::max(hd / 64, 2) * kAtom + 64 + 1024; }
 static int bwd_smem(int hd) { return 4 * (hd / 64) * kAtom + 4 * kAtom + 4 * 4096 + 64 + 1024; }
+
+#ifdef SV4_ATTN_TRACE
+torch::Tensor attn_trace() {
+  long long h[128];
+  C10_CUDA_CHECK(cudaMemcpyFromSymbol(h, g_attn_trace, sizeof(h)));
+  auto t = torch::empty({128}, torch::kInt64);
+  memcpy(t.data_ptr<int64_t>(), h, sizeof(h));
+  return t;
+}
+#endif
 
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
               int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,

@@ -90,6 +90,9 @@ void ep_dispatch_bwd(std::vector<int64_t> dx_ptrs, torch::Tensor gpos, int64_t C
                      torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch, int64_t timeout_ns,
                      torch::Tensor err);
 std::tuple<torch::Tensor, std::string> symm_alloc(int64_t nbytes, int64_t device);
+#ifdef SV4_ATTN_TRACE
+torch::Tensor attn_trace();
+#endif
 // indexer.cu
 void indexer_scores(torch::Tensor q, torch::Tensor keys, torch::Tensor w, c10::optional<torch::Tensor> vis,
                     int64_t m, int64_t q_start, torch::Tensor out, torch::Tensor err);
@@ -129,6 +132,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_norm_bwd", &sv4::rope_norm_bwd);
   m.def("row_sumsq", &sv4::row_sumsq);
   m.def("indexer_scores", &sv4::indexer_scores);
+#ifdef SV4_ATTN_TRACE
+  m.def("attn_trace", &sv4::attn_trace);
+#endif
   m.def("ep_signal", &sv4::ep_signal);
   m.def("ep_post_counts", &sv4::ep_post_counts);
   m.def("ep_plan", &sv4::ep_plan);

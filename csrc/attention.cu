@@ -315,7 +315,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           const bool vis = key >= klo && key <= khi && ((word >> j) & 1u);
           float sv = __uint_as_float(r[j]) * scale;
           if (cap) sv = softcap * tanhf(sv / softcap);
-          const float pr = vis ? __expf(sv - m_run) : 0.f;
+          const float pr = __expf(vis ? sv - m_run : -INFINITY);  // masked lanes: exp(-inf) = 0
           lp[j & 3] += pr;
           pv[j] = pr;
         }
@@ -554,7 +554,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
             sv = softcap * th;
             dcap = 1.f - th * th;
           }
-          const float pr = vis ? __expf(sv - lse_b) : 0.f;
+          const float pr = __expf(vis ? sv - lse_b : -INFINITY);
           pv[j] = pr;
           dv[j] = pr * (__uint_as_float(rp[j]) - dv_b) * dcap * scale;
         }

@@ -69,6 +69,15 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t base, int s) {  // contract
 }
 
 // 32 fp32 values of row r, columns [c0, c0 + 32), as bf16 into a canonical tile.
+// e^x as one special-function-unit instruction: 2^(x log2 e) with ex2.approx.ftz
+// (flush-to-zero: results below the normal range become 0, which the bf16 P tile could
+// not represent anyway).
+__device__ __forceinline__ float exp_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
 __device__ __forceinline__ void put_row32(uint8_t* tile, int r, int c0, const float (&v)[32]) {
   uint8_t* rowp = tile + (c0 >> 6) * kAtom + r * 128;
   const int q0 = (c0 & 63) >> 3;
@@ -315,7 +324,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           const bool vis = key >= klo && key <= khi && ((word >> j) & 1u);
           float sv = __uint_as_float(r[j]) * scale;
           if (cap) sv = softcap * tanhf(sv / softcap);
-          const float pr = __expf(vis ? sv - m_run : -INFINITY);  // masked lanes: exp(-inf) = 0
+          const float pr = exp_sfu(vis ? sv - m_run : -INFINITY);  // masked lanes: e^-inf = 0
           lp[j & 3] += pr;
           pv[j] = pr;
         }
@@ -554,7 +563,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
             sv = softcap * th;
             dcap = 1.f - th * th;
           }
-          const float pr = __expf(vis ? sv - lse_b : -INFINITY);
+          const float pr = exp_sfu(vis ? sv - lse_b : -INFINITY);
           pv[j] = pr;
           dv[j] = pr * (__uint_as_float(rp[j]) - dv_b) * dcap * scale;
         }

@@ -192,6 +192,82 @@ class _SharedSwiGLUFn(torch.autograd.Function):
         return dh, dwg, dwu, dwd, None
 
 
+def _cat(ws: list[Tensor], dim: int) -> Tensor:
+    # rebuilt on every call: native optimizer kernels update weights in place without
+    # bumping torch's version counters, so a cached copy could go stale
+    return torch.cat([_bf16c(w.detach()) for w in ws], dim=dim)
+
+
+class _SharedGroupFn(torch.autograd.Function):
+    """Several shared SwiGLU experts as one: sum_e SwiGLU_e(h) = [Wd_1 .. Wd_n] SwiGLU(h;
+    [Wg_1; ..; Wg_n], [Wu_1; ..; Wu_n]) because the activation is element-wise, so the
+    forward is one fused SwiGLU GEMM (intermediate width sum I_e) and one down GEMM, and the
+    backward one dgrad per GEMM (and one add fewer per extra expert in each direction);
+    weight gradients still go to each expert's own weights."""
+
+    @staticmethod
+    def forward(ctx, h: Tensor, clamps: tuple[float, float, float], *ws: Tensor):  # type: ignore[override]
+        ext = backend.ext()
+        dev = h.device
+        n = len(ws) // 3
+        wgs, wus, wds = list(ws[:n]), list(ws[n:2 * n]), list(ws[2 * n:])
+        wg, wu, wd = _cat(wgs, 0), _cat(wus, 0), _cat(wds, 1)
+        T = h.shape[0]
+        I = wg.shape[0]
+        hb = _bf16c(h)
+        act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+        pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
+        y = gemm.gemm_nt(act, wd)
+        ctx.save_for_backward(hb, act, pre, *ws)
+        ctx.clamps, ctx.n = clamps, n
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        hb, act, pre, *ws = ctx.saved_tensors
+        n = ctx.n
+        wgs, wus, wds = ws[:n], ws[n:2 * n], ws[2 * n:]
+        ext = backend.ext()
+        dev = hb.device
+        wg, wu, wd = _cat(list(wgs), 0), _cat(list(wus), 0), _cat(list(wds), 1)
+        I = wg.shape[0]
+        dyb = _bf16c(dy)
+        dact = gemm.gemm_nt(dyb, wd.t())
+        grads: list[Tensor | None] = []
+        dpre = torch.empty_like(pre)
+        ext.swiglu_bwd(dact, pre, dpre, *ctx.clamps)
+        dh = torch.empty_like(hb)
+        ext.swiglu_dense_dgrad(dpre, wg, wu, dh, gemm.error_word(dev))
+        off = 0
+        dg, du, dd = [], [], []
+        for e in range(n):
+            ie = wgs[e].shape[0]
+            dg.append(accumulate_weight_grad(wgs[e], dpre[:, off:off + ie], hb))
+            du.append(accumulate_weight_grad(wus[e], dpre[:, I + off:I + off + ie], hb))
+            dd.append(accumulate_weight_grad(wds[e], dyb, act[:, off:off + ie]))
+            off += ie
+        grads = dg + du + dd
+        return (dh, None, *grads)
+
+
+def shared_experts(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> Tensor | None:
+    """Sum of the shared SwiGLU experts on h (T, D); None when there are none."""
+    ex = list(experts)
+    if not ex:
+        return None
+    if len(ex) == 1:
+        return shared_swiglu(h, ex[0])
+    clamps = {(float(e.clamp_gate_max), float(e.clamp_linear[0]), float(e.clamp_linear[1])) for e in ex}
+    if len(clamps) != 1 or any(e.gate_proj.weight.shape[0] % 64 for e in ex):
+        out = shared_swiglu(h, ex[0])
+        for e in ex[1:]:
+            out = out + shared_swiglu(h, e)
+        return out
+    ws = [e.gate_proj.weight for e in ex] + [e.up_proj.weight for e in ex] + [e.down_proj.weight for e in ex]
+    return _SharedGroupFn.apply(h, clamps.pop(), *ws)
+
+
 def shared_swiglu(h: Tensor, expert: nn.Module) -> Tensor:
     lin = expert.clamp_linear
     return _SharedSwiGLUFn.apply(h, expert.gate_proj.weight, expert.up_proj.weight, expert.down_proj.weight,
@@ -220,8 +296,9 @@ def moe_forward(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual
     k = layer.cfg.experts_per_token
     h2 = h.reshape(b * t, d)
     out = routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts)
-    for expert in layer.shared_experts:
-        out = out + shared_swiglu(h2, expert)
+    sh = shared_experts(h2, layer.shared_experts)
+    if sh is not None:
+        out = out + sh
     return out.view(b, t, d)
 
 
@@ -247,4 +324,4 @@ def _moe_per_module(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vi
     return out.view(b, t, d)
 
 
-__all__ = ["RoutePlan", "moe_forward", "routed_experts", "shared_swiglu"]
+__all__ = ["RoutePlan", "moe_forward", "routed_experts", "shared_experts", "shared_swiglu"]

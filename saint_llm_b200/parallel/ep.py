@@ -141,7 +141,7 @@ def moe_forward_ep(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vis
     ge = layer.grouped_experts
     native = backend.native_for(x)
     if native:
-        from saint_llm_b200.ops.moe_native import routed_experts, shared_swiglu
+        from saint_llm_b200.ops.moe_native import routed_experts, shared_experts
 
         ones = torch.ones(local_ids.shape[0], 1, dtype=torch.float32, device=x.device)
         y_recv = routed_experts(recv_x, local_ids, ones, ge)
@@ -153,8 +153,13 @@ def moe_forward_ep(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vis
     inv[order] = torch.arange(order.numel(), device=order.device)
     y_pair = back.index_select(0, inv).view(T, k, d)
     out = (y_pair.float() * gate.reshape(T, k, 1).float()).sum(1).to(h2.dtype)
-    for expert in layer.shared_experts:
-        out = out + (shared_swiglu(h2, expert) if native else expert(h2))
+    if native:
+        sh = shared_experts(h2, layer.shared_experts)
+        if sh is not None:
+            out = out + sh
+    else:
+        for expert in layer.shared_experts:
+            out = out + expert(h2)
     return out.view(b, t, d)
 
 

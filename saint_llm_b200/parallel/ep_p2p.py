@@ -386,7 +386,7 @@ def p2p_routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module,
 
 
 def moe_forward_p2p(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
-    from saint_llm_b200.ops.moe_native import shared_swiglu
+    from saint_llm_b200.ops.moe_native import shared_experts
 
     b, t, d = x.shape
     h = layer.norm(x)
@@ -396,8 +396,9 @@ def moe_forward_p2p(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vi
     h2 = h.reshape(b * t, d)
     out = p2p_routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts,
                              layer.ep_comm, layer.layer_idx)
-    for expert in layer.shared_experts:
-        out = out + shared_swiglu(h2, expert)
+    sh = shared_experts(h2, layer.shared_experts)
+    if sh is not None:
+        out = out + sh
     return out.view(b, t, d)
 
 

@@ -279,3 +279,29 @@ def test_native_muon_step_matches_reference_direction(cuda):
     da, db = (a.detach() - w0).flatten(1), (b.detach().float() - w0).flatten(1)
     assert (F.cosine_similarity(da, db, dim=1) > 0.97).all()
     assert abs(da.norm().item() / db.norm().item() - 1) < 0.05
+
+
+def test_shared_expert_group_matches_separate(cuda):
+    """Two shared experts fused into one SwiGLU of twice the width == their sum."""
+    from saint_llm_b200.models.moe import SwiGLU
+    from saint_llm_b200.ops.moe_native import shared_experts, shared_swiglu
+
+    torch.manual_seed(0)
+    ex = [SwiGLU(512, 384, (-10.0, 10.0), 10.0).to(cuda) for _ in range(2)]
+    with torch.no_grad():
+        for e in ex:
+            for p in e.parameters():
+                p.copy_(_bf(p * 3))
+    h = _bf(torch.randn(333, 512, device=cuda)).requires_grad_(True)
+    g = torch.randn(333, 512, device=cuda)
+    y0 = shared_swiglu(h, ex[0]) + shared_swiglu(h, ex[1])
+    y0.float().backward(g)
+    ref = [h.grad.clone()] + [p.grad.clone() for e in ex for p in e.parameters()]
+    h.grad = None
+    for e in ex:
+        e.zero_grad()
+    y1 = shared_experts(h, ex)
+    y1.float().backward(g)
+    assert _rel(y1, y0) < 1e-2
+    for got, want in zip([h.grad] + [p.grad for e in ex for p in e.parameters()], ref, strict=True):
+        assert _rel(got, want) < 2e-2

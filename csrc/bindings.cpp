@@ -15,6 +15,12 @@ void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t
 int64_t problem_bytes();
 void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor out, bool a_mn, bool b_mn,
                 double alpha, double beta, torch::Tensor err, bool symmetric);
+// gemm_fp8.cu
+void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale);
+void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale);
+void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
+              torch::Tensor err);
+int64_t fp8_sf_bytes(int64_t rows, int64_t k);
 // optim.cu
 void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_t slice, double mu);
 void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
@@ -115,6 +121,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("problem_bytes", &sv4::problem_bytes);
   m.def("gemm_axpby", &sv4::gemm_axpby);
   m.def("sym_mirror", &sv4::sym_mirror);
+  m.def("fp8_quant_rows", &sv4::fp8_quant_rows);
+  m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
+  m.def("gemm_fp8", &sv4::gemm_fp8);
+  m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
   m.def("muon_momentum", &sv4::muon_momentum);
   m.def("muon_normalize", &sv4::muon_normalize);
   m.def("muon_apply", &sv4::muon_apply);

@@ -1,0 +1,445 @@
+// Block-scaled FP8 GEMM on the sm_100a tensor cores, and the quantisation kernels feeding it.
+//
+//   D[m, n] = sum_k (A[m, k] * sa[m, k / 128]) * (B[n, k] * sb[n / 128, k / 128])      (bf16 D)
+//
+// A (activations) is quantised in 1 x 128 blocks, B (weights, (N, K) row-major) in 128 x 128
+// blocks; values are E4M3, scales powers of two stored as UE8M0 bytes (2^(byte - 127)).  The
+// forward recipe follows the reference's FP8 linear (kernels/fp8_gemm.py:24-101 scales a
+// rowwise activation and a per-channel weight through torch._scaled_mm); here the blocks are
+// finer and the scaling is done by the MMA itself: tcgen05.mma kind::mxf8f6f4.block_scale reads
+// one scale per row of A and per column of B for every 32-element K step from tensor memory, so
+// no per-block promotion runs on the CUDA cores.
+//
+// Scale-factor layout (produced by the quantisation kernels, consumed by the GEMM): for an
+// operand of R rows (padded to a multiple of 128) and K columns, chunk (rb, kb) covers rows
+// [128 rb, 128 rb + 128) and columns [128 kb, 128 kb + 128) and is 512 contiguous bytes at
+// ((rb * K/128) + kb) * 512.  Row r of the chunk owns the 32-bit word at byte
+// 16 * (r % 32) + 4 * (r / 32); its four bytes are the scales of the four 32-wide K steps (all
+// equal here, since a block spans 128 columns).  That is the shape tcgen05.cp 32x128b.warpx4
+// copies into tensor memory: smem row r % 32 (16 bytes) lands in lane r % 32 of every lane
+// quarter, word j in column j, which is where the MMA looks for the scale of row r % 32 + 32 j.
+//
+// GEMM roles (one CTA per SM, persistent over 128 x 128 output tiles):
+//   warp 0     : producer -- TMA loads of the A and B k-blocks (128 x 128 bytes each, 128B
+//                swizzle) and bulk copies of the two 512-byte scale chunks into a 5-deep ring;
+//   warp 1     : MMA issuer -- tcgen05.cp of the stage's scale chunks into tensor memory, then
+//                four M=128, N=128, K=32 block-scaled MMAs into one of two accumulators;
+//   warps 2..5 : epilogue -- tcgen05.ld, bf16 pack, TMA stores through swizzled staging.
+// Tensor memory: accumulators in columns [0, 256), scale factors of stage s in columns
+// 256 + 8 s (A) and 256 + 8 s + 4 (B).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_fp8.h>
+#include <torch/extension.h>
+
+#include "gemm.cuh"
+
+namespace sv4 {
+
+CUtensorMap make_map_3d(const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0, uint64_t d1,
+                        uint64_t d2, uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1,
+                        CUtensorMapSwizzle swz);
+
+namespace {
+
+constexpr float kE4M3Max = 448.0f;
+constexpr int kF8BN = 128;
+constexpr int kF8BK = 128;  // elements = bytes = one 128B swizzle row
+constexpr int kF8Stages = 5;
+constexpr int kF8ABytes = kBM * kF8BK;
+constexpr int kF8BBytes = kF8BN * kF8BK;
+constexpr int kF8StageBytes = kF8ABytes + kF8BBytes;
+constexpr int kSfChunk = 512;
+constexpr int kF8SfOffset = kF8Stages * kF8StageBytes;
+constexpr int kF8EpiOffset = kF8SfOffset + kF8Stages * 2 * kSfChunk;
+constexpr int kF8BarOffset = kF8EpiOffset + 4 * kEpiBufs * kEpiStageBytes;
+constexpr int kF8SmemTotal = kF8BarOffset + 256 + 1024;
+constexpr int kF8SfTmemCol = 2 * kF8BN;
+constexpr uint32_t kF8TmemCols = 512;
+static_assert(kF8SfTmemCol + 8 * kF8Stages <= static_cast<int>(kF8TmemCols), "tensor memory budget");
+static_assert(kF8SmemTotal <= 232448, "shared memory budget");
+
+// Exponent e of the smallest power of two with amax / 2^e <= 448 (amax == 0 -> 0): the
+// exponent of r = amax / 448 rounded up, read from its bits (exact, no log2).
+__device__ __forceinline__ int pow2_exponent(float amax) {
+  if (!(amax > 0.f)) return 0;
+  const uint32_t b = __float_as_uint(__fdiv_rn(amax, kE4M3Max));
+  int e = static_cast<int>((b >> 23) & 0xFFu) - 127;
+  if ((b & 0x7FFFFFu) != 0u) e += 1;
+  return max(-126, min(126, e));
+}
+
+__device__ __forceinline__ float exp2_int(int e) {  // 2^e for e in [-126, 127]
+  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+__device__ __forceinline__ uint2 quant8x(const float* v, float inv) {
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const __nv_fp8x2_storage_t p =
+        __nv_cvt_float2_to_fp8x2(make_float2(v[i] * inv, v[i + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+    w[i / 4] |= static_cast<uint32_t>(p) << (8 * (i % 4));
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ int64_t sf_word_offset(int64_t rb, int64_t kb, int64_t kblocks, int r) {
+  return (rb * kblocks + kb) * kSfChunk + 16 * (r & 31) + 4 * (r >> 5);
+}
+
+// 1 x 128 activation quantisation: one 16-lane group per block, 8 elements per lane.  Rows in
+// [M, Mpad) get the neutral scale byte (their A rows are zero-filled by TMA).
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M,
+                                                         int Mpad, int K, uint8_t* __restrict__ q, int64_t ldq,
+                                                         uint8_t* __restrict__ sf, float* __restrict__ scale) {
+  const int kblocks = K / 128;
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * 16 + threadIdx.x / 16;
+  const int sub = threadIdx.x & 15;
+  const bool active = g < static_cast<int64_t>(Mpad) * kblocks;
+  const int row = active ? static_cast<int>(g / kblocks) : 0;
+  const int kb = active ? static_cast<int>(g % kblocks) : 0;
+  const bool live = active && row < M;
+  float v[8];
+  if (live) {
+    unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + kb * 128 + sub * 8), v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const int e = pow2_exponent(amax);
+  if (live) *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v, exp2_int(-e));
+  if (active && sub == 0) {
+    const uint32_t byte = static_cast<uint32_t>(e + 127);
+    *reinterpret_cast<uint32_t*>(sf + sf_word_offset(row / 128, kb, kblocks, row & 127)) = byte * 0x01010101u;
+    if (live && scale != nullptr) scale[static_cast<int64_t>(row) * kblocks + kb] = exp2_int(e);
+  }
+}
+
+// 128 x 128 weight quantisation: one CTA per block; lane group (warp w, half h) covers rows
+// {16 i + 2 w + h}, 16 lanes x 8 columns.
+__global__ void __launch_bounds__(256) quant_blocks_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw, int K,
+                                                           uint8_t* __restrict__ q, int64_t ldq,
+                                                           uint8_t* __restrict__ sf, float* __restrict__ scale) {
+  __shared__ float red[8];
+  const int nb = blockIdx.y, kb = blockIdx.x, kblocks = K / 128;
+  const int r0 = threadIdx.x / 16, sub = threadIdx.x & 15;
+  float v[8][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = static_cast<int64_t>(nb) * 128 + r0 + 16 * i;
+    unpack8(*reinterpret_cast<const uint4*>(w + row * ldw + kb * 128 + sub * 8), v[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+  const int e = pow2_exponent(amax);
+  const float inv = exp2_int(-e);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = static_cast<int64_t>(nb) * 128 + r0 + 16 * i;
+    *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v[i], inv);
+  }
+  if (threadIdx.x < 128) {
+    const uint32_t byte = static_cast<uint32_t>(e + 127);
+    *reinterpret_cast<uint32_t*>(sf + (static_cast<int64_t>(nb) * kblocks + kb) * kSfChunk + 4 * threadIdx.x) =
+        byte * 0x01010101u;
+  }
+  if (threadIdx.x == 0 && scale != nullptr) scale[static_cast<int64_t>(nb) * kblocks + kb] = exp2_int(e);
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 rows x 16 bytes of shared memory -> 4 columns of every lane quarter of tensor memory.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// kind::mxf8f6f4 block-scaled instruction descriptor: E4M3 x E4M3, K-major A and B, UE8M0
+// scales, scale-factor byte 0 of each word (the four bytes of a word are equal here).
+__host__ __device__ constexpr uint32_t make_idesc_mxf8(int m, int n) {
+  return (0u << 7)                                 // A format E4M3
+         | (0u << 10)                              // B format E4M3
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (1u << 23)                              // scale format UE8M0
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+struct F8Params {
+  int m, n, k;
+  int tiles_n, total;
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int* err;
+};
+
+__global__ void __launch_bounds__(192, 1)
+gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const __grid_constant__ CUtensorMap map_d, const F8Params P) {
+  constexpr uint32_t kIdesc = make_idesc_mxf8(kBM, kF8BN);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kF8BarOffset);
+  uint64_t* empty = full + kF8Stages;
+  uint64_t* acc_full = empty + kF8Stages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kblocks = P.k / kF8BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kF8Stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kF8TmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_d);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < P.total && ok; t += gridDim.x) {
+        const int mt = t / P.tiles_n, nt = t % P.tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, P.err, kErrTimeoutEmpty)) { ok = false; break; }
+          uint8_t* sa = smem + stage * kF8StageBytes;
+          uint8_t* sfs = smem + kF8SfOffset + stage * 2 * kSfChunk;
+          mbar_arrive_expect_tx(&full[stage], kF8StageBytes + 2 * kSfChunk);
+          tma_load_3d(sa, &map_a, &full[stage], kb * kF8BK, mt * kBM, 0);
+          tma_load_3d(sa + kF8ABytes, &map_b, &full[stage], kb * kF8BK, nt * kF8BN, 0);
+          bulk_load(sfs, P.sfa + (static_cast<int64_t>(mt) * kblocks + kb) * kSfChunk, kSfChunk, &full[stage]);
+          bulk_load(sfs + kSfChunk, P.sfb + (static_cast<int64_t>(nt) * kblocks + kb) * kSfChunk, kSfChunk,
+                    &full[stage]);
+          if (++stage == kF8Stages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < P.total && ok; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, P.err, kErrTimeoutAccum)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kF8BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, P.err, kErrTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kF8StageBytes);
+          const uint32_t sb = sa + kF8ABytes;
+          const uint32_t sfs = smem_u32(smem + kF8SfOffset + stage * 2 * kSfChunk);
+          const uint32_t t_sfa = tmem_base + kF8SfTmemCol + 8 * stage;
+          const uint32_t t_sfb = t_sfa + 4;
+          // no-swizzle K-major core matrices of 8 rows x 16 bytes, 128 bytes apart
+          tmem_cp_sf(t_sfa, make_smem_desc(sfs, 128, 128, 0));
+          tmem_cp_sf(t_sfb, make_smem_desc(sfs + kSfChunk, 128, 128, 0));
+#pragma unroll
+          for (int kk = 0; kk < kF8BK / 32; ++kk) {
+            const uint64_t da = make_smem_desc(sa + kk * 32, 16, 1024, 2);
+            const uint64_t db = make_smem_desc(sb + kk * 32, 16, 1024, 2);
+            mma_mxf8(d_tmem, da, db, kIdesc, t_sfa, t_sfb, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kF8Stages) { stage = 0; phase ^= 1; }
+        }
+        mma_commit(&acc_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    uint8_t* stg = smem + kF8EpiOffset + quarter * kEpiBufs * kEpiStageBytes;
+    int sbuf = 0, acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < P.total; t += gridDim.x) {
+      const int mt = t / P.tiles_n, nt = t % P.tiles_n;
+      if (!mbar_wait(&acc_full[acc], acc_phase, P.err, kErrTimeoutAccum)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + acc * kF8BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int drow = mt * kBM + quarter * 32;
+      const bool issue = drow < P.m;
+#pragma unroll 1
+      for (int c = 0; c < kF8BN; c += 64) {
+        float v[64];
+#pragma unroll
+        for (int h = 0; h < 64; h += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c + h, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[h + j] = __uint_as_float(r[j]);
+        }
+        stage_store(stg, sbuf, lane, [&](int q) { return pack_bf16x8(v + 8 * q); }, &map_d, false,
+                    nt * kF8BN + c, drow, 0, issue);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kF8TmemCols);
+  }
+}
+
+int sm_count(int dev) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+void check_fp8_operand(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.element_size() == 1, name, ": 2-D one-byte CUDA tensor required");
+  TORCH_CHECK(t.stride(1) == 1 && t.stride(0) % 16 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              name, ": rows must be contiguous, 16-byte aligned");
+}
+
+}  // namespace
+
+// x (M, K) bf16 -> q (M, K) e4m3 bytes, sf (ceil(M/128) * K/128 * 512) bytes, scale (M, K/128) fp32.
+void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x: 2-D bf16, unit inner stride");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 128 == 0, "K must be a multiple of 128");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x rows 16-byte aligned");
+  check_fp8_operand(q, "q");
+  TORCH_CHECK(q.size(0) == M && q.size(1) == K, "q shape");
+  const int64_t Mpad = (M + 127) / 128 * 128;
+  TORCH_CHECK(sf.numel() >= Mpad / 128 * (K / 128) * kSfChunk && sf.element_size() == 1, "sf size");
+  float* sp = nullptr;
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() && scale->numel() == M * (K / 128),
+                "scale (M, K/128) fp32");
+    sp = scale->data_ptr<float>();
+  }
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t groups = Mpad * (K / 128);
+  quant_rows_kernel<<<static_cast<unsigned>((groups + 15) / 16), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), static_cast<int>(M), static_cast<int>(Mpad),
+      static_cast<int>(K), reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0),
+      reinterpret_cast<uint8_t*>(sf.data_ptr()), sp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// w (N, K) bf16 -> q (N, K) e4m3 bytes, sf (N/128 * K/128 * 512) bytes, scale (N/128, K/128) fp32.
+void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.stride(1) == 1, "w: 2-D bf16, unit inner stride");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(N % 128 == 0 && K % 128 == 0, "N and K must be multiples of 128");
+  TORCH_CHECK(w.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "w rows 16-byte aligned");
+  check_fp8_operand(q, "q");
+  TORCH_CHECK(q.size(0) == N && q.size(1) == K, "q shape");
+  TORCH_CHECK(sf.numel() >= N / 128 * (K / 128) * kSfChunk && sf.element_size() == 1, "sf size");
+  float* sp = nullptr;
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() &&
+                    scale->numel() == (N / 128) * (K / 128), "scale (N/128, K/128) fp32");
+    sp = scale->data_ptr<float>();
+  }
+  if (N == 0) return;
+  c10::cuda::CUDAGuard guard(w.device());
+  const dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
+  quant_blocks_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), w.stride(0), static_cast<int>(K),
+      reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), reinterpret_cast<uint8_t*>(sf.data_ptr()), sp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out (M, N) bf16 = block-scaled a (M, K) x b (N, K)^T.
+void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
+              torch::Tensor err) {
+  check_fp8_operand(a, "a");
+  check_fp8_operand(b, "b");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K, "K mismatch");
+  TORCH_CHECK(K % 128 == 0 && K > 0 && N % 128 == 0, "K and N must be multiples of 128");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(0) == M && out.size(1) == N &&
+                  out.stride(1) == 1 && (out.stride(0) * 2) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "out: (M, N) bf16, 16-byte aligned rows");
+  const int64_t mt = (M + 127) / 128;
+  TORCH_CHECK(sfa.numel() >= mt * (K / 128) * kSfChunk && sfb.numel() >= N / 128 * (K / 128) * kSfChunk,
+              "scale-factor buffers too small");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(sfa.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(sfb.data_ptr()) % 16 == 0, "scale-factor buffers 16-byte aligned");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  const CUtensorMap ma = make_map_3d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, 1, a.stride(0),
+                                     a.stride(0) * M, kF8BK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap mb = make_map_3d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, 1, b.stride(0),
+                                     b.stride(0) * N, kF8BK, kF8BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap md = make_map_3d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 1, out.stride(0) * 2,
+                                     out.stride(0) * 2 * M, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  F8Params p{};
+  p.m = static_cast<int>(M);
+  p.n = static_cast<int>(N);
+  p.k = static_cast<int>(K);
+  p.tiles_n = static_cast<int>(N / kF8BN);
+  p.total = static_cast<int>(mt * p.tiles_n);
+  p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
+  p.err = err.data_ptr<int>();
+  const int grid = std::min(p.total, sm_count(a.get_device()));
+  cudaFuncSetAttribute(gemm_mxf8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kF8SmemTotal);
+  gemm_mxf8_kernel<<<grid, 192, kF8SmemTotal, at::cuda::getCurrentCUDAStream()>>>(ma, mb, md, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t fp8_sf_bytes(int64_t rows, int64_t k) { return (rows + 127) / 128 * (k / 128) * kSfChunk; }
+
+}  // namespace sv4

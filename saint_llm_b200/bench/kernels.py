@@ -6,13 +6,15 @@
     python -m saint_llm_b200.bench.kernels rmsnorm --rows 4096 --dim 2048
     python -m saint_llm_b200.bench.kernels mhc --tokens 4096 --dim 2048 --hc 4
     python -m saint_llm_b200.bench.kernels indexer --t 4096 --index-heads 64 --index-dim 128 --index-m 4
+    python -m saint_llm_b200.bench.kernels fp8 --m 16384 --n 2048 --k 2048
 
 Timing: CUDA events on the launching stream around ``--iters`` launches after
 ``--warmup`` launches, with an L2 flush (a write larger than the 126 MB L2) before every
 timed launch, excluded from the timing.  Achieved rates are algorithmic FLOPs or bytes over
 the measured time, reported as a fraction of the peaks in ``MEASURED_PEAKS.json`` at the
 repository root ("of measured") or of a fixed fallback (6.65 TB/s, 1.59 PFLOP/s) when the
-file is absent.  ``--launches N`` runs N launches and exits (for profiler captures).
+file is absent.  FP8 tensor work is reported against twice the measured bf16 rate (the
+dense FP8 rate of the part is twice its bf16 rate).  ``--launches N`` runs N launches and exits (for profiler captures).
 """
 
 from __future__ import annotations
@@ -57,8 +59,11 @@ def timeit(fn: Callable[[], object], *, warmup: int, iters: int) -> float:
     return times[len(times) // 2]
 
 
-def report(name: str, ms: float, *, flops: float = 0.0, bytes_: float = 0.0) -> dict:
+def report(name: str, ms: float, *, flops: float = 0.0, bytes_: float = 0.0, peak_mult: float = 1.0) -> dict:
     hbm, tf, tag = peaks()
+    tf *= peak_mult
+    if peak_mult != 1.0:
+        tag = f"{tag} x{peak_mult:g}"
     out = {"kernel": name, "ms": round(ms, 4)}
     if flops:
         out["tflops"] = round(flops / ms / 1e9, 1)
@@ -91,6 +96,33 @@ def bench_gemm(args: argparse.Namespace) -> None:
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     _run(args, f"gemm_bf16 {m}x{n}x{k}", lambda: gemm.gemm_nt(a, b, out=out),
          flops=2.0 * m * n * k, bytes_=2.0 * (m * k + n * k + m * n))
+
+
+def bench_fp8(args: argparse.Namespace) -> None:
+    """Block-scaled FP8: activation / weight quantisation and the tcgen05 block-scaled GEMM,
+    with the bf16 GEMM of the same shape for comparison."""
+    from saint_llm_b200.ops import fp8, gemm
+
+    m, n, k = args.m, args.n, args.k
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    a, b = fp8.quantize_rows(x), fp8.quantize_blocks(w)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    err = gemm.error_word(torch.device("cuda"))
+    ext = __import__("saint_llm_b200.ops.backend", fromlist=["ext"]).ext()
+    if args.launches:
+        _run(args, "gemm_fp8", lambda: ext.gemm_fp8(a.q, a.sf, b.q, b.sf, out, err))
+        return
+    _run(args, f"fp8_quant_rows {m}x{k}", lambda: ext.fp8_quant_rows(x, a.q, a.sf, a.scale),
+         bytes_=2.0 * m * k + m * k + 4.0 * m * k / 128)
+    _run(args, f"fp8_quant_blocks {n}x{k}", lambda: ext.fp8_quant_blocks(w, b.q, b.sf, b.scale),
+         bytes_=2.0 * n * k + n * k)
+    _run(args, f"gemm_fp8 {m}x{n}x{k}", lambda: ext.gemm_fp8(a.q, a.sf, b.q, b.sf, out, err),
+         flops=2.0 * m * n * k, bytes_=1.0 * (m * k + n * k) + 2.0 * m * n, peak_mult=2.0)
+    xb = x.clone()
+    _run(args, f"gemm_bf16 {m}x{n}x{k}", lambda: gemm.gemm_nt(xb, w, out=out),
+         flops=2.0 * m * n * k, bytes_=2.0 * (m * k + n * k + m * n))
+    gemm.check_errors(torch.device("cuda"))
 
 
 def bench_attention(args: argparse.Namespace) -> None:
@@ -213,7 +245,7 @@ def bench_indexer(args: argparse.Namespace) -> None:
 
 def main(argv: list[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["gemm", "attention", "moe", "rmsnorm", "mhc", "indexer"])
+    ap.add_argument("kernel", choices=["gemm", "attention", "moe", "rmsnorm", "mhc", "indexer", "fp8"])
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--launches", type=int, default=0, help="run N launches and exit (profiler captures)")
@@ -238,7 +270,7 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--index-m", type=int, default=4)
     args = ap.parse_args(argv)
     {"gemm": bench_gemm, "attention": bench_attention, "moe": bench_moe, "rmsnorm": bench_rmsnorm,
-     "mhc": bench_mhc, "indexer": bench_indexer}[args.kernel](args)
+     "mhc": bench_mhc, "indexer": bench_indexer, "fp8": bench_fp8}[args.kernel](args)
 
 
 if __name__ == "__main__":

@@ -7,8 +7,9 @@ no bf16 rounding of gradients across micro-batches and no extra add kernel.  Wit
 ``main_grad`` the gradient is returned to autograd in the parameter's dtype.
 
 ``fp8_linear`` applies the block-scaled FP8 recipe (1x128 activation / 128x128 weight
-blocks, power-of-two scales): operands are quantised and dequantised with that
-blocking and the product runs on the bf16 tensor-core GEMM.
+blocks, power-of-two scales): both operands are quantised by native kernels and the
+product runs on the block-scaled FP8 tensor-core GEMM (``ops.fp8``); the backward is the
+straight-through estimator in bf16, as in the reference (``kernels/fp8_gemm.py:71-83``).
 """
 
 from __future__ import annotations
@@ -16,8 +17,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-from saint_llm_b200.ops import gemm
-from saint_llm_b200.ops.quant import dequantize_fp8_blocks, dequantize_fp8_rows, quantize_fp8_blocks, quantize_fp8_rows
+from saint_llm_b200.ops import fp8, gemm
 
 
 def _bf16(t: Tensor) -> Tensor:
@@ -76,10 +76,7 @@ class _Fp8LinearFn(torch.autograd.Function):
     def forward(ctx, x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:  # type: ignore[override]
         k = x.shape[-1]
         x2 = x.reshape(-1, k)
-        xq, xs = quantize_fp8_rows(x2)
-        wq, ws = quantize_fp8_blocks(weight)
-        y = gemm.gemm_nt(dequantize_fp8_rows(xq, xs).to(torch.bfloat16),
-                         dequantize_fp8_blocks(wq, ws).to(torch.bfloat16))
+        y = fp8.gemm(fp8.quantize_rows(x2), fp8.quantize_blocks(weight))
         if bias is not None:
             y = y + bias.to(y.dtype)
         ctx.save_for_backward(_bf16(x2), weight)

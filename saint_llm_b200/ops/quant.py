@@ -123,8 +123,12 @@ E4M3_MAX = 448.0
 
 def pow2_scale(amax: Tensor, fmax: float = E4M3_MAX) -> Tensor:
     """Smallest power of two s with amax / s <= fmax (amax == 0 -> 1)."""
-    raw = torch.where(amax > 0, amax / fmax, torch.ones_like(amax))
-    return torch.exp2(torch.ceil(torch.log2(raw)))
+    raw = torch.where(amax > 0, amax.float() / fmax, torch.ones_like(amax, dtype=torch.float32))
+    # exact ceil(log2(raw)) from the binary exponent (log2 rounding can land on an integer
+    # just below the true value): raw = m * 2^e, m in [0.5, 1)
+    m, e = torch.frexp(raw)
+    e = torch.where(m == 0.5, e - 1, e).clamp(-126, 126)
+    return torch.ldexp(torch.ones_like(raw), e)
 
 
 def quantize_fp8_rows(x: Tensor, block: int = 128) -> tuple[Tensor, Tensor]:

@@ -1,0 +1,96 @@
+"""Block-scaled FP8: native quantisation kernels vs the PyTorch oracle (identical bytes and
+scales) and the tcgen05 block-scaled GEMM vs a plain fp32 product of the dequantised
+operands."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _operand(rows, k, device, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(rows, k, generator=g)
+    # row and column-block magnitudes spread over many binades exercise every scale
+    x = x * torch.exp2(torch.randint(-12, 12, (rows, 1), generator=g).float())
+    x = x * torch.exp2(torch.randint(-4, 4, (1, k // 128), generator=g).float()).repeat_interleave(128, 1)
+    return x.to(torch.bfloat16).to(device)
+
+
+def _sf_byte(sf, r, kb, kblocks):
+    return int(sf[(r // 128 * kblocks + kb) * 512 + 16 * (r % 32) + 4 * ((r % 128) // 32)])
+
+
+@pytest.mark.parametrize("m,k", [(300, 512), (128, 128), (1, 256), (4096, 2048)])
+def test_quant_rows_matches_oracle(cuda, m, k):
+    from saint_llm_b200.ops import fp8
+
+    x = _operand(m, k, cuda, 0)
+    nat = fp8.quantize_rows(x)
+    ref = fp8._oracle_rows(x.cpu())
+    torch.cuda.synchronize()
+    assert torch.equal(nat.scale.cpu(), ref.scale)
+    assert torch.equal(nat.q.cpu(), ref.q)
+    sf = nat.sf.cpu()
+    kb_n = k // 128
+    for r in {0, m // 2, m - 1}:
+        for kb in {0, kb_n - 1}:
+            e = int(torch.log2(ref.scale[r, kb]).item())
+            assert _sf_byte(sf, r, kb, kb_n) == e + 127
+            assert len({int(v) for v in sf[(r // 128 * kb_n + kb) * 512 + 16 * (r % 32) + 4 * ((r % 128) // 32):][:4]}) == 1
+
+
+@pytest.mark.parametrize("n,k", [(128, 128), (384, 512), (2048, 2048)])
+def test_quant_blocks_matches_oracle(cuda, n, k):
+    from saint_llm_b200.ops import fp8
+
+    w = _operand(n, k, cuda, 1)
+    nat = fp8.quantize_blocks(w)
+    ref = fp8._oracle_blocks(w.cpu())
+    torch.cuda.synchronize()
+    assert torch.equal(nat.scale.cpu(), ref.scale)
+    assert torch.equal(nat.q.cpu(), ref.q)
+    sf = nat.sf.cpu()
+    kb_n = k // 128
+    e = int(torch.log2(ref.scale[-1, -1]).item())
+    assert _sf_byte(sf, n - 1, kb_n - 1, kb_n) == e + 127
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 128), (300, 384, 512), (1, 256, 256), (4096, 2048, 2048),
+                                   (1000, 1408, 2048)])
+def test_gemm_fp8_matches_fp32(cuda, m, n, k):
+    from saint_llm_b200.ops import fp8, gemm
+
+    a = fp8.quantize_rows(_operand(m, k, cuda, 2))
+    b = fp8.quantize_blocks(_operand(n, k, cuda, 3))
+    out = fp8.gemm(a, b)
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    ref = a.dequantize() @ b.dequantize().t()
+    err = (out.float() - ref).abs()
+    # bf16 output rounding: relative to each row's magnitude
+    row_scale = ref.abs().amax(1, keepdim=True) + 1e-30
+    assert (err / row_scale).max().item() < 1e-2
+    assert torch.isfinite(out).all()
+
+
+def test_fp8_linear_forward_and_ste_backward(cuda):
+    from saint_llm_b200.ops import fp8
+    from saint_llm_b200.ops.linear import fp8_linear, linear
+
+    torch.manual_seed(4)
+    x = (torch.randn(2, 200, 512, device=cuda) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(384, 512, device=cuda) * 0.05).to(torch.bfloat16).requires_grad_(True)
+    y = fp8_linear(x, w)
+    ref = fp8.quantize_rows(x.detach().reshape(-1, 512)).dequantize() @ fp8.quantize_blocks(w.detach()).dequantize().t()
+    assert (y.float().reshape(-1, 384) - ref).abs().max().item() < 1e-2 * ref.abs().max().item()
+    # quantisation error of the whole recipe against the exact bf16 product stays small
+    exact = x.detach().float().reshape(-1, 512) @ w.detach().float().t()
+    assert (y.float().reshape(-1, 384) - exact).norm().item() < 0.08 * exact.norm().item()
+    g = torch.randn_like(y)
+    y.backward(g)
+    x2 = x.detach().clone().requires_grad_(True)
+    w2 = w.detach().clone().requires_grad_(True)
+    linear(x2, w2).backward(g)
+    assert torch.allclose(x.grad.float(), x2.grad.float(), atol=1e-2, rtol=1e-2)
+    assert torch.allclose(w.grad.float(), w2.grad.float(), atol=1e-2, rtol=1e-2)

@@ -11,22 +11,26 @@
 // no per-block promotion runs on the CUDA cores.
 //
 // Scale-factor layout (produced by the quantisation kernels, consumed by the GEMM): for an
-// operand of R rows (padded to a multiple of 128) and K columns, chunk (rb, kb) covers rows
-// [128 rb, 128 rb + 128) and columns [128 kb, 128 kb + 128) and is 512 contiguous bytes at
-// ((rb * K/128) + kb) * 512.  Row r of the chunk owns the 32-bit word at byte
-// 16 * (r % 32) + 4 * (r / 32); its four bytes are the scales of the four 32-wide K steps (all
-// equal here, since a block spans 128 columns).  That is the shape tcgen05.cp 32x128b.warpx4
-// copies into tensor memory: smem row r % 32 (16 bytes) lands in lane r % 32 of every lane
-// quarter, word j in column j, which is where the MMA looks for the scale of row r % 32 + 32 j.
+// operand of R rows (padded to a multiple of 128) and K columns, chunk (rb, kg) covers rows
+// [128 rb, 128 rb + 128) and the four 128-column K blocks 4 kg .. 4 kg + 3; it is 512
+// contiguous bytes at ((rb * KG) + kg) * 512 with KG = ceil(K / 512).  Row r of the chunk owns
+// the 32-bit word at byte 16 * (r % 32) + 4 * (r / 32), whose byte j is the scale of K block
+// 4 kg + j.  That is the shape tcgen05.cp 32x128b.warpx4 copies into tensor memory: smem row
+// r % 32 (16 bytes) lands in lane r % 32 of every lane quarter, word i in column i, which is
+// where the MMA looks for the scales of row r % 32 + 32 i; the instruction descriptor's
+// scale-factor id picks byte j for the MMAs of K block 4 kg + j.  One copy per 512 columns of
+// K keeps tcgen05.cp off the MMA stream's critical path.
 //
 // GEMM roles (one CTA per SM, persistent over 128 x 128 output tiles):
 //   warp 0     : producer -- TMA loads of the A and B k-blocks (128 x 128 bytes each, 128B
-//                swizzle) and bulk copies of the two 512-byte scale chunks into a 5-deep ring;
-//   warp 1     : MMA issuer -- tcgen05.cp of the stage's scale chunks into tensor memory, then
-//                four M=128, N=128, K=32 block-scaled MMAs into one of two accumulators;
+//                swizzle) into a 6-deep ring, plus bulk copies of the two 512-byte scale chunks
+//                with the first k-block of every group of four;
+//   warp 1     : MMA issuer -- tcgen05.cp of a group's scale chunks into tensor memory, then
+//                four M=128, N=128, K=32 block-scaled MMAs per k-block into one of two
+//                accumulators;
 //   warps 2..5 : epilogue -- tcgen05.ld, bf16 pack, TMA stores through swizzled staging.
-// Tensor memory: accumulators in columns [0, 256), scale factors of stage s in columns
-// 256 + 8 s (A) and 256 + 8 s + 4 (B).
+// Tensor memory: accumulators in columns [0, 256), scale factors in two alternating slots at
+// columns 256 + 8 s (A) and 256 + 8 s + 4 (B).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_fp8.h>
@@ -45,18 +49,18 @@ namespace {
 constexpr float kE4M3Max = 448.0f;
 constexpr int kF8BN = 128;
 constexpr int kF8BK = 128;  // elements = bytes = one 128B swizzle row
-constexpr int kF8Stages = 5;
+constexpr int kF8Stages = 6;
 constexpr int kF8ABytes = kBM * kF8BK;
 constexpr int kF8BBytes = kF8BN * kF8BK;
 constexpr int kF8StageBytes = kF8ABytes + kF8BBytes;
 constexpr int kSfChunk = 512;
 constexpr int kF8SfOffset = kF8Stages * kF8StageBytes;
 constexpr int kF8EpiOffset = kF8SfOffset + kF8Stages * 2 * kSfChunk;
-constexpr int kF8BarOffset = kF8EpiOffset + 4 * kEpiBufs * kEpiStageBytes;
+constexpr int kF8BarOffset = kF8EpiOffset + 4 * kEpiStageBytes;  // one staging buffer per epilogue warp
 constexpr int kF8SmemTotal = kF8BarOffset + 256 + 1024;
 constexpr int kF8SfTmemCol = 2 * kF8BN;
 constexpr uint32_t kF8TmemCols = 512;
-static_assert(kF8SfTmemCol + 8 * kF8Stages <= static_cast<int>(kF8TmemCols), "tensor memory budget");
+static_assert(kF8SfTmemCol + 16 <= static_cast<int>(kF8TmemCols), "tensor memory budget");
 static_assert(kF8SmemTotal <= 232448, "shared memory budget");
 
 // Exponent e of the smallest power of two with amax / 2^e <= 448 (amax == 0 -> 0): the
@@ -94,8 +98,11 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* v) {
   }
 }
 
-__device__ __forceinline__ int64_t sf_word_offset(int64_t rb, int64_t kb, int64_t kblocks, int r) {
-  return (rb * kblocks + kb) * kSfChunk + 16 * (r & 31) + 4 * (r >> 5);
+__host__ __device__ __forceinline__ int64_t sf_groups(int64_t k) { return (k / 128 + 3) / 4; }
+
+// Byte holding the scale of row r (of its 128-row block rb) for K block kb.
+__device__ __forceinline__ int64_t sf_byte_offset(int64_t rb, int64_t kb, int64_t kgroups, int r) {
+  return (rb * kgroups + kb / 4) * kSfChunk + 16 * (r & 31) + 4 * (r >> 5) + (kb & 3);
 }
 
 // 1 x 128 activation quantisation: one 16-lane group per block, 8 elements per lane.  Rows in
@@ -125,8 +132,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
   const int e = pow2_exponent(amax);
   if (live) *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v, exp2_int(-e));
   if (active && sub == 0) {
-    const uint32_t byte = static_cast<uint32_t>(e + 127);
-    *reinterpret_cast<uint32_t*>(sf + sf_word_offset(row / 128, kb, kblocks, row & 127)) = byte * 0x01010101u;
+    sf[sf_byte_offset(row / 128, kb, sf_groups(K), row & 127)] = static_cast<uint8_t>(e + 127);
     if (live && scale != nullptr) scale[static_cast<int64_t>(row) * kblocks + kb] = exp2_int(e);
   }
 }
@@ -162,11 +168,7 @@ __global__ void __launch_bounds__(256) quant_blocks_kernel(const __nv_bfloat16* 
     const int64_t row = static_cast<int64_t>(nb) * 128 + r0 + 16 * i;
     *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v[i], inv);
   }
-  if (threadIdx.x < 128) {
-    const uint32_t byte = static_cast<uint32_t>(e + 127);
-    *reinterpret_cast<uint32_t*>(sf + (static_cast<int64_t>(nb) * kblocks + kb) * kSfChunk + 4 * threadIdx.x) =
-        byte * 0x01010101u;
-  }
+  if (threadIdx.x < 128) sf[sf_byte_offset(nb, kb, sf_groups(K), threadIdx.x)] = static_cast<uint8_t>(e + 127);
   if (threadIdx.x == 0 && scale != nullptr) scale[static_cast<int64_t>(nb) * kblocks + kb] = exp2_int(e);
 }
 
@@ -212,6 +214,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kblocks = P.k / kF8BK;
+  const int kgroups = static_cast<int>(sf_groups(P.k));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kF8Stages; ++s) {
@@ -249,12 +252,15 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           if (!mbar_wait(&empty[stage], phase ^ 1, P.err, kErrTimeoutEmpty)) { ok = false; break; }
           uint8_t* sa = smem + stage * kF8StageBytes;
           uint8_t* sfs = smem + kF8SfOffset + stage * 2 * kSfChunk;
-          mbar_arrive_expect_tx(&full[stage], kF8StageBytes + 2 * kSfChunk);
+          const bool group_start = (kb & 3) == 0;
+          mbar_arrive_expect_tx(&full[stage], kF8StageBytes + (group_start ? 2 * kSfChunk : 0));
           tma_load_3d(sa, &map_a, &full[stage], kb * kF8BK, mt * kBM, 0);
           tma_load_3d(sa + kF8ABytes, &map_b, &full[stage], kb * kF8BK, nt * kF8BN, 0);
-          bulk_load(sfs, P.sfa + (static_cast<int64_t>(mt) * kblocks + kb) * kSfChunk, kSfChunk, &full[stage]);
-          bulk_load(sfs + kSfChunk, P.sfb + (static_cast<int64_t>(nt) * kblocks + kb) * kSfChunk, kSfChunk,
-                    &full[stage]);
+          if (group_start) {
+            bulk_load(sfs, P.sfa + (static_cast<int64_t>(mt) * kgroups + kb / 4) * kSfChunk, kSfChunk, &full[stage]);
+            bulk_load(sfs + kSfChunk, P.sfb + (static_cast<int64_t>(nt) * kgroups + kb / 4) * kSfChunk, kSfChunk,
+                      &full[stage]);
+          }
           if (++stage == kF8Stages) { stage = 0; phase ^= 1; }
         }
       }
@@ -265,6 +271,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t slot = 1;
       bool ok = true;
       for (int t = blockIdx.x; t < P.total && ok; t += gridDim.x) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, P.err, kErrTimeoutAccum)) break;
@@ -275,17 +282,26 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * kF8StageBytes);
           const uint32_t sb = sa + kF8ABytes;
-          const uint32_t sfs = smem_u32(smem + kF8SfOffset + stage * 2 * kSfChunk);
-          const uint32_t t_sfa = tmem_base + kF8SfTmemCol + 8 * stage;
-          const uint32_t t_sfb = t_sfa + 4;
-          // no-swizzle K-major core matrices of 8 rows x 16 bytes, 128 bytes apart
-          tmem_cp_sf(t_sfa, make_smem_desc(sfs, 128, 128, 0));
-          tmem_cp_sf(t_sfb, make_smem_desc(sfs + kSfChunk, 128, 128, 0));
+          if ((kb & 3) == 0) {
+            // a new group of four K blocks: its scales go to the other tensor-memory slot (the
+            // MMAs still reading the previous slot were issued earlier and execute in order)
+            slot ^= 1u;
+            const uint32_t sfs = smem_u32(smem + kF8SfOffset + stage * 2 * kSfChunk);
+            const uint32_t t_sf = tmem_base + kF8SfTmemCol + 8 * slot;
+            // no-swizzle K-major core matrices of 8 rows x 16 bytes, 128 bytes apart
+            tmem_cp_sf(t_sf, make_smem_desc(sfs, 128, 128, 0));
+            tmem_cp_sf(t_sf + 4, make_smem_desc(sfs + kSfChunk, 128, 128, 0));
+          }
+          // scale-factor byte j of each word: in the descriptor ids and the address's top bits
+          const uint32_t j = static_cast<uint32_t>(kb & 3);
+          const uint32_t idesc = kIdesc | (j << 29) | (j << 4);
+          const uint32_t t_sfa = (tmem_base + kF8SfTmemCol + 8 * slot) | (j << 30);
+          const uint32_t t_sfb = (tmem_base + kF8SfTmemCol + 8 * slot + 4) | (j << 30);
 #pragma unroll
           for (int kk = 0; kk < kF8BK / 32; ++kk) {
             const uint64_t da = make_smem_desc(sa + kk * 32, 16, 1024, 2);
             const uint64_t db = make_smem_desc(sb + kk * 32, 16, 1024, 2);
-            mma_mxf8(d_tmem, da, db, kIdesc, t_sfa, t_sfb, (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_mxf8(d_tmem, da, db, idesc, t_sfa, t_sfb, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == kF8Stages) { stage = 0; phase ^= 1; }
@@ -296,8 +312,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     }
   } else {
     const int quarter = warp & 3;
-    uint8_t* stg = smem + kF8EpiOffset + quarter * kEpiBufs * kEpiStageBytes;
-    int sbuf = 0, acc = 0;
+    uint8_t* stg = smem + kF8EpiOffset + quarter * kEpiStageBytes;
+    int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < P.total; t += gridDim.x) {
       const int mt = t / P.tiles_n, nt = t % P.tiles_n;
@@ -317,8 +333,18 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[h + j] = __uint_as_float(r[j]);
         }
-        stage_store(stg, sbuf, lane, [&](int q) { return pack_bf16x8(v + 8 * q); }, &map_d, false,
-                    nt * kF8BN + c, drow, 0, issue);
+        // one staging buffer per warp: wait until the previous store has read it
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        uint8_t* myrow = stg + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pack_bf16x8(v + 8 * q);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && issue) {
+          tma_store_3d(&map_d, stg, nt * kF8BN + c, drow, 0);
+          bulk_commit_group();
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -359,7 +385,7 @@ void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::opt
   check_fp8_operand(q, "q");
   TORCH_CHECK(q.size(0) == M && q.size(1) == K, "q shape");
   const int64_t Mpad = (M + 127) / 128 * 128;
-  TORCH_CHECK(sf.numel() >= Mpad / 128 * (K / 128) * kSfChunk && sf.element_size() == 1, "sf size");
+  TORCH_CHECK(sf.numel() >= Mpad / 128 * sf_groups(K) * kSfChunk && sf.element_size() == 1, "sf size");
   float* sp = nullptr;
   if (scale.has_value()) {
     TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() && scale->numel() == M * (K / 128),
@@ -384,7 +410,7 @@ void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::o
   TORCH_CHECK(w.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "w rows 16-byte aligned");
   check_fp8_operand(q, "q");
   TORCH_CHECK(q.size(0) == N && q.size(1) == K, "q shape");
-  TORCH_CHECK(sf.numel() >= N / 128 * (K / 128) * kSfChunk && sf.element_size() == 1, "sf size");
+  TORCH_CHECK(sf.numel() >= N / 128 * sf_groups(K) * kSfChunk && sf.element_size() == 1, "sf size");
   float* sp = nullptr;
   if (scale.has_value()) {
     TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() &&
@@ -413,7 +439,7 @@ void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor
                   reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
               "out: (M, N) bf16, 16-byte aligned rows");
   const int64_t mt = (M + 127) / 128;
-  TORCH_CHECK(sfa.numel() >= mt * (K / 128) * kSfChunk && sfb.numel() >= N / 128 * (K / 128) * kSfChunk,
+  TORCH_CHECK(sfa.numel() >= mt * sf_groups(K) * kSfChunk && sfb.numel() >= N / 128 * sf_groups(K) * kSfChunk,
               "scale-factor buffers too small");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(sfa.data_ptr()) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(sfb.data_ptr()) % 16 == 0, "scale-factor buffers 16-byte aligned");
@@ -440,6 +466,6 @@ void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-int64_t fp8_sf_bytes(int64_t rows, int64_t k) { return (rows + 127) / 128 * (k / 128) * kSfChunk; }
+int64_t fp8_sf_bytes(int64_t rows, int64_t k) { return (rows + 127) / 128 * sf_groups(k) * kSfChunk; }
 
 }  // namespace sv4

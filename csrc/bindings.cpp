@@ -21,6 +21,12 @@ void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::o
 void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
               torch::Tensor err);
 int64_t fp8_sf_bytes(int64_t rows, int64_t k);
+// decode_attn.cu
+void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win, torch::Tensor pos,
+                      c10::optional<torch::Tensor> sink_sw, double softcap, int64_t mode,
+                      c10::optional<torch::Tensor> comp, c10::optional<torch::Tensor> norm_w, double eps, int64_t m,
+                      c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c, double scale,
+                      torch::Tensor out);
 // optim.cu
 void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_t slice, double mu);
 void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
@@ -124,6 +130,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quant_rows", &sv4::fp8_quant_rows);
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);
+  m.def("decode_attention", &sv4::decode_attention);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
   m.def("muon_momentum", &sv4::muon_momentum);
   m.def("muon_normalize", &sv4::muon_normalize);

@@ -1,0 +1,360 @@
+// Single-token decode attention over the heterogeneous cache, one kernel per layer.
+//
+// For every sequence b and query head h (one query token, MQA: one K/V head):
+//
+//   out[b, h] = SW(b, h) + C(b, h)
+//   SW : softmax over the sliding-window ring (W slots; slot j is live iff its age
+//        (pos % W - j) mod W is <= pos), scores softcapped, plus an optional per-head sink
+//        logit in the denominator;
+//   C  : softmax over compressed entries with K = V = RMSNorm(entry) (weight w, eps):
+//        mode 1 (HCA): entries 0..n-1, entry s visible iff s*m + m - 1 < pos, optional sink;
+//        mode 2 (CSA): the entries listed in top[b, :] (-1 = none), no sink.
+//   A branch with no visible key and no sink contributes zero.
+//
+// This is the decode step of the reference's cached attention (core/attention/swa.py,
+// hca.py and csa.py with kv_cache; the scores follow common.py's scaled_dot_product and
+// softmax_with_sink) with every mask, gather, normalisation and both softmaxes in one
+// pass: the eager composition is ~40 small launches per layer, which made a CUDA-graph
+// decode step launch-bound.
+//
+// Layout: one CTA per (b, group of 4 heads), 128 threads.  Scores: thread t owns keys
+// t, t + 128, ... and computes the 4 heads' dot products from its own key row (the
+// queries, pre-multiplied by the norm weight for C, are broadcast from shared memory).
+// Softmax: warp h reduces head h.  Output: thread t owns dimension t and streams the value
+// rows (coalesced 256-byte rows) against the 4 heads' probabilities.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cuda_bf16.h>
+
+namespace sv4 {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kHeads = 4;  // heads per CTA
+constexpr int kThreads = 128;
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;      // (B, H, kD)
+  const __nv_bfloat16* kw;     // (B, W, kD)
+  const __nv_bfloat16* vw;     // (B, W, kD)
+  const int64_t* pos;          // device scalar
+  const float* sink_sw;        // (H) or null
+  const __nv_bfloat16* comp;   // (B, n, kD) raw entries or null
+  const float* norm_w;         // (kD)
+  const int64_t* top;          // (B, ktop) or null
+  const float* sink_c;         // (H) or null
+  __nv_bfloat16* out;          // (B, H, kD)
+  int H, W, n, m, ktop, mode;
+  float scale, softcap, eps;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// One attention branch over L keys whose key and value are the same normalised row
+// (K = V = w * x * rsqrt(mean(x^2) + eps), w folded into the queries by the caller); adds
+// (p @ x * rsqrt) / denominator into acc[4] for dimension t.  key_row(j) returns the raw
+// row or null when key j is not visible.
+template <bool NORM, typename RowFn>
+__device__ void branch(const float (*qs)[kD], float4* s, float* rs, float* red, int L, RowFn key_row,
+                       const float* sink, int h0, float scale, float softcap, float eps, float* acc) {
+  const int t = threadIdx.x, warp = t / 32, lane = t % 32;
+  // scores
+  for (int j = t; j < L; j += kThreads) {
+    const __nv_bfloat16* row = key_row(j);
+    float4 sc = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (row != nullptr) {
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f, ss = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < kD; c += 8) {
+        float x[8];
+        load8(row + c, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          d0 = fmaf(qs[0][c + e], x[e], d0);
+          d1 = fmaf(qs[1][c + e], x[e], d1);
+          d2 = fmaf(qs[2][c + e], x[e], d2);
+          d3 = fmaf(qs[3][c + e], x[e], d3);
+          if (NORM) ss = fmaf(x[e], x[e], ss);
+        }
+      }
+      float r = scale;
+      if (NORM) {
+        const float rn = rsqrtf(ss / kD + eps);
+        rs[j] = rn;
+        r *= rn;
+      }
+      sc = make_float4(d0 * r, d1 * r, d2 * r, d3 * r);
+      if (softcap > 0.f) {
+        sc.x = softcap * tanhf(sc.x / softcap);
+        sc.y = softcap * tanhf(sc.y / softcap);
+        sc.z = softcap * tanhf(sc.z / softcap);
+        sc.w = softcap * tanhf(sc.w / softcap);
+      }
+    } else if (NORM) {
+      rs[j] = 0.f;
+    }
+    s[j] = sc;
+  }
+  __syncthreads();
+  // softmax of head h0 + warp; probabilities overwrite the scores, 1 / denominator in red[warp]
+  {
+    float* sh = reinterpret_cast<float*>(s) + warp;
+    const float sk = sink != nullptr ? sink[h0 + warp] : -INFINITY;
+    float mx = sk;
+    for (int j = lane; j < L; j += 32) mx = fmaxf(mx, sh[4 * j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    if (mx == -INFINITY) {
+      for (int j = lane; j < L; j += 32) sh[4 * j] = 0.f;
+    } else {
+      for (int j = lane; j < L; j += 32) {
+        const float p = __expf(sh[4 * j] - mx);
+        sh[4 * j] = p;
+        sum += p;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      const float den = sum + (sink != nullptr && mx != -INFINITY ? __expf(sk - mx) : 0.f);
+      red[warp] = den > 0.f ? 1.0f / den : 0.f;
+    }
+  }
+  __syncthreads();
+  // p @ V for dimension t
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll 4
+  for (int j = 0; j < L; ++j) {
+    float4 p = s[j];
+    if (NORM) {
+      const float rn = rs[j];
+      p.x *= rn; p.y *= rn; p.z *= rn; p.w *= rn;
+    }
+    if (p.x == 0.f && p.y == 0.f && p.z == 0.f && p.w == 0.f) continue;  // also skips invisible rows
+    const __nv_bfloat16* row = key_row(j);
+    const float v = __bfloat162float(row[t]);
+    o0 = fmaf(p.x, v, o0);
+    o1 = fmaf(p.y, v, o1);
+    o2 = fmaf(p.z, v, o2);
+    o3 = fmaf(p.w, v, o3);
+  }
+  // (for NORM the value rows still lack the norm weight: the caller applies it)
+  acc[0] += o0 * red[0];
+  acc[1] += o1 * red[1];
+  acc[2] += o2 * red[2];
+  acc[3] += o3 * red[3];
+  __syncthreads();  // scores / probabilities are reused by the next branch
+}
+
+__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(16) float dsm[];
+  __shared__ float qs[kHeads][kD];
+  __shared__ float red[kHeads];
+  float4* s = reinterpret_cast<float4*>(dsm);
+  const int lmax = max(a.W, a.mode == 2 ? a.ktop : a.n);
+  float* rs = dsm + 4 * lmax;
+  const int b = blockIdx.x, h0 = blockIdx.y * kHeads, t = threadIdx.x;
+  const int64_t pos = *a.pos;
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) qs[h][t] = __bfloat162float(a.q[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t]);
+  __syncthreads();
+  float acc[kHeads] = {0.f, 0.f, 0.f, 0.f};
+
+  // sliding-window ring
+  const int slot = static_cast<int>(pos % a.W);
+  const __nv_bfloat16* kb = a.kw + static_cast<int64_t>(b) * a.W * kD;
+  const __nv_bfloat16* vb = a.vw + static_cast<int64_t>(b) * a.W * kD;
+  {
+    // keys and values are different rows: score with K, then accumulate with V
+    const int W = a.W;
+    auto krow = [&](int j) -> const __nv_bfloat16* {
+      const int age = ((slot - j) % W + W) % W;
+      return age <= pos ? kb + static_cast<int64_t>(j) * kD : nullptr;
+    };
+    // scores over K
+    for (int j = t; j < W; j += kThreads) {
+      const __nv_bfloat16* row = krow(j);
+      float4 sc = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (row != nullptr) {
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < kD; c += 8) {
+          float x[8];
+          load8(row + c, x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            d0 = fmaf(qs[0][c + e], x[e], d0);
+            d1 = fmaf(qs[1][c + e], x[e], d1);
+            d2 = fmaf(qs[2][c + e], x[e], d2);
+            d3 = fmaf(qs[3][c + e], x[e], d3);
+          }
+        }
+        sc = make_float4(d0 * a.scale, d1 * a.scale, d2 * a.scale, d3 * a.scale);
+        if (a.softcap > 0.f) {
+          sc.x = a.softcap * tanhf(sc.x / a.softcap);
+          sc.y = a.softcap * tanhf(sc.y / a.softcap);
+          sc.z = a.softcap * tanhf(sc.z / a.softcap);
+          sc.w = a.softcap * tanhf(sc.w / a.softcap);
+        }
+      }
+      s[j] = sc;
+    }
+  }
+  __syncthreads();
+  {
+    const int warp = t / 32, lane = t % 32;
+    float* sh = reinterpret_cast<float*>(s) + warp;
+    const float sk = a.sink_sw != nullptr ? a.sink_sw[h0 + warp] : -INFINITY;
+    float mx = sk;
+    for (int j = lane; j < a.W; j += 32) mx = fmaxf(mx, sh[4 * j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < a.W; j += 32) {
+      const float p = mx == -INFINITY ? 0.f : __expf(sh[4 * j] - mx);
+      sh[4 * j] = p;
+      sum += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      const float den = sum + (a.sink_sw != nullptr && mx != -INFINITY ? __expf(sk - mx) : 0.f);
+      red[warp] = den > 0.f ? 1.0f / den : 0.f;
+    }
+  }
+  __syncthreads();
+  {
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < a.W; ++j) {
+      const float4 p = s[j];
+      if (p.x == 0.f && p.y == 0.f && p.z == 0.f && p.w == 0.f) continue;
+      const float v = __bfloat162float(vb[static_cast<int64_t>(j) * kD + t]);
+      o0 = fmaf(p.x, v, o0);
+      o1 = fmaf(p.y, v, o1);
+      o2 = fmaf(p.z, v, o2);
+      o3 = fmaf(p.w, v, o3);
+    }
+    acc[0] = o0 * red[0];
+    acc[1] = o1 * red[1];
+    acc[2] = o2 * red[2];
+    acc[3] = o3 * red[3];
+  }
+  __syncthreads();
+
+  if (a.mode != 0) {
+    // compressed branch: queries pre-multiplied by the norm weight (K = V = w * x * rsqrt)
+    const float w_t = a.norm_w[t];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) qs[h][t] *= w_t;
+    __syncthreads();
+    const __nv_bfloat16* cb = a.comp + static_cast<int64_t>(b) * a.n * kD;
+    float cacc[kHeads] = {0.f, 0.f, 0.f, 0.f};
+    if (a.mode == 1) {
+      const int64_t m = a.m;
+      auto row = [&](int j) -> const __nv_bfloat16* {
+        return static_cast<int64_t>(j) * m + m - 1 < pos ? cb + static_cast<int64_t>(j) * kD : nullptr;
+      };
+      branch<true>(qs, s, rs, red, a.n, row, a.sink_c, h0, a.scale, 0.f, a.eps, cacc);
+    } else {
+      const int64_t* tb = a.top + static_cast<int64_t>(b) * a.ktop;
+      const int n = a.n;
+      auto row = [&](int j) -> const __nv_bfloat16* {
+        const int64_t e = tb[j];
+        return (e >= 0 && e < n) ? cb + e * kD : nullptr;
+      };
+      branch<true>(qs, s, rs, red, a.ktop, row, nullptr, h0, a.scale, 0.f, a.eps, cacc);
+    }
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) acc[h] += cacc[h] * w_t;
+  }
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h)
+    a.out[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t] = __float2bfloat16(acc[h]);
+}
+
+const __nv_bfloat16* bf16_ptr(const torch::Tensor& t) {
+  return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
+}
+
+}  // namespace
+
+// q (B, H, 128); k_win / v_win (B, W, 128); pos int64 scalar; out (B, H, 128).
+// mode 0: window only; 1: + prefix-visible compressed entries (HCA); 2: + listed entries (CSA).
+void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win, torch::Tensor pos,
+                      c10::optional<torch::Tensor> sink_sw, double softcap, int64_t mode,
+                      c10::optional<torch::Tensor> comp, c10::optional<torch::Tensor> norm_w, double eps, int64_t m,
+                      c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c, double scale,
+                      torch::Tensor out) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3 && q.size(2) == kD,
+              "q: contiguous (B, H, 128) bf16");
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(H % kHeads == 0, "heads must be a multiple of 4");
+  TORCH_CHECK(k_win.is_contiguous() && v_win.is_contiguous() && k_win.scalar_type() == at::kBFloat16 &&
+                  v_win.scalar_type() == at::kBFloat16 && k_win.size(0) == B && k_win.size(2) == kD &&
+                  v_win.sizes() == k_win.sizes(), "window K/V: contiguous (B, W, 128) bf16");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.numel() == 1, "pos: int64 scalar");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == q.numel(), "out");
+  DecodeArgs a{};
+  a.q = bf16_ptr(q);
+  a.kw = bf16_ptr(k_win);
+  a.vw = bf16_ptr(v_win);
+  a.pos = pos.data_ptr<int64_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.H = static_cast<int>(H);
+  a.W = static_cast<int>(k_win.size(1));
+  a.scale = static_cast<float>(scale);
+  a.softcap = static_cast<float>(softcap);
+  a.eps = static_cast<float>(eps);
+  a.mode = static_cast<int>(mode);
+  if (sink_sw.has_value()) {
+    TORCH_CHECK(sink_sw->scalar_type() == at::kFloat && sink_sw->numel() == H && sink_sw->is_contiguous(), "sink");
+    a.sink_sw = sink_sw->data_ptr<float>();
+  }
+  if (mode != 0) {
+    TORCH_CHECK(comp.has_value() && norm_w.has_value(), "compressed entries and norm weight required");
+    TORCH_CHECK(comp->is_contiguous() && comp->scalar_type() == at::kBFloat16 && comp->size(0) == B &&
+                    comp->size(2) == kD, "entries: contiguous (B, n, 128) bf16");
+    TORCH_CHECK(norm_w->scalar_type() == at::kFloat && norm_w->numel() == kD && norm_w->is_contiguous(), "norm w");
+    a.comp = bf16_ptr(*comp);
+    a.n = static_cast<int>(comp->size(1));
+    a.norm_w = norm_w->data_ptr<float>();
+    a.m = static_cast<int>(m);
+    if (sink_c.has_value()) {
+      TORCH_CHECK(sink_c->scalar_type() == at::kFloat && sink_c->numel() == H && sink_c->is_contiguous(), "sink");
+      a.sink_c = sink_c->data_ptr<float>();
+    }
+    if (mode == 2) {
+      TORCH_CHECK(top.has_value() && top->scalar_type() == at::kLong && top->is_contiguous() && top->size(0) == B,
+                  "top: contiguous (B, k) int64");
+      a.top = top->data_ptr<int64_t>();
+      a.ktop = static_cast<int>(top->numel() / B);
+    } else {
+      TORCH_CHECK(m > 0, "compression rate");
+    }
+  }
+  if (B == 0) return;
+  const int lmax = std::max(a.W, mode == 2 ? a.ktop : a.n);
+  const size_t smem = static_cast<size_t>(lmax) * 5 * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "too many keys for one CTA");
+  c10::cuda::CUDAGuard guard(q.device());
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  decode_attn_kernel<<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(H / kHeads)), kThreads, smem,
+                       at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace sv4

@@ -32,6 +32,8 @@ from saint_llm_b200.infer.kv_cache import CompressedKVLayer, KVCacheBundle
 from saint_llm_b200.models.attention import CSA, HCA, SWAttention
 from saint_llm_b200.models.attention.common import rope_tables, scaled_dot_product
 from saint_llm_b200.models.mhc import MHC
+from saint_llm_b200.ops import backend
+from saint_llm_b200.ops import decode as decode_ops
 
 
 class _Ring:
@@ -78,10 +80,58 @@ class _LayerState:
         if isinstance(attn, CSA):
             mi = attn.indexer.compressor.m
             self.idx = _Ring(attn.indexer.compressor, b, (max_len + mi - 1) // mi, dev, dt)
+        # fp32 copies of the sink logits and the entry-norm weight for the native kernel
+        # (inference weights are fixed while a decoder lives)
+        sink = getattr(attn, "sink_logit", None)
+        self.sink = None if sink is None else sink.detach().float().contiguous()
+        norm = getattr(attn, "k_norm", None)
+        self.norm_w = None if norm is None else norm.weight.detach().float().contiguous()
 
 
 def _attend_layer(st: _LayerState, h: Tensor, pos: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
-    """Decode attention of one layer for h (B, 1, D) at device position ``pos``."""
+    """Decode attention of one layer for h (B, 1, D) at device position ``pos``: one native
+    kernel on CUDA (``ops.decode``), the eager composition otherwise."""
+    a = st.attn
+    cfg = a.attn_cfg
+    if not (backend.native_for(h) and decode_ops.supported(cfg.head_dim, cfg.query_heads)):
+        return _attend_layer_eager(st, h, pos, cos, sin)
+    q = a._queries(h, cos, sin)
+    k, v = a._sw_kv(h, cos, sin)
+    slot = (pos % st.W).view(1)
+    st.k.index_copy_(1, slot, k.to(st.k.dtype))
+    st.v.index_copy_(1, slot, v.to(st.v.dtype))
+    kw = {"sink": st.sink, "softcap": cfg.logit_softcap}
+    if st.kv is not None:
+        st.kv.push(h, pos)
+        kw.update(entries=st.kv.entries, norm_weight=st.norm_w, norm_eps=a.k_norm.eps, m=st.kv.m)
+        if isinstance(a, HCA):
+            kw.update(mode=1, comp_sink=st.sink)
+        else:
+            assert st.idx is not None
+            st.idx.push(h, pos)
+            kw.update(mode=2, top=_indexer_topk(a, st, h, pos))
+    return a.output(decode_ops.decode_attention(q, st.k, st.v, pos, **kw))
+
+
+def _indexer_topk(a: nn.Module, st: _LayerState, h: Tensor, pos: Tensor) -> Tensor:
+    """CSA lightning-indexer picks of the visible blocks (B, 1, k); -1 = none."""
+    assert st.idx is not None
+    idx = a.indexer
+    n = st.idx.entries.shape[1]
+    m = st.kv.m if st.kv is not None else st.idx.m
+    visible = (torch.arange(n, device=h.device) * m + (m - 1) < pos).view(1, n)
+    bq = h.shape[0]
+    qi = idx.w_iuq(idx.w_dq(h)).view(bq, 1, idx.n_heads, idx.c_indexer)
+    w = idx.w_w(h)
+    head = torch.einsum("bthc,bnc->bthn", qi, st.idx.entries.to(qi.dtype)).clamp(min=0.0)
+    s = (w.unsqueeze(-1) * head).sum(dim=-2)
+    s = s.masked_fill(~visible.view(1, 1, n), float("-inf"))
+    vals, top = s.topk(min(idx.top_k, n), dim=-1)
+    return torch.where(torch.isfinite(vals), top, torch.full_like(top, -1))
+
+
+def _attend_layer_eager(st: _LayerState, h: Tensor, pos: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
+    """The same step as ``_attend_layer`` in plain PyTorch (the oracle)."""
     a = st.attn
     cfg = a.attn_cfg
     q = a._queries(h, cos, sin)
@@ -107,16 +157,7 @@ def _attend_layer(st: _LayerState, h: Tensor, pos: Tensor, cos: Tensor, sin: Ten
         else:
             assert st.idx is not None
             st.idx.push(h, pos)
-            idx = a.indexer
-            bq = h.shape[0]
-            qi = idx.w_iuq(idx.w_dq(h)).view(bq, 1, idx.n_heads, idx.c_indexer)
-            w = idx.w_w(h)
-            head = torch.einsum("bthc,bnc->bthn", qi, st.idx.entries.to(qi.dtype)).clamp(min=0.0)
-            s = (w.unsqueeze(-1) * head).sum(dim=-2)
-            s = s.masked_fill(~visible.view(1, 1, n), float("-inf"))
-            vals, top = s.topk(min(idx.top_k, n), dim=-1)
-            top = torch.where(torch.isfinite(vals), top, torch.full_like(top, -1))
-            out = out + a.sparse_branch(q, st.kv.entries, top)
+            out = out + a.sparse_branch(q, st.kv.entries, _indexer_topk(a, st, h, pos))
     return a.output(out)
 
 

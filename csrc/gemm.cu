@@ -264,15 +264,25 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   }
   int tiles = batch * ((M + 127) / 128) * ((N + 255) / 256);
   if (tiles == 0) return;
+  const int sms = num_sms(a.get_device());
+  // Skinny bf16 products (decode: a few dozen token rows against a whole weight matrix) are
+  // weight-bandwidth bound but cover only N / 256 tiles: split K over the idle SMs into an fp32
+  // workspace (reduce-add epilogue) and round once at the end.
+  if (!symmetric && batch == 1 && epi == kEpiBF16 && M <= 256 && tiles * 4 <= sms && K >= 512) {
+    auto ws = at::empty({M, N}, out.options().dtype(at::kFloat));
+    gemm(a, b, ws, a_mn, b_mn, false, alpha, err, false);
+    out.copy_(ws);
+    return;
+  }
   CUtensorMap md = ma;
   p.tma_d = map_d_for(out.data_ptr(), epi != kEpiBF16, N, M, batch, s.d_ld, s.d_bstride, md) ? 1 : 0;
-  const int sms = num_sms(a.get_device());
   p.splitk = 1;
   p.kc = static_cast<int>(K);
   // Few output tiles and a long K (weight gradients of small layers, skinny projections):
   // split K across SMs; every slice reduce-adds its partial tile into the fp32 output.
-  if (!symmetric && batch == 1 && epi != kEpiBF16 && p.tma_d && tiles * 2 <= sms && K >= 1024) {
-    int S = static_cast<int>(std::min<int64_t>(sms / tiles, K / 512));
+  const bool skinny = M <= 256;  // weight-streaming: slices down to 128 columns of K
+  if (!symmetric && batch == 1 && epi != kEpiBF16 && p.tma_d && tiles * 2 <= sms && K >= (skinny ? 512 : 1024)) {
+    int S = static_cast<int>(std::min<int64_t>(sms / tiles, K / (skinny ? 128 : 512)));
     if (S > 1) {
       const int64_t kc = ((K + S - 1) / S + 63) / 64 * 64;
       S = static_cast<int>((K + kc - 1) / kc);

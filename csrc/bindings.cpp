@@ -21,6 +21,9 @@ void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::o
 void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
               torch::Tensor err);
 int64_t fp8_sf_bytes(int64_t rows, int64_t k);
+void grouped_gemm_fp8(int64_t mode, torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb,
+                      torch::Tensor out, c10::optional<torch::Tensor> pre, torch::Tensor probs, torch::Tensor total,
+                      int64_t n_probs, int64_t b_rows, double gmax, double lo, double hi, torch::Tensor err);
 // decode_attn.cu
 void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win, torch::Tensor pos,
                       c10::optional<torch::Tensor> sink_sw, double softcap, int64_t mode,
@@ -132,6 +135,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
+  m.def("grouped_gemm_fp8", &sv4::grouped_gemm_fp8);
   m.def("muon_momentum", &sv4::muon_momentum);
   m.def("muon_normalize", &sv4::muon_normalize);
   m.def("muon_apply", &sv4::muon_apply);

@@ -526,60 +526,81 @@ void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, 
 // (int32, E) describe each expert's row segment in the padded permuted buffer.
 __global__ void build_moe_problems_kernel(const int* seg_start, const int* seg_rows, int n_experts, int mode,
                                           int D, int I, int bn_out, GemmProblem* probs, int* total) {
-  // one thread: n_experts is small (<= a few hundred)
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int tiles = 0;
-  int np = 0;
-  for (int e = 0; e < n_experts; ++e) {
-    const int rows = seg_rows[e];
-    const int start = seg_start[e];
-    const int reps = (mode == 4) ? 2 : 1;  // wgrad of gate/up: two problems per expert
-    for (int r = 0; r < reps; ++r) {
-      GemmProblem pr{};
-      pr.batch = 1;
-      if (mode == 0) {         // SwiGLU fprop: m = rows, n = I, k = D
-        pr.m = rows; pr.n = I; pr.k = D;
-        pr.a_m = start; pr.a_k = 0; pr.a_b = 0;
-        pr.b_n = 0; pr.b_k = 0; pr.b_b = e;
-        pr.d_off = static_cast<long long>(start) * I; pr.d_ld = I;
-        pr.aux_off = static_cast<long long>(start) * 2 * I; pr.aux_ld = 2 * I;
-      } else if (mode == 1) {  // down fprop: m = rows, n = D, k = I
-        pr.m = rows; pr.n = D; pr.k = I;
-        pr.a_m = start; pr.b_b = e;
-        pr.d_off = static_cast<long long>(start) * D; pr.d_ld = D;
-        pr.aux_off = start;
-      } else if (mode == 2) {  // down dgrad: m = rows, n = I, k = D
-        pr.m = rows; pr.n = I; pr.k = D;
-        pr.a_m = start; pr.b_b = e;
-        pr.d_off = static_cast<long long>(start) * I; pr.d_ld = I;
-      } else if (mode == 3) {  // gate/up dgrad: m = rows, n = D, k = 2I
-        pr.m = rows; pr.n = D; pr.k = 2 * I;
-        pr.a_m = start; pr.b_b = e;
-        pr.d_off = static_cast<long long>(start) * D; pr.d_ld = D;
-      } else if (mode == 4) {  // gate/up wgrad: dW_{g|u}[e] (I x D) = dpre[:, r*I:(r+1)*I]^T x
-        pr.m = I; pr.n = D; pr.k = rows;
-        pr.a_m = r * I; pr.a_k = start; pr.b_n = 0; pr.b_k = start;
-        pr.d_off = (static_cast<long long>(r) * n_experts + e) * static_cast<long long>(I) * D; pr.d_ld = D;
-      } else {                 // mode 5: down wgrad: dWd[e] (D x I) = d_out^T act
-        pr.m = D; pr.n = I; pr.k = rows;
-        pr.a_m = 0; pr.a_k = start; pr.b_n = 0; pr.b_k = start;
-        pr.d_off = static_cast<long long>(e) * D * I; pr.d_ld = I;
+  // one warp: lane l builds the problems of experts l, l + 32, ...; tile ids by a warp scan
+  const int lane = threadIdx.x;
+  const int reps = (mode == 4) ? 2 : 1;  // wgrad of gate/up: two problems per expert
+  const int base_mode = mode >= 6 ? mode - 6 : mode;  // 6 / 7: the FP8 kernel's tiles of modes 0 / 1
+  int base = 0;
+  for (int e0 = 0; e0 < n_experts; e0 += 32) {
+    const int e = e0 + lane;
+    GemmProblem pr[2];
+    int cnt[2] = {0, 0};
+    if (e < n_experts) {
+      const int rows = seg_rows[e];
+      const int start = seg_start[e];
+      for (int r = 0; r < reps; ++r) {
+        GemmProblem& q = pr[r];
+        q = GemmProblem{};
+        q.batch = 1;
+        if (base_mode == 0) {         // SwiGLU fprop: m = rows, n = I, k = D
+          q.m = rows; q.n = I; q.k = D;
+          q.a_m = start; q.b_b = e;
+          q.d_off = static_cast<long long>(start) * I; q.d_ld = I;
+          q.aux_off = static_cast<long long>(start) * 2 * I; q.aux_ld = 2 * I;
+        } else if (base_mode == 1) {  // down fprop: m = rows, n = D, k = I
+          q.m = rows; q.n = D; q.k = I;
+          q.a_m = start; q.b_b = e;
+          q.d_off = static_cast<long long>(start) * D; q.d_ld = D;
+          q.aux_off = start;
+        } else if (base_mode == 2) {  // down dgrad: m = rows, n = I, k = D
+          q.m = rows; q.n = I; q.k = D;
+          q.a_m = start; q.b_b = e;
+          q.d_off = static_cast<long long>(start) * I; q.d_ld = I;
+        } else if (base_mode == 3) {  // gate/up dgrad: m = rows, n = D, k = 2I
+          q.m = rows; q.n = D; q.k = 2 * I;
+          q.a_m = start; q.b_b = e;
+          q.d_off = static_cast<long long>(start) * D; q.d_ld = D;
+        } else if (base_mode == 4) {  // gate/up wgrad: dW_{g|u}[e] (I x D) = dpre[:, r*I:(r+1)*I]^T x
+          q.m = I; q.n = D; q.k = rows;
+          q.a_m = r * I; q.a_k = start; q.b_k = start;
+          q.d_off = (static_cast<long long>(r) * n_experts + e) * static_cast<long long>(I) * D; q.d_ld = D;
+        } else {                      // mode 5: down wgrad: dWd[e] (D x I) = d_out^T act
+          q.m = D; q.n = I; q.k = rows;
+          q.a_k = start; q.b_k = start;
+          q.d_off = static_cast<long long>(e) * D * I; q.d_ld = I;
+        }
+        const int tn = (q.n + bn_out - 1) / bn_out;
+        const int tm = (q.m + 127) / 128;
+        cnt[r] = (q.k == 0 && base_mode < 4) ? 0 : tm * tn;
       }
-      pr.tile_begin = tiles;
-      const int tn = (pr.n + bn_out - 1) / bn_out;
-      const int tm = (pr.m + 127) / 128;
-      tiles += (pr.k == 0 && mode < 4) ? 0 : tm * tn;
-      probs[np++] = pr;
     }
+    const int mine = cnt[0] + cnt[1];
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (e < n_experts) {
+      int tb = base + incl - mine;
+      for (int r = 0; r < reps; ++r) {
+        pr[r].tile_begin = tb;
+        tb += cnt[r];
+        probs[e * reps + r] = pr[r];
+      }
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
-  *total = tiles;
+  if (lane == 0) *total = base;
 }
 
 void build_moe_problems(torch::Tensor seg_start, torch::Tensor seg_rows, int64_t mode, int64_t D, int64_t I,
                         torch::Tensor probs, torch::Tensor total) {
   c10::cuda::CUDAGuard guard(seg_start.device());
   const int E = seg_start.numel();
-  const int bn_out = (mode == 0) ? 128 : 256;
+  TORCH_CHECK(mode >= 0 && mode <= 7, "problem-table mode");
+  // output columns per tile of the kernel that consumes the table
+  const int bn_out = mode == 0 ? 128 : mode == 6 ? 64 : mode == 7 ? 128 : 256;
   build_moe_problems_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       seg_start.data_ptr<int>(), seg_rows.data_ptr<int>(), E, static_cast<int>(mode), static_cast<int>(D),
       static_cast<int>(I), bn_out, reinterpret_cast<GemmProblem*>(probs.data_ptr()), total.data_ptr<int>());

@@ -194,16 +194,81 @@ __host__ __device__ constexpr uint32_t make_idesc_mxf8(int m, int n) {
 }
 
 struct F8Params {
+  // single problem: D (m x n) = A (m x k) B (n x k)^T, tiles row-major over (m / 128, n / 128)
   int m, n, k;
   int tiles_n, total;
+  // grouped (table) mode: per-expert problems of the MoE layer (rows of A in 128-aligned
+  // segments, B = experts stacked along rows, b_rows rows each)
+  const GemmProblem* probs;
+  const int* total_tiles;
+  int n_probs, b_rows;
+  int write_pre;                   // SwiGLU: also store the gate / up pre-activations
+  float gate_max, lin_lo, lin_hi;  // SwiGLU clamps
   const uint8_t* sfa;
   const uint8_t* sfb;
   int* err;
 };
 
+enum F8Epi : int { kF8EpiBF16 = 0, kF8EpiSwiGLU = 1 };
+
+// Where one output tile reads and writes.
+struct F8Tile {
+  int a_row, b_row;   // first row of the A / B tile (multiples of 128)
+  int k;              // reduction length
+  int d_row, d_col;   // first output row / column
+  int aux_row, n;     // SwiGLU: first pre-activation row; problem width (I)
+  bool store;         // rows of this tile exist in D
+};
+
+template <int EPI, bool TABLE>
+__device__ __forceinline__ bool f8_locate(const F8Params& P, int t, int& hint, F8Tile& tl) {
+  constexpr int kOut = EPI == kF8EpiSwiGLU ? kF8BN / 2 : kF8BN;  // output columns per tile
+  if (!TABLE) {
+    const int mt = t / P.tiles_n, nt = t % P.tiles_n;
+    tl.a_row = mt * kBM; tl.b_row = nt * kF8BN; tl.k = P.k;
+    tl.d_row = mt * kBM; tl.d_col = nt * kOut; tl.aux_row = tl.d_row; tl.n = P.n;
+    tl.store = true;
+    return true;
+  }
+  while (hint + 1 < P.n_probs && P.probs[hint + 1].tile_begin <= t) ++hint;
+  const GemmProblem& pr = P.probs[hint];
+  const int tn = (pr.n + kOut - 1) / kOut;
+  const int local = t - pr.tile_begin;
+  if (local < 0 || tn == 0 || local >= ((pr.m + kBM - 1) / kBM) * tn) return false;
+  const int mt = local / tn, nt = local % tn;
+  tl.a_row = pr.a_m + mt * kBM;
+  tl.b_row = pr.b_b * P.b_rows + nt * kF8BN;
+  tl.k = pr.k;
+  tl.d_row = static_cast<int>(pr.d_off / pr.d_ld) + mt * kBM;
+  tl.d_col = nt * kOut;
+  tl.aux_row = EPI == kF8EpiSwiGLU ? static_cast<int>(pr.aux_off / pr.aux_ld) + mt * kBM : tl.d_row;
+  tl.n = pr.n;
+  tl.store = true;  // whole 128-row tiles: segments are padded to 128 rows inside the buffers
+  return true;
+}
+
+// Stage 32 rows x 128 bytes (row = lane) in this warp's buffer and TMA-store them.
+template <typename Pack>
+__device__ __forceinline__ void f8_store(uint8_t* stg, int lane, Pack pack, const CUtensorMap* map, int c0, int c1,
+                                         bool issue) {
+  if (lane == 0) bulk_wait_read<0>();  // one buffer per warp: the previous store has read it
+  __syncwarp();
+  uint8_t* myrow = stg + lane * 128;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pack(q);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && issue) {
+    tma_store_3d(map, stg, c0, c1, 0);
+    bulk_commit_group();
+  }
+}
+
+template <int EPI, bool TABLE>
 __global__ void __launch_bounds__(192, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const __grid_constant__ CUtensorMap map_d, const F8Params P) {
+                 const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_aux,
+                 const F8Params P) {
   constexpr uint32_t kIdesc = make_idesc_mxf8(kBM, kF8BN);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -213,8 +278,6 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int kblocks = P.k / kF8BK;
-  const int kgroups = static_cast<int>(sf_groups(P.k));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kF8Stages; ++s) {
@@ -235,30 +298,35 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
     tma_prefetch_desc(&map_d);
+    if (EPI == kF8EpiSwiGLU) tma_prefetch_desc(&map_aux);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int total = TABLE ? *P.total_tiles : P.total;
 
   if (warp == 0) {
     if (elect_one()) {
-      int stage = 0;
+      int stage = 0, hint = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < P.total && ok; t += gridDim.x) {
-        const int mt = t / P.tiles_n, nt = t % P.tiles_n;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        F8Tile tl;
+        if (!f8_locate<EPI, TABLE>(P, t, hint, tl)) continue;
+        const int kblocks = tl.k / kF8BK;
+        const int64_t kgroups = sf_groups(tl.k);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, P.err, kErrTimeoutEmpty)) { ok = false; break; }
           uint8_t* sa = smem + stage * kF8StageBytes;
           uint8_t* sfs = smem + kF8SfOffset + stage * 2 * kSfChunk;
           const bool group_start = (kb & 3) == 0;
           mbar_arrive_expect_tx(&full[stage], kF8StageBytes + (group_start ? 2 * kSfChunk : 0));
-          tma_load_3d(sa, &map_a, &full[stage], kb * kF8BK, mt * kBM, 0);
-          tma_load_3d(sa + kF8ABytes, &map_b, &full[stage], kb * kF8BK, nt * kF8BN, 0);
+          tma_load_3d(sa, &map_a, &full[stage], kb * kF8BK, tl.a_row, 0);
+          tma_load_3d(sa + kF8ABytes, &map_b, &full[stage], kb * kF8BK, tl.b_row, 0);
           if (group_start) {
-            bulk_load(sfs, P.sfa + (static_cast<int64_t>(mt) * kgroups + kb / 4) * kSfChunk, kSfChunk, &full[stage]);
-            bulk_load(sfs + kSfChunk, P.sfb + (static_cast<int64_t>(nt) * kgroups + kb / 4) * kSfChunk, kSfChunk,
+            bulk_load(sfs, P.sfa + (tl.a_row / kBM * kgroups + kb / 4) * kSfChunk, kSfChunk, &full[stage]);
+            bulk_load(sfs + kSfChunk, P.sfb + (tl.b_row / kF8BN * kgroups + kb / 4) * kSfChunk, kSfChunk,
                       &full[stage]);
           }
           if (++stage == kF8Stages) { stage = 0; phase ^= 1; }
@@ -267,16 +335,19 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      int stage = 0;
+      int stage = 0, hint = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       uint32_t slot = 1;
       bool ok = true;
-      for (int t = blockIdx.x; t < P.total && ok; t += gridDim.x) {
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        F8Tile tl;
+        if (!f8_locate<EPI, TABLE>(P, t, hint, tl)) continue;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, P.err, kErrTimeoutAccum)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kF8BN;
+        const int kblocks = tl.k / kF8BK;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, P.err, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
@@ -313,37 +384,57 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   } else {
     const int quarter = warp & 3;
     uint8_t* stg = smem + kF8EpiOffset + quarter * kEpiStageBytes;
-    int acc = 0;
+    int acc = 0, hint = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < P.total; t += gridDim.x) {
-      const int mt = t / P.tiles_n, nt = t % P.tiles_n;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      F8Tile tl;
+      if (!f8_locate<EPI, TABLE>(P, t, hint, tl)) continue;
       if (!mbar_wait(&acc_full[acc], acc_phase, P.err, kErrTimeoutAccum)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + acc * kF8BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      const int drow = mt * kBM + quarter * 32;
-      const bool issue = drow < P.m;
-#pragma unroll 1
-      for (int c = 0; c < kF8BN; c += 64) {
-        float v[64];
+      const int drow = tl.d_row + quarter * 32;
+      const bool issue = tl.store && (TABLE || drow < P.m);
+      if constexpr (EPI == kF8EpiSwiGLU) {
+        // columns [0, 64): gate, [64, 128): up  ->  act, and the pre-activations for backward
+        float g[64], u[64];
 #pragma unroll
         for (int h = 0; h < 64; h += 32) {
           uint32_t r[32];
-          tmem_ld32(t_row + c + h, r);
+          tmem_ld32(t_row + h, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[h + j] = __uint_as_float(r[j]);
-        }
-        // one staging buffer per warp: wait until the previous store has read it
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
-        uint8_t* myrow = stg + lane * 128;
+          for (int q = 0; q < 32; ++q) g[h + q] = __uint_as_float(r[q]);
+          tmem_ld32(t_row + 64 + h, r);
+          tmem_ld_wait();
 #pragma unroll
-        for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(myrow + ((q ^ (lane & 7)) << 4)) = pack_bf16x8(v + 8 * q);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && issue) {
-          tma_store_3d(&map_d, stg, nt * kF8BN + c, drow, 0);
-          bulk_commit_group();
+          for (int q = 0; q < 32; ++q) u[h + q] = __uint_as_float(r[q]);
+        }
+        const float gmax = P.gate_max, lo = P.lin_lo, hi = P.lin_hi;
+        const int arow = tl.aux_row + quarter * 32;
+        f8_store(stg, lane, [&](int q) {
+          float a8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            a8[e] = silu_f(fminf(g[8 * q + e], gmax)) * fminf(fmaxf(u[8 * q + e], lo), hi);
+          return pack_bf16x8(a8);
+        }, &map_d, tl.d_col, drow, issue);
+        if (P.write_pre) {
+          f8_store(stg, lane, [&](int q) { return pack_bf16x8(g + 8 * q); }, &map_aux, tl.d_col, arow, issue);
+          f8_store(stg, lane, [&](int q) { return pack_bf16x8(u + 8 * q); }, &map_aux, tl.n + tl.d_col, arow, issue);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kF8BN; c += 64) {
+          float v[64];
+#pragma unroll
+          for (int h = 0; h < 64; h += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c + h, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 32; ++q) v[h + q] = __uint_as_float(r[q]);
+          }
+          f8_store(stg, lane, [&](int q) { return pack_bf16x8(v + 8 * q); }, &map_d, tl.d_col + c, drow, issue);
         }
       }
       tc_fence_before();
@@ -461,8 +552,67 @@ void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor
   p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
   p.err = err.data_ptr<int>();
   const int grid = std::min(p.total, sm_count(a.get_device()));
-  cudaFuncSetAttribute(gemm_mxf8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kF8SmemTotal);
-  gemm_mxf8_kernel<<<grid, 192, kF8SmemTotal, at::cuda::getCurrentCUDAStream()>>>(ma, mb, md, p);
+  auto kern = gemm_mxf8_kernel<kF8EpiBF16, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kF8SmemTotal);
+  kern<<<grid, 192, kF8SmemTotal, at::cuda::getCurrentCUDAStream()>>>(ma, mb, md, md, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Grouped (MoE) block-scaled FP8 GEMM over a device problem table (build_moe_problems modes
+// 6 / 7).  a: (rows, K) quantised rows, expert segments 128-aligned; b: (E * b_rows, K)
+// quantised expert weights stacked along rows.
+//   mode 0: out = act (rows, I) = SwiGLU of the tile's gate | up halves, pre (rows, 2 I) = gate | up;
+//           b rows of expert e: 64-row groups alternating gate and up (b_rows = 2 I)
+//   mode 1: out (rows, N) = a b_e^T (b_rows = N)
+void grouped_gemm_fp8(int64_t mode, torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb,
+                      torch::Tensor out, c10::optional<torch::Tensor> pre, torch::Tensor probs, torch::Tensor total,
+                      int64_t n_probs, int64_t b_rows, double gmax, double lo, double hi, torch::Tensor err) {
+  check_fp8_operand(a, "a");
+  check_fp8_operand(b, "b");
+  const int64_t M = a.size(0), K = a.size(1);
+  TORCH_CHECK(b.size(1) == K && K % 128 == 0 && K > 0, "K mismatch or K % 128");
+  TORCH_CHECK(b_rows % 128 == 0 && b.size(0) % b_rows == 0, "b_rows must be a multiple of 128 dividing b's rows");
+  TORCH_CHECK(sfa.numel() >= (M + 127) / 128 * sf_groups(K) * kSfChunk &&
+                  sfb.numel() >= b.size(0) / 128 * sf_groups(K) * kSfChunk, "scale-factor buffers too small");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.size(0) == M, "out: (rows, N) bf16");
+  c10::cuda::CUDAGuard guard(a.device());
+  const CUtensorMap ma = make_map_3d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, 1, a.stride(0),
+                                     a.stride(0) * M, kF8BK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap mb = make_map_3d(b.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, b.size(0), 1, b.stride(0),
+                                     b.stride(0) * b.size(0), kF8BK, kF8BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int64_t N = out.size(1);
+  TORCH_CHECK((N * 2) % 16 == 0, "output rows must be 16-byte multiples");
+  const CUtensorMap md = make_map_3d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, 1, N * 2, N * 2 * M,
+                                     64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap mx = md;
+  if (mode == 0) {
+    TORCH_CHECK(b_rows == 2 * N && N % 64 == 0, "SwiGLU: b_rows = 2 I, I % 64 == 0");
+    if (pre.has_value()) {
+      TORCH_CHECK(pre->scalar_type() == at::kBFloat16 && pre->is_contiguous() && pre->size(0) == M &&
+                      pre->size(1) == 2 * N, "pre: (rows, 2 I) bf16");
+      mx = make_map_3d(pre->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 2 * N, M, 1, 4 * N, 4 * N * M, 64, 32,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+  } else {
+    TORCH_CHECK(mode == 1 && b_rows == N, "mode 1: b_rows = N");
+  }
+  F8Params p{};
+  p.probs = reinterpret_cast<const GemmProblem*>(probs.data_ptr());
+  p.total_tiles = total.data_ptr<int>();
+  p.n_probs = static_cast<int>(n_probs);
+  p.b_rows = static_cast<int>(b_rows);
+  p.write_pre = pre.has_value() ? 1 : 0;
+  p.gate_max = static_cast<float>(gmax);
+  p.lin_lo = static_cast<float>(lo);
+  p.lin_hi = static_cast<float>(hi);
+  p.sfa = reinterpret_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = reinterpret_cast<const uint8_t*>(sfb.data_ptr());
+  p.err = err.data_ptr<int>();
+  if (M == 0 || n_probs == 0) return;
+  const int grid = sm_count(a.get_device());
+  auto kern = mode == 0 ? gemm_mxf8_kernel<kF8EpiSwiGLU, true> : gemm_mxf8_kernel<kF8EpiBF16, true>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kF8SmemTotal);
+  kern<<<grid, 192, kF8SmemTotal, at::cuda::getCurrentCUDAStream()>>>(ma, mb, md, mx, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -31,6 +31,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=512)
     ap.add_argument("--chunk", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="(development only) override n_layers")
+    ap.add_argument("--fp8-experts", action="store_true",
+                    help="routed experts on block-scaled FP8 weights (quantised once before the prefill)")
     ap.add_argument("--engine", choices=["graph", "cached"], default="graph",
                     help="graph: static-shape step captured in a CUDA graph; cached: the eager cached path")
     args = ap.parse_args()
@@ -54,6 +56,10 @@ def main() -> None:
         model = SaintLLM(cfg)
     cast_params(model, torch.bfloat16)
     model.eval()
+    if args.fp8_experts:
+        from saint_llm_b200.ops.moe_native import enable_fp8_experts
+
+        enable_fp8_experts(model)
     B, P, S = args.batch, args.prompt, args.steps
     ids = torch.randint(0, cfg.vocab_size, (B, P), device=dev)
     bundle = KVCacheBundle.for_model(model, max_seq_len=P + S, batch_size=B, device=dev)
@@ -96,7 +102,8 @@ def main() -> None:
     print(json.dumps({
         "bench": "decode", "metric": "decode tok/s", "value": B * S / (decode_ms / 1000.0), "unit": "tokens/s",
         "prefill_tokens_per_s": B * P / (prefill_ms / 1000.0), "decode_ms_per_step": decode_ms / S,
-        "n_gpus": 1, "dtype": "bf16", "data": "synthetic uniform-random prompts; random-init weights",
+        "n_gpus": 1, "dtype": "bf16 + fp8 routed experts" if args.fp8_experts else "bf16",
+        "data": "synthetic uniform-random prompts; random-init weights",
         "config": {"model": "config-3 architecture (d2048 L%d, 64 routed top-6)" % cfg.n_layers, "batch": B,
                    "prompt": P, "decode_steps": S, "prefill_chunk": args.chunk,
                    "kv_cache_gb": round(kv_gb, 2), "engine": args.engine,

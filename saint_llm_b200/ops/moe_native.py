@@ -281,6 +281,70 @@ def routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module) -> 
                                    float(experts.clamp_linear[1])))
 
 
+class Fp8ExpertWeights:
+    """Block-scaled FP8 copies of a grouped expert pool (inference: built once, reused).
+
+    ``gu``: gate and up weights stacked per expert as (E * 2I, D) with 64-row groups
+    alternating gate / up, so one 128-column tile of the grouped GEMM holds 64 gate and
+    the matching 64 up columns (the SwiGLU epilogue needs both); each 128 x 128 scale block
+    covers one such group pair.  ``down``: (E * D, I) in 128 x 128 blocks."""
+
+    def __init__(self, experts: nn.Module) -> None:
+        from saint_llm_b200.ops import fp8
+
+        wg, wu, wd = experts.gate_weight.detach(), experts.up_weight.detach(), experts.down_weight.detach()
+        e, i, d = wg.shape
+        if i % 64 or d % 128 or i % 128:
+            raise ValueError(f"FP8 experts need I % 128 == 0 and D % 128 == 0 (got I={i}, D={d})")
+        gu = torch.stack([wg.reshape(e, i // 64, 64, d), wu.reshape(e, i // 64, 64, d)], dim=2).reshape(e * 2 * i, d)
+        self.gu = fp8.quantize_blocks(gu.to(torch.bfloat16))
+        self.down = fp8.quantize_blocks(wd.reshape(e * d, i).to(torch.bfloat16))
+        self.E, self.I, self.D = e, i, d
+        self.clamps = (float(experts.clamp_gate_max), float(experts.clamp_linear[0]), float(experts.clamp_linear[1]))
+
+
+@torch.no_grad()
+def routed_experts_fp8(h: Tensor, idx: Tensor, gate: Tensor, w8: Fp8ExpertWeights) -> Tensor:
+    """Inference forward of the routed experts on the block-scaled FP8 grouped GEMM:
+    gathered rows and SwiGLU activations are quantised in 1 x 128 blocks on the fly."""
+    from saint_llm_b200.ops import fp8
+
+    ext = backend.ext()
+    dev = h.device
+    T, D = h.shape
+    k = idx.shape[1]
+    E, I = w8.E, w8.I
+    err = gemm.error_word(dev)
+    plan = RoutePlan(idx, E, k)
+    x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+    ext.moe_gather(_bf16c(h), plan.row_token, x_p)
+    xq = fp8.quantize_rows(x_p)
+    act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
+    pr, tot, n = plan.problems(6, D, I)
+    gmax, lo, hi = w8.clamps
+    ext.grouped_gemm_fp8(0, xq.q, xq.sf, w8.gu.q, w8.gu.sf, act, None, pr, tot, n, 2 * I, gmax, lo, hi, err)
+    aq = fp8.quantize_rows(act)
+    y = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+    pr, tot, n = plan.problems(7, D, I)
+    ext.grouped_gemm_fp8(1, aq.q, aq.sf, w8.down.q, w8.down.sf, y, None, pr, tot, n, D, 0.0, 0.0, 0.0, err)
+    out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    ext.moe_combine(y, plan.pos, gate.float().contiguous(), out)
+    return out
+
+
+def enable_fp8_experts(model: nn.Module) -> int:
+    """Quantise every grouped expert pool of ``model`` to block-scaled FP8 for inference;
+    the no-grad CUDA forward then runs the FP8 grouped GEMMs.  Returns the number of pools.
+    Call again after the weights change (the copies are not refreshed automatically)."""
+    n = 0
+    for mod in model.modules():
+        ge = getattr(mod, "grouped_experts", None)
+        if ge is not None and hasattr(ge, "gate_weight"):
+            ge._fp8_weights = Fp8ExpertWeights(ge)
+            n += 1
+    return n
+
+
 def moe_forward(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
     """CUDA forward of ``DeepSeekMoE``."""
     if getattr(layer, "ep_size", 1) > 1:
@@ -295,7 +359,11 @@ def moe_forward(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual
     layer._last_aux_loss = aux
     k = layer.cfg.experts_per_token
     h2 = h.reshape(b * t, d)
-    out = routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts)
+    w8 = getattr(layer.grouped_experts, "_fp8_weights", None)
+    if w8 is not None and not torch.is_grad_enabled():
+        out = routed_experts_fp8(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), w8)
+    else:
+        out = routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts)
     sh = shared_experts(h2, layer.shared_experts)
     if sh is not None:
         out = out + sh
@@ -324,4 +392,5 @@ def _moe_per_module(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vi
     return out.view(b, t, d)
 
 
-__all__ = ["RoutePlan", "moe_forward", "routed_experts", "shared_experts", "shared_swiglu"]
+__all__ = ["Fp8ExpertWeights", "RoutePlan", "enable_fp8_experts", "moe_forward", "routed_experts",
+           "routed_experts_fp8", "shared_experts", "shared_swiglu"]

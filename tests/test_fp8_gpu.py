@@ -95,3 +95,26 @@ def test_fp8_linear_forward_and_ste_backward(cuda):
     linear(x2, w2).backward(g)
     assert torch.allclose(x.grad.float(), x2.grad.float(), atol=1e-2, rtol=1e-2)
     assert torch.allclose(w.grad.float(), w2.grad.float(), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("used", [8, 3])
+def test_fp8_routed_experts_match_bf16(cuda, used):
+    """Grouped FP8 GEMMs (SwiGLU epilogue, then the down projection) against the bf16 grouped
+    path; ``used`` < E leaves experts without rows (no tiles)."""
+    from saint_llm_b200.ops import gemm, moe_native
+    from saint_llm_b200.ops.moe import GroupedSwiGLUExperts
+
+    torch.manual_seed(5)
+    E, D, I, T, k = 8, 256, 384, 300, 2
+    ex = GroupedSwiGLUExperts(D, I, E).to(cuda).to(torch.bfloat16)
+    h = torch.randn(T, D, device=cuda, dtype=torch.bfloat16)
+    idx = torch.stack([torch.randperm(used)[:k] for _ in range(T)]).to(cuda)
+    gate = torch.rand(T, k, device=cuda)
+    with torch.no_grad():
+        ref = moe_native.routed_experts(h, idx, gate, ex)
+        got = moe_native.routed_experts_fp8(h, idx, gate, moe_native.Fp8ExpertWeights(ex))
+    torch.cuda.synchronize()
+    gemm.check_errors(cuda)
+    assert torch.isfinite(got).all()
+    rel = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
+    assert rel < 0.08, rel

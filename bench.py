@@ -238,8 +238,9 @@ def main() -> None:
                     help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
     ap.add_argument("--no-zero", action="store_true",
                     help="N > 1: all-reduce replicated gradients and update them on every rank (no hybrid ZeRO)")
-    ap.add_argument("--ep-capacity", type=float, default=2.0,
-                    help="receive capacity per rank in units of its own (token, slot) pairs; an overflow raises")
+    ap.add_argument("--ep-capacity", type=float, default=None,
+                    help="receive capacity per rank in units of its own (token, slot) pairs (default: the group "
+                         "size, which no routing can overflow); an overflow raises")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--linear-quant", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--ckpt", action="store_true", help="activation checkpointing per block")

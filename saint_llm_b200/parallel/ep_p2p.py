@@ -18,13 +18,16 @@ and the backward pushes ``gate * dout`` to the owners (``ep_combine_bwd``), runs
 expert backward there and pulls the input gradients back (``ep_dispatch_bwd``).
 
 Buffers (all ranks allocate the same sizes collectively; mapped into every peer by CUDA
-IPC): a flag table, a two-slot count table, one receive buffer per MoE layer (kept until
-that layer's backward: it is the saved input of the expert weight gradients) and three
-shared buffers for the expert outputs, the output gradients and the input gradients.
-Capacity ``C`` rows per rank: ``min(ws, capacity_factor) * T * k`` plus 128 rows of
-padding per local expert.  With the default factor (``ws``) no routing can overflow; a
-smaller factor saves memory and an overflow is reported as a native kernel error (never
-silently dropped).
+IPC): a flag table, a two-slot count table and four buffers shared by every MoE layer --
+the receive buffer and the buffers of the expert outputs, the output gradients and the
+input gradients.  Capacity ``C`` rows per rank: ``min(ws, capacity_factor) * T * k`` plus
+128 rows of padding per local expert.  With the default factor (``ws``) no routing can
+overflow: an untrained router can send most tokens to a few ranks.  The owner reads its
+received row count once per layer (one host synchronisation) and keeps a right-sized copy of
+the received rows as the saved input of the expert weight gradients; the expert
+activations are sized the same way, so memory follows the actual routing, not the worst
+case.  A smaller factor saves the shared buffers' memory; an overflow is reported as a
+native kernel error (never silently dropped).
 
 Reuse of the shared buffers across layers is safe by stream order: a rank dispatches
 layer L+1 only after its combine of layer L, which waited for every owner's "outputs
@@ -170,8 +173,7 @@ class P2PExpertComm:
         self.epoch = [0] * 5
         self.tokens = 0
         self.C = 0
-        self.y = self.dy = self.dx = None
-        self.x: dict[int, SymmetricBuffer] = {}
+        self.y = self.dy = self.dx = self.xr = None
 
     def next_epoch(self, phase: int) -> int:
         self.epoch[phase] = (self.epoch[phase] + 1) & 0xFFFFFFFF
@@ -188,21 +190,12 @@ class P2PExpertComm:
         self.tokens = tokens
         self.C = self.capacity_for(tokens)
         row_bytes = self.C * self.D * 2
-        self.y, self.dy, self.dx = (self.heap.alloc(row_bytes) for _ in range(3))
-        self.x = {}
+        self.xr, self.y, self.dy, self.dx = (self.heap.alloc(row_bytes) for _ in range(4))
 
     def close(self) -> None:
         """Collective release of every buffer (see ``SymmetricHeap.close``)."""
-        self.y = self.dy = self.dx = None
-        self.x = {}
+        self.y = self.dy = self.dx = self.xr = None
         self.heap.close()
-
-    def x_buffer(self, layer_key: int) -> SymmetricBuffer:
-        buf = self.x.get(layer_key)
-        if buf is None:
-            buf = self.heap.alloc(self.C * self.D * 2)
-            self.x[layer_key] = buf
-        return buf
 
     def rows(self, buf: SymmetricBuffer) -> Tensor:
         return buf.view(torch.bfloat16, self.C, self.D)
@@ -260,7 +253,7 @@ class EPCall:
                     c.flags.local.view(torch.int32), self.e_cnt & 1, self.e_cnt, c.rank, c.ws, c.C, self.gpos,
                     self.seg_start, self.seg_rows, self.seg_pad, c.timeout_ns, self.err)
         del self.local
-        ext.ep_dispatch(self.hb, self.gpos, c.C, c.x_buffer(self.layer_key).ptrs)
+        ext.ep_dispatch(self.hb, self.gpos, c.C, c.xr.ptrs)
         self.e_x = c.next_epoch(PH_X)
         ext.ep_signal(c.flags.ptrs, PH_X, c.rank, self.e_x)
 
@@ -268,13 +261,18 @@ class EPCall:
         c, ext = self.comm, backend.ext()
         D, (E_loc, I, _) = self.D, self.wg.shape
         gmax, lo, hi = self.clamps
-        x_rows = c.rows(c.x[self.layer_key])
-        ext.ep_wait_zero(c.flags.local.view(torch.int32), PH_X, c.ws, self.e_x, x_rows, self.seg_start,
+        xr = c.rows(c.xr)
+        ext.ep_wait_zero(c.flags.local.view(torch.int32), PH_X, c.ws, self.e_x, xr, self.seg_start,
                          self.seg_rows, c.timeout_ns, self.err)
+        # rows this owner received (expert segments are contiguous and 128-padded): one host
+        # read per layer sizes the saved input and the activations by the actual routing
+        self.R = int((self.seg_start[-1] + self.seg_pad[-1]).item()) if E_loc else 0
+        x_rows = xr[:self.R].clone()
+        self.x_saved = x_rows
         plan = _SegPlan(self.seg_start, self.seg_pad)
         e0 = _empty(self.dev)
-        self.act = torch.empty(c.C, I, dtype=torch.bfloat16, device=self.dev)
-        self.pre = torch.empty(c.C, 2 * I, dtype=torch.bfloat16, device=self.dev)
+        self.act = torch.empty(self.R, I, dtype=torch.bfloat16, device=self.dev)
+        self.pre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=self.dev)
         pr, tot, n = plan.problems(0, D, I)
         ext.grouped_gemm(0, x_rows, _bf16c(self.wg), _bf16c(self.wu), self.act, self.pre, e0, pr, tot, n, gmax, lo,
                          hi, 0, False, self.err)
@@ -314,7 +312,7 @@ class EPCall:
         plan = _SegPlan(self.seg_start, self.seg_pad)
         e0 = _empty(dev)
         wdb = _bf16c(self.wd)
-        dact = torch.empty(c.C, I, dtype=torch.bfloat16, device=dev)
+        dact = torch.empty(self.R, I, dtype=torch.bfloat16, device=dev)
         pr, tot, n = plan.problems(2, D, I)
         ext.grouped_gemm(2, dy, wdb, wdb, dact, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
         dwd_buf = getattr(self.wd, "main_grad", None)
@@ -323,13 +321,13 @@ class EPCall:
             dwd_buf = torch.zeros(E_loc, D, I, dtype=torch.float32, device=dev)
         pr, tot, n = plan.problems(5, D, I)
         ext.grouped_gemm(4, dy, self.act, self.act, dwd_buf, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
-        dpre = torch.empty(c.C, 2 * I, dtype=torch.bfloat16, device=dev)
+        dpre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=dev)
         ext.swiglu_bwd(dact, self.pre, dpre, gmax, lo, hi)
         del self.act, self.pre, dact
         pr, tot, n = plan.problems(3, D, I)
         ext.grouped_gemm(3, dpre, _bf16c(self.wg), _bf16c(self.wu), c.rows(c.dx), e0, e0, pr, tot, n, 0.0, 0.0, 0.0,
                          I, False, err)
-        x_rows = c.rows(c.x[self.layer_key])
+        x_rows = self.x_saved
         mg_g, mg_u = getattr(self.wg, "main_grad", None), getattr(self.wu, "main_grad", None)
         if mg_g is not None and mg_u is not None and mg_u.data_ptr() == mg_g.data_ptr() + mg_g.numel() * 4:
             joint, self.acc_gu = mg_g, True
@@ -338,6 +336,7 @@ class EPCall:
         pr, tot, n = plan.problems(4, D, I)
         ext.grouped_gemm(4, dpre, x_rows, x_rows, joint, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
         self.joint, self.dwd_buf = joint, dwd_buf
+        del self.x_saved
         self.e_dx = c.next_epoch(PH_DX)
         ext.ep_signal(c.flags.ptrs, PH_DX, c.rank, self.e_dx)
 

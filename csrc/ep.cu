@@ -348,12 +348,15 @@ void ep_combine(std::vector<int64_t> y_ptrs, torch::Tensor gpos, torch::Tensor g
 __global__ void ep_combine_bwd_kernel(const uint4* __restrict__ dout, const uint4* __restrict__ ypair,
                                       const float* __restrict__ gate, const int* __restrict__ gpos, int k, int C,
                                       int vpr, PeerTable dybuf, float* __restrict__ dgate) {
+  // Loops over the k slots are unrolled to the maximum (16) with an early exit, so the
+  // per-slot arrays stay in registers and the k row loads of a chunk are issued together.
   const int t = blockIdx.x;
   int p[16];
   float g[16], dot[16];
-  for (int j = 0; j < k; ++j) {
-    p[j] = gpos[t * k + j];
-    g[j] = gate[t * k + j];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    p[j] = j < k ? gpos[t * k + j] : -1;
+    g[j] = j < k ? gate[t * k + j] : 0.f;
     dot[j] = 0.f;
   }
   for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
@@ -366,26 +369,35 @@ __global__ void ep_combine_bwd_kernel(const uint4* __restrict__ dout, const uint
       fa[2 * q] = f.x;
       fa[2 * q + 1] = f.y;
     }
-    for (int j = 0; j < k; ++j) {
-      const uint4 b = ypair[(static_cast<int64_t>(t) * k + j) * vpr + v];
-      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+    uint4 yb[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= k) break;
+      yb[j] = ypair[(static_cast<int64_t>(t) * k + j) * vpr + v];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j >= k) break;
+      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&yb[j]);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const float2 f = __bfloat1622float2(hb[q]);
         dot[j] += fa[2 * q] * f.x + fa[2 * q + 1] * f.y;
       }
       if (p[j] >= 0) {
-        float s[8];
+        float s8[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) s[q] = fa[q] * g[j];
+        for (int q = 0; q < 8; ++q) s8[q] = fa[q] * g[j];
         const int d = p[j] / C, r = p[j] - d * C;
-        reinterpret_cast<uint4*>(dybuf.p[d])[static_cast<int64_t>(r) * vpr + v] = pack_bf16x8(s);
+        reinterpret_cast<uint4*>(dybuf.p[d])[static_cast<int64_t>(r) * vpr + v] = pack_bf16x8(s8);
       }
     }
   }
   __shared__ float red[8][16];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  for (int j = 0; j < k; ++j) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j >= k) break;
     float x = dot[j];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

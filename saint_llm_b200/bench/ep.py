@@ -65,7 +65,7 @@ def main() -> None:
     dh = torch.empty_like(out)
     ypair = torch.empty(T * k, D, device=dev, dtype=torch.bfloat16)
     dgate = torch.empty(T, k, device=dev)
-    xb = comm.x_buffer(0)
+    xb = comm.xr
     x_rows, y_rows, dy_rows = comm.rows(xb), comm.rows(comm.y), comm.rows(comm.dy)
 
     # routing layout (untimed)

@@ -266,13 +266,28 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   if (tiles == 0) return;
   const int sms = num_sms(a.get_device());
   // Skinny bf16 products (decode: a few dozen token rows against a whole weight matrix) are
-  // weight-bandwidth bound but cover only N / 256 tiles: split K over the idle SMs into an fp32
-  // workspace (reduce-add epilogue) and round once at the end.
-  if (!symmetric && batch == 1 && epi == kEpiBF16 && M <= 256 && tiles * 4 <= sms && K >= 512) {
-    auto ws = at::empty({M, N}, out.options().dtype(at::kFloat));
-    gemm(a, b, ws, a_mn, b_mn, false, alpha, err, false);
-    out.copy_(ws);
-    return;
+  // weight-bandwidth bound but cover only N / 256 tiles: split K over the idle SMs.  The
+  // slices run as a batch (A and B viewed as (S, rows, K / S)) into separate fp32 partials
+  // that are summed in a fixed order, so the result is deterministic (no reduce-add races).
+  if (!symmetric && batch == 1 && !a_mn && !b_mn && M <= 256 && tiles * 4 <= sms && K >= 512 && K % 128 == 0) {
+    const int64_t kb = K / 128;
+    int64_t S = 1;
+    for (int64_t d = std::min<int64_t>(kb, sms / tiles); d >= 2; --d) {
+      if (kb % d == 0) { S = d; break; }
+    }
+    if (S > 1) {
+      const int64_t kc = K / S;
+      auto a3 = a.as_strided({S, M, kc}, {kc, a.stride(0), 1});
+      auto b3 = b.as_strided({S, N, kc}, {kc, b.stride(0), 1});
+      auto part = at::empty({S, M, N}, out.options().dtype(at::kFloat));
+      gemm(a3, b3, part, false, false, false, alpha, err, false);
+      if (epi == kEpiF32Acc) {
+        out.add_(part.sum(0));
+      } else {
+        out.copy_(part.sum(0));
+      }
+      return;
+    }
   }
   CUtensorMap md = ma;
   p.tma_d = map_d_for(out.data_ptr(), epi != kEpiBF16, N, M, batch, s.d_ld, s.d_bstride, md) ? 1 : 0;
@@ -280,9 +295,8 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   p.kc = static_cast<int>(K);
   // Few output tiles and a long K (weight gradients of small layers, skinny projections):
   // split K across SMs; every slice reduce-adds its partial tile into the fp32 output.
-  const bool skinny = M <= 256;  // weight-streaming: slices down to 128 columns of K
-  if (!symmetric && batch == 1 && epi != kEpiBF16 && p.tma_d && tiles * 2 <= sms && K >= (skinny ? 512 : 1024)) {
-    int S = static_cast<int>(std::min<int64_t>(sms / tiles, K / (skinny ? 128 : 512)));
+  if (!symmetric && batch == 1 && epi != kEpiBF16 && p.tma_d && tiles * 2 <= sms && K >= 1024) {
+    int S = static_cast<int>(std::min<int64_t>(sms / tiles, K / 512));
     if (S > 1) {
       const int64_t kc = ((K + S - 1) / S + 63) / 64 * 64;
       S = static_cast<int>((K + kc - 1) / kc);

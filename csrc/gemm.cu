@@ -211,6 +211,48 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
   TORCH_CHECK(false, "unsupported GEMM variant a_mn=", a_mn, " b_mn=", b_mn, " bmode=", bmode, " epi=", epi);
 }
 
+// out (M, N) (+)= sum_s part[s] in slice order (fp32 sums; bf16 or fp32 out, any row stride).
+__global__ void sum_partials_kernel(const float4* __restrict__ part, int S, int64_t mn4, int64_t n4, void* out,
+                                    int64_t ld, int bf16_out, int accumulate) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= mn4) return;
+  float4 acc = part[i];
+  for (int s = 1; s < S; ++s) {
+    const float4 v = part[s * mn4 + i];
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  const int64_t row = i / n4, col = (i % n4) * 4;
+  if (bf16_out) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + row * ld + col;
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(acc.x, acc.y);
+    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(acc.z, acc.w);
+  } else {
+    float* o = reinterpret_cast<float*>(out) + row * ld + col;
+    if (accumulate) {
+      o[0] += acc.x; o[1] += acc.y; o[2] += acc.z; o[3] += acc.w;
+    } else {
+      o[0] = acc.x; o[1] = acc.y; o[2] = acc.z; o[3] = acc.w;
+    }
+  }
+}
+
+static void sum_partials(const torch::Tensor& part, torch::Tensor& out, bool accumulate) {
+  const int64_t S = part.size(0), M = part.size(1), N = part.size(2);
+  const bool bf16 = out.scalar_type() == at::kBFloat16;
+  if (N % 4 != 0 || out.stride(1) != 1 || (bf16 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 3) != 0) ||
+      (out.stride(0) % 2 != 0 && bf16)) {
+    if (accumulate) out.add_(part.sum(0)); else out.copy_(part.sum(0));
+    return;
+  }
+  const int64_t mn4 = M * N / 4;
+  const int threads = 256;
+  sum_partials_kernel<<<static_cast<unsigned>((mn4 + threads - 1) / threads), threads, 0,
+                        at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const float4*>(part.data_ptr()), static_cast<int>(S), mn4, N / 4, out.data_ptr(),
+      out.stride(0), bf16 ? 1 : 0, accumulate ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // ------------------------------------------------------------------ entry points
 // Dense / batched:  out[b, m, n] (+)= alpha * sum_k A[b, m, k] B[b, n, k]
 //   a: (.., M, K) if !a_mn  else (.., K, M)      (unit inner stride, bf16)
@@ -281,11 +323,7 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
       auto b3 = b.as_strided({S, N, kc}, {kc, b.stride(0), 1});
       auto part = at::empty({S, M, N}, out.options().dtype(at::kFloat));
       gemm(a3, b3, part, false, false, false, alpha, err, false);
-      if (epi == kEpiF32Acc) {
-        out.add_(part.sum(0));
-      } else {
-        out.copy_(part.sum(0));
-      }
+      sum_partials(part, out, epi == kEpiF32Acc);
       return;
     }
   }

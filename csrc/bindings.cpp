@@ -30,6 +30,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win,
                       c10::optional<torch::Tensor> comp, c10::optional<torch::Tensor> norm_w, double eps, int64_t m,
                       c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c, double scale,
                       torch::Tensor out);
+// router.cu
+void router_fwd(torch::Tensor z, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias,
+                c10::optional<torch::Tensor> modality_bias, c10::optional<torch::Tensor> is_visual,
+                torch::Tensor aff, torch::Tensor idx, torch::Tensor gate);
 // optim.cu
 void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_t slice, double mu);
 void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
@@ -134,6 +138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);
+  m.def("router_fwd", &sv4::router_fwd);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
   m.def("grouped_gemm_fp8", &sv4::grouped_gemm_fp8);
   m.def("muon_momentum", &sv4::muon_momentum);

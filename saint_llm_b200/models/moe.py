@@ -96,6 +96,13 @@ class LearnedRouter(nn.Module):
         return torch.sigmoid(logits)
 
     def forward(self, x: Tensor, is_visual: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+        if backend.native_for(x) and self.n_routed <= 256 and self.top_k <= 16:
+            from saint_llm_b200.ops.linear import linear
+            from saint_llm_b200.ops.router import fused_route
+
+            logits = linear(x, self.score_proj.weight).float()
+            return fused_route(logits, self.top_k, self.cfg.affinity_fn, self.aux_free_bias,
+                               self.modality_bias, is_visual)
         aff = self.affinity(x)
         biased = aff + self.aux_free_bias
         if self.modality_bias is not None and is_visual is not None:

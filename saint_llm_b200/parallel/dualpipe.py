@@ -1,6 +1,7 @@
 """DualPipe-V: a V-shaped pipeline schedule (absent in the reference, which lists
-DualPipe / DualPipeV as planned in ``distributed/__init__.py:9-13``; the build plan keeps
-pipeline traffic on NCCL point-to-point, overlapped with compute).
+DualPipe / DualPipeV as planned in ``distributed/__init__.py:9-13``).  Pipeline traffic is
+NCCL (or gloo) point-to-point; the exchange of a tick runs between ticks, not yet
+overlapped with the next tick's compute.
 
 Placement.  The block stack is cut into ``2P`` virtual stages for ``P`` ranks; rank ``r``
 holds virtual stage ``r`` (chunk 0) and virtual stage ``2P-1-r`` (chunk 1).  A micro-batch

@@ -12,8 +12,9 @@ any sharding -- contiguous (rank r holds block r) or zigzag (rank r holds blocks
   gets the whole sequence for H / P heads), attention runs locally, a second all-to-all
   turns the result back.  Communication: 4 all-to-alls of the local activations.
 * ``ring_attention``: K / V shards travel around the ring (P - 1 hops); each rank merges
-  the partial softmax of every block with a running log-sum-exp, skipping blocks the mask
-  hides completely.  Communication overlaps the next block's math in the NCCL stream.
+  the partial softmax of every block with a running log-sum-exp, skipping the math of
+  blocks the mask hides completely.  Each hop completes before the next block's math (no
+  overlap yet).
 
 Both are differentiable: the all-to-all's backward is the inverse all-to-all, the ring hop's
 backward sends the gradient the opposite way.  Point-to-point exchanges use grouped

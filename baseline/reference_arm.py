@@ -11,13 +11,19 @@ B200 at all, each a public switch of the reference:
 per-expert module layout (``moe_use_grouped_gemm=False``; its Muon raises on the stacked
 3-D expert weights).  Weights stay fp32 under bf16 autocast -- the reference's own
 mixed-precision mode (``Trainer(mixed_precision="bf16")``); casting its parameters to bf16
-breaks its einsums.  fp32 weights + gradients + Muon momentum of the ~16B-parameter
-model need ~192 GB, more than one B200 holds, so at one GPU the arm reports
-``unavailable`` with that arithmetic instead of running out of memory.
+breaks its einsums.
 
 Every step accumulates gradients over the same ``seqs_per_gpu`` sequences of 4096
 tokens as the framework arm, then steps the optimizers.  Timing: CUDA events around K
 steps after W warm-up steps, barrier + synchronize on both sides, max over ranks.
+
+Time budget (``SV4_REF_BUDGET_S``, default 600 s of wall clock from the start of the arm):
+the arm first times single micro-batches (one untimed, one timed with CUDA events, max over
+ranks) and one optimizer step, extrapolates the W + K steps and runs them only if they fit
+the budget.  Otherwise -- and when the model's fp32 training state does not fit the GPUs at
+all, in which case the micro-batches are timed on the largest layer cut that fits and scaled
+linearly to the full depth -- it prints its ``unavailable`` line carrying those measured
+times and the extrapolated step time, so the record shows that the reference ran on the box.
 """
 
 from __future__ import annotations
@@ -31,19 +37,22 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(HERE, "_ref")
+METRIC = "train tokens/sec/box (max over ranks) FP8 MoE at 1/2/4/8 B200; decode tok/s"
 
 
-def _unavailable(why: str) -> dict:
-    return {"impl": "reference", "unavailable": why}
+def _unavailable(why: str, measured: dict | None = None) -> dict:
+    out: dict = {"impl": "reference", "unavailable": why}
+    if measured:
+        out["measured"] = measured
+    return out
 
 
-def _reference_config(ModelConfig, args):  # noqa: N803
+def _reference_config(ModelConfig, args, n_layers: int | None = None):  # noqa: N803
     """Config 3 expressed with the reference's own config classes (same pinned fields)."""
     from saint_llm_core.config import AttentionConfig, MoEConfig, MTPConfig, TokenizerSlots
 
-    n_layers = args.layers or 28
     return ModelConfig(
-        n_layers=n_layers, hidden_dim=2048, vocab_size=32768, first_dense_swa_layers=0,
+        n_layers=n_layers or args.layers or 28, hidden_dim=2048, vocab_size=32768, first_dense_swa_layers=0,
         attention=AttentionConfig(query_heads=16, head_dim=128),
         moe=MoEConfig(hash_routed_layers=0, shared_experts=2, routed_experts=64, experts_per_token=6,
                       expert_intermediate_dim=1408),
@@ -64,7 +73,21 @@ def run(args) -> dict:
         return _unavailable(f"reference run failed: {msg}")
 
 
+def _max_over_ranks(x: float, dev: torch.device, world: int) -> float:
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _param_count(SaintLLM, cfg) -> int:  # noqa: N803
+    with torch.device("meta"):
+        return sum(p.numel() for p in SaintLLM(cfg).parameters())
+
+
 def _run(args) -> dict:
+    t_arm = time.perf_counter()
+    budget = float(os.environ.get("SV4_REF_BUDGET_S", "600"))
     if not os.path.isdir(os.path.join(REF, "saint_llm_core")):
         return _unavailable("reference not installed in baseline/_ref (run baseline/install_reference.sh)")
     if REF not in sys.path:
@@ -79,16 +102,33 @@ def _run(args) -> dict:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800), device_id=dev)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
+    try:
+        return _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn, rank, world,
+                              dev, t_arm, budget)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn,  # noqa: N803
+                   rank, world, dev, t_arm, budget) -> dict:
     cfg = _reference_config(ModelConfig, args)
-    # parameter count from the architecture (no allocation) and the fp32 training-state footprint
-    with torch.device("meta"):
-        n_params = sum(p.numel() for p in SaintLLM(cfg).parameters())
-    need = n_params * 12 / world  # fp32 weights + grads + Muon momentum (AdamW share is small)
+    full_layers = cfg.n_layers
     have = torch.cuda.get_device_properties(dev).total_memory
-    if need > 0.95 * have:
-        return _unavailable(f"reference keeps fp32 weights, grads and Muon momentum: {n_params / 1e9:.1f}B params x "
-                            f"12 B / {world} GPU(s) = {need / 1e9:.0f} GB > {have / 1e9:.0f} GB per GPU")
+    # fp32 weights + grads + Muon momentum per GPU (the AdamW share is small)
+    n_params = _param_count(SaintLLM, cfg)
+    need = n_params * 12 / world
+    fits = need <= 0.9 * have
+    run_layers = full_layers
+    if not fits:
+        # largest layer cut whose fp32 state takes at most half the memory (activations are
+        # checkpointed per block): its micro-batch time scales linearly to the full depth
+        per_layer = (n_params - _param_count(SaintLLM, _reference_config(ModelConfig, args, 1))) / max(
+            full_layers - 1, 1)
+        base = n_params - per_layer * full_layers
+        run_layers = int(max(1, min(full_layers, (0.5 * have * world / 12 - base) // per_layer)))
+        cfg = _reference_config(ModelConfig, args, run_layers)
     torch.manual_seed(0)
     with torch.device(dev):
         model = SaintLLM(cfg)
@@ -104,28 +144,66 @@ def _run(args) -> dict:
     g = torch.Generator().manual_seed(rank)
     host = torch.randint(0, cfg.vocab_size, (n_micro, args.micro_batch, args.seq_len), generator=g).pin_memory()
 
-    def step() -> torch.Tensor:
-        total = torch.zeros((), device=dev)
-        toks = host.to(dev, non_blocking=True)
-        for i in range(n_micro):
-            with torch.autocast("cuda", dtype=torch.bfloat16):
-                loss = loss_fn(model, toks[i]).float() / n_micro
-            loss.backward()
-            total += loss.detach()
+    def micro(toks: torch.Tensor, i: int) -> torch.Tensor:
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = loss_fn(model, toks[i]).float() / n_micro
+        loss.backward()
+        return loss.detach()
+
+    def opt_step() -> None:
         muon.step()
         adamw.step()
         muon.zero_grad(set_to_none=True)
         adamw.zero_grad(set_to_none=True)
+
+    def step() -> torch.Tensor:
+        total = torch.zeros((), device=dev)
+        toks = host.to(dev, non_blocking=True)
+        for i in range(n_micro):
+            total += micro(toks, i)
+        opt_step()
         return total
 
-    budget = float(os.environ.get("SV4_REF_BUDGET_S", "1200"))
-    t0 = time.perf_counter()
+    # --- probe: one untimed micro-batch, one timed micro-batch, one timed optimizer step
+    toks = host.to(dev, non_blocking=True)
+    micro(toks, 0)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    micro(toks, min(1, n_micro - 1))
+    ev[1].record()
+    opt_step()
+    ev[2].record()
+    torch.cuda.synchronize()
+    scale = full_layers / run_layers
+    mb_ms = _max_over_ranks(ev[0].elapsed_time(ev[1]), dev, world)
+    opt_ms = _max_over_ranks(ev[1].elapsed_time(ev[2]), dev, world)
+    est_step_ms = (n_micro * mb_ms + opt_ms) * scale
+    elapsed = _max_over_ranks(time.perf_counter() - t_arm, dev, world)
+    tokens = world * args.seqs_per_gpu * args.seq_len
+    measured = {
+        "layers_run": run_layers, "layers_config": full_layers, "micro_batch_tokens": args.micro_batch * args.seq_len,
+        "micro_batch_ms": round(mb_ms, 1), "optimizer_step_ms": round(opt_ms, 1),
+        "micro_batches_per_step": n_micro, "extrapolated_step_ms": round(est_step_ms, 1),
+        "extrapolated_tokens_per_s": round(tokens / (est_step_ms / 1000.0), 1),
+        "extrapolation": "linear in layers" if scale != 1 else "micro-batches x measured micro-batch + optimizer",
+        "n_gpus": world, "parallelism": f"fsdp2 dp{world}" if world > 1 else "single-gpu",
+        "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "elapsed_s": round(elapsed, 1),
+    }
+    if not fits:
+        return _unavailable(
+            f"reference keeps fp32 weights, grads and Muon momentum: {n_params / 1e9:.1f}B params x 12 B / "
+            f"{world} GPU(s) = {need / 1e9:.0f} GB > {have / 1e9:.0f} GB per GPU; micro-batches timed on a "
+            f"{run_layers}-layer cut", measured) if rank == 0 else {}
+    remaining = (args.warmup + args.steps) * est_step_ms / 1000.0
+    if elapsed + remaining > budget:
+        return _unavailable(
+            f"reference step of {n_micro} x {args.micro_batch * args.seq_len} tokens takes ~{est_step_ms / 1000:.0f} s "
+            f"(measured micro-batch + optimizer); {args.warmup}+{args.steps} steps exceed the {budget:.0f} s budget",
+            measured) if rank == 0 else {}
+
     for _ in range(args.warmup):
         step()
-        torch.cuda.synchronize()
-        if time.perf_counter() - t0 > budget:
-            return _unavailable(f"reference step exceeds the time budget: {args.warmup} warm-up steps of "
-                                f"{n_micro} x {args.seq_len} tokens took > {budget:.0f} s")
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -137,13 +215,10 @@ def _run(args) -> dict:
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    t = torch.tensor([start.elapsed_time(end) / args.steps], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t.item())
-    tokens = world * args.seqs_per_gpu * args.seq_len
+    ms = _max_over_ranks(start.elapsed_time(end) / args.steps, dev, world)
+    final_loss = float(loss.item())
     res = {
-        "impl": "reference", "metric": "train tokens/sec/box (max over ranks) FP8 MoE at 1/2/4/8 B200; decode tok/s",
+        "impl": "reference", "metric": METRIC,
         "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16" if args.linear_quant == "bf16" else "fp8",
@@ -153,8 +228,7 @@ def _run(args) -> dict:
                    "parallelism": f"fsdp2 dp{world}" if world > 1 else "single-gpu",
                    "reference_settings": "fp32 params + bf16 autocast, activation checkpointing, "
                                          "per-expert modules",
-                   "final_loss": float(loss.item())},
+                   "final_loss": final_loss},
+        "measured": measured,
     }
-    if world > 1:
-        torch.distributed.destroy_process_group()
     return res if rank == 0 else {}

@@ -139,6 +139,25 @@ def build_ours(args, device, world):
     return cfg, model, step
 
 
+def _uniform_loss(cfg) -> float:
+    """The training loss of a model that predicts every token uniformly: ln V for the main
+    head plus the MTP heads' weighted ln V (the balance term is excluded)."""
+    import math
+
+    from saint_llm_b200.train.losses import mtp_weight
+
+    w = 1.0 + sum(mtp_weight(cfg.mtp, k) for k in range(cfg.mtp.depth))
+    return w * math.log(cfg.vocab_size)
+
+
+def _rank_mean(x: torch.Tensor, world: int) -> float:
+    t = x.detach().float().reshape(1).clone()
+    if world > 1:
+        torch.distributed.all_reduce(t)
+        t /= world
+    return float(t.item())
+
+
 def run_ours(args) -> dict:
     rank, world, local = _dist_env()
     torch.cuda.set_device(local)
@@ -148,15 +167,21 @@ def run_ours(args) -> dict:
     cfg, model, step = build_ours(args, device, world)
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.engine import SyntheticTokens
+    from saint_llm_b200.utils.profiling import PhaseRecorder
 
     n_micro = args.seqs_per_gpu // args.micro_batch
-    host = SyntheticTokens(cfg.vocab_size, args.micro_batch, args.seq_len, n_micro, seed=rank).buf
+    data = SyntheticTokens(cfg.vocab_size, args.micro_batch, args.seq_len, n_micro, seed=rank,
+                           n_batches=args.data_pool)
+    it = iter(range(1 << 30))
 
     def device_step():
-        return step.run_device(host.to(device, non_blocking=True))
+        return step.run_device(data.batch(next(it)).to(device, non_blocking=True))
 
+    first_loss = None
     for _ in range(args.warmup):
-        device_step()
+        loss = device_step()
+        if first_loss is None:
+            first_loss = _rank_mean(loss, world)
     torch.cuda.synchronize()
     check_errors(device)
     if world > 1:
@@ -169,28 +194,35 @@ def run_ours(args) -> dict:
             loss = device_step()
         end.record()
         torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    t_ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
-    if world > 1:
-        torch.distributed.all_reduce(t_ms, op=torch.distributed.ReduceOp.MAX)
-    ms = float(t_ms.item())
-    final_loss = float(loss.item())
-    check_errors(device)
+        if world > 1:
+            torch.distributed.barrier()
+        t_ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+        if world > 1:
+            torch.distributed.all_reduce(t_ms, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t_ms.item())
+        final_loss = _rank_mean(loss, world)
+        check_errors(device)
 
-    # end-to-end through the public call: host batch in, float loss out
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step(host)
-    torch.cuda.synchronize()
-    t_e = torch.tensor([(time.perf_counter() - t0) * 1000 / args.steps], device=device)
+        # end-to-end through the public call: host batch in, float loss out (same clock
+        # sampling as the device-timed loop, so both run under the same host load)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step(data.batch(next(it)))
+        torch.cuda.synchronize()
+        t_e = torch.tensor([(time.perf_counter() - t0) * 1000 / args.steps], device=device)
     if world > 1:
         torch.distributed.all_reduce(t_e, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = float(t_e.item())
 
+    # one more step with per-phase CUDA events (outside the timed regions), max over ranks
+    if world > 1:
+        torch.distributed.barrier()
+    with PhaseRecorder(device) as rec:
+        device_step()
+    phases = rec.summary()
     launches = count_native_launches(device_step) * args.steps
     tokens_per_step = world * args.seqs_per_gpu * args.seq_len
     result = {
@@ -205,11 +237,15 @@ def run_ours(args) -> dict:
                    "ep_transport": args.ep_transport if world > 1 else None,
                    "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
                    "l2": "inputs larger than L2 (the weights stream through HBM every step)",
+                   "data_pool_batches": args.data_pool,
+                   "loss": {"first_warmup": first_loss, "final": final_loss, "uniform_prediction": _uniform_loss(cfg),
+                            "note": "mean over ranks; main CE + MTP-weighted CE + balance term"},
                    "final_loss": final_loss,
+                   "phases_ms": phases,
                    "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(host.numel() * host.element_size()), "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": int(data.bytes_per_step), "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
     }
     if world > 1:
@@ -242,6 +278,8 @@ def main() -> None:
                     help="receive capacity per rank in units of its own (token, slot) pairs (default: the group "
                          "size, which no routing can overflow); an overflow raises")
     ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--data-pool", type=int, default=8,
+                    help="distinct synthetic step batches cycled through (pinned host memory)")
     ap.add_argument("--linear-quant", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--ckpt", action="store_true", help="activation checkpointing per block")
     ap.add_argument("--layers", type=int, default=0, help="(development only) override n_layers")

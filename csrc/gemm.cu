@@ -319,8 +319,10 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
     }
     if (S > 1) {
       const int64_t kc = K / S;
-      auto a3 = a.as_strided({S, M, kc}, {kc, a.stride(0), 1});
-      auto b3 = b.as_strided({S, N, kc}, {kc, b.stride(0), 1});
+      // row strides are stride(-2): a batch-1 operand may arrive as (1, rows, K), whose
+      // stride(0) is the batch stride
+      auto a3 = a.as_strided({S, M, kc}, {kc, a.stride(-2), 1});
+      auto b3 = b.as_strided({S, N, kc}, {kc, b.stride(-2), 1});
       auto part = at::empty({S, M, N}, out.options().dtype(at::kFloat));
       gemm(a3, b3, part, false, false, false, alpha, err, false);
       sum_partials(part, out, epi == kEpiF32Acc);

@@ -165,58 +165,82 @@ class Agent:
         return list(self.history)
 
 
+@dataclass
+class _Seat:
+    """One agent at the round table and the messages waiting for it."""
+
+    agent: Agent
+    waiting: list[Message] = field(default_factory=list)
+
+    def take(self) -> list[Message]:
+        got, self.waiting = self.waiting, []
+        return got
+
+
 class Runtime:
-    """Round-robin: each tick steps one agent and forwards its non-empty assistant text to the next."""
+    """Several agents taking turns (reference ``agents/runtime.py``: round-robin, each
+    agent's non-empty assistant text goes to the next agent as a user message).
+
+    The table is a ring of seats; ``tick()`` lets the agent at the current seat act on
+    everything queued for it, appends what it produced to the shared transcript and
+    passes its spoken text (assistant messages with content; tool traffic stays private)
+    to the next seat, then moves on."""
 
     def __init__(self, agents: Sequence[Agent]) -> None:
-        if len(agents) < 2:
-            raise ValueError(f"Runtime needs at least 2 agents; got {len(agents)}")
-        names = [a.name for a in agents]
-        if len(set(names)) != len(names):
-            raise ValueError(f"agent names must be unique; got {names}")
-        self._agents = list(agents)
-        self._inboxes: dict[str, list[Message]] = {n: [] for n in names}
-        self._cursor = 0
-        self._transcript: list[Message] = []
+        seats = [_Seat(a) for a in agents]
+        if len(seats) < 2:
+            raise ValueError(f"a Runtime is a conversation between agents: pass two or more (got {len(seats)})")
+        by_name: dict[str, _Seat] = {}
+        for seat in seats:
+            if seat.agent.name in by_name:
+                raise ValueError(f"two agents share the name {seat.agent.name!r}; names address the inboxes")
+            by_name[seat.agent.name] = seat
+        self._seats = seats
+        self._by_name = by_name
+        self._turn = 0
+        self._log: list[Message] = []
 
     @property
     def agents(self) -> tuple[Agent, ...]:
-        return tuple(self._agents)
+        return tuple(seat.agent for seat in self._seats)
 
     @property
     def transcript(self) -> list[Message]:
-        return list(self._transcript)
+        return list(self._log)
 
     @property
     def cursor(self) -> int:
-        return self._cursor
+        return self._turn % len(self._seats)
+
+    def _seat(self, name: str) -> _Seat:
+        try:
+            return self._by_name[name]
+        except KeyError:
+            raise KeyError(f"no agent named {name!r} at this table") from None
 
     def inbox_for(self, name: str) -> list[Message]:
-        if name not in self._inboxes:
-            raise KeyError(f"unknown agent {name!r}")
-        return list(self._inboxes[name])
+        return list(self._seat(name).waiting)
 
     def send(self, *, to: str, content: str, sender: str = "user") -> None:
-        if to not in self._inboxes:
-            raise KeyError(f"unknown agent {to!r}")
-        m = Message(role="user", content=content, name=sender)
-        self._inboxes[to].append(m)
-        self._transcript.append(m)
+        """Queue an outside message for agent ``to`` (it is also logged)."""
+        msg = Message(role="user", content=content, name=sender)
+        self._seat(to).waiting.append(msg)
+        self._log.append(msg)
 
     def tick(self) -> list[Message]:
-        agent = self._agents[self._cursor]
-        inbox, self._inboxes[agent.name] = self._inboxes[agent.name], []
-        produced = agent.step(inbox)
-        self._transcript.extend(produced)
-        nxt = self._agents[(self._cursor + 1) % len(self._agents)].name
-        self._inboxes[nxt].extend(Message(role="user", content=m.content, name=agent.name)
-                                  for m in produced if m.role == "assistant" and m.content)
-        self._cursor = (self._cursor + 1) % len(self._agents)
+        n = len(self._seats)
+        seat, nxt = self._seats[self._turn % n], self._seats[(self._turn + 1) % n]
+        produced = seat.agent.step(seat.take())
+        self._log += produced
+        spoken = [m.content for m in produced if m.role == "assistant" and m.content]
+        nxt.waiting += [Message(role="user", content=text, name=seat.agent.name) for text in spoken]
+        self._turn = (self._turn + 1) % n
         return produced
 
     def run(self, *, max_ticks: int = 20) -> list[Message]:
-        if max_ticks <= 0:
-            raise ValueError(f"max_ticks must be positive; got {max_ticks}")
+        """Exactly ``max_ticks`` turns; returns the transcript."""
+        if max_ticks < 1:
+            raise ValueError(f"max_ticks={max_ticks}: run needs at least one turn")
         for _ in range(max_ticks):
             self.tick()
         return self.transcript

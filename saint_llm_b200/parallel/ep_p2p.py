@@ -47,6 +47,7 @@ from torch import Tensor, nn
 
 from saint_llm_b200.ops import backend, gemm
 from saint_llm_b200.ops.moe_native import RoutePlan, _bf16c, _empty, _prob_table
+from saint_llm_b200.utils.profiling import phase as _phase
 
 PH_CNT, PH_X, PH_Y, PH_DY, PH_DX = 0, 1, 2, 3, 4
 MAX_RANKS = 8
@@ -359,18 +360,24 @@ class _P2PExpertsFn(torch.autograd.Function):
     def forward(ctx, h: Tensor, idx: Tensor, gate: Tensor, wg: Tensor, wu: Tensor, wd: Tensor,  # type: ignore[override]
                 comm: P2PExpertComm, layer_key: int, clamps: tuple[float, float, float]) -> Tensor:
         call = EPCall(comm, layer_key, h, idx, gate, wg, wu, wd, clamps)
-        call.f1_counts()
-        call.f2_dispatch()
-        call.f3_experts()
+        with _phase("ep.dispatch"):
+            call.f1_counts()
+            call.f2_dispatch()
+        with _phase("ep.experts_fwd"):
+            call.f3_experts()
         ctx.call = call
-        return call.f4_combine()
+        with _phase("ep.combine"):
+            return call.f4_combine()
 
     @staticmethod
     def backward(ctx, dout: Tensor):  # type: ignore[override]
         call: EPCall = ctx.call
-        call.b1_push(dout)
-        call.b2_experts()
-        dh, dgate, dwg, dwu, dwd = call.b3_pull()
+        with _phase("ep.combine_bwd"):
+            call.b1_push(dout)
+        with _phase("ep.experts_bwd"):
+            call.b2_experts()
+        with _phase("ep.dispatch_bwd"):
+            dh, dgate, dwg, dwu, dwd = call.b3_pull()
         del ctx.call
         return dh, None, dgate, dwg, dwu, dwd, None, None, None
 

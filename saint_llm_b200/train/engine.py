@@ -68,15 +68,24 @@ def grad_of(p: Tensor) -> Tensor | None:
 class SyntheticTokens:
     """Uniform-random token batches generated on the host into pinned memory.
 
-    Every step's batch is copied host->device inside the timed region, like a data
-    loader feeding the GPU.
+    ``n_batches`` distinct step batches (each ``(n_micro, micro_batch, seq_len)``) are
+    drawn up front; ``batch(i)`` cycles through them, so consecutive steps train on
+    different tokens (a single repeated batch would be memorised, and its loss would fall
+    faster the fewer sequences a job trains on).  Every step's batch is copied
+    host->device inside the timed region, like a data loader feeding the GPU.
     """
 
-    def __init__(self, vocab: int, micro_batch: int, seq_len: int, n_micro: int, seed: int = 0) -> None:
+    def __init__(self, vocab: int, micro_batch: int, seq_len: int, n_micro: int, seed: int = 0,
+                 n_batches: int = 1) -> None:
         g = torch.Generator().manual_seed(seed)
-        buf = torch.randint(0, vocab, (n_micro, micro_batch, seq_len), generator=g, dtype=torch.int64)
-        self.buf = buf.pin_memory() if torch.cuda.is_available() else buf
+        bufs = torch.randint(0, vocab, (n_batches, n_micro, micro_batch, seq_len), generator=g, dtype=torch.int64)
+        self.bufs = bufs.pin_memory() if torch.cuda.is_available() else bufs
+        self.buf = self.bufs[0]
         self.n_micro = n_micro
+        self.n_batches = n_batches
+
+    def batch(self, i: int) -> Tensor:
+        return self.bufs[i % self.n_batches]
 
     def __iter__(self) -> Iterator[Tensor]:
         yield from self.buf

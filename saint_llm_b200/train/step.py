@@ -16,6 +16,7 @@ import torch
 from torch import Tensor, nn
 
 from saint_llm_b200.train.engine import zero_main_grads
+from saint_llm_b200.utils.profiling import phase
 from saint_llm_b200.train.losses import make_loss_fn
 
 
@@ -37,15 +38,20 @@ class TrainStep:
         self.model.train()
         total = torch.zeros((), dtype=torch.float32, device=self.device)
         for i in range(self.micro_batches):
-            loss = self.loss_fn(self.model, tokens[i]) / self.micro_batches
-            loss.backward()
+            with phase("forward"):
+                loss = self.loss_fn(self.model, tokens[i]) / self.micro_batches
+            with phase("backward"):
+                loss.backward()
             total += loss.detach()
         if self.grad_sync is not None:
-            self.grad_sync(self.params)
-        self.optimizer.step()
+            with phase("grad_sync"):
+                self.grad_sync(self.params)
+        with phase("optimizer"):
+            self.optimizer.step()
         post = getattr(self.grad_sync, "post_step", None)
         if post is not None:
-            post()
+            with phase("param_sync"):
+                post()
         zero_main_grads(self.params)
         return total
 

@@ -6,6 +6,10 @@
   attention / MoE module, through module hooks;
 * ``DeviceTimer``: CUDA-event timing on the launching stream, synchronised on both sides,
   reported as the max over the ranks of a process group;
+* ``PhaseRecorder``: named CUDA-event spans on the current stream (forward, backward,
+  each expert-parallel stage, gradient sync, optimizer ...) summed per name and reported
+  as the max over ranks; recording happens only while a recorder is active, so the
+  instrumented code paths cost one global lookup otherwise;
 * ``mfu``: model FLOP utilisation of a training step against a peak.
 """
 
@@ -81,9 +85,64 @@ class DeviceTimer:
         self.ms = float(t.item())
 
 
+class PhaseRecorder:
+    """Per-phase device time of one (or a few) training steps.
+
+    ``with PhaseRecorder(device) as rec: step()`` then ``rec.summary(group)`` returns
+    ``{phase: ms}`` summed over every span of that phase, max over the ranks of ``group``.
+    Instrumented code calls ``phase("name")`` (a context manager); spans of the same name
+    add up, spans may nest (an outer "backward" contains the inner expert-parallel stages).
+    Every rank must record the same phase names for the max-reduction to line up; the
+    summary handles missing names by reducing over the sorted union gathered on the host."""
+
+    _active: PhaseRecorder | None = None
+
+    def __init__(self, device: torch.device | None = None) -> None:
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.spans: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    def __enter__(self) -> PhaseRecorder:
+        PhaseRecorder._active = self
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        PhaseRecorder._active = None
+
+    def summary(self, group: dist.ProcessGroup | None = None) -> dict[str, float]:
+        torch.cuda.synchronize(self.device)
+        tot: dict[str, float] = {}
+        for name, a, b in self.spans:
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+        if dist.is_available() and dist.is_initialized():
+            names: list = [None] * dist.get_world_size(group)
+            dist.all_gather_object(names, sorted(tot), group=group)
+            keys = sorted(set().union(*map(set, names)))
+            t = torch.tensor([tot.get(k, 0.0) for k in keys], dtype=torch.float64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            tot = dict(zip(keys, t.tolist(), strict=True))
+        return {k: round(v, 3) for k, v in sorted(tot.items())}
+
+
+@contextlib.contextmanager
+def phase(name: str) -> Iterator[None]:
+    """A named span on the current CUDA stream while a ``PhaseRecorder`` is active."""
+    rec = PhaseRecorder._active
+    if rec is None:
+        yield
+        return
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    try:
+        yield
+    finally:
+        b.record()
+        rec.spans.append((name, a, b))
+
+
 def mfu(tokens_per_s: float, active_params: float, peak_flops: float, *, attn_flops_per_token: float = 0.0) -> float:
     """6 N (+ attention) FLOPs per trained token over the peak (both per GPU or both per job)."""
     return tokens_per_s * (6.0 * active_params + attn_flops_per_token) / peak_flops
 
 
-__all__ = ["DeviceTimer", "annotate_blocks", "mfu", "nvtx_enabled", "nvtx_range"]
+__all__ = ["DeviceTimer", "PhaseRecorder", "annotate_blocks", "mfu", "nvtx_enabled", "nvtx_range", "phase"]

@@ -70,6 +70,40 @@ def test_gemm_split_k_skinny(cuda, m, n, k, accumulate):
     _close(out, want, 1e-3)
 
 
+@pytest.mark.parametrize("out_dtype,accumulate", [(torch.bfloat16, False), (torch.float32, False),
+                                                   (torch.float32, True)])
+@pytest.mark.parametrize("m,n,k", [(24, 8192, 4096), (64, 2048, 1024), (256, 512, 512)])
+@pytest.mark.parametrize("batch1", [False, True])
+def test_gemm_skinny_k_major_fixed_order(cuda, m, n, k, out_dtype, accumulate, batch1):
+    """Skinny K-major products (decode projections): K slices into separate fp32 partials
+    summed in a fixed order.  Checked against fp32, bit-identical across two calls, and
+    the same when the operands arrive as (1, rows, K) batch-1 views."""
+    from saint_llm_b200.ops import gemm
+
+    torch.manual_seed(4)
+    a = torch.randn(m, k, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(n, k, device=cuda, dtype=torch.bfloat16)
+    base = torch.randn(m, n, device=cuda, dtype=torch.float32)
+    want = _ref(a, b) + (base if accumulate else 0)
+    if batch1:
+        a, b = a.unsqueeze(0), b.unsqueeze(0)
+
+    def run():
+        shape = (1, m, n) if batch1 else (m, n)
+        if accumulate:
+            out = base.clone().reshape(shape)
+            gemm.gemm_nt(a, b, out=out, accumulate=True)
+        else:
+            out = gemm.gemm_nt(a, b, out_dtype=out_dtype)
+        torch.cuda.synchronize()
+        gemm.check_errors(cuda)
+        return out.reshape(m, n)
+
+    o1, o2 = run(), run()
+    _close(o1, want, 1e-3 if out_dtype == torch.float32 else 2e-2)
+    assert torch.equal(o1, o2), "split-K partial sum is not deterministic"
+
+
 def test_gemm_bf16_output_view_with_row_stride(cuda):
     """bf16 output written through a TMA map into a column slice of a wider buffer."""
     from saint_llm_b200.ops import gemm

@@ -206,3 +206,43 @@ def test_train_step_api_cpu():
     tok = torch.randint(0, cfg.vocab_size, (2, 1, 24))
     losses = [step(tok) for _ in range(5)]
     assert losses[-1] < losses[0]
+
+
+def test_trainer_window_one_host_read_and_skip_rules():
+    """``train_window``: a whole accumulation window per call; a non-finite loss anywhere
+    in it drops the window; the spike rule needs four accepted step losses first."""
+    from saint_llm_b200.train import Trainer
+    from saint_llm_b200.train.trainer import SkipRule
+
+    rule = SkipRule(nonfinite=True, spike_factor=2.0, window=8)
+    assert rule.reason(float("inf")) == "nan" and rule.reason(1e9) is None  # no history yet
+    for v in (1.0, 1.1, 0.9, 1.0):
+        rule.accept(v)
+    assert rule.reason(2.5) == "spike" and rule.reason(1.5) is None
+    codes = rule.reasons_device(torch.tensor([1.0, float("nan"), 3.0]))
+    assert codes.tolist() == [0, 1, 2]
+
+    torch.manual_seed(0)
+    m = nn.Linear(8, 1)
+    opt = torch.optim.SGD(m.parameters(), lr=0.1)
+    seen = []
+
+    def loss_fn(model, b):
+        return ((model(b.float()) - 1.0) ** 2).mean()
+
+    tr = Trainer(m, opt, loss_fn=loss_fn, gradient_accumulation_steps=2,
+                 metrics_callback=lambda s, d: seen.append(d))
+    xs = [torch.randn(4, 8) for _ in range(2)]
+    w0 = m.weight.detach().clone()
+    vals = tr.train_window(xs)
+    assert len(vals) == 2 and tr.step == 1 and not torch.equal(w0, m.weight)
+    assert "perf/step_s" in seen[-1] or len(seen) == 1
+    w1 = m.weight.detach().clone()
+    tr.loss_fn = lambda model, b: (model(b.float()).sum() * float("nan"))
+    tr.train_window(xs)
+    assert tr.skipped_steps == 1 and tr.step == 1 and torch.equal(w1, m.weight)
+    assert seen[-1].get("skip_reason_nan") == 1.0
+    with pytest.raises(ValueError):
+        tr.train_window(xs[:1])
+    with pytest.raises(ValueError, match="grad_clip_norm"):
+        Trainer(m, opt, loss_fn=loss_fn, grad_clip_norm=0.0)

@@ -120,15 +120,37 @@ def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make
     n_params = _param_count(SaintLLM, cfg)
     need = n_params * 12 / world
     fits = need <= 0.9 * have
-    run_layers = full_layers
+    cuts = [full_layers]
     if not fits:
-        # largest layer cut whose fp32 state takes at most half the memory (activations are
-        # checkpointed per block): its micro-batch time scales linearly to the full depth
+        # layer cuts whose fp32 state takes at most a third of the memory (the reference's
+        # activations and optimizer temporaries take the rest: 133 GB at 2 layers and 2 x 4096
+        # tokens); on an out-of-memory error the next smaller cut is tried.  The measured
+        # micro-batch time scales linearly to the full depth.
         per_layer = (n_params - _param_count(SaintLLM, _reference_config(ModelConfig, args, 1))) / max(
             full_layers - 1, 1)
         base = n_params - per_layer * full_layers
-        run_layers = int(max(1, min(full_layers, (0.5 * have * world / 12 - base) // per_layer)))
-        cfg = _reference_config(ModelConfig, args, run_layers)
+        top = int(max(1, min(full_layers, (have * world / 36 - base) // per_layer)))
+        cuts = sorted({top, max(1, top // 2), max(1, top // 4), 2, 1}, reverse=True)
+    last_err = None
+    for run_layers in cuts:
+        try:
+            return _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn, rank, world, dev,
+                            t_arm, budget, run_layers, full_layers, fits, n_params, need, have)
+        except torch.OutOfMemoryError as e:  # only the layer-cut probe retries
+            if fits or world > 1:
+                raise
+            last_err = str(e).splitlines()[0][:120]  # keep no traceback: it would pin the model
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+    raise RuntimeError(f"every layer cut ran out of memory ({last_err})")
+
+
+def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn,  # noqa: N803
+             rank, world, dev, t_arm, budget, run_layers, full_layers, fits, n_params, need, have) -> dict:
+    cfg = _reference_config(ModelConfig, args, run_layers)
+    torch.cuda.reset_peak_memory_stats(dev)
     torch.manual_seed(0)
     with torch.device(dev):
         model = SaintLLM(cfg)

@@ -20,7 +20,6 @@ Rank 0 prints one JSON line.
 from __future__ import annotations
 
 import argparse
-import datetime
 import json
 import os
 import statistics
@@ -107,36 +106,27 @@ def count_native_launches(fn) -> int:
                if ev.device_type == torch.autograd.DeviceType.CUDA and "sv4::" in ev.name)
 
 
+def run_config(args, world: int):
+    """The run layout of this bench as a ``RunConfig`` (consumed by ``build_training``)."""
+    from saint_llm_b200.config import RunConfig
+
+    return RunConfig(ep=world, zero="dp" if args.no_zero else "hybrid_zero", fused_ep=args.ep_transport == "p2p",
+                     fused_zero=not args.no_overlap_reduce, micro_batch=args.micro_batch, seq_len=args.seq_len,
+                     grad_accum=args.seqs_per_gpu // args.micro_batch, lr=2.7e-4, adamw_lr=2.7e-4,
+                     pg_timeout_s=600.0, seed=0)
+
+
 def build_ours(args, device, world):
     from saint_llm_b200.config import ModelConfig
-    from saint_llm_b200.models import SaintLLM
-    from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
-    from saint_llm_b200.train.engine import attach_main_grads, cast_params
-    from saint_llm_b200.train.step import TrainStep
+    from saint_llm_b200.train.launch import build_training
 
     upd = {"linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt}
     if args.layers:
         upd["n_layers"] = args.layers
     cfg = ModelConfig.bench_16b().model_copy(update=upd)
-    torch.manual_seed(0)
-    with torch.device(device):
-        model = SaintLLM(cfg)
-    cast_params(model, torch.bfloat16)
-    grad_sync = None
-    if world > 1:
-        from saint_llm_b200.parallel import ep as ep_mod
-
-        grad_sync = ep_mod.setup_expert_parallel(model, transport=args.ep_transport,
-                                                 capacity_factor=args.ep_capacity, zero=not args.no_zero)
-        torch.cuda.empty_cache()
-    params = attach_main_grads(model)
-    muon, adamw = split_for_muon_adamw(model)
-    opt = MuonAdamW(muon, adamw, lr=2.7e-4, qk_clip_layers=model.attention_layers())
-    if grad_sync is not None:
-        grad_sync.configure_optimizer(opt)
-    step = TrainStep(model, opt, micro_batches=args.seqs_per_gpu // args.micro_batch, params=params,
-                     grad_sync=grad_sync)
-    return cfg, model, step
+    run = run_config(args, world)
+    job = build_training(cfg, run, device)
+    return cfg, job.model, job.step
 
 
 def _uniform_loss(cfg) -> float:
@@ -163,7 +153,9 @@ def run_ours(args) -> dict:
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+        from saint_llm_b200.train.launch import init_distributed
+
+        init_distributed(run_config(args, world), device)
     cfg, model, step = build_ours(args, device, world)
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.engine import SyntheticTokens
@@ -274,9 +266,8 @@ def main() -> None:
                     help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
     ap.add_argument("--no-zero", action="store_true",
                     help="N > 1: all-reduce replicated gradients and update them on every rank (no hybrid ZeRO)")
-    ap.add_argument("--ep-capacity", type=float, default=None,
-                    help="receive capacity per rank in units of its own (token, slot) pairs (default: the group "
-                         "size, which no routing can overflow); an overflow raises")
+    ap.add_argument("--no-overlap-reduce", action="store_true",
+                    help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--data-pool", type=int, default=8,
                     help="distinct synthetic step batches cycled through (pinned host memory)")

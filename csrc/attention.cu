@@ -26,14 +26,6 @@
 
 namespace sv4 {
 
-#ifdef SV4_ATTN_TRACE
-__device__ long long g_attn_trace[128];
-#define ATR(i) do { if (trace_cta && tid == 0 && (i) < 128) g_attn_trace[(i)] = clock64(); } while (0)
-#define ATRN() do { if (trace_cta && tid == 0 && tr < 128) g_attn_trace[tr] = clock64(); ++tr; } while (0)
-#else
-#define ATR(i) do { } while (0)
-#define ATRN() do { } while (0)
-#endif
 
 CUtensorMap make_map_nd(const void* base, CUtensorMapDataType dt, int rank, const uint64_t* dims,
                         const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
@@ -145,10 +137,6 @@ __global__ void __launch_bounds__(128, 2)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                 const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mkv,
                 const AttnParams P) {
-#ifdef SV4_ATTN_TRACE
-  const bool trace_cta = blockIdx.x == gridDim.x / 2 && blockIdx.y == 0 && blockIdx.z == 0;
-  int tr = 2;
-#endif
   constexpr int A = HD / 64;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -186,7 +174,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
   const uint32_t tS = tbase + lane_off, tO = tbase + 128 + lane_off;
   constexpr uint32_t kIdS = make_idesc_f16(128, 128, 1, 1, false, false);
   constexpr uint32_t kIdO = make_idesc_f16(128, HD, 1, 1, false, true);
-  ATR(0);
 
   if (leader) {
     mbar_arrive_expect_tx(&bar[0], A * kAtom);
@@ -218,9 +205,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           mbar_arrive_expect_tx(&bar[1], A * kAtom);
           for (int a = 0; a < A; ++a) tma_load_3d(sV + a * kAtom, &mkv, &bar[1], a * 64, kb * 128, b);
         }
-        ATRN();
         mbar_wait(&bar[1], n_kv & 1, P.err, kErrTimeoutFull);
-        ATRN();
         if (q_wait) {
           mbar_wait(&bar[0], 0, P.err, kErrTimeoutFull);
           q_wait = false;
@@ -234,7 +219,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
       __syncwarp();
       ++n_kv;
       mbar_wait(&bar[2], n_s & 1, P.err, kErrTimeoutAccum);
-      ATRN();
       __syncwarp();  // reconverge before warp-collective tcgen05.ld
       ++n_s;
       tc_fence_after();
@@ -269,7 +253,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
         const uint32_t word = !bits ? 0xffffffffu : (c == 0 ? wmask[0] : c == 1 ? wmask[1] : c == 2 ? wmask[2] : wmask[3]);
         const int base = kb * 128 + c * 32;
         tmem_ld_wait();
-        if (c == 0) ATRN();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int key = base + j;
@@ -279,10 +262,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           if (cap) sv = softcap * tanhf(sv / softcap);
           rmax = fmaxf(rmax, vis ? sv : -INFINITY);
         }
-        if (c == 0) ATRN();
       }
       const float m_new = fmaxf(m_run, rmax);
-      ATRN();
       if (n_o > o_before) {  // previous PV of this branch must finish before P / O are touched
         mbar_wait(&bar[3], (n_o - 1) & 1, P.err, kErrTimeoutAccum);
         __syncwarp();  // reconverge before warp-collective tcgen05.ld
@@ -307,7 +288,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
         l_run *= __expf(m_run - m_new);  // only the sink contributed so far
       }
       m_run = m_new;
-      ATRN();
       // pass 2: probabilities -> bf16 P tile
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -330,13 +310,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
         }
         l_run += (lp[0] + lp[1]) + (lp[2] + lp[3]);
         put_row32(sP, tid, c * 32, pv);
-        if (c == 0) ATRN();
       }
-      ATRN();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
-      ATRN();
       if (leader) {
         tc_fence_after();
         const uint32_t ap = smem_u32(sP), av = smem_u32(sV);
@@ -345,7 +322,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
           mma_bf16(tbase + 128, desc_k(ap, s), desc_mn(av, s), kIdO, (n_o > o_before || s > 0) ? 1u : 0u);
         mma_commit(&bar[3]);
       }
-      ATRN();
       __syncwarp();
       ++n_o;
     }
@@ -389,7 +365,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ 
     tc_fence_after();
   }
 
-  ATR(1);
   if (P.max_logit != nullptr) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
@@ -724,15 +699,6 @@ static void check_inputs(const torch::Tensor& q, const torch::Tensor& k, const t
 static int fwd_smem(int hd) { return 2 * (hd / 64) * kAtom + std::max(hd / 64, 2) * kAtom + 64 + 1024; }
 static int bwd_smem(int hd) { return 4 * (hd / 64) * kAtom + 4 * kAtom + 4 * 4096 + 64 + 1024; }
 
-#ifdef SV4_ATTN_TRACE
-torch::Tensor attn_trace() {
-  long long h[128];
-  C10_CUDA_CHECK(cudaMemcpyFromSymbol(h, g_attn_trace, sizeof(h)));
-  auto t = torch::empty({128}, torch::kInt64);
-  memcpy(t.data_ptr<int64_t>(), h, sizeof(h));
-  return t;
-}
-#endif
 
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
               int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
@@ -799,28 +765,31 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor k
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// CSA selection bitmask from the indexer's top-k ids (-1 = none): sel[b, t, i / 32] |= 1 << (i % 32)
+// CSA selection bitmask from the indexer's top-k ids (-1 = none): sel[b, t, i / 32] |= 1 << (i % 32).
+// An id outside [-1, n) records kErrBounds and selects nothing.
 __global__ void csa_select_mask_kernel(const int64_t* __restrict__ top, int rows, int k, int n, int words,
-                                       uint32_t* __restrict__ sel) {
+                                       uint32_t* __restrict__ sel, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   for (int i = lane; i < k; i += 32) {
     const int64_t id = top[static_cast<int64_t>(row) * k + i];
-    if (id >= 0 && id < n) atomicOr(sel + static_cast<int64_t>(row) * words + id / 32, 1u << (id % 32));
+    if (index_ok(id, -1, n, err) && id >= 0)
+      atomicOr(sel + static_cast<int64_t>(row) * words + id / 32, 1u << (id % 32));
   }
 }
 
-void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel) {
+void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(top.device());
   TORCH_CHECK(top.scalar_type() == at::kLong && top.is_contiguous(), "top: int64 contiguous");
+  TORCH_CHECK(sel.size(-1) * 32 >= n, "sel has fewer bits per row than blocks");
   const int k = top.size(-1);
   const int rows = top.numel() / std::max(k, 1);
   sel.zero_();
   if (rows == 0 || k == 0) return;
   csa_select_mask_kernel<<<(rows + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       top.data_ptr<int64_t>(), rows, k, static_cast<int>(n), static_cast<int>(sel.size(-1)),
-      reinterpret_cast<uint32_t*>(sel.data_ptr<int32_t>()));
+      reinterpret_cast<uint32_t*>(sel.data_ptr<int32_t>()), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -46,10 +46,11 @@ void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, 
 void moe_route_plan(torch::Tensor idx, int64_t n_experts, int64_t k, torch::Tensor counts, torch::Tensor seg_start,
                     torch::Tensor seg_rows, torch::Tensor total, torch::Tensor pos, torch::Tensor row_token,
                     torch::Tensor err);
-void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out);
-void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out);
+void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out, torch::Tensor err);
+void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out,
+                 torch::Tensor err);
 void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor dy,
-                     torch::Tensor dw);
+                     torch::Tensor dw, torch::Tensor err);
 void moe_zero_pad_rows(torch::Tensor row_token, torch::Tensor buf);
 void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi);
 // norm.cu
@@ -82,7 +83,7 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor k
               int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
               torch::Tensor o_c, torch::Tensor lse, torch::Tensor dout, torch::Tensor dq, torch::Tensor dk,
               torch::Tensor dv, torch::Tensor dkv, torch::Tensor dsink, torch::Tensor err);
-void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel);
+void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel, torch::Tensor err);
 // ce.cu
 void ce_fwd(torch::Tensor z, torch::Tensor target, double softcap, torch::Tensor lse, torch::Tensor nll);
 void ce_bwd(torch::Tensor z, torch::Tensor target, torch::Tensor lse, double softcap, torch::Tensor scale,
@@ -97,21 +98,18 @@ void ep_plan(torch::Tensor idx, torch::Tensor pos_local, torch::Tensor seg_start
              torch::Tensor my_flags, int64_t slot, int64_t epoch, int64_t rank, int64_t ws, int64_t C,
              torch::Tensor gpos, torch::Tensor seg_start_dst, torch::Tensor seg_rows_dst, torch::Tensor seg_pad_dst,
              int64_t timeout_ns, torch::Tensor err);
-void ep_dispatch(torch::Tensor h, torch::Tensor gpos, int64_t C, std::vector<int64_t> x_ptrs);
+void ep_dispatch(torch::Tensor h, torch::Tensor gpos, int64_t C, std::vector<int64_t> x_ptrs, torch::Tensor err);
 void ep_wait_zero(torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch, torch::Tensor buf,
                   torch::Tensor seg_start, torch::Tensor seg_rows, int64_t timeout_ns, torch::Tensor err);
 void ep_combine(std::vector<int64_t> y_ptrs, torch::Tensor gpos, torch::Tensor gate, int64_t C, torch::Tensor out,
                 c10::optional<torch::Tensor> ypair, torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch,
                 int64_t timeout_ns, torch::Tensor err);
 void ep_combine_bwd(torch::Tensor dout, torch::Tensor ypair, torch::Tensor gate, torch::Tensor gpos, int64_t C,
-                    std::vector<int64_t> dy_ptrs, torch::Tensor dgate);
+                    std::vector<int64_t> dy_ptrs, torch::Tensor dgate, torch::Tensor err);
 void ep_dispatch_bwd(std::vector<int64_t> dx_ptrs, torch::Tensor gpos, int64_t C, torch::Tensor dh,
                      torch::Tensor my_flags, int64_t phase, int64_t ws, int64_t epoch, int64_t timeout_ns,
                      torch::Tensor err);
 std::tuple<torch::Tensor, std::string> symm_alloc(int64_t nbytes, int64_t device);
-#ifdef SV4_ATTN_TRACE
-torch::Tensor attn_trace();
-#endif
 // indexer.cu
 void indexer_scores(torch::Tensor q, torch::Tensor keys, torch::Tensor w, c10::optional<torch::Tensor> vis,
                     int64_t m, int64_t q_start, torch::Tensor out, torch::Tensor err);
@@ -158,9 +156,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_norm_bwd", &sv4::rope_norm_bwd);
   m.def("row_sumsq", &sv4::row_sumsq);
   m.def("indexer_scores", &sv4::indexer_scores);
-#ifdef SV4_ATTN_TRACE
-  m.def("attn_trace", &sv4::attn_trace);
-#endif
   m.def("ep_signal", &sv4::ep_signal);
   m.def("ep_post_counts", &sv4::ep_post_counts);
   m.def("ep_plan", &sv4::ep_plan);

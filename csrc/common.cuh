@@ -22,12 +22,23 @@ enum ErrorCode : int {
   kErrTimeoutAccum = 3,     // MMA / epilogue waited too long for TMEM
   kErrBadShape = 4,
   kErrPeerTimeout = 5,      // cross-GPU flag never arrived
-  kErrBounds = 6,           // gathered index out of range (bounds-check mode)
+  kErrBounds = 6,           // gathered / scattered index out of range (index_ok)
   kErrCapacity = 7,         // expert-parallel receive layout exceeded the buffer capacity
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// Range check of a gathered / scattered index (expert rows, top-k ids, peer offsets, page
+// ids).  Compiled into every gather and scatter kernel (one compare per row, negligible
+// next to the row copy): an index outside [lo, hi) records kErrBounds in the error word
+// and the caller skips the access, so a corrupt routing table shows up as a Python
+// exception from check_errors() instead of a stray read or write.
+__device__ __forceinline__ bool index_ok(int64_t i, int64_t lo, int64_t hi, int* err) {
+  if (i >= lo && i < hi) return true;
+  record_error(err, kErrBounds);
+  return false;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -211,13 +211,22 @@ void ep_plan(torch::Tensor idx, torch::Tensor pos_local, torch::Tensor seg_start
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// A global receive row (destination rank * C + row) of a (token, slot) pair, or -1 for a
+// dropped pair.  Anything outside [-1, ws * C) is a corrupt layout: thread 0 of the CTA
+// records kErrBounds and every thread treats the pair as dropped (no peer access).
+__device__ __forceinline__ int checked_gpos(int p, int ws, int C, int* err) {
+  const bool ok = threadIdx.x == 0 ? index_ok(p, -1, static_cast<int64_t>(ws) * C, err)
+                                   : (p >= -1 && p < ws * C);
+  return ok ? p : -1;
+}
+
 // ----------------------------------------------------------------- dispatch (push)
 // One CTA per token: the row is read once and stored into each of its k destinations.
 __global__ void ep_dispatch_kernel(const uint4* __restrict__ h, const int* __restrict__ gpos, int k, int vpr, int C,
-                                   PeerTable xbuf) {
+                                   PeerTable xbuf, int ws, int* err) {
   const int t = blockIdx.x;
   int p[16];
-  for (int j = 0; j < k; ++j) p[j] = gpos[t * k + j];
+  for (int j = 0; j < k; ++j) p[j] = checked_gpos(gpos[t * k + j], ws, C, err);
   for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
     const uint4 val = h[static_cast<int64_t>(t) * vpr + v];
     for (int j = 0; j < k; ++j) {
@@ -229,14 +238,15 @@ __global__ void ep_dispatch_kernel(const uint4* __restrict__ h, const int* __res
   __threadfence_system();
 }
 
-void ep_dispatch(torch::Tensor h, torch::Tensor gpos, int64_t C, std::vector<int64_t> x_ptrs) {
+void ep_dispatch(torch::Tensor h, torch::Tensor gpos, int64_t C, std::vector<int64_t> x_ptrs, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(h.device());
   const int T = h.size(0), k = gpos.size(1);
   TORCH_CHECK(h.is_contiguous() && h.size(1) * h.element_size() % 16 == 0 && k <= 16, "ep_dispatch layout");
   if (T == 0) return;
   const int vpr = h.size(1) * h.element_size() / 16;
   ep_dispatch_kernel<<<T, std::min(256, std::max(32, vpr)), 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const uint4*>(h.data_ptr()), gpos.data_ptr<int>(), k, vpr, C, make_table(x_ptrs));
+      reinterpret_cast<const uint4*>(h.data_ptr()), gpos.data_ptr<int>(), k, vpr, C, make_table(x_ptrs),
+      static_cast<int>(x_ptrs.size()), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -299,7 +309,7 @@ __global__ void ep_combine_kernel(PeerTable ybuf, const int* __restrict__ gpos, 
   int p[16];
   float g[16];
   for (int j = 0; j < k; ++j) {
-    p[j] = ok ? gpos[t * k + j] : -1;
+    p[j] = ok ? checked_gpos(gpos[t * k + j], ws, C, err) : -1;
     g[j] = gate[t * k + j];
   }
   for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
@@ -347,7 +357,7 @@ void ep_combine(std::vector<int64_t> y_ptrs, torch::Tensor gpos, torch::Tensor g
 // dy row = gate[t,j] * dout[t].
 __global__ void ep_combine_bwd_kernel(const uint4* __restrict__ dout, const uint4* __restrict__ ypair,
                                       const float* __restrict__ gate, const int* __restrict__ gpos, int k, int C,
-                                      int vpr, PeerTable dybuf, float* __restrict__ dgate) {
+                                      int vpr, PeerTable dybuf, float* __restrict__ dgate, int ws, int* err) {
   // Loops over the k slots are unrolled to the maximum (16) with an early exit, so the
   // per-slot arrays stay in registers and the k row loads of a chunk are issued together.
   const int t = blockIdx.x;
@@ -355,7 +365,7 @@ __global__ void ep_combine_bwd_kernel(const uint4* __restrict__ dout, const uint
   float g[16], dot[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    p[j] = j < k ? gpos[t * k + j] : -1;
+    p[j] = j < k ? checked_gpos(gpos[t * k + j], ws, C, err) : -1;
     g[j] = j < k ? gate[t * k + j] : 0.f;
     dot[j] = 0.f;
   }
@@ -413,7 +423,7 @@ __global__ void ep_combine_bwd_kernel(const uint4* __restrict__ dout, const uint
 }
 
 void ep_combine_bwd(torch::Tensor dout, torch::Tensor ypair, torch::Tensor gate, torch::Tensor gpos, int64_t C,
-                    std::vector<int64_t> dy_ptrs, torch::Tensor dgate) {
+                    std::vector<int64_t> dy_ptrs, torch::Tensor dgate, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(dout.device());
   const int T = dout.size(0), k = gpos.size(1);
   TORCH_CHECK(dout.is_contiguous() && ypair.is_contiguous() && k <= 16, "ep_combine_bwd layout");
@@ -422,7 +432,8 @@ void ep_combine_bwd(torch::Tensor dout, torch::Tensor ypair, torch::Tensor gate,
   const int threads = std::min(256, std::max(32, (vpr + 31) / 32 * 32));
   ep_combine_bwd_kernel<<<T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const uint4*>(dout.data_ptr()), reinterpret_cast<const uint4*>(ypair.data_ptr()),
-      gate.data_ptr<float>(), gpos.data_ptr<int>(), k, C, vpr, make_table(dy_ptrs), dgate.data_ptr<float>());
+      gate.data_ptr<float>(), gpos.data_ptr<int>(), k, C, vpr, make_table(dy_ptrs), dgate.data_ptr<float>(),
+      static_cast<int>(dy_ptrs.size()), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -435,7 +446,7 @@ __global__ void ep_dispatch_bwd_kernel(PeerTable dxbuf, const int* __restrict__ 
   __syncthreads();
   const int t = blockIdx.x;
   int p[16];
-  for (int j = 0; j < k; ++j) p[j] = ok ? gpos[t * k + j] : -1;
+  for (int j = 0; j < k; ++j) p[j] = ok ? checked_gpos(gpos[t * k + j], ws, C, err) : -1;
   for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
     uint4 val[16];
 #pragma unroll

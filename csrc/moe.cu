@@ -113,13 +113,15 @@ void moe_route_plan(torch::Tensor idx, int64_t n_experts, int64_t k, torch::Tens
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// x_perm[r, :] = h[row_token[r], :] or 0.  One warp per row, 16-byte vectors.
+// x_perm[r, :] = h[row_token[r], :] or 0.  One warp per row, 16-byte vectors.  A token id
+// outside [-1, T) records kErrBounds and leaves the row zero.
 __global__ void gather_rows_kernel(const uint4* __restrict__ h, const int* __restrict__ row_token,
-                                   uint4* __restrict__ out, int rows, int vec_per_row) {
+                                   uint4* __restrict__ out, int rows, int vec_per_row, int T, int* err) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
-  const int t = row_token[warp];
+  int t = row_token[warp];
+  if (!index_ok(t, -1, T, err)) t = -1;
   uint4* dst = out + static_cast<int64_t>(warp) * vec_per_row;
   if (t < 0) {
     for (int v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
@@ -129,7 +131,7 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ h, const int* __res
   }
 }
 
-void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out) {
+void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(h.device());
   TORCH_CHECK(h.is_contiguous() && out.is_contiguous() && h.scalar_type() == out.scalar_type(), "layout");
   TORCH_CHECK(h.size(1) * h.element_size() % 16 == 0, "row bytes must be a multiple of 16");
@@ -138,19 +140,26 @@ void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out) {
   if (rows == 0) return;
   gather_rows_kernel<<<(rows * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const uint4*>(h.data_ptr()), row_token.data_ptr<int>(),
-      reinterpret_cast<uint4*>(out.data_ptr()), rows, vpr);
+      reinterpret_cast<uint4*>(out.data_ptr()), rows, vpr, static_cast<int>(h.size(0)), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // out[t, :] = sum_j w[t, j] * y[pos[t, j], :]   (w == nullptr -> weight 1).  One CTA per token.
+// A slot position outside [0, rows_y) records kErrBounds and contributes nothing.
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* __restrict__ pos,
-                               const float* __restrict__ w, __nv_bfloat16* __restrict__ out, int D, int kk) {
+                               const float* __restrict__ w, __nv_bfloat16* __restrict__ out, int D, int kk,
+                               int rows_y, int* err) {
   const int t = blockIdx.x;
   int p[16];
   float g[16];
   for (int j = 0; j < kk; ++j) {
     p[j] = pos[t * kk + j];
     g[j] = w ? w[t * kk + j] : 1.0f;
+    const bool ok = threadIdx.x == 0 ? index_ok(p[j], 0, rows_y, err) : (p[j] >= 0 && p[j] < rows_y);
+    if (!ok) {
+      p[j] = 0;
+      g[j] = 0.f;
+    }
   }
   for (int d = threadIdx.x * 8; d < D; d += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -172,7 +181,8 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y, const int* _
   }
 }
 
-void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out) {
+void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out,
+                 torch::Tensor err) {
   c10::cuda::CUDAGuard guard(y.device());
   const int T = out.size(0), D = out.size(1), k = pos.size(1);
   TORCH_CHECK(D % 8 == 0 && k <= 16, "combine: D % 8 == 0 and k <= 16");
@@ -181,7 +191,7 @@ void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor
   const int threads = std::min(256, std::max(32, D / 8));
   combine_kernel<<<T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), pos.data_ptr<int>(), wp,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, k);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), D, k, static_cast<int>(y.size(0)), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -190,12 +200,17 @@ void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor
 __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ pos, const float* __restrict__ w,
                                    __nv_bfloat16* __restrict__ dy, float* __restrict__ dw, int n_pairs, int k,
-                                   int D) {
+                                   int D, int rows, int* err) {
   const int pair = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (pair >= n_pairs) return;
   const int t = pair / k;
   const int p = pos[pair];
+  const bool ok = lane == 0 ? index_ok(p, 0, rows, err) : (p >= 0 && p < rows);
+  if (!ok) {  // the pair's gradient row cannot be placed: no write, zero gate gradient
+    if (lane == 0) dw[pair] = 0.f;
+    return;
+  }
   const float g = w[pair];
   float dot = 0.f;
   for (int d = lane * 8; d < D; d += 32 * 8) {
@@ -220,7 +235,7 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const
 }
 
 void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor dy,
-                     torch::Tensor dw) {
+                     torch::Tensor dw, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(dout.device());
   const int n_pairs = pos.numel(), k = pos.size(1), D = dout.size(1);
   TORCH_CHECK(D % 8 == 0, "D % 8");
@@ -228,7 +243,7 @@ void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, tor
   combine_bwd_kernel<<<(n_pairs * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()),
       pos.data_ptr<int>(), w.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()),
-      dw.data_ptr<float>(), n_pairs, k, D);
+      dw.data_ptr<float>(), n_pairs, k, D, static_cast<int>(std::min(y.size(0), dy.size(0))), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

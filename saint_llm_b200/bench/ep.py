@@ -81,7 +81,7 @@ def main() -> None:
     y_rows.normal_()
 
     def dispatch() -> None:
-        ext.ep_dispatch(h, gpos, C, xb.ptrs)
+        ext.ep_dispatch(h, gpos, C, xb.ptrs, err)
         ep = comm.next_epoch(PH_X)
         ext.ep_signal(comm.flags.ptrs, PH_X, rank, ep)
         ext.ep_wait_zero(flags, PH_X, ws, ep, x_rows, ss, sr, comm.timeout_ns, err)
@@ -92,7 +92,7 @@ def main() -> None:
         ext.ep_combine(comm.y.ptrs, gpos, gate, C, out, ypair, flags, PH_Y, ws, ep, comm.timeout_ns, err)
 
     def combine_bwd() -> None:
-        ext.ep_combine_bwd(dout, ypair, gate, gpos, C, comm.dy.ptrs, dgate)
+        ext.ep_combine_bwd(dout, ypair, gate, gpos, C, comm.dy.ptrs, dgate, err)
         ep = comm.next_epoch(PH_DY)
         ext.ep_signal(comm.flags.ptrs, PH_DY, rank, ep)
         ext.ep_wait_zero(flags, PH_DY, ws, ep, dy_rows, ss, sr, comm.timeout_ns, err)

@@ -126,7 +126,7 @@ def bench_fp8(args: argparse.Namespace) -> None:
 
 
 def bench_attention(args: argparse.Namespace) -> None:
-    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops import backend, gemm
     from saint_llm_b200.ops.attention import fused_attention
 
     t, h, d, w = args.t, args.heads, args.head_dim, args.window
@@ -146,7 +146,7 @@ def bench_attention(args: argparse.Namespace) -> None:
         pick = causal & (torch.rand(t, n, device="cuda") < 0.5)
         top = torch.where(pick, torch.arange(n, device="cuda").expand(t, n), -1).unsqueeze(0).contiguous()
         sel = torch.empty(1, t, (n + 31) // 32, dtype=torch.int32, device="cuda")
-        backend.ext().csa_select_mask(top, n, sel)
+        backend.ext().csa_select_mask(top, n, sel, gemm.error_word(top.device))
         keys_c = float(pick.sum())
     elif mode == 1:  # entry j visible to query i iff j*m + m - 1 < i
         keys_c = float(sum(min(n, i // m) for i in range(t)))

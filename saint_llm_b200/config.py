@@ -324,7 +324,9 @@ class RunConfig(_Frozen):
     adamw_lr: float = 2.7e-4
     # runtime
     pg_timeout_s: float = 120.0
-    device_wait_timeout_ms: int = 2000
+    # bound of every cross-GPU flag wait in the peer-memory kernels (ranks may start a step
+    # seconds apart, e.g. after an uneven optimizer step); a timed-out wait raises
+    device_wait_timeout_ms: int = 30000
     seed: int = 0
 
     @classmethod

@@ -220,7 +220,7 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
                 top = indexer_topk(layer.indexer, hb, is_visual)
                 if top.shape[-1] > 0:
                     sel = torch.empty(b, t, (n_blocks + 31) // 32, dtype=torch.int32, device=h.device)
-                    backend.ext().csa_select_mask(top.contiguous(), n_blocks, sel)
+                    backend.ext().csa_select_mask(top.contiguous(), n_blocks, sel, gemm.error_word(h.device))
                     mode = 2
             else:
                 mode = 1

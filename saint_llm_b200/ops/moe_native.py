@@ -90,7 +90,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         plan = RoutePlan(idx, E, k)
         hb = _bf16c(h)
         x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-        ext.moe_gather(hb, plan.row_token, x_p)
+        ext.moe_gather(hb, plan.row_token, x_p, err)
         wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
         act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
         pre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
@@ -102,7 +102,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         ext.grouped_gemm(1, act, wdb, wdb, y, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
         out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
         gf = gate.float().contiguous()
-        ext.moe_combine(y, plan.pos, gf, out)
+        ext.moe_combine(y, plan.pos, gf, out, err)
         ctx.save_for_backward(hb, gf, act, pre, y, wg, wu, wd)
         ctx.plan = plan
         ctx.clamps = clamps
@@ -121,7 +121,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         e0 = _empty(dev)
         dy = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
         dgate = torch.empty_like(gf)
-        ext.moe_combine_bwd(_bf16c(dout), y, plan.pos, gf, dy, dgate)
+        ext.moe_combine_bwd(_bf16c(dout), y, plan.pos, gf, dy, dgate, err)
         ext.moe_zero_pad_rows(plan.row_token, dy)
         wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
         # down projection: d_act = dy Wd ; dWd += dy^T act
@@ -142,7 +142,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         pr, tot, n = plan.problems(3, D, I)
         ext.grouped_gemm(3, dpre, wgb, wub, dxp, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, I, False, err)
         x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-        ext.moe_gather(hb, plan.row_token, x_p)
+        ext.moe_gather(hb, plan.row_token, x_p, err)
         mg_g, mg_u = getattr(wg, "main_grad", None), getattr(wu, "main_grad", None)
         if mg_g is not None and mg_u is not None and mg_u.data_ptr() == mg_g.data_ptr() + mg_g.numel() * 4:
             joint, acc_gu = mg_g, True
@@ -151,7 +151,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         pr, tot, n = plan.problems(4, D, I)
         ext.grouped_gemm(4, dpre, x_p, x_p, joint, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
         dh = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
-        ext.moe_combine(dxp, plan.pos, None, dh)
+        ext.moe_combine(dxp, plan.pos, None, dh, err)
         dwg = None if acc_gu else joint[0].to(wg.dtype)
         dwu = None if acc_gu else joint[1].to(wu.dtype)
         dwd = None if acc_d else dwd_buf.to(wd.dtype)
@@ -317,7 +317,7 @@ def routed_experts_fp8(h: Tensor, idx: Tensor, gate: Tensor, w8: Fp8ExpertWeight
     err = gemm.error_word(dev)
     plan = RoutePlan(idx, E, k)
     x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-    ext.moe_gather(_bf16c(h), plan.row_token, x_p)
+    ext.moe_gather(_bf16c(h), plan.row_token, x_p, err)
     xq = fp8.quantize_rows(x_p)
     act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
     pr, tot, n = plan.problems(6, D, I)
@@ -328,7 +328,7 @@ def routed_experts_fp8(h: Tensor, idx: Tensor, gate: Tensor, w8: Fp8ExpertWeight
     pr, tot, n = plan.problems(7, D, I)
     ext.grouped_gemm_fp8(1, aq.q, aq.sf, w8.down.q, w8.down.sf, y, None, pr, tot, n, D, 0.0, 0.0, 0.0, err)
     out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
-    ext.moe_combine(y, plan.pos, gate.float().contiguous(), out)
+    ext.moe_combine(y, plan.pos, gate.float().contiguous(), out, err)
     return out
 
 

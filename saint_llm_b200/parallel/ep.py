@@ -245,13 +245,14 @@ class ParallelSync:
     loss is the global mean)."""
 
     def __init__(self, model: nn.Module, expert_params: list[Tensor], group: dist.ProcessGroup | None,
-                 *, zero: bool) -> None:
+                 *, zero: bool, overlap_reduce: bool = False) -> None:
         self.model, self.group = model, group
         self.ws = dist.get_world_size(group)
         self.expert_ids = {id(p) for p in expert_params}
         self.expert_params = expert_params
         self.zero = None
         self._plain = None
+        self.overlap = False
         if zero:
             from saint_llm_b200.optim import split_for_muon_adamw
             from saint_llm_b200.parallel.zero import ZeroOptimizerSync
@@ -260,8 +261,26 @@ class ParallelSync:
             kinds = {id(p): "muon" for p in muon} | {id(p): "adamw" for p in adamw}
             rep = [p for p in model.parameters() if id(p) not in self.expert_ids and p.requires_grad]
             self.zero = ZeroOptimizerSync(rep, [kinds.get(id(p), "adamw") for p in rep], group=group)
+            blocks = list(getattr(model, "blocks", []))
+            if overlap_reduce and blocks:
+                self._hook_blocks(blocks)
         else:
             self._plain = make_grad_sync(expert_params, group)
+
+    def _hook_blocks(self, blocks: list[nn.Module]) -> None:
+        """Overlapped reduce: block i's backward hook reduces block i + 1's group (one
+        block of slack, so late gradient accumulations of block i + 1 have landed)."""
+        self.zero.overlap_groups([[p for p in b.parameters() if p.requires_grad] for b in blocks])
+        n = len(blocks)
+        for i, b in enumerate(blocks):
+            if i + 1 < n:
+                b.register_full_backward_hook(lambda m, gi, go, g=i + 1: self.zero.group_done(g))
+        self.overlap = True
+
+    def before_last_backward(self) -> None:
+        """Called by ``TrainStep`` before the backward of a step's last micro-batch."""
+        if self.overlap:
+            self.zero.final_micro = True
 
     def is_updated_here(self, p: Tensor) -> bool:
         return self.zero is None or id(p) in self.expert_ids or self.zero.is_owned(p)
@@ -276,7 +295,10 @@ class ParallelSync:
         if self._plain is not None:
             self._plain(params)
             return
-        self.zero.reduce_grads()
+        if self.overlap:
+            self.zero.finish_reduce()
+        else:
+            self.zero.reduce_grads()
         for p in self.expert_params:
             g = getattr(p, "main_grad", None)
             (g if g is not None else p.grad).div_(self.ws)
@@ -288,16 +310,21 @@ class ParallelSync:
 
 
 def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",
-                          capacity_factor: float | None = None, zero: bool = False) -> ParallelSync:
+                          capacity_factor: float | None = None, zero: bool = False, timeout_s: float = 30.0,
+                          overlap_reduce: bool = False) -> ParallelSync:
     """Shard the experts over ``group`` and return the gradient synchroniser.
 
     ``transport``: "p2p" moves tokens with the peer-memory kernels of ``parallel.ep_p2p``
     (CUDA only), "nccl" with ``all_to_all_single``; "auto" picks p2p on CUDA.
     ``zero``: hybrid ZeRO for the replicated parameters (see ``ParallelSync``); call
-    ``sync.configure_optimizer(opt)`` once and ``sync.post_step()`` after every step."""
+    ``sync.configure_optimizer(opt)`` once and ``sync.post_step()`` after every step.
+    ``overlap_reduce`` (with ``zero``): issue each block's owner reductions from its
+    backward hook during the last micro-batch.  ``timeout_s``: bound of every cross-GPU
+    flag wait of the peer-memory kernels."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
-    sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero)
+    sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero,
+                        overlap_reduce=overlap_reduce)
     dev = next(model.parameters()).device
     if transport not in ("auto", "p2p", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")
@@ -306,7 +333,7 @@ def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
             raise ValueError("the p2p transport needs CUDA parameters")
         from saint_llm_b200.parallel.ep_p2p import attach_p2p_comm
 
-        attach_p2p_comm(model, group, dev, capacity_factor=capacity_factor)
+        attach_p2p_comm(model, group, dev, capacity_factor=capacity_factor, timeout_s=timeout_s)
     return sync
 
 

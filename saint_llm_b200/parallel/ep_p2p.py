@@ -254,7 +254,7 @@ class EPCall:
                     c.flags.local.view(torch.int32), self.e_cnt & 1, self.e_cnt, c.rank, c.ws, c.C, self.gpos,
                     self.seg_start, self.seg_rows, self.seg_pad, c.timeout_ns, self.err)
         del self.local
-        ext.ep_dispatch(self.hb, self.gpos, c.C, c.xr.ptrs)
+        ext.ep_dispatch(self.hb, self.gpos, c.C, c.xr.ptrs, self.err)
         self.e_x = c.next_epoch(PH_X)
         ext.ep_signal(c.flags.ptrs, PH_X, c.rank, self.e_x)
 
@@ -297,7 +297,7 @@ class EPCall:
     def b1_push(self, dout: Tensor) -> None:
         c, ext = self.comm, backend.ext()
         self.dgate = torch.empty_like(self.gf)
-        ext.ep_combine_bwd(_bf16c(dout), self.ypair, self.gf, self.gpos, c.C, c.dy.ptrs, self.dgate)
+        ext.ep_combine_bwd(_bf16c(dout), self.ypair, self.gf, self.gpos, c.C, c.dy.ptrs, self.dgate, self.err)
         del self.ypair
         self.e_dy = c.next_epoch(PH_DY)
         ext.ep_signal(c.flags.ptrs, PH_DY, c.rank, self.e_dy)

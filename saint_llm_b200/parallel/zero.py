@@ -12,6 +12,14 @@ owner runs Muon/AdamW on a parameter (Newton-Schulz needs the whole matrix, so o
 per tensor), and the owner broadcasts the updated weights in the same buckets.  Traffic per
 step equals one all-reduce (reduce + broadcast) while the optimizer work and the optimizer
 state are split across ranks.
+
+Overlapped mode (``overlap_groups``): the parameters are also partitioned into groups that
+finish their gradients together (one transformer block each, plus a tail of everything
+else).  During the last micro-batch of a step the caller marks ``final_micro``; a group's
+reductions are issued from the block's backward hook the moment its gradients are written,
+so they run on NCCL's stream while the backward of the earlier blocks continues.  Groups are
+visited in backward order, which is the same on every rank, so every rank issues the same
+collectives in the same order.
 """
 
 from __future__ import annotations
@@ -133,6 +141,64 @@ class ZeroOptimizerSync:
             if cur:
                 self._buckets.append((r, cur))
 
+    # ------------------------------------------------------------ overlapped reduce
+    def overlap_groups(self, groups: list[list[Tensor]]) -> None:
+        """Partition the parameters into ``groups`` (each reduced from a backward hook) and
+        a tail (the parameters in no group, reduced after the backward)."""
+        index = {id(p): i for i, p in enumerate(self.params)}
+        self._groups: list[list[tuple[int, list[int]]]] = []
+        grouped: set[int] = set()
+        for g in groups:
+            idx = [index[id(p)] for p in g if id(p) in index]
+            grouped.update(idx)
+            self._groups.append(self._by_owner(idx))
+        self._tail = self._by_owner([i for i in range(len(self.params)) if i not in grouped])
+        self._done: set[int] = set()
+        self.final_micro = False
+
+    def _by_owner(self, idx: list[int]) -> list[tuple[int, list[int]]]:
+        per: dict[int, list[int]] = {}
+        for i in idx:
+            per.setdefault(self.owner[i], []).append(i)
+        return sorted(per.items())
+
+    def group_done(self, g: int) -> None:
+        """Backward hook of group ``g``: reduce its gradients now if this is the step's
+        last micro-batch (each group once per step)."""
+        if not self.final_micro or g in self._done or self.world == 1:
+            return
+        self._done.add(g)
+        for owner, idx in self._groups[g]:
+            self._reduce_bucket(owner, idx)
+
+    def _reduce_bucket(self, owner: int, idx: list[int]) -> None:
+        grads = [_grad_buf(self.params[i]) for i in idx]
+        flat = torch.cat([g.reshape(-1).float() for g in grads])
+        dist.reduce(flat, dst=self._global_rank(owner), op=dist.ReduceOp.SUM, group=self.group)
+        if owner == self.rank:
+            flat.div_(self.world)
+            off = 0
+            for g in grads:
+                g.copy_(flat[off:off + g.numel()].view_as(g))
+                off += g.numel()
+        else:
+            for g in grads:
+                g.zero_()
+
+    @torch.no_grad()
+    def finish_reduce(self) -> None:
+        """After the backward of an overlapped step: reduce every group whose hook did not
+        fire (in group order) and the tail, then re-arm for the next step."""
+        if self.world > 1:
+            for g in range(len(self._groups)):
+                if g not in self._done:
+                    for owner, idx in self._groups[g]:
+                        self._reduce_bucket(owner, idx)
+            for owner, idx in self._tail:
+                self._reduce_bucket(owner, idx)
+        self._done = set()
+        self.final_micro = False
+
     def _global_rank(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
@@ -142,18 +208,7 @@ class ZeroOptimizerSync:
         if self.world == 1:
             return
         for owner, idx in self._buckets:
-            grads = [_grad_buf(self.params[i]) for i in idx]
-            flat = torch.cat([g.reshape(-1).float() for g in grads])
-            dist.reduce(flat, dst=self._global_rank(owner), op=dist.ReduceOp.SUM, group=self.group)
-            if owner == self.rank:
-                flat.div_(self.world)
-                off = 0
-                for g in grads:
-                    g.copy_(flat[off:off + g.numel()].view_as(g))
-                    off += g.numel()
-            else:
-                for g in grads:
-                    g.zero_()
+            self._reduce_bucket(owner, idx)
 
     @torch.no_grad()
     def broadcast_params(self) -> None:

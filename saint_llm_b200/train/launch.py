@@ -1,0 +1,150 @@
+"""Build a training job from a ``ModelConfig`` (what the model is) and a ``RunConfig`` (how
+it runs): the public entry point behind ``bench.py`` and user scripts.
+
+    job = build_training(model_cfg, run_cfg, device)
+    loss = job.step(host_tokens)          # (grad_accum, micro_batch, seq_len) int64
+
+What each ``RunConfig`` field selects here:
+
+* ``ep`` / ``zero``: ``ep > 1`` shards the routed experts over the process group (EP must
+  equal the world size, one node); ``zero="hybrid_zero"`` gives every replicated
+  parameter one owner that reduces, updates and broadcasts it, ``"dp"`` all-reduces the
+  replicated gradients and updates them everywhere.
+* ``fused_ep``: the expert-parallel token traffic runs in this framework's peer-memory
+  kernels (True) or over NCCL ``all_to_all`` (False, the baseline and oracle).
+* ``fused_zero``: with hybrid ZeRO, each transformer block's per-owner gradient reductions
+  are issued from a backward hook during the step's last micro-batch, so they run on
+  NCCL's stream while the backward of the earlier blocks continues (True), or all after
+  the backward (False).
+* ``kernels``: "native" (sm_100a kernels) or "torch" (the eager oracle path on CUDA,
+  through ``backend.eager_mode``; every step then runs inside that mode).
+* ``micro_batch`` / ``seq_len`` / ``grad_accum``: the shape of one step's token batch.
+* ``lr`` / ``adamw_lr``: Muon and AdamW learning rates.
+* ``pg_timeout_s``: the process-group timeout (used when this function initialises it);
+  ``device_wait_timeout_ms``: the bound of every cross-GPU flag wait of the EP kernels.
+* ``seed``: the model initialisation seed.
+* ``param_dtype`` / ``grad_dtype`` / ``compute_dtype``: parameters in bf16 (or fp32),
+  gradients accumulated in fp32 ``main_grad`` buffers; bf16 parameters compute in bf16.
+  Other combinations raise.
+* ``tp`` / ``cp`` / ``pp``: tensor, context and pipeline parallelism have their own
+  drivers (``parallel.tp`` / ``parallel.cp`` / ``parallel.pipeline`` / ``parallel.dualpipe``);
+  this builder accepts only 1 for them and says so.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import datetime
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from saint_llm_b200.config import ModelConfig, RunConfig
+
+
+@dataclass
+class TrainingJob:
+    model: nn.Module
+    optimizer: torch.optim.Optimizer
+    step: TrainStepLike
+    grad_sync: object | None
+    run: RunConfig
+
+    def close(self) -> None:
+        """Collective release of the expert-parallel peer buffers (call on every rank)."""
+        comm = getattr(self.model, "ep_comm", None)
+        if comm is not None:
+            comm.close()
+
+
+class TrainStepLike:  # typing helper: TrainStep or its eager wrapper
+    def __call__(self, host_tokens: Tensor) -> float: ...
+
+    def run_device(self, tokens: Tensor) -> Tensor: ...
+
+
+class _EagerStep:
+    """Runs every call of a ``TrainStep`` under ``backend.eager_mode`` (kernels="torch")."""
+
+    def __init__(self, inner) -> None:
+        self.inner = inner
+
+    def _ctx(self) -> contextlib.AbstractContextManager:
+        from saint_llm_b200.ops import backend
+
+        return backend.eager_mode(True)
+
+    def __call__(self, host_tokens: Tensor) -> float:
+        with self._ctx():
+            return self.inner(host_tokens)
+
+    def run_device(self, tokens: Tensor) -> Tensor:
+        with self._ctx():
+            return self.inner.run_device(tokens)
+
+    def __getattr__(self, name: str):
+        return getattr(self.inner, name)
+
+
+def _check(run: RunConfig, world: int) -> None:
+    problems = []
+    for dim in ("tp", "cp", "pp"):
+        if getattr(run, dim) != 1:
+            problems.append(f"{dim}={getattr(run, dim)} (use the parallel.{dim} driver)")
+    if run.ep not in (1, world):
+        problems.append(f"ep={run.ep} must be 1 or the world size {world}")
+    if run.zero not in ("dp", "hybrid_zero", "none"):
+        problems.append(f"zero={run.zero!r} (this builder runs 'dp' or 'hybrid_zero'; FSDP has parallel.fsdp)")
+    if run.grad_dtype != "float32":
+        problems.append("grad_dtype must be float32 (gradients accumulate in fp32 main_grad buffers)")
+    if run.param_dtype == "bfloat16" and run.compute_dtype != "bfloat16":
+        problems.append("bf16 parameters compute in bf16")
+    if problems:
+        raise ValueError("RunConfig not supported by build_training: " + "; ".join(problems))
+
+
+def init_distributed(run: RunConfig, device: torch.device) -> None:
+    """NCCL process group with the run's timeout (no-op when already initialised)."""
+    if dist.is_initialized():
+        return
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=run.pg_timeout_s), device_id=device)
+
+
+def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device, *,
+                   group: dist.ProcessGroup | None = None, qk_clip: bool = True) -> TrainingJob:
+    from saint_llm_b200.models import SaintLLM
+    from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
+    from saint_llm_b200.train.engine import attach_main_grads, cast_params
+    from saint_llm_b200.train.step import TrainStep
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    _check(run, world)
+    torch.manual_seed(run.seed)
+    with torch.device(device):
+        model = SaintLLM(model_cfg)
+    bf16 = run.param_dtype == "bfloat16"
+    if bf16:
+        cast_params(model, torch.bfloat16)
+    grad_sync = None
+    if world > 1:
+        from saint_llm_b200.parallel import ep as ep_mod
+
+        grad_sync = ep_mod.setup_expert_parallel(
+            model, group, transport="p2p" if run.fused_ep else "nccl", zero=run.zero == "hybrid_zero",
+            timeout_s=run.device_wait_timeout_ms / 1000.0, overlap_reduce=run.fused_zero)
+        if device.type == "cuda":
+            torch.cuda.empty_cache()
+    params = attach_main_grads(model)
+    muon, adamw = split_for_muon_adamw(model)
+    opt = MuonAdamW(muon, adamw, lr=run.lr, adamw_lr=run.adamw_lr,
+                    qk_clip_layers=model.attention_layers() if qk_clip else None)
+    if grad_sync is not None:
+        grad_sync.configure_optimizer(opt)
+    step = TrainStep(model, opt, micro_batches=run.grad_accum, params=params, grad_sync=grad_sync)
+    wrapped = _EagerStep(step) if run.kernels == "torch" else step
+    return TrainingJob(model, opt, wrapped, grad_sync, run)
+
+
+__all__ = ["TrainingJob", "build_training", "init_distributed"]

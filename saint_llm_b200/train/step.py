@@ -37,9 +37,12 @@ class TrainStep:
         """tokens: (micro_batches, mb, T) on the device.  Returns the mean loss (device scalar)."""
         self.model.train()
         total = torch.zeros((), dtype=torch.float32, device=self.device)
+        last_hook = getattr(self.grad_sync, "before_last_backward", None)
         for i in range(self.micro_batches):
             with phase("forward"):
                 loss = self.loss_fn(self.model, tokens[i]) / self.micro_batches
+            if last_hook is not None and i == self.micro_batches - 1:
+                last_hook()
             with phase("backward"):
                 loss.backward()
             total += loss.detach()

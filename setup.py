@@ -28,10 +28,6 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("SV4_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
-if os.environ.get("SV4_BOUNDS_CHECK"):
-    NVCC_FLAGS.append("-DSV4_BOUNDS_CHECK=1")
-if os.environ.get("SV4_ATTN_TRACE"):  # per-phase clock64 trace of one attention CTA (development)
-    NVCC_FLAGS.append("-DSV4_ATTN_TRACE=1")
 
 os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 os.environ.setdefault("MAX_JOBS", str(max(4, (os.cpu_count() or 8))))
@@ -45,8 +41,7 @@ setup(
             name="saint_llm_b200._C",
             sources=SOURCES,
             include_dirs=[os.path.join(HERE, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"] + (["-DSV4_ATTN_TRACE=1"] if os.environ.get(
-                "SV4_ATTN_TRACE") else []), "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -82,7 +82,7 @@ def test_fused_attention_matches_reference(cuda, case):
         sel = torch.empty(b, t, (n + 31) // 32, dtype=torch.int32, device=cuda)
         from saint_llm_b200.ops import backend
 
-        backend.ext().csa_select_mask(top.contiguous(), n, sel)
+        backend.ext().csa_select_mask(top.contiguous(), n, sel, gemm.error_word(cuda))
     leaves = [x.detach().clone().requires_grad_(True) if x is not None else None for x in (q, k, v, kv, sink)]
     ml = torch.zeros((), device=cuda)
     out = fused_attention(leaves[0], leaves[1], leaves[2], window=window, sink=leaves[4], softcap=softcap,

@@ -84,7 +84,7 @@ def test_dispatch_simulation_mode():
     assert torch.equal(ep.combine_outputs_by_expert(plan.permuted_tokens, plan), tok)
 
 
-def _step_worker(rank: int, ws: int, port: int, zero: bool, q) -> None:
+def _step_worker(rank: int, ws: int, port: int, zero: bool, q, overlap: bool = False, micro: int = 1) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=ws)
@@ -103,21 +103,22 @@ def _step_worker(rank: int, ws: int, port: int, zero: bool, q) -> None:
         ref = SaintLLM(cfg)
         model = copy.deepcopy(ref)
         torch.manual_seed(11)
-        data = [torch.randint(0, cfg.vocab_size, (1, 1, 16)) for _ in range(ws)]
+        data = [torch.randint(0, cfg.vocab_size, (micro, 1, 16)) for _ in range(ws)]
         init = {n: p.detach().clone() for n, p in ref.named_parameters()}
         # reference: one process, the mean of every rank's loss, one optimizer step
         rp = attach_main_grads(ref)
         ropt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, qk_clip_enabled=False)
         rstep = TrainStep(ref, ropt, micro_batches=1, params=rp)
         for d in data:
-            (rstep.loss_fn(ref, d[0]) / ws).backward()
+            for i in range(micro):
+                (rstep.loss_fn(ref, d[i]) / (ws * micro)).backward()
         ropt.step()
         # expert + data parallel with (or without) hybrid ZeRO
-        sync = ep.setup_expert_parallel(model, transport="nccl", zero=zero)
+        sync = ep.setup_expert_parallel(model, transport="nccl", zero=zero, overlap_reduce=overlap)
         params = attach_main_grads(model)
         opt = MuonAdamW(*split_for_muon_adamw(model), lr=0.02, qk_clip_enabled=False)
         sync.configure_optimizer(opt)
-        step = TrainStep(model, opt, micro_batches=1, params=params, grad_sync=sync)
+        step = TrainStep(model, opt, micro_batches=micro, params=params, grad_sync=sync)
         step.run_device(data[rank])
         per = cfg.moe.routed_experts // ws
         refp = dict(ref.named_parameters())
@@ -134,12 +135,15 @@ def _step_worker(rank: int, ws: int, port: int, zero: bool, q) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("zero", [False, True])
-def test_ep_dp_step_matches_single_process(zero):
+@pytest.mark.parametrize("zero,overlap,micro", [(False, False, 1), (True, False, 1), (True, True, 2)])
+def test_ep_dp_step_matches_single_process(zero, overlap, micro):
+    """One step of expert + data parallel training (plain, hybrid ZeRO, and hybrid ZeRO
+    with the per-block reductions overlapped with the last micro-batch's backward)
+    equals one process stepping on the mean of every rank's loss."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_step_worker, args=(r, 2, port, zero, q)) for r in range(2)]
+    procs = [ctx.Process(target=_step_worker, args=(r, 2, port, zero, q, overlap, micro)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=180) for _ in range(2)]

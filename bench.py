@@ -95,15 +95,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def count_native_launches(fn) -> int:
-    """Number of this framework's kernels (namespace sv4) launched by one call of fn."""
+def count_native_launches(fn) -> tuple[int, float]:
+    """Kernels of this framework (namespace sv4) launched by one call of fn, and the summed
+    device time of every kernel of that call in ms (compared with the step time it shows how
+    much of the step the GPU spends between kernels)."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         fn()
         torch.cuda.synchronize()
-    return sum(1 for ev in prof.events()
-               if ev.device_type == torch.autograd.DeviceType.CUDA and "sv4::" in ev.name)
+    kernels = [ev for ev in prof.events() if ev.device_type == torch.autograd.DeviceType.CUDA]
+    busy_us = sum(ev.time_range.elapsed_us() for ev in kernels if "Memcpy" not in ev.name and "Memset" not in ev.name)
+    return sum(1 for ev in kernels if "sv4::" in ev.name), busy_us / 1000.0
 
 
 def run_config(args, world: int):
@@ -111,7 +114,9 @@ def run_config(args, world: int):
     from saint_llm_b200.config import RunConfig
 
     return RunConfig(ep=world, zero="dp" if args.no_zero else "hybrid_zero", fused_ep=args.ep_transport == "p2p",
-                     fused_zero=not args.no_overlap_reduce, micro_batch=args.micro_batch, seq_len=args.seq_len,
+                     fused_zero=not args.no_overlap_reduce, cuda_graphs=not args.no_cuda_graph,
+                     fp8_expert_cache=args.fp8_expert_cache,
+                     micro_batch=args.micro_batch, seq_len=args.seq_len,
                      grad_accum=args.seqs_per_gpu // args.micro_batch, lr=2.7e-4, adamw_lr=2.7e-4,
                      pg_timeout_s=600.0, seed=0)
 
@@ -215,7 +220,8 @@ def run_ours(args) -> dict:
     with PhaseRecorder(device) as rec:
         device_step()
     phases = rec.summary()
-    launches = count_native_launches(device_step) * args.steps
+    n_native, busy_ms = count_native_launches(device_step)
+    launches = n_native * args.steps
     tokens_per_step = world * args.seqs_per_gpu * args.seq_len
     result = {
         "metric": METRIC, "value": tokens_per_step / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
@@ -227,13 +233,17 @@ def run_ours(args) -> dict:
                    "parallelism": (f"ep{world}+dp{world}" + ("" if args.no_zero else "+zero")) if world > 1
                    else "single-gpu",
                    "ep_transport": args.ep_transport if world > 1 else None,
+                   "cuda_graph": bool(getattr(step, "_graph", None) is not None),
+                   "cuda_graph_error": getattr(step, "graph_error", None),
                    "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
+                   "fp8_expert_cache": args.fp8_expert_cache if args.linear_quant == "fp8" else None,
                    "l2": "inputs larger than L2 (the weights stream through HBM every step)",
                    "data_pool_batches": args.data_pool,
                    "loss": {"first_warmup": first_loss, "final": final_loss, "uniform_prediction": _uniform_loss(cfg),
                             "note": "mean over ranks; main CE + MTP-weighted CE + balance term"},
                    "final_loss": final_loss,
                    "phases_ms": phases,
+                   "kernel_busy_ms_per_step": round(busy_ms, 1),
                    "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
@@ -266,6 +276,10 @@ def main() -> None:
                     help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
     ap.add_argument("--no-zero", action="store_true",
                     help="N > 1: all-reduce replicated gradients and update them on every rank (no hybrid ZeRO)")
+    ap.add_argument("--fp8-expert-cache", default="auto", choices=["auto", "always", "never"],
+                    help="FP8: keep the routed experts' FP8 weight copies between steps (auto: when sharded by EP)")
+    ap.add_argument("--no-cuda-graph", action="store_true",
+                    help="N = 1: launch every kernel eagerly instead of replaying the captured micro-batch graph")
     ap.add_argument("--no-overlap-reduce", action="store_true",
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)

@@ -17,6 +17,9 @@ void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor
                 double alpha, double beta, torch::Tensor err, bool symmetric);
 // gemm_fp8.cu
 void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale);
+void fp8_gather_quant_rows(torch::Tensor h, torch::Tensor row_token, torch::Tensor q, torch::Tensor sf,
+                           torch::Tensor err);
+void fp8_quant_blocks_gu(torch::Tensor wg, torch::Tensor wu, torch::Tensor q, torch::Tensor sf);
 void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale);
 void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
               torch::Tensor err);
@@ -133,6 +136,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_axpby", &sv4::gemm_axpby);
   m.def("sym_mirror", &sv4::sym_mirror);
   m.def("fp8_quant_rows", &sv4::fp8_quant_rows);
+  m.def("fp8_gather_quant_rows", &sv4::fp8_gather_quant_rows);
+  m.def("fp8_quant_blocks_gu", &sv4::fp8_quant_blocks_gu);
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);

@@ -106,20 +106,29 @@ __device__ __forceinline__ int64_t sf_byte_offset(int64_t rb, int64_t kb, int64_
 }
 
 // 1 x 128 activation quantisation: one 16-lane group per block, 8 elements per lane.  Rows in
-// [M, Mpad) get the neutral scale byte (their A rows are zero-filled by TMA).
+// [M, Mpad) get the neutral scale byte (their A rows are zero-filled by TMA).  With a row map
+// (MoE gather fused into the quantisation) output row r takes source row row_map[r] (-1: a zero
+// padding row); a source row outside [-1, src_rows) records kErrBounds and is zero.
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M,
                                                          int Mpad, int K, uint8_t* __restrict__ q, int64_t ldq,
-                                                         uint8_t* __restrict__ sf, float* __restrict__ scale) {
+                                                         uint8_t* __restrict__ sf, float* __restrict__ scale,
+                                                         const int* __restrict__ row_map, int src_rows, int* err) {
   const int kblocks = K / 128;
   const int64_t g = static_cast<int64_t>(blockIdx.x) * 16 + threadIdx.x / 16;
   const int sub = threadIdx.x & 15;
   const bool active = g < static_cast<int64_t>(Mpad) * kblocks;
   const int row = active ? static_cast<int>(g / kblocks) : 0;
   const int kb = active ? static_cast<int>(g % kblocks) : 0;
-  const bool live = active && row < M;
+  const bool in_rows = active && row < M;
+  int64_t src = row;
+  if (row_map != nullptr && in_rows) {
+    const int t = row_map[row];
+    src = (sub == 0 && kb == 0) ? (index_ok(t, -1, src_rows, err) ? t : -1) : ((t >= -1 && t < src_rows) ? t : -1);
+  }
+  const bool live = in_rows && src >= 0;
   float v[8];
   if (live) {
-    unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + kb * 128 + sub * 8), v);
+    unpack8(*reinterpret_cast<const uint4*>(x + src * ldx + kb * 128 + sub * 8), v);
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
@@ -130,27 +139,37 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const int e = pow2_exponent(amax);
-  if (live) *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v, exp2_int(-e));
+  if (in_rows) *reinterpret_cast<uint2*>(q + row * ldq + kb * 128 + sub * 8) = quant8x(v, exp2_int(-e));
   if (active && sub == 0) {
     sf[sf_byte_offset(row / 128, kb, sf_groups(K), row & 127)] = static_cast<uint8_t>(e + 127);
-    if (live && scale != nullptr) scale[static_cast<int64_t>(row) * kblocks + kb] = exp2_int(e);
+    if (in_rows && scale != nullptr) scale[static_cast<int64_t>(row) * kblocks + kb] = exp2_int(e);
   }
 }
 
 // 128 x 128 weight quantisation: one CTA per block; lane group (warp w, half h) covers rows
-// {16 i + 2 w + h}, 16 lanes x 8 columns.
-__global__ void __launch_bounds__(256) quant_blocks_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw, int K,
-                                                           uint8_t* __restrict__ q, int64_t ldq,
+// {16 i + 2 w + h}, 16 lanes x 8 columns.  With a second source (gate / up pair of a SwiGLU
+// expert pool, each (E * I, K) with I % 64 == 0) the quantised matrix is the interleave the
+// SwiGLU epilogue reads: block row nb of expert e = nb / (2I / 128) holds 64 gate rows then the
+// matching 64 up rows (rows j * 64 .. j * 64 + 63 of that expert, j = nb mod (2I / 128)).
+__global__ void __launch_bounds__(256) quant_blocks_kernel(const __nv_bfloat16* __restrict__ w,
+                                                           const __nv_bfloat16* __restrict__ w_up, int I,
+                                                           int64_t ldw, int K, uint8_t* __restrict__ q, int64_t ldq,
                                                            uint8_t* __restrict__ sf, float* __restrict__ scale) {
   __shared__ float red[8];
   const int nb = blockIdx.y, kb = blockIdx.x, kblocks = K / 128;
   const int r0 = threadIdx.x / 16, sub = threadIdx.x & 15;
+  auto src_row = [&](int r) -> const __nv_bfloat16* {
+    if (w_up == nullptr) return w + (static_cast<int64_t>(nb) * 128 + r) * ldw;
+    const int per = 2 * I / 128;
+    const int64_t e = nb / per, j = nb % per;
+    const int64_t row = e * I + j * 64 + (r & 63);
+    return (r < 64 ? w : w_up) + row * ldw;
+  };
   float v[8][8];
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int64_t row = static_cast<int64_t>(nb) * 128 + r0 + 16 * i;
-    unpack8(*reinterpret_cast<const uint4*>(w + row * ldw + kb * 128 + sub * 8), v[i]);
+    unpack8(*reinterpret_cast<const uint4*>(src_row(r0 + 16 * i) + kb * 128 + sub * 8), v[i]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
   }
@@ -489,7 +508,30 @@ void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::opt
   quant_rows_kernel<<<static_cast<unsigned>((groups + 15) / 16), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), static_cast<int>(M), static_cast<int>(Mpad),
       static_cast<int>(K), reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0),
-      reinterpret_cast<uint8_t*>(sf.data_ptr()), sp);
+      reinterpret_cast<uint8_t*>(sf.data_ptr()), sp, nullptr, 0, nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// MoE gather fused into the 1 x 128 quantisation: q[r] = quant(h[row_token[r]]) (zero rows
+// for -1), sf in the GEMM's scale-factor layout.  h (T, K) bf16; q (M, K) bytes.
+void fp8_gather_quant_rows(torch::Tensor h, torch::Tensor row_token, torch::Tensor q, torch::Tensor sf,
+                           torch::Tensor err) {
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.dim() == 2 && h.stride(1) == 1, "h: 2-D bf16, unit inner stride");
+  const int64_t K = h.size(1), M = q.size(0);
+  TORCH_CHECK(K % 128 == 0 && h.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0,
+              "h rows: K % 128 == 0, 16-byte aligned");
+  check_fp8_operand(q, "q");
+  TORCH_CHECK(q.size(1) == K && row_token.scalar_type() == at::kInt && row_token.numel() >= M, "q / row_token");
+  const int64_t Mpad = (M + 127) / 128 * 128;
+  TORCH_CHECK(sf.numel() >= Mpad / 128 * sf_groups(K) * kSfChunk && sf.element_size() == 1, "sf size");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(h.device());
+  const int64_t groups = Mpad * (K / 128);
+  quant_rows_kernel<<<static_cast<unsigned>((groups + 15) / 16), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), h.stride(0), static_cast<int>(M), static_cast<int>(Mpad),
+      static_cast<int>(K), reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0),
+      reinterpret_cast<uint8_t*>(sf.data_ptr()), nullptr, row_token.data_ptr<int>(), static_cast<int>(h.size(0)),
+      err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -512,8 +554,29 @@ void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::o
   c10::cuda::CUDAGuard guard(w.device());
   const dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
   quant_blocks_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), w.stride(0), static_cast<int>(K),
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), nullptr, 0, w.stride(0), static_cast<int>(K),
       reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0), reinterpret_cast<uint8_t*>(sf.data_ptr()), sp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// SwiGLU expert pool gate / up weights (each (E, I, K) bf16, contiguous) -> q (E * 2I, K) in
+// the interleaved 64-row group layout of the FP8 SwiGLU epilogue, 128 x 128 block scales.
+void fp8_quant_blocks_gu(torch::Tensor wg, torch::Tensor wu, torch::Tensor q, torch::Tensor sf) {
+  TORCH_CHECK(wg.scalar_type() == at::kBFloat16 && wu.scalar_type() == at::kBFloat16 && wg.is_contiguous() &&
+                  wu.is_contiguous() && wg.sizes() == wu.sizes() && wg.dim() == 3, "wg / wu: (E, I, K) bf16");
+  const int64_t E = wg.size(0), I = wg.size(1), K = wg.size(2);
+  TORCH_CHECK(I % 64 == 0 && K % 128 == 0, "I % 64 == 0 and K % 128 == 0");
+  check_fp8_operand(q, "q");
+  TORCH_CHECK(q.size(0) == E * 2 * I && q.size(1) == K, "q shape (E * 2I, K)");
+  const int64_t N = E * 2 * I;
+  TORCH_CHECK(sf.numel() >= N / 128 * sf_groups(K) * kSfChunk && sf.element_size() == 1, "sf size");
+  if (N == 0) return;
+  c10::cuda::CUDAGuard guard(wg.device());
+  const dim3 grid(static_cast<unsigned>(K / 128), static_cast<unsigned>(N / 128));
+  quant_blocks_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(wg.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(wu.data_ptr()),
+      static_cast<int>(I), K, static_cast<int>(K), reinterpret_cast<uint8_t*>(q.data_ptr()), q.stride(0),
+      reinterpret_cast<uint8_t*>(sf.data_ptr()), nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

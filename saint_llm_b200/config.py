@@ -316,6 +316,12 @@ class RunConfig(_Frozen):
     kernels: Literal["native", "torch"] = "native"
     fused_ep: bool = True
     fused_zero: bool = True
+    # single GPU: replay each micro-batch's forward + backward from one captured CUDA graph
+    cuda_graphs: bool = True
+    # FP8 training (linear_quant="fp8"): keep the routed experts' FP8 weight copies between
+    # steps ("always"), quantise them per forward ("never"), or cache them only when expert
+    # parallelism shards the pools ("auto": an unsharded 16B pool's copy does not fit)
+    fp8_expert_cache: Literal["auto", "always", "never"] = "auto"
     # training loop
     micro_batch: int = 1
     seq_len: int = 4096

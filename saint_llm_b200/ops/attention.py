@@ -35,14 +35,22 @@ def _bf16(t: Tensor) -> Tensor:
 
 
 class _FusedLinearFn(torch.autograd.Function):
-    """y = x [W_0; W_1; ...]^T with per-weight gradients (into main_grad when present)."""
+    """y = x [W_0; W_1; ...]^T with per-weight gradients (into main_grad when present).
+
+    ``fp8_owner`` (a module): the forward runs the block-scaled FP8 GEMM against the joint
+    weight's FP8 copy cached on that module; the backward stays bf16 (straight-through)."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, *weights: Tensor) -> Tensor:  # type: ignore[override]
+    def forward(ctx, x: Tensor, fp8_owner: nn.Module | None, *weights: Tensor) -> Tensor:  # type: ignore[override]
         k = x.shape[-1]
         x2 = _bf16(x.reshape(-1, k))
         w = torch.cat([_bf16(wi) for wi in weights], 0)
-        y = gemm.gemm_nt(x2, w)
+        if fp8_owner is not None:
+            from saint_llm_b200.ops import fp8
+
+            y = fp8.gemm(fp8.quantize_rows(x2), fp8.cached_weight(fp8_owner, "_fp8_fused", list(weights)))
+        else:
+            y = gemm.gemm_nt(x2, w)
         ctx.save_for_backward(x2, w, *weights)
         ctx.xshape = x.shape
         return y.view(*x.shape[:-1], w.shape[0])
@@ -64,11 +72,16 @@ class _FusedLinearFn(torch.autograd.Function):
                     mg.add_(part)
                 else:
                     grads[i] = part.to(wi.dtype)
-        return (dx, *grads)
+        return (dx, None, *grads)
 
 
-def fused_linear(x: Tensor, weights: list[Tensor]) -> Tensor:
-    return _FusedLinearFn.apply(x, *weights)
+def fused_linear(x: Tensor, weights: list[Tensor], fp8_owner: nn.Module | None = None) -> Tensor:
+    return _FusedLinearFn.apply(x, fp8_owner, *weights)
+
+
+def uses_fp8(linear: nn.Module) -> bool:
+    """Whether a projection module runs the real block-scaled FP8 forward on CUDA."""
+    return bool(getattr(linear, "use_real_fp8_gemm", False))
 
 
 def _pool(c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int) -> Tensor:
@@ -200,11 +213,15 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
     if kind != "swa":
         ws += [layer.kv_compressor.w_b_kv.weight, layer.kv_compressor.w_b_z.weight]
         sizes += [d, d]
-    parts = torch.split(fused_linear(hb, ws), sizes, dim=-1)
+    fp8_proj = uses_fp8(layer.q_compressor) and all(w.shape[0] % 128 == 0 for w in ws) and hb.shape[-1] % 128 == 0
+    parts = torch.split(fused_linear(hb, ws, layer if fp8_proj else None), sizes, dim=-1)
     c_q, k, v = parts[0], parts[1], parts[2]
     cos, sin = rope_tables(t, rd, cfg.rope_theta, h.device)
     cos_b, sin_b = cos.repeat(b, 1), sin.repeat(b, 1)
-    q = lin.linear(c_q, layer.q_up.weight).reshape(b * t, H, d)
+    if uses_fp8(layer.q_up) and lin.fp8_shape_ok(layer.q_up.in_features, layer.q_up.out_features):
+        q = lin.fp8_linear(c_q, layer.q_up.weight).reshape(b * t, H, d)
+    else:
+        q = lin.linear(c_q, layer.q_up.weight).reshape(b * t, H, d)
     q = rope_norm(q, layer.q_norm.weight, cos_b, sin_b, rd, norm_first=False, eps=layer.q_norm.eps)
     k = rope_norm(k.reshape(b * t, 1, d), layer.k_norm.weight, cos_b, sin_b, rd,
                   norm_first=(kind == "csa"), eps=layer.k_norm.eps).view(b, t, d)

@@ -123,3 +123,142 @@ def linear(x: Tensor, w: Tensor) -> Tensor:
 
 
 __all__ = ["BLOCK", "Fp8Operand", "gemm", "linear", "quantize_blocks", "quantize_rows"]
+
+
+# ---------------------------------------------------------------- training weight cache
+_EPOCH = [0]
+
+
+def bump_weight_epoch() -> None:
+    """Mark every cached FP8 weight stale (the optimizer updated the bf16 weights in place;
+    native optimizer kernels do not move torch's version counters)."""
+    _EPOCH[0] += 1
+
+
+def weight_epoch() -> int:
+    return _EPOCH[0]
+
+
+class Fp8WeightCache:
+    """Block-scaled FP8 copy of one weight matrix (or a fixed arrangement of several) kept in
+    persistent buffers and re-quantised in place when the weights change.
+
+    ``kind``: "rows" -- ``sources`` stacked along the output dimension (2-D (N_i, K) each, or
+    one 3-D (E, N, K) pool flattened to (E * N, K)); "cols" -- 2-D (N, K_i) sources joined
+    along K; "gu" -- the gate and up weights of a SwiGLU pool (two (E, I, K) tensors, or E
+    gate then E up (I, K) matrices), quantised into the interleaved 64-row layout of the FP8
+    SwiGLU epilogue.  Every piece spans whole 128 x 128 blocks, so quantising the arrangement
+    equals quantising each piece alone.
+
+    The buffers never move, so a CUDA graph that reads them stays valid across steps: the
+    training step refreshes every cache once after the optimizer (``refresh_all``), outside
+    any capture.  ``get()`` refreshes lazily when the weights changed since the last refresh
+    (the epoch moved, or a weight's version counter did) and no capture is running."""
+
+    _live: list = []
+
+    def __init__(self, sources: list[Tensor], kind: str = "rows") -> None:
+        import weakref
+
+        self.sources = list(sources)
+        self.kind = kind
+        dev = sources[0].device
+        if kind == "gu":
+            if sources[0].dim() == 3:
+                e, i, k = sources[0].shape
+            else:
+                e, (i, k) = len(sources) // 2, sources[0].shape
+            n = e * 2 * i
+        elif kind == "cols":
+            n, k = sources[0].shape[0], sum(s.shape[1] for s in sources)
+        else:
+            k = sources[0].shape[-1]
+            n = sum(s.numel() // k for s in sources)
+        if n % BLOCK or k % BLOCK:
+            raise ValueError(f"FP8 weight cache needs rows and K multiples of 128 (got {n} x {k})")
+        self.shape = (n, k)
+        self.q = torch.empty((n, k), dtype=torch.uint8, device=dev)
+        self.sf = torch.empty(backend.ext().fp8_sf_bytes(n, k), dtype=torch.uint8, device=dev)
+        self._stamp: tuple | None = None
+        Fp8WeightCache._live.append(weakref.ref(self))
+
+    def _current(self) -> tuple:
+        return (_EPOCH[0], *(s._version for s in self.sources))
+
+    def refresh(self) -> None:
+        ext = backend.ext()
+        with torch.no_grad():
+            src = [s.detach().to(torch.bfloat16) for s in self.sources]
+            if self.kind == "gu":
+                if src[0].dim() == 3:
+                    wg, wu = src[0].contiguous(), src[1].contiguous()
+                else:
+                    e = len(src) // 2
+                    wg, wu = torch.stack(src[:e]), torch.stack(src[e:])
+                ext.fp8_quant_blocks_gu(wg, wu, self.q, self.sf)
+                self._stamp = self._current()
+                return
+            if self.kind == "cols":
+                w = src[0].contiguous() if len(src) == 1 else torch.cat(src, 1)
+            else:
+                k = src[0].shape[-1]
+                flat = [t.reshape(-1, k) for t in src]
+                w = flat[0].contiguous() if len(flat) == 1 else torch.cat(flat, 0)
+            ext.fp8_quant_blocks(w, self.q, self.sf, None)
+        self._stamp = self._current()
+
+    def get(self) -> Fp8Operand:
+        if self._stamp != self._current() and not torch.cuda.is_current_stream_capturing():
+            self.refresh()
+        return Fp8Operand(self.q, torch.empty(0), self.sf, "blocks")
+
+    @classmethod
+    def refresh_all(cls) -> int:
+        """Re-quantise every live cache whose weights changed; returns how many."""
+        n = 0
+        alive = []
+        for ref in cls._live:
+            c = ref()
+            if c is None:
+                continue
+            alive.append(ref)
+            if c._stamp != c._current():
+                c.refresh()
+                n += 1
+        cls._live = alive
+        return n
+
+
+def transient_weight(sources: list[Tensor], kind: str = "rows") -> Fp8Operand:
+    """Quantise now into fresh buffers (no cache): for weights whose FP8 copy would not fit
+    next to the training state."""
+    c = Fp8WeightCache(sources, kind)
+    c.refresh()
+    Fp8WeightCache._live.pop()  # not tracked: it dies with the caller
+    return Fp8Operand(c.q, torch.empty(0), c.sf, "blocks")
+
+
+def cached_weight(owner: object, attr: str, sources: list[Tensor], kind: str = "rows") -> Fp8Operand:
+    """The FP8 copy of ``sources`` cached on ``owner`` (a module) under ``attr``."""
+    cache = getattr(owner, attr, None)
+    if cache is None or len(cache.sources) != len(sources) or any(
+            a is not b for a, b in zip(cache.sources, sources, strict=True)):
+        cache = Fp8WeightCache(sources, kind)
+        object.__setattr__(owner, attr, cache)  # not a submodule / parameter
+    return cache.get()
+
+
+def gather_quantize_rows(h: Tensor, row_token: Tensor, rows: int) -> Fp8Operand:
+    """1 x 128 quantisation of the gathered rows ``h[row_token[r]]`` (zero for -1), r < rows."""
+    from saint_llm_b200.ops.gemm import error_word
+
+    h = h.to(torch.bfloat16).contiguous()
+    k = h.shape[1]
+    q = torch.empty((rows, k), dtype=torch.uint8, device=h.device)
+    sf = torch.empty(backend.ext().fp8_sf_bytes(rows, k), dtype=torch.uint8, device=h.device)
+    backend.ext().fp8_gather_quant_rows(h, row_token, q, sf, error_word(h.device))
+    return Fp8Operand(q, torch.empty(0), sf, "rows")
+
+
+__all__ += ["Fp8WeightCache", "bump_weight_epoch", "cached_weight", "gather_quantize_rows", "transient_weight",
+            "weight_epoch"]

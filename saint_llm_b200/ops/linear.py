@@ -10,6 +10,8 @@ no bf16 rounding of gradients across micro-batches and no extra add kernel.  Wit
 blocks, power-of-two scales): both operands are quantised by native kernels and the
 product runs on the block-scaled FP8 tensor-core GEMM (``ops.fp8``); the backward is the
 straight-through estimator in bf16, as in the reference (``kernels/fp8_gemm.py:71-83``).
+The weight's FP8 copy is cached on the parameter (``ops.fp8.Fp8WeightCache``) and
+re-quantised once per optimizer step, not once per micro-batch.
 """
 
 from __future__ import annotations
@@ -76,7 +78,7 @@ class _Fp8LinearFn(torch.autograd.Function):
     def forward(ctx, x: Tensor, weight: Tensor, bias: Tensor | None) -> Tensor:  # type: ignore[override]
         k = x.shape[-1]
         x2 = x.reshape(-1, k)
-        y = fp8.gemm(fp8.quantize_rows(x2), fp8.quantize_blocks(weight))
+        y = fp8.gemm(fp8.quantize_rows(x2), fp8.cached_weight(weight, "_fp8_cache", [weight]))
         if bias is not None:
             y = y + bias.to(y.dtype)
         ctx.save_for_backward(_bf16(x2), weight)

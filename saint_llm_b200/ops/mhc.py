@@ -22,6 +22,21 @@ def _bf16c(t: Tensor) -> Tensor:
     return (t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)).contiguous()
 
 
+_GROUPS: dict[tuple[int, torch.device], Tensor] = {}
+
+
+def _column_groups(n: int, dev: torch.device) -> Tensor:
+    """Group id (0 pre, 1 res, 2 post) of each gate column, cached per device so the
+    backward makes no host-to-device copy (CUDA-graph capturable)."""
+    key = (n, dev)
+    g = _GROUPS.get(key)
+    if g is None:
+        g = torch.cat([torch.full((n,), 0, dtype=torch.long), torch.full((n * n,), 1, dtype=torch.long),
+                       torch.full((n,), 2, dtype=torch.long)]).to(dev)
+        _GROUPS[key] = g
+    return g
+
+
 class _SplitFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, X: Tensor, w_fold: Tensor, alpha: Tensor, s_pre: Tensor, s_res: Tensor,  # type: ignore[override]
@@ -69,7 +84,7 @@ class _SplitFn(torch.autograd.Function):
         dz = torch.empty(T, P, dtype=torch.float32, device=dev)
         ext.mhc_gates_bwd(p, al, sp, sr, so, da.contiguous(), dbf, dcf, dz, n, iters)
         # z = alpha_g * p + s ; column groups: [0, n) pre, [n, n+n^2) res, [n+n^2, P) post
-        grp = torch.tensor([0] * n + [1] * (n * n) + [2] * n, dtype=torch.long, device=dev)
+        grp = _column_groups(n, dev)
         dp = dz * al[grp]
         d_alpha = torch.zeros(3, dtype=torch.float32, device=dev).index_add_(0, grp, (dz * p).sum(0))
         dzs = dz.sum(0)

@@ -76,10 +76,59 @@ def _empty(dev: torch.device) -> Tensor:
     return t
 
 
+def fp8_expert_weights(pool: nn.Module) -> tuple:
+    """Block-scaled FP8 gate/up (interleaved 64-row groups) and down weights of a routed
+    expert pool: cached on the pool when ``pool.fp8_weight_cache`` says so ("always", or
+    "auto" for a pool sharded by expert parallelism, whose FP8 copy is small), otherwise
+    quantised for this call only (a whole unsharded pool's FP8 copy, 15.5 GB for config 3,
+    does not fit on one GPU next to its bf16 weights, fp32 gradients and Muon state)."""
+    from saint_llm_b200.ops import fp8
+
+    policy = getattr(pool, "fp8_weight_cache", "auto")
+    sharded = getattr(pool, "n_global_experts", pool.n_experts) > pool.n_experts
+    wg, wu, wd = pool.gate_weight, pool.up_weight, pool.down_weight
+    if policy == "always" or (policy == "auto" and sharded):
+        return (fp8.cached_weight(pool, "_fp8_gu", [wg, wu], "gu"),
+                fp8.cached_weight(pool, "_fp8_down", [wd], "rows"))
+    return fp8.transient_weight([wg, wu], "gu"), fp8.transient_weight([wd], "rows")
+
+
+def fp8_swiglu_experts(xq, gu, down, plan, D: int, I: int, clamps, err,
+                       y_out: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """FP8 forward of a grouped SwiGLU expert pool over quantised rows ``xq`` laid out by
+    ``plan`` (``RoutePlan`` or an owner-side segment plan).  Returns (act, pre, y): the
+    bf16 SwiGLU output and pre-activations [gate | up] (saved for the bf16 backward) and the
+    down projection (written into ``y_out`` when given: contiguous, one row per row of xq)."""
+    from saint_llm_b200.ops import fp8
+
+    ext = backend.ext()
+    rows = xq.q.shape[0]
+    dev = xq.q.device
+    gmax, lo, hi = clamps
+    act = torch.empty(rows, I, dtype=torch.bfloat16, device=dev)
+    pre = torch.empty(rows, 2 * I, dtype=torch.bfloat16, device=dev)
+    pr, tot, n = plan.problems(6, D, I)
+    ext.grouped_gemm_fp8(0, xq.q, xq.sf, gu.q, gu.sf, act, pre, pr, tot, n, 2 * I, gmax, lo, hi, err)
+    aq = fp8.quantize_rows(act)
+    y = torch.empty(rows, D, dtype=torch.bfloat16, device=dev) if y_out is None else y_out
+    pr, tot, n = plan.problems(7, D, I)
+    ext.grouped_gemm_fp8(1, aq.q, aq.sf, down.q, down.sf, y, None, pr, tot, n, D, 0.0, 0.0, 0.0, err)
+    return act, pre, y
+
+
+def fp8_pool_ok(pool: nn.Module) -> bool:
+    """The pool trains with the block-scaled FP8 forward (``linear_quant == "fp8"``, CUDA
+    shapes that fit the FP8 GEMM: I and D multiples of 128)."""
+    if getattr(pool, "linear_quant", "bf16") != "fp8":
+        return False
+    _, i, d = pool.gate_weight.shape
+    return i % 128 == 0 and d % 128 == 0
+
+
 class _RoutedExpertsFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h: Tensor, idx: Tensor, gate: Tensor, wg: Tensor, wu: Tensor, wd: Tensor,  # type: ignore[override]
-                clamps: tuple[float, float, float]) -> Tensor:
+                clamps: tuple[float, float, float], pool: nn.Module | None = None) -> Tensor:
         ext = backend.ext()
         dev = h.device
         T, D = h.shape
@@ -89,17 +138,26 @@ class _RoutedExpertsFn(torch.autograd.Function):
         err = gemm.error_word(dev)
         plan = RoutePlan(idx, E, k)
         hb = _bf16c(h)
-        x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-        ext.moe_gather(hb, plan.row_token, x_p, err)
-        wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
-        act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
-        pre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
-        e0 = _empty(dev)
-        pr, tot, n = plan.problems(0, D, I)
-        ext.grouped_gemm(0, x_p, wgb, wub, act, pre, e0, pr, tot, n, gmax, lo, hi, 0, False, err)
-        y = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-        pr, tot, n = plan.problems(1, D, I)
-        ext.grouped_gemm(1, act, wdb, wdb, y, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+        if pool is not None:  # block-scaled FP8 forward, bf16 straight-through backward
+            from saint_llm_b200.ops import fp8
+
+            gu, down = fp8_expert_weights(pool)
+            xq = fp8.gather_quantize_rows(hb, plan.row_token, plan.m_cap)
+            act, pre, y = fp8_swiglu_experts(xq, gu, down, plan, D, I, clamps, err)
+            del xq, gu, down
+        else:
+            x_p = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+            ext.moe_gather(hb, plan.row_token, x_p, err)
+            wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
+            act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
+            pre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
+            e0 = _empty(dev)
+            pr, tot, n = plan.problems(0, D, I)
+            ext.grouped_gemm(0, x_p, wgb, wub, act, pre, e0, pr, tot, n, gmax, lo, hi, 0, False, err)
+            y = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
+            pr, tot, n = plan.problems(1, D, I)
+            ext.grouped_gemm(1, act, wdb, wdb, y, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+            del x_p
         out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
         gf = gate.float().contiguous()
         ext.moe_combine(y, plan.pos, gf, out, err)
@@ -155,7 +213,7 @@ class _RoutedExpertsFn(torch.autograd.Function):
         dwg = None if acc_gu else joint[0].to(wg.dtype)
         dwu = None if acc_gu else joint[1].to(wu.dtype)
         dwd = None if acc_d else dwd_buf.to(wd.dtype)
-        return dh, None, dgate, dwg, dwu, dwd, None
+        return dh, None, dgate, dwg, dwu, dwd, None, None
 
 
 class _SharedSwiGLUFn(torch.autograd.Function):
@@ -198,27 +256,53 @@ def _cat(ws: list[Tensor], dim: int) -> Tensor:
     return torch.cat([_bf16c(w.detach()) for w in ws], dim=dim)
 
 
+class _DensePlan:
+    """Problem table of one dense (T-row) SwiGLU / down product for the FP8 grouped GEMM."""
+
+    def __init__(self, rows: int, device: torch.device) -> None:
+        self.seg_start = torch.zeros(1, dtype=torch.int32, device=device)
+        self.seg_rows = torch.full((1,), rows, dtype=torch.int32, device=device)
+
+    def problems(self, mode: int, D: int, I: int) -> tuple[Tensor, Tensor, int]:
+        probs = _prob_table(1, self.seg_start.device)
+        total = torch.empty(1, dtype=torch.int32, device=self.seg_start.device)
+        backend.ext().build_moe_problems(self.seg_start, self.seg_rows, mode, D, I, probs, total)
+        return probs, total, 1
+
+
 class _SharedGroupFn(torch.autograd.Function):
     """Several shared SwiGLU experts as one: sum_e SwiGLU_e(h) = [Wd_1 .. Wd_n] SwiGLU(h;
     [Wg_1; ..; Wg_n], [Wu_1; ..; Wu_n]) because the activation is element-wise, so the
     forward is one fused SwiGLU GEMM (intermediate width sum I_e) and one down GEMM, and the
     backward one dgrad per GEMM (and one add fewer per extra expert in each direction);
-    weight gradients still go to each expert's own weights."""
+    weight gradients still go to each expert's own weights.
+
+    ``fp8_owner`` (the first expert module): the forward runs the block-scaled FP8 GEMMs
+    against the joint weights' FP8 copies cached on that module; the backward is bf16."""
 
     @staticmethod
-    def forward(ctx, h: Tensor, clamps: tuple[float, float, float], *ws: Tensor):  # type: ignore[override]
+    def forward(ctx, h: Tensor, clamps: tuple[float, float, float], fp8_owner: nn.Module | None,  # type: ignore[override]
+                *ws: Tensor) -> Tensor:
         ext = backend.ext()
         dev = h.device
         n = len(ws) // 3
         wgs, wus, wds = list(ws[:n]), list(ws[n:2 * n]), list(ws[2 * n:])
-        wg, wu, wd = _cat(wgs, 0), _cat(wus, 0), _cat(wds, 1)
         T = h.shape[0]
-        I = wg.shape[0]
+        I = sum(w.shape[0] for w in wgs)
         hb = _bf16c(h)
-        act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
-        pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
-        ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
-        y = gemm.gemm_nt(act, wd)
+        if fp8_owner is not None:
+            from saint_llm_b200.ops import fp8
+
+            gu = fp8.cached_weight(fp8_owner, "_fp8_shared_gu", wgs + wus, "gu")
+            down = fp8.cached_weight(fp8_owner, "_fp8_shared_down", wds, "cols")
+            act, pre, y = fp8_swiglu_experts(fp8.quantize_rows(hb), gu, down, _DensePlan(T, dev), hb.shape[1], I,
+                                             clamps, gemm.error_word(dev))
+        else:
+            wg, wu, wd = _cat(wgs, 0), _cat(wus, 0), _cat(wds, 1)
+            act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+            pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
+            ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
+            y = gemm.gemm_nt(act, wd)
         ctx.save_for_backward(hb, act, pre, *ws)
         ctx.clamps, ctx.n = clamps, n
         return y
@@ -248,7 +332,7 @@ class _SharedGroupFn(torch.autograd.Function):
             dd.append(accumulate_weight_grad(wds[e], dyb, act[:, off:off + ie]))
             off += ie
         grads = dg + du + dd
-        return (dh, None, *grads)
+        return (dh, None, None, *grads)
 
 
 def shared_experts(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> Tensor | None:
@@ -265,7 +349,9 @@ def shared_experts(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> Tenso
             out = out + shared_swiglu(h, e)
         return out
     ws = [e.gate_proj.weight for e in ex] + [e.up_proj.weight for e in ex] + [e.down_proj.weight for e in ex]
-    return _SharedGroupFn.apply(h, clamps.pop(), *ws)
+    fp8_ok = (getattr(ex[0].gate_proj, "use_real_fp8_gemm", False) and h.shape[-1] % 128 == 0
+              and all(e.gate_proj.weight.shape[0] % 128 == 0 for e in ex))
+    return _SharedGroupFn.apply(h, clamps.pop(), ex[0] if fp8_ok else None, *ws)
 
 
 def shared_swiglu(h: Tensor, expert: nn.Module) -> Tensor:
@@ -275,10 +361,11 @@ def shared_swiglu(h: Tensor, expert: nn.Module) -> Tensor:
 
 
 def routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module) -> Tensor:
-    """h (T, D); idx / gate (T, k): sum_j gate[t,j] * expert_{idx[t,j]}(h[t]) over the local expert pool."""
+    """h (T, D); idx / gate (T, k): sum_j gate[t,j] * expert_{idx[t,j]}(h[t]) over the local expert pool
+    (block-scaled FP8 forward when the pool's ``linear_quant`` is "fp8")."""
     return _RoutedExpertsFn.apply(h, idx, gate, experts.gate_weight, experts.up_weight, experts.down_weight,
                                   (float(experts.clamp_gate_max), float(experts.clamp_linear[0]),
-                                   float(experts.clamp_linear[1])))
+                                   float(experts.clamp_linear[1])), experts if fp8_pool_ok(experts) else None)
 
 
 class Fp8ExpertWeights:

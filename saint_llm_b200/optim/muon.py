@@ -291,6 +291,9 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
                 self._adamw_group_step(group)
         if self.qk_clip_enabled and self._qk_clip_layers:
             self._apply_qk_clip()
+        from saint_llm_b200.ops.fp8 import bump_weight_epoch
+
+        bump_weight_epoch()  # cached FP8 weight copies are stale now
         return loss
 
     @torch.no_grad()

@@ -307,6 +307,9 @@ class ParallelSync:
     def post_step(self) -> None:
         if self.zero is not None:
             self.zero.broadcast_params()
+            from saint_llm_b200.ops.fp8 import bump_weight_epoch
+
+            bump_weight_epoch()  # broadcast weights replace the local ones
 
 
 def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",

@@ -224,8 +224,9 @@ class EPCall:
     emulation of several ranks runs each stage for every rank before the next one."""
 
     def __init__(self, comm: P2PExpertComm, layer_key: int, h: Tensor, idx: Tensor, gate: Tensor, wg: Tensor,
-                 wu: Tensor, wd: Tensor, clamps: tuple[float, float, float]) -> None:
+                 wu: Tensor, wd: Tensor, clamps: tuple[float, float, float], fp8_pool: nn.Module | None = None) -> None:
         self.comm, self.layer_key, self.clamps = comm, layer_key, clamps
+        self.fp8_pool = fp8_pool  # block-scaled FP8 forward of the owner-side experts
         self.hb = _bf16c(h)
         self.T, self.D = h.shape
         self.idx = idx
@@ -271,15 +272,24 @@ class EPCall:
         x_rows = xr[:self.R].clone()
         self.x_saved = x_rows
         plan = _SegPlan(self.seg_start, self.seg_pad)
-        e0 = _empty(self.dev)
-        self.act = torch.empty(self.R, I, dtype=torch.bfloat16, device=self.dev)
-        self.pre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=self.dev)
-        pr, tot, n = plan.problems(0, D, I)
-        ext.grouped_gemm(0, x_rows, _bf16c(self.wg), _bf16c(self.wu), self.act, self.pre, e0, pr, tot, n, gmax, lo,
-                         hi, 0, False, self.err)
-        wdb = _bf16c(self.wd)
-        pr, tot, n = plan.problems(1, D, I)
-        ext.grouped_gemm(1, self.act, wdb, wdb, c.rows(c.y), e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, self.err)
+        if self.fp8_pool is not None:
+            from saint_llm_b200.ops import fp8
+            from saint_llm_b200.ops.moe_native import fp8_expert_weights, fp8_swiglu_experts
+
+            gu, down = fp8_expert_weights(self.fp8_pool)
+            self.act, self.pre, _ = fp8_swiglu_experts(fp8.quantize_rows(x_rows), gu, down, plan, D, I, self.clamps,
+                                                       self.err, y_out=c.rows(c.y)[:self.R])
+        else:
+            e0 = _empty(self.dev)
+            self.act = torch.empty(self.R, I, dtype=torch.bfloat16, device=self.dev)
+            self.pre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=self.dev)
+            pr, tot, n = plan.problems(0, D, I)
+            ext.grouped_gemm(0, x_rows, _bf16c(self.wg), _bf16c(self.wu), self.act, self.pre, e0, pr, tot, n, gmax,
+                             lo, hi, 0, False, self.err)
+            wdb = _bf16c(self.wd)
+            pr, tot, n = plan.problems(1, D, I)
+            ext.grouped_gemm(1, self.act, wdb, wdb, c.rows(c.y), e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False,
+                             self.err)
         self.e_y = c.next_epoch(PH_Y)
         ext.ep_signal(c.flags.ptrs, PH_Y, c.rank, self.e_y)
 
@@ -358,8 +368,9 @@ FORWARD_STAGES = ("f1_counts", "f2_dispatch", "f3_experts", "f4_combine")
 class _P2PExpertsFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h: Tensor, idx: Tensor, gate: Tensor, wg: Tensor, wu: Tensor, wd: Tensor,  # type: ignore[override]
-                comm: P2PExpertComm, layer_key: int, clamps: tuple[float, float, float]) -> Tensor:
-        call = EPCall(comm, layer_key, h, idx, gate, wg, wu, wd, clamps)
+                comm: P2PExpertComm, layer_key: int, clamps: tuple[float, float, float],
+                fp8_pool: nn.Module | None = None) -> Tensor:
+        call = EPCall(comm, layer_key, h, idx, gate, wg, wu, wd, clamps, fp8_pool)
         with _phase("ep.dispatch"):
             call.f1_counts()
             call.f2_dispatch()
@@ -379,16 +390,18 @@ class _P2PExpertsFn(torch.autograd.Function):
         with _phase("ep.dispatch_bwd"):
             dh, dgate, dwg, dwu, dwd = call.b3_pull()
         del ctx.call
-        return dh, None, dgate, dwg, dwu, dwd, None, None, None
+        return dh, None, dgate, dwg, dwu, dwd, None, None, None, None
 
 
 def p2p_routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module, comm: P2PExpertComm,
                        layer_key: int) -> Tensor:
     """h (T, D) this rank's tokens; idx / gate (T, k) with global expert ids.  Returns
     sum_j gate[t,j] * expert_{idx[t,j]}(h[t]) with the experts sharded over the group."""
+    from saint_llm_b200.ops.moe_native import fp8_pool_ok
+
     return _P2PExpertsFn.apply(h, idx, gate, experts.gate_weight, experts.up_weight, experts.down_weight, comm,
                                layer_key, (float(experts.clamp_gate_max), float(experts.clamp_linear[0]),
-                                           float(experts.clamp_linear[1])))
+                                           float(experts.clamp_linear[1])), experts if fp8_pool_ok(experts) else None)
 
 
 def moe_forward_p2p(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:

@@ -16,6 +16,11 @@ What each ``RunConfig`` field selects here:
   are issued from a backward hook during the step's last micro-batch, so they run on
   NCCL's stream while the backward of the earlier blocks continues (True), or all after
   the backward (False).
+* ``cuda_graphs``: on one GPU, each micro-batch's forward + backward replays one captured
+  CUDA graph (``TrainStep(cuda_graph=True)``); ignored when gradients are synchronised
+  across ranks (the expert-parallel step reads routing sizes on the host).
+* ``fp8_expert_cache``: with ``linear_quant="fp8"``, whether the routed experts' FP8 weight
+  copies persist between steps (set on every expert pool as ``fp8_weight_cache``).
 * ``kernels``: "native" (sm_100a kernels) or "torch" (the eager oracle path on CUDA,
   through ``backend.eager_mode``; every step then runs inside that mode).
 * ``micro_batch`` / ``seq_len`` / ``grad_accum``: the shape of one step's token batch.
@@ -124,9 +129,11 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
     torch.manual_seed(run.seed)
     with torch.device(device):
         model = SaintLLM(model_cfg)
-    bf16 = run.param_dtype == "bfloat16"
-    if bf16:
+    if run.param_dtype == "bfloat16":
         cast_params(model, torch.bfloat16)
+    for mod in model.modules():
+        if hasattr(mod, "gate_weight") and hasattr(mod, "linear_quant"):
+            mod.fp8_weight_cache = run.fp8_expert_cache
     grad_sync = None
     if world > 1:
         from saint_llm_b200.parallel import ep as ep_mod
@@ -142,7 +149,8 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
                     qk_clip_layers=model.attention_layers() if qk_clip else None)
     if grad_sync is not None:
         grad_sync.configure_optimizer(opt)
-    step = TrainStep(model, opt, micro_batches=run.grad_accum, params=params, grad_sync=grad_sync)
+    step = TrainStep(model, opt, micro_batches=run.grad_accum, params=params, grad_sync=grad_sync,
+                     cuda_graph=run.cuda_graphs and run.kernels == "native")
     wrapped = _EagerStep(step) if run.kernels == "torch" else step
     return TrainingJob(model, opt, wrapped, grad_sync, run)
 

@@ -246,3 +246,23 @@ def test_trainer_window_one_host_read_and_skip_rules():
         tr.train_window(xs[:1])
     with pytest.raises(ValueError, match="grad_clip_norm"):
         Trainer(m, opt, loss_fn=loss_fn, grad_clip_norm=0.0)
+
+
+def test_build_training_consumes_run_config():
+    """``build_training``: a CPU job from ModelConfig + RunConfig steps and learns; fields
+    this builder cannot honour raise instead of being ignored."""
+    from saint_llm_b200.config import ModelConfig, RunConfig
+    from saint_llm_b200.train.launch import build_training
+
+    cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+    run = RunConfig(grad_accum=2, micro_batch=1, seq_len=16, lr=0.02, adamw_lr=3e-3, seed=3,
+                    param_dtype="float32", compute_dtype="float32")
+    job = build_training(cfg, run, torch.device("cpu"))
+    torch.manual_seed(0)
+    batch = torch.randint(0, cfg.vocab_size, (2, 1, 16))
+    losses = [job.step(batch) for _ in range(4)]
+    assert losses[-1] < losses[0]
+    assert job.optimizer.param_groups[0]["lr"] == 0.02
+    for bad in ({"tp": 2}, {"grad_dtype": "bfloat16"}, {"zero": "fsdp"}):
+        with pytest.raises(ValueError):
+            build_training(cfg, run.model_copy(update=bad), torch.device("cpu"))

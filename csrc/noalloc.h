@@ -15,8 +15,15 @@
 // different streams, or from different threads without ordering) race on it.
 //
 // Set-up: the first call on a device looks up the array's device address with that
-// device current (cudaGetSymbolAddress) and caches it.  Make that first call before
-// any stream capture starts on the device.
+// device current (cudaGetSymbolAddress), raises the partial kernel's shared-memory limit
+// (cudaFuncSetAttribute) and caches both.  Make that first call before any stream capture
+// starts on the device.
+//
+// Determinism: dw is summed in a fixed order (per-warp rows, then blocks), so repeated
+// calls on the same inputs give bit-identical results.
+//
+// Errors: a CUDA error already pending on the calling thread is returned as its own code
+// and left pending (this call does not consume it).
 #pragma once
 
 #include <cuda_runtime.h>

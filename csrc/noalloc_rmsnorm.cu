@@ -4,8 +4,11 @@
 //   dw = sum over rows of dy * x * r
 //
 // Pass 1: up to SV4_NOALLOC_MAX_BLOCKS blocks each take a contiguous range of rows,
-// write dx, and store their partial dw row in the static scratch array.
-// Pass 2: one thread per column sums the partial rows into the caller's dw.
+// write dx, and store their partial dw row in the static scratch array.  Inside a block
+// each of the four warps accumulates its rows' dw into its own shared-memory row (every
+// lane owns its columns, so no atomics), and the four rows are summed in a fixed order.
+// Pass 2: one thread per column sums the partial rows into the caller's dw, in block
+// order.  The result is therefore bit-reproducible from call to call.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -30,9 +33,13 @@ enum : int {
   kSetupFailed = 5,
   kLaunchFailed = 6,
   kNoDevice = 7,
+  kPriorError = 8,
 };
 
+constexpr int kWarps = 4;  // shared memory: kWarps x dim floats (128 KiB at dim 8192)
+
 float* g_scratch_addr[kMaxDevices] = {nullptr};
+bool g_smem_ready[kMaxDevices] = {false};
 std::mutex g_setup_mutex;
 
 __device__ __forceinline__ float warp_sum32(float v) {
@@ -56,14 +63,15 @@ __global__ void noalloc_rmsnorm_bwd_partial(const __nv_bfloat16* __restrict__ dy
                                             const float* __restrict__ w, const float* __restrict__ rstd,
                                             __nv_bfloat16* __restrict__ dx, float* __restrict__ scratch, int rows,
                                             int D, int rows_per_block) {
-  extern __shared__ float sdw[];  // D floats
-  for (int d = threadIdx.x; d < D; d += blockDim.x) sdw[d] = 0.f;
+  extern __shared__ float sdw[];  // kWarps rows of D floats: one partial dw row per warp
+  for (int d = threadIdx.x; d < kWarps * D; d += blockDim.x) sdw[d] = 0.f;
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5;
+  float* mine = sdw + static_cast<long long>(warp) * D;
   const int row0 = blockIdx.x * rows_per_block;
   const int row1 = min(rows, row0 + rows_per_block);
-  for (int row = row0 + (threadIdx.x >> 5); row < row1; row += warps) {
+  for (int row = row0 + warp; row < row1; row += kWarps) {
     const float r = rstd[row];
     const __nv_bfloat16* xr = x + static_cast<long long>(row) * D;
     const __nv_bfloat16* gr = dy + static_cast<long long>(row) * D;
@@ -75,7 +83,7 @@ __global__ void noalloc_rmsnorm_bwd_partial(const __nv_bfloat16* __restrict__ dy
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         dot += w[d + q] * fg[q] * fx[q];
-        atomicAdd(&sdw[d + q], fg[q] * fx[q] * r);
+        mine[d + q] += fg[q] * fx[q] * r;  // this lane's own columns of this warp's row
       }
     }
     dot = warp_sum32(dot) / D;
@@ -96,8 +104,14 @@ __global__ void noalloc_rmsnorm_bwd_partial(const __nv_bfloat16* __restrict__ dy
     }
   }
   __syncthreads();
-  // every block writes its full partial row, so the scratch never needs clearing
-  for (int d = threadIdx.x; d < D; d += blockDim.x) scratch[static_cast<long long>(blockIdx.x) * D + d] = sdw[d];
+  // every block writes its full partial row (warps summed in order), so the scratch never
+  // needs clearing
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) acc += sdw[static_cast<long long>(k) * D + d];
+    scratch[static_cast<long long>(blockIdx.x) * D + d] = acc;
+  }
 }
 
 __global__ void noalloc_rmsnorm_bwd_reduce(const float* __restrict__ scratch, float* __restrict__ dw, int D,
@@ -126,6 +140,15 @@ float* scratch_for_current_device(int* code) {
     }
     g_scratch_addr[dev] = static_cast<float*>(p);
   }
+  if (!g_smem_ready[dev]) {  // the per-warp partial rows need more than the default 48 KiB
+    const int bytes = static_cast<int>(sizeof(float)) * kWarps * SV4_NOALLOC_MAX_DIM;
+    if (cudaFuncSetAttribute(noalloc_rmsnorm_bwd_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess) {
+      *code = kSetupFailed;
+      return nullptr;
+    }
+    g_smem_ready[dev] = true;
+  }
   return g_scratch_addr[dev];
 }
 
@@ -139,6 +162,9 @@ extern "C" __attribute__((visibility("default"))) int sv4_rmsnorm_bwd_noalloc(
   if (dim <= 0 || dim % 8 != 0 || dim > SV4_NOALLOC_MAX_DIM) return kBadDim;
   if (rows < 0) return kBadRows;
   if (!aligned16(dy) || !aligned16(x) || !aligned16(dx)) return kMisaligned;
+  // an error left pending by earlier work on this thread is reported, not consumed: the
+  // launch-error checks below would otherwise mistake it for this call's
+  if (cudaPeekAtLastError() != cudaSuccess) return kPriorError;
   int code = kOk;
   float* scratch = scratch_for_current_device(&code);
   if (scratch == nullptr) return code;
@@ -150,7 +176,7 @@ extern "C" __attribute__((visibility("default"))) int sv4_rmsnorm_bwd_noalloc(
   const int rows_per_block = (rows + SV4_NOALLOC_MAX_BLOCKS - 1) / SV4_NOALLOC_MAX_BLOCKS;
   const int n_blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (n_blocks > SV4_NOALLOC_MAX_BLOCKS) return kTooManyBlocks;
-  noalloc_rmsnorm_bwd_partial<<<n_blocks, 256, sizeof(float) * dim, s>>>(
+  noalloc_rmsnorm_bwd_partial<<<n_blocks, 32 * kWarps, sizeof(float) * kWarps * dim, s>>>(
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), w, rstd,
       static_cast<__nv_bfloat16*>(dx), scratch, rows, dim, rows_per_block);
   if (cudaGetLastError() != cudaSuccess) return kLaunchFailed;
@@ -166,9 +192,10 @@ extern "C" __attribute__((visibility("default"))) const char* sv4_noalloc_error_
     case kBadRows: return "rows must be non-negative";
     case kTooManyBlocks: return "internal: block count exceeds SV4_NOALLOC_MAX_BLOCKS";
     case kMisaligned: return "dy, x and dx must be 16-byte aligned";
-    case kSetupFailed: return "cudaGetSymbolAddress failed for the scratch array on this device";
+    case kSetupFailed: return "set-up failed on this device (scratch address lookup or shared-memory opt-in)";
     case kLaunchFailed: return "kernel launch failed";
     case kNoDevice: return "no current CUDA device (or device index too large)";
+    case kPriorError: return "a CUDA error from earlier work is pending on this thread (left for its owner to read)";
     default: return "unknown error code";
   }
 }

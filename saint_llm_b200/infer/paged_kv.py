@@ -39,6 +39,7 @@ class PagePool:
         self.page_rows, self.dim = page_rows, dim
         self.storage = torch.zeros(n_pages, page_rows, dim, dtype=dtype, device=device)
         self._free = list(range(n_pages - 1, -1, -1))  # pop() hands out low page ids first
+        self._is_free = set(self._free)
 
     @property
     def n_pages(self) -> int:
@@ -51,11 +52,26 @@ class PagePool:
     def alloc(self) -> int:
         if not self._free:
             raise PoolExhausted(f"all {self.n_pages} pages are in use")
-        return self._free.pop()
+        p = self._free.pop()
+        self._is_free.discard(p)
+        return p
+
+    def alloc_many(self, n: int) -> list[int]:
+        """``n`` pages at once, or none (PoolExhausted) when fewer are free."""
+        if n > len(self._free):
+            raise PoolExhausted(f"{n} pages requested, {len(self._free)} of {self.n_pages} free")
+        return [self.alloc() for _ in range(n)]
 
     def free(self, pages: Iterable[int]) -> None:
+        """Return pages to the pool.  A page that is already free (a double free would hand
+        one page to two requests) or not a page of this pool raises, and nothing is freed."""
+        pages = list(pages)
+        bad = [p for p in pages if not 0 <= p < self.n_pages or p in self._is_free]
+        if bad or len(set(pages)) != len(pages):
+            raise ValueError(f"pages already free, repeated or out of range: {sorted(set(bad)) or pages}")
         for p in pages:
             self._free.append(p)
+            self._is_free.add(p)
 
 
 class PagedStream:
@@ -67,18 +83,21 @@ class PagedStream:
         self.length = 0
 
     def append(self, rows: Tensor) -> None:
-        """rows (n, dim)."""
+        """rows (n, dim).  All or nothing: the pages the rows need are reserved before any
+        row is written, so a full pool raises PoolExhausted with the stream unchanged."""
         if rows.dim() != 2 or rows.shape[1] != self.pool.dim:
             raise ValueError(f"rows must be (n, {self.pool.dim})")
         pr = self.pool.page_rows
-        i = 0
         n = rows.shape[0]
+        need = math.ceil((self.length + n) / pr) - len(self.pages)
+        fresh = self.pool.alloc_many(max(need, 0))
+        self.pages.extend(fresh)
+        i = 0
         while i < n:
             off = self.length % pr
-            if off == 0:
-                self.pages.append(self.pool.alloc())
             take = min(pr - off, n - i)
-            self.pool.storage[self.pages[-1], off:off + take] = rows[i:i + take].to(self.pool.storage.dtype)
+            self.pool.storage[self.pages[self.length // pr], off:off + take] = rows[i:i + take].to(
+                self.pool.storage.dtype)
             self.length += take
             i += take
 

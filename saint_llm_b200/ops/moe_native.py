@@ -270,6 +270,61 @@ class _DensePlan:
         return probs, total, 1
 
 
+def shared_group_forward(h: Tensor, clamps: tuple[float, float, float], fp8_owner: nn.Module | None,
+                         ws: list[Tensor]) -> tuple[Tensor, tuple]:
+    """Forward of several shared SwiGLU experts fused into one (see ``_SharedGroupFn``).
+    Returns the output and what the backward needs."""
+    ext = backend.ext()
+    dev = h.device
+    n = len(ws) // 3
+    wgs, wus, wds = list(ws[:n]), list(ws[n:2 * n]), list(ws[2 * n:])
+    T = h.shape[0]
+    I = sum(w.shape[0] for w in wgs)
+    hb = _bf16c(h)
+    if fp8_owner is not None:
+        from saint_llm_b200.ops import fp8
+
+        gu = fp8.cached_weight(fp8_owner, "_fp8_shared_gu", wgs + wus, "gu")
+        down = fp8.cached_weight(fp8_owner, "_fp8_shared_down", wds, "cols")
+        act, pre, y = fp8_swiglu_experts(fp8.quantize_rows(hb), gu, down, _DensePlan(T, dev), hb.shape[1], I,
+                                         clamps, gemm.error_word(dev))
+    else:
+        wg, wu, wd = _cat(wgs, 0), _cat(wus, 0), _cat(wds, 1)
+        act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+        pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
+        y = gemm.gemm_nt(act, wd)
+    return y, (hb, act, pre)
+
+
+def shared_group_backward(saved: tuple, ws: list[Tensor], clamps: tuple[float, float, float],
+                          dy: Tensor) -> tuple[Tensor, list[Tensor | None]]:
+    """Backward of ``shared_group_forward``: (dh, weight gradients in ``ws`` order; None
+    where they went into ``main_grad``)."""
+    hb, act, pre = saved
+    n = len(ws) // 3
+    wgs, wus, wds = ws[:n], ws[n:2 * n], ws[2 * n:]
+    ext = backend.ext()
+    dev = hb.device
+    wg, wu, wd = _cat(list(wgs), 0), _cat(list(wus), 0), _cat(list(wds), 1)
+    I = wg.shape[0]
+    dyb = _bf16c(dy)
+    dact = gemm.gemm_nt(dyb, wd.t())
+    dpre = torch.empty_like(pre)
+    ext.swiglu_bwd(dact, pre, dpre, *clamps)
+    dh = torch.empty_like(hb)
+    ext.swiglu_dense_dgrad(dpre, wg, wu, dh, gemm.error_word(dev))
+    off = 0
+    dg, du, dd = [], [], []
+    for e in range(n):
+        ie = wgs[e].shape[0]
+        dg.append(accumulate_weight_grad(wgs[e], dpre[:, off:off + ie], hb))
+        du.append(accumulate_weight_grad(wus[e], dpre[:, I + off:I + off + ie], hb))
+        dd.append(accumulate_weight_grad(wds[e], dyb, act[:, off:off + ie]))
+        off += ie
+    return dh, dg + du + dd
+
+
 class _SharedGroupFn(torch.autograd.Function):
     """Several shared SwiGLU experts as one: sum_e SwiGLU_e(h) = [Wd_1 .. Wd_n] SwiGLU(h;
     [Wg_1; ..; Wg_n], [Wu_1; ..; Wu_n]) because the activation is element-wise, so the
@@ -283,56 +338,30 @@ class _SharedGroupFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h: Tensor, clamps: tuple[float, float, float], fp8_owner: nn.Module | None,  # type: ignore[override]
                 *ws: Tensor) -> Tensor:
-        ext = backend.ext()
-        dev = h.device
-        n = len(ws) // 3
-        wgs, wus, wds = list(ws[:n]), list(ws[n:2 * n]), list(ws[2 * n:])
-        T = h.shape[0]
-        I = sum(w.shape[0] for w in wgs)
-        hb = _bf16c(h)
-        if fp8_owner is not None:
-            from saint_llm_b200.ops import fp8
-
-            gu = fp8.cached_weight(fp8_owner, "_fp8_shared_gu", wgs + wus, "gu")
-            down = fp8.cached_weight(fp8_owner, "_fp8_shared_down", wds, "cols")
-            act, pre, y = fp8_swiglu_experts(fp8.quantize_rows(hb), gu, down, _DensePlan(T, dev), hb.shape[1], I,
-                                             clamps, gemm.error_word(dev))
-        else:
-            wg, wu, wd = _cat(wgs, 0), _cat(wus, 0), _cat(wds, 1)
-            act = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
-            pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
-            ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
-            y = gemm.gemm_nt(act, wd)
-        ctx.save_for_backward(hb, act, pre, *ws)
-        ctx.clamps, ctx.n = clamps, n
+        y, saved = shared_group_forward(h, clamps, fp8_owner, list(ws))
+        ctx.save_for_backward(*saved, *ws)
+        ctx.clamps = clamps
         return y
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
         hb, act, pre, *ws = ctx.saved_tensors
-        n = ctx.n
-        wgs, wus, wds = ws[:n], ws[n:2 * n], ws[2 * n:]
-        ext = backend.ext()
-        dev = hb.device
-        wg, wu, wd = _cat(list(wgs), 0), _cat(list(wus), 0), _cat(list(wds), 1)
-        I = wg.shape[0]
-        dyb = _bf16c(dy)
-        dact = gemm.gemm_nt(dyb, wd.t())
-        grads: list[Tensor | None] = []
-        dpre = torch.empty_like(pre)
-        ext.swiglu_bwd(dact, pre, dpre, *ctx.clamps)
-        dh = torch.empty_like(hb)
-        ext.swiglu_dense_dgrad(dpre, wg, wu, dh, gemm.error_word(dev))
-        off = 0
-        dg, du, dd = [], [], []
-        for e in range(n):
-            ie = wgs[e].shape[0]
-            dg.append(accumulate_weight_grad(wgs[e], dpre[:, off:off + ie], hb))
-            du.append(accumulate_weight_grad(wus[e], dpre[:, I + off:I + off + ie], hb))
-            dd.append(accumulate_weight_grad(wds[e], dyb, act[:, off:off + ie]))
-            off += ie
-        grads = dg + du + dd
+        dh, grads = shared_group_backward((hb, act, pre), list(ws), ctx.clamps, dy)
         return (dh, None, None, *grads)
+
+
+def shared_group_args(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> tuple | None:
+    """(clamps, fp8_owner, weights) when the shared experts can run fused as one, else None."""
+    ex = list(experts)
+    if len(ex) < 2:
+        return None
+    clamps = {(float(e.clamp_gate_max), float(e.clamp_linear[0]), float(e.clamp_linear[1])) for e in ex}
+    if len(clamps) != 1 or any(e.gate_proj.weight.shape[0] % 64 for e in ex):
+        return None
+    ws = [e.gate_proj.weight for e in ex] + [e.up_proj.weight for e in ex] + [e.down_proj.weight for e in ex]
+    fp8_ok = (getattr(ex[0].gate_proj, "use_real_fp8_gemm", False) and h.shape[-1] % 128 == 0
+              and all(e.gate_proj.weight.shape[0] % 128 == 0 for e in ex))
+    return clamps.pop(), ex[0] if fp8_ok else None, ws
 
 
 def shared_experts(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> Tensor | None:
@@ -342,16 +371,14 @@ def shared_experts(h: Tensor, experts: nn.ModuleList | list[nn.Module]) -> Tenso
         return None
     if len(ex) == 1:
         return shared_swiglu(h, ex[0])
-    clamps = {(float(e.clamp_gate_max), float(e.clamp_linear[0]), float(e.clamp_linear[1])) for e in ex}
-    if len(clamps) != 1 or any(e.gate_proj.weight.shape[0] % 64 for e in ex):
+    args = shared_group_args(h, ex)
+    if args is None:
         out = shared_swiglu(h, ex[0])
         for e in ex[1:]:
             out = out + shared_swiglu(h, e)
         return out
-    ws = [e.gate_proj.weight for e in ex] + [e.up_proj.weight for e in ex] + [e.down_proj.weight for e in ex]
-    fp8_ok = (getattr(ex[0].gate_proj, "use_real_fp8_gemm", False) and h.shape[-1] % 128 == 0
-              and all(e.gate_proj.weight.shape[0] % 128 == 0 for e in ex))
-    return _SharedGroupFn.apply(h, clamps.pop(), ex[0] if fp8_ok else None, *ws)
+    clamps, owner, ws = args
+    return _SharedGroupFn.apply(h, clamps, owner, *ws)
 
 
 def shared_swiglu(h: Tensor, expert: nn.Module) -> Tensor:

@@ -175,6 +175,9 @@ class P2PExpertComm:
         self.tokens = 0
         self.C = 0
         self.y = self.dy = self.dx = self.xr = None
+        # side stream for the token traffic that overlaps the shared experts (see moe_forward_p2p)
+        dev = heap.device
+        self.side = torch.cuda.Stream(dev) if torch.device(dev).type == "cuda" else None
 
     def next_epoch(self, phase: int) -> int:
         self.epoch[phase] = (self.epoch[phase] + 1) & 0xFFFFFFFF
@@ -235,6 +238,13 @@ class EPCall:
         self.dev = h.device
         self.err = gemm.error_word(self.dev)
         comm.ensure(self.T)
+        # outputs of the dispatch stage, allocated on the caller's stream so they may be
+        # written on the side stream and read back on this one after the join
+        E_loc, k = wg.shape[0], idx.shape[1]
+        self.gpos = torch.empty(self.T, k, dtype=torch.int32, device=self.dev)
+        self.seg_start = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
+        self.seg_rows = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
+        self.seg_pad = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
 
     # ---------------------------------------------------------------- forward
     def f1_counts(self) -> None:
@@ -245,11 +255,6 @@ class EPCall:
 
     def f2_dispatch(self) -> None:
         c, ext = self.comm, backend.ext()
-        E_loc, k = self.wg.shape[0], self.idx.shape[1]
-        self.gpos = torch.empty(self.T, k, dtype=torch.int32, device=self.dev)
-        self.seg_start = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
-        self.seg_rows = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
-        self.seg_pad = torch.empty(E_loc, dtype=torch.int32, device=self.dev)
         idx64 = self.idx.reshape(-1).to(torch.int64).contiguous()
         ext.ep_plan(idx64, self.local.pos, self.local.seg_start, c.cnt.local.view(torch.int32),
                     c.flags.local.view(torch.int32), self.e_cnt & 1, self.e_cnt, c.rank, c.ws, c.C, self.gpos,
@@ -304,10 +309,11 @@ class EPCall:
         return out
 
     # --------------------------------------------------------------- backward
-    def b1_push(self, dout: Tensor) -> None:
+    def b1_push(self, dout: Tensor, dgate: Tensor | None = None) -> None:
         c, ext = self.comm, backend.ext()
-        self.dgate = torch.empty_like(self.gf)
+        self.dgate = torch.empty_like(self.gf) if dgate is None else dgate
         ext.ep_combine_bwd(_bf16c(dout), self.ypair, self.gf, self.gpos, c.C, c.dy.ptrs, self.dgate, self.err)
+        self.ypair.record_stream(torch.cuda.current_stream(self.dev))  # may be a side stream
         del self.ypair
         self.e_dy = c.next_epoch(PH_DY)
         ext.ep_signal(c.flags.ptrs, PH_DY, c.rank, self.e_dy)
@@ -393,6 +399,65 @@ class _P2PExpertsFn(torch.autograd.Function):
         return dh, None, dgate, dwg, dwu, dwd, None, None, None, None
 
 
+class _P2PMoEFn(torch.autograd.Function):
+    """Routed experts over peer memory plus the fused shared experts, overlapped: the count
+    exchange and the token dispatch run on the communicator's side stream while the shared
+    experts' GEMMs run on the caller's stream (the dispatch is NVLink-bound, the GEMMs are
+    tensor-core-bound); the owner-side experts start after both streams join.  The backward
+    pushes the output gradients to the owners on the side stream while the shared experts'
+    backward runs.  Every tensor the side stream touches is either allocated on the
+    caller's stream before the fork or recorded on the side stream before it is freed."""
+
+    @staticmethod
+    def forward(ctx, h: Tensor, idx: Tensor, gate: Tensor, comm: P2PExpertComm, layer_key: int,  # type: ignore[override]
+                clamps: tuple[float, float, float], fp8_pool: nn.Module | None, s_clamps: tuple[float, float, float],
+                s_owner: nn.Module | None, *ws: Tensor) -> Tensor:
+        from saint_llm_b200.ops.moe_native import shared_group_forward
+
+        wg, wu, wd = ws[:3]
+        sws = list(ws[3:])
+        call = EPCall(comm, layer_key, h, idx, gate, wg, wu, wd, clamps, fp8_pool)
+        main, side = torch.cuda.current_stream(h.device), comm.side
+        side.wait_stream(main)
+        with torch.cuda.stream(side), _phase("ep.dispatch"):
+            call.f1_counts()
+            call.f2_dispatch()
+        with _phase("moe.shared_fwd"):
+            ys, saved = shared_group_forward(h, s_clamps, s_owner, sws)
+        main.wait_stream(side)
+        with _phase("ep.experts_fwd"):
+            call.f3_experts()
+        with _phase("ep.combine"):
+            out = call.f4_combine()
+        out += ys
+        ctx.call, ctx.saved_shared, ctx.s_clamps, ctx.n_sws = call, saved, s_clamps, len(sws)
+        ctx.save_for_backward(*sws)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        from saint_llm_b200.ops.moe_native import shared_group_backward
+
+        call: EPCall = ctx.call
+        sws = list(ctx.saved_tensors)
+        main, side = torch.cuda.current_stream(dout.device), call.comm.side
+        dgate = torch.empty_like(call.gf)
+        doutb = _bf16c(dout)
+        side.wait_stream(main)
+        with torch.cuda.stream(side), _phase("ep.combine_bwd"):
+            call.b1_push(doutb, dgate)
+        with _phase("moe.shared_bwd"):
+            dh_s, sgrads = shared_group_backward(ctx.saved_shared, sws, ctx.s_clamps, doutb)
+        main.wait_stream(side)
+        with _phase("ep.experts_bwd"):
+            call.b2_experts()
+        with _phase("ep.dispatch_bwd"):
+            dh, dgate, dwg, dwu, dwd = call.b3_pull()
+        dh += dh_s
+        del ctx.call, ctx.saved_shared
+        return (dh, None, dgate, None, None, None, None, None, None, dwg, dwu, dwd, *sgrads)
+
+
 def p2p_routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module, comm: P2PExpertComm,
                        layer_key: int) -> Tensor:
     """h (T, D) this rank's tokens; idx / gate (T, k) with global expert ids.  Returns
@@ -405,7 +470,7 @@ def p2p_routed_experts(h: Tensor, idx: Tensor, gate: Tensor, experts: nn.Module,
 
 
 def moe_forward_p2p(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
-    from saint_llm_b200.ops.moe_native import shared_experts
+    from saint_llm_b200.ops.moe_native import fp8_pool_ok, shared_experts, shared_group_args
 
     b, t, d = x.shape
     h = layer.norm(x)
@@ -413,6 +478,16 @@ def moe_forward_p2p(layer: nn.Module, x: Tensor, token_ids: Tensor | None, is_vi
     layer._last_aux_loss = aux
     k = layer.cfg.experts_per_token
     h2 = h.reshape(b * t, d)
+    comm: P2PExpertComm = layer.ep_comm
+    shared = shared_group_args(h2, layer.shared_experts)
+    if comm.side is not None and shared is not None and getattr(comm, "overlap", True):
+        ex = layer.grouped_experts
+        s_clamps, s_owner, sws = shared
+        out = _P2PMoEFn.apply(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), comm, layer.layer_idx,
+                              (float(ex.clamp_gate_max), float(ex.clamp_linear[0]), float(ex.clamp_linear[1])),
+                              ex if fp8_pool_ok(ex) else None, s_clamps, s_owner, ex.gate_weight, ex.up_weight,
+                              ex.down_weight, *sws)
+        return out.view(b, t, d)
     out = p2p_routed_experts(h2, idx.reshape(b * t, k), gate.reshape(b * t, k), layer.grouped_experts,
                              layer.ep_comm, layer.layer_idx)
     sh = shared_experts(h2, layer.shared_experts)

@@ -71,3 +71,26 @@ def test_manager_mixed_lengths_and_attention():
         assert torch.allclose(out[i], p @ v, atol=1e-5)
     mgr.release("b")
     assert pools["k"].free_pages == 64 - 1 - 1  # "a" (5 rows) and "c" (1 row): one page each
+
+
+def test_append_is_all_or_nothing_and_double_free_raises():
+    import pytest
+
+    from saint_llm_b200.infer.paged_kv import PagedStream, PagePool, PoolExhausted
+
+    pool = PagePool(3, 4, 2, dtype=torch.float32)
+    s = PagedStream(pool)
+    s.append(torch.ones(6, 2))  # 2 pages
+    before = (list(s.pages), s.length, pool.free_pages)
+    with pytest.raises(PoolExhausted):
+        s.append(torch.zeros(7, 2))  # needs 2 more pages, 1 free
+    assert (list(s.pages), s.length, pool.free_pages) == before
+    assert torch.equal(s.gather(), torch.ones(6, 2))
+    s.append(torch.full((2, 2), 2.0))  # fills page 2 exactly
+    assert s.length == 8 and pool.free_pages == 1
+    with pytest.raises(ValueError):
+        pool.free([s.pages[0], s.pages[0]])
+    s.release()
+    with pytest.raises(ValueError):
+        pool.free([0])  # already free
+    assert pool.free_pages == 3

@@ -3,8 +3,9 @@
 Callers that cannot allocate device memory (memory pools they do not own, runtimes
 without an allocator hook, applications that forbid cudaMalloc after start-up) use
 ``sv4_rmsnorm_bwd_noalloc``.  This test calls it through its exported C symbol and
-checks dx and dw against the torch-facing ``rmsnorm_bwd`` entry point on two calls in
-a row (the second call reuses the shared scratch array the first one left behind).
+checks dx and dw against the torch-facing ``rmsnorm_bwd`` entry point and against the
+fp32 formula on two calls in a row (the second call reuses the shared scratch array the
+first one left behind), and that repeating a call reproduces dw bit for bit.
 It lives in its own file, collected last, so a failure here never hides other tests.
 """
 
@@ -57,6 +58,16 @@ def test_rmsnorm_bwd_noalloc_matches_regular_entry_point(cuda):
         assert rc == 0, err(rc).decode()
         assert _rel(dx, dx_ref) < 1e-2
         assert _rel(dw, dw_ref) < 1e-3
+        # fp32 formula: dx = r (w dy - x r^2 mean(w dy x)), dw = sum_rows dy x r
+        xf, gf, r = x.float(), dy.float(), rstd[:, None]
+        dot = (w * gf * xf).mean(-1, keepdim=True)
+        assert _rel(dx, r * (w * gf - xf * r * r * dot)) < 1e-2
+        assert _rel(dw, (gf * xf * r).sum(0)) < 1e-4
+        dw2 = torch.full_like(dw, float("nan"))
+        rc = fn(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), dw2.data_ptr(),
+                rows, dim, stream)
+        torch.cuda.synchronize()
+        assert rc == 0 and torch.equal(dw, dw2), "dw is not reproducible"
 
 
 def test_rmsnorm_bwd_noalloc_rejects_oversized_dim(cuda):

@@ -67,10 +67,90 @@ def _reference_config(ModelConfig, args, n_layers: int | None = None):  # noqa: 
 
 def run(args) -> dict:
     try:
-        return _run(args)
+        res = _run(args)
     except Exception as e:  # noqa: BLE001 - report any failure of the reference as unavailable
         msg = f"{type(e).__name__}: {e}".splitlines()[0][:300]
-        return _unavailable(f"reference run failed: {msg}")
+        res = _unavailable(f"reference run failed: {msg}")
+    if res and not getattr(args, "no_decode", False) and int(os.environ.get("WORLD_SIZE", 1)) == 1:
+        try:
+            res["decode"] = _decode(args)
+        except Exception as e:  # noqa: BLE001
+            res["decode"] = {"unavailable": f"reference decode failed: {type(e).__name__}: {e}".splitlines()[0][:300]}
+    return res
+
+
+def _decode(args) -> dict:
+    """Config 5 on one GPU through the reference's public ``greedy_decode_cached`` with its
+    ``KVCacheBundle``: prefill (one forward over the prompt, as the API does) and greedy
+    steps, timed as two calls (1 new token, then 1 + n new tokens; the difference is n
+    decode steps).  Its prefill materialises (B, H, T, T) attention scores, so the batch is
+    halved from the configured 64 until it fits; n is capped to fit the time budget and the
+    step time is extrapolated to the configured step count.  Reported as measured, with
+    ``unavailable`` whenever the configured batch or step count could not be run as is."""
+    import gc
+
+    from saint_llm_core.config import ModelConfig
+    from saint_llm_core.model import SaintLLM
+    from saint_llm_inference.generate import greedy_decode_cached
+
+    gc.collect()
+    torch.cuda.empty_cache()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    cfg = _reference_config(ModelConfig, args).model_copy(update={"activation_checkpointing": False})
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = SaintLLM(cfg)
+    model.eval()
+    want_b, P, S = args.decode_batch, args.seq_len, args.decode_steps
+    budget = float(os.environ.get("SV4_REF_DECODE_BUDGET_S", "240"))
+    b, err = want_b, None
+    while b >= 1:
+        ids = torch.randint(0, cfg.vocab_size, (b, P), device=dev)
+        try:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                torch.cuda.synchronize(dev)
+                ev[0].record()
+                greedy_decode_cached(model, ids, max_new_tokens=1)
+                ev[1].record()
+                torch.cuda.synchronize(dev)
+                prefill_s = ev[0].elapsed_time(ev[1]) / 1000.0
+                n = 8
+                ev[2].record()
+                greedy_decode_cached(model, ids, max_new_tokens=1 + n)
+                ev[3].record()
+                torch.cuda.synchronize(dev)
+                step_s = max(ev[2].elapsed_time(ev[3]) / 1000.0 - prefill_s, 1e-6) / n
+            break
+        except torch.OutOfMemoryError as e:
+            err = str(e).splitlines()[0][:120]
+            ids = None
+            gc.collect()
+            torch.cuda.empty_cache()
+            b //= 2
+    if b < 1:
+        return {"unavailable": f"reference decode ran out of memory at every batch ({err})"}
+    measured = {"batch_run": b, "batch_config": want_b, "prompt": P, "prefill_s": round(prefill_s, 3),
+                "prefill_tokens_per_s": round(b * P / prefill_s, 1), "decode_ms_per_step": round(step_s * 1000, 2),
+                "decode_tokens_per_s_at_batch_run": round(b / step_s, 1), "steps_timed": 8,
+                "steps_config": S, "api": "saint_llm_inference.greedy_decode_cached + KVCacheBundle"}
+    full_s = prefill_s + S * step_s
+    if b == want_b and full_s <= budget:
+        ids = torch.randint(0, cfg.vocab_size, (b, P), device=dev)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            greedy_decode_cached(model, ids, max_new_tokens=S)
+            e1.record()
+            torch.cuda.synchronize(dev)
+        total = e0.elapsed_time(e1) / 1000.0
+        dec = max(total - prefill_s, 1e-6)
+        return {"metric": "decode tok/s", "value": b * (S - 1) / dec, "unit": "tokens/s",
+                "prefill_tokens_per_s": b * P / prefill_s, "n_gpus": 1, "measured": measured,
+                "timing": "CUDA events; decode = full call minus the measured prefill"}
+    why = (f"prefill at batch {want_b} ran out of memory" if b != want_b else
+           f"{S} steps take ~{full_s:.0f} s, over the {budget:.0f} s decode budget")
+    return {"unavailable": f"reference decode: {why}; timed at batch {b}, {8} steps", "measured": measured}
 
 
 def _max_over_ranks(x: float, dev: torch.device, world: int) -> float:

@@ -254,8 +254,36 @@ def run_ours(args) -> dict:
         comm = getattr(model, "ep_comm", None)
         if comm is not None:
             comm.close()  # collective: peers stop touching each other's buffers first
+    if not args.no_decode:
+        import gc
+
+        del step, model
+        gc.collect()
+        torch.cuda.empty_cache()
+        result["decode"] = run_decode(args, device, world)
+    if world > 1:
         torch.distributed.destroy_process_group()
     return result if rank == 0 else {}
+
+
+def run_decode(args, device, world: int) -> dict:
+    """Config 5's serving measurement on every rank (one independent replica per GPU, the
+    reference's only multi-GPU inference layout): 64 prompts of 4096 tokens prefilled in
+    chunks, then greedy decode; box tokens/s from the slowest rank's time."""
+    from saint_llm_b200.bench.decode import measure_decode
+
+    r = measure_decode(batch=args.decode_batch, prompt=args.seq_len, steps=args.decode_steps, layers=args.layers,
+                       device=device)
+    B, P, S = args.decode_batch, args.seq_len, args.decode_steps
+    t = torch.tensor([B * S / r["value"], B * P / r["prefill_tokens_per_s"]], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dec_s, pre_s = float(t[0]), float(t[1])
+    return {"metric": "decode tok/s", "value": world * B * S / dec_s, "unit": "tokens/s",
+            "prefill_tokens_per_s": world * B * P / pre_s, "decode_ms_per_step": dec_s * 1000.0 / S,
+            "n_gpus": world, "parallelism": f"{world} replica(s), one per GPU", "dtype": r["dtype"],
+            "timing": "CUDA events, max over ranks; prefill and decode timed separately",
+            "config": r["config"]}
 
 
 def run_reference(args) -> dict:
@@ -283,6 +311,9 @@ def main() -> None:
     ap.add_argument("--no-overlap-reduce", action="store_true",
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode (config 5) measurement")
+    ap.add_argument("--decode-batch", type=int, default=64)
+    ap.add_argument("--decode-steps", type=int, default=512)
     ap.add_argument("--data-pool", type=int, default=8,
                     help="distinct synthetic step batches cycled through (pinned host memory)")
     ap.add_argument("--linear-quant", default="bf16", choices=["bf16", "fp8"])

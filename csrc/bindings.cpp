@@ -34,6 +34,9 @@ void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win,
                       c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c, double scale,
                       torch::Tensor out);
 // router.cu
+void router_bwd(torch::Tensor z, torch::Tensor aff, torch::Tensor idx, torch::Tensor gate,
+                c10::optional<torch::Tensor> d_gate, c10::optional<torch::Tensor> d_aff, int64_t mode,
+                torch::Tensor dz);
 void router_fwd(torch::Tensor z, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias,
                 c10::optional<torch::Tensor> modality_bias, c10::optional<torch::Tensor> is_visual,
                 torch::Tensor aff, torch::Tensor idx, torch::Tensor gate);
@@ -42,6 +45,9 @@ void muon_momentum(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, int64_
 void muon_normalize(torch::Tensor m, torch::Tensor g, torch::Tensor sumsq, torch::Tensor y, int64_t slice, double mu,
                     double eps);
 void muon_apply(torch::Tensor p, torch::Tensor o, double decay, double step);
+void adamw_multi(torch::Tensor table, torch::Tensor chunks, double lr, double beta1, double beta2, double eps,
+                 double weight_decay, double step);
+int64_t adamw_chunk_elems();
 void swiglu_dense(torch::Tensor x, torch::Tensor wg, torch::Tensor wu, torch::Tensor act, torch::Tensor pre,
                   double gmax, double lo, double hi, torch::Tensor err);
 void swiglu_dense_dgrad(torch::Tensor dpre, torch::Tensor wg, torch::Tensor wu, torch::Tensor dx, torch::Tensor err);
@@ -87,6 +93,9 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor k
               torch::Tensor o_c, torch::Tensor lse, torch::Tensor dout, torch::Tensor dq, torch::Tensor dk,
               torch::Tensor dv, torch::Tensor dkv, torch::Tensor dsink, torch::Tensor err);
 void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel, torch::Tensor err);
+// sampling.cu
+void sample_tokens(torch::Tensor logits, c10::optional<torch::Tensor> bias, double temperature, int64_t top_k,
+                   double top_p, torch::Tensor u, torch::Tensor out, c10::optional<torch::Tensor> thr);
 // ce.cu
 void ce_fwd(torch::Tensor z, torch::Tensor target, double softcap, torch::Tensor lse, torch::Tensor nll);
 void ce_bwd(torch::Tensor z, torch::Tensor target, torch::Tensor lse, double softcap, torch::Tensor scale,
@@ -127,6 +136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &sv4::attn_fwd);
   m.def("attn_bwd", &sv4::attn_bwd);
   m.def("csa_select_mask", &sv4::csa_select_mask);
+  m.def("sample_tokens", &sv4::sample_tokens);
   m.def("ce_fwd", &sv4::ce_fwd);
   m.def("ce_bwd", &sv4::ce_bwd);
   m.def("gemm", &sv4::gemm);
@@ -142,11 +152,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);
   m.def("router_fwd", &sv4::router_fwd);
+  m.def("router_bwd", &sv4::router_bwd);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
   m.def("grouped_gemm_fp8", &sv4::grouped_gemm_fp8);
   m.def("muon_momentum", &sv4::muon_momentum);
   m.def("muon_normalize", &sv4::muon_normalize);
   m.def("muon_apply", &sv4::muon_apply);
+  m.def("adamw_multi", &sv4::adamw_multi);
+  m.def("adamw_chunk_elems", &sv4::adamw_chunk_elems);
   m.def("swiglu_dense", &sv4::swiglu_dense);
   m.def("swiglu_dense_dgrad", &sv4::swiglu_dense_dgrad);
   m.def("moe_route_plan", &sv4::moe_route_plan);

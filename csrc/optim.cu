@@ -3,10 +3,12 @@
 //   muon_momentum : M <- mu M + G  (in place), U = mu M + G, per-matrix sum of U^2
 //   muon_normalize: Y = U / (||U||_F + eps) as bf16 (the Newton-Schulz input)
 //   muon_apply    : W <- W (1 - lr wd) - (lr * scale) O
+//   adamw_multi   : decoupled-weight-decay Adam over a table of tensors in one launch
 //
 // Tensors are flat views of one parameter holding `n / slice` matrices of `slice`
 // elements each (a 2-D weight is one slice; stacked expert weights hold E slices).
 #include <ATen/cuda/CUDAContext.h>
+#include <cmath>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
@@ -130,5 +132,70 @@ void muon_apply(torch::Tensor p, torch::Tensor o, double decay, double step) {
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ------------------------------------------------------------------ AdamW, multi-tensor
+// One entry per parameter: fp32 gradient (main_grad), the parameter (bf16 or fp32) and its
+// fp32 moments.  The grid walks a chunk list (entry, first element) so one launch covers
+// every AdamW parameter of the optimizer group:
+//   m <- b1 m + (1 - b1) g;  v <- b2 v + (1 - b2) g^2
+//   p <- p (1 - lr wd) - lr (m / bc1) / (sqrt(v / bc2) + eps)
+struct AdamEntry {
+  const float* g;
+  void* p;
+  float* m;
+  float* v;
+  int64_t n;
+  int64_t bf16;
+};
+
+constexpr int64_t kAdamChunk = 1 << 16;
+
+__global__ void __launch_bounds__(256) adamw_multi_kernel(const AdamEntry* __restrict__ entries,
+                                                          const int64_t* __restrict__ chunks, float lr, float b1,
+                                                          float b2, float eps, float wd, float inv_bc1,
+                                                          float inv_bc2) {
+  const int64_t c = chunks[blockIdx.x];
+  const AdamEntry e = entries[c >> 32];
+  const int64_t start = (c & 0xFFFFFFFFll) * kAdamChunk;
+  const int64_t end = min(e.n, start + kAdamChunk);
+  const float decay = 1.f - lr * wd;
+  for (int64_t i = start + threadIdx.x; i < end; i += blockDim.x) {
+    const float g = e.g[i];
+    const float m = b1 * e.m[i] + (1.f - b1) * g;
+    const float v = b2 * e.v[i] + (1.f - b2) * g * g;
+    e.m[i] = m;
+    e.v[i] = v;
+    const float upd = (m * inv_bc1) / (sqrtf(v * inv_bc2) + eps);
+    if (e.bf16) {
+      __nv_bfloat16* p = static_cast<__nv_bfloat16*>(e.p);
+      p[i] = __float2bfloat16(__bfloat162float(p[i]) * decay - lr * upd);
+    } else {
+      float* p = static_cast<float*>(e.p);
+      p[i] = p[i] * decay - lr * upd;
+    }
+  }
+}
+
+// table: (n_entries, 6) int64 on the device (AdamEntry rows); chunks: (n_chunks) int64 on
+// the device, entry << 32 | chunk index.
+void adamw_multi(torch::Tensor table, torch::Tensor chunks, double lr, double beta1, double beta2, double eps,
+                 double weight_decay, double step) {
+  TORCH_CHECK(table.scalar_type() == at::kLong && table.is_cuda() && table.dim() == 2 && table.size(1) == 6,
+              "table: (entries, 6) int64 on the device");
+  TORCH_CHECK(chunks.scalar_type() == at::kLong && chunks.is_cuda() && chunks.dim() == 1, "chunks: int64");
+  static_assert(sizeof(AdamEntry) == 6 * sizeof(int64_t), "AdamEntry layout");
+  const int64_t n_chunks = chunks.numel();
+  if (n_chunks == 0) return;
+  c10::cuda::CUDAGuard guard(table.device());
+  const float inv_bc1 = static_cast<float>(1.0 / (1.0 - std::pow(beta1, step)));
+  const float inv_bc2 = static_cast<float>(1.0 / (1.0 - std::pow(beta2, step)));
+  adamw_multi_kernel<<<static_cast<unsigned>(n_chunks), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const AdamEntry*>(table.data_ptr<int64_t>()), chunks.data_ptr<int64_t>(),
+      static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2), static_cast<float>(eps),
+      static_cast<float>(weight_decay), inv_bc1, inv_bc2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t adamw_chunk_elems() { return kAdamChunk; }
 
 }  // namespace sv4

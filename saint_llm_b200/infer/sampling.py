@@ -6,6 +6,11 @@ multiplied, over the ids present in the history), a top-p nucleus that always ke
 best token and is the smallest prefix whose mass reaches ``p``, top-k as a cutoff at the
 k-th largest logit (ties kept), and sampling by ``torch.multinomial`` so a seeded
 generator reproduces a run.  Everything stays on the device (no host round trips).
+
+On CUDA, bias, temperature, top-k, top-p and the draw run as one native kernel per call
+(``csrc/sampling.cu``: radix selection of the top-k / top-p thresholds, inverse-CDF draw
+against a uniform from the caller's generator); the PyTorch functions below are its
+oracle and the CPU path.
 """
 
 from __future__ import annotations
@@ -81,6 +86,29 @@ def sample_from_topk(logits: Tensor, k: int, generator: torch.Generator | None) 
     return idx.gather(-1, pick)
 
 
+def fused_sample(logits: Tensor, *, temperature: float, top_k: int | None = None, top_p: float = 1.0,
+                 bias: Tensor | None = None, generator: torch.Generator | None = None,
+                 return_threshold: bool = False) -> Tensor | tuple[Tensor, Tensor]:
+    """(B, V) logits -> (B, 1) token ids in one native kernel (CUDA only).
+
+    The uniform of each row comes from ``generator`` (torch.rand), so a seeded generator
+    reproduces the draws.  ``return_threshold`` also returns the order-preserving integer
+    key of the smallest kept logit per row (for testing the kept set)."""
+    from saint_llm_b200.ops import backend
+
+    b = logits.shape[0]
+    x = logits if logits.dtype in (torch.float32, torch.bfloat16) else logits.float()
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    gdev = generator.device if generator is not None else x.device
+    u = torch.rand(b, generator=generator, device=gdev, dtype=torch.float32).to(x.device, non_blocking=True)
+    out = torch.empty(b, dtype=torch.long, device=x.device)
+    thr = torch.empty(b, dtype=torch.int32, device=x.device) if return_threshold else None
+    bv = None if bias is None else bias.float().contiguous()
+    backend.ext().sample_tokens(x, bv, float(temperature), int(top_k or 0), float(top_p), u, out, thr)
+    return (out.view(b, 1), thr) if return_threshold else out.view(b, 1)
+
+
 def next_token(last_logits: Tensor, params: SamplingParams, *, history: Tensor | None = None,
                generator: torch.Generator | None = None, bias: Tensor | None = None,
                draw: str = "full") -> Tensor:
@@ -89,6 +117,16 @@ def next_token(last_logits: Tensor, params: SamplingParams, *, history: Tensor |
     ``draw="topk"`` samples within the top-k set directly (``top_k_sample`` semantics);
     ``"full"`` masks then samples from the full softmax (``top_p_sample`` semantics).
     """
+    from saint_llm_b200.ops import backend
+
+    if backend.native_for(last_logits) and last_logits.dim() == 2:
+        x = last_logits
+        if params.repetition_penalty is not None and history is not None and not params.greedy:
+            # the penalty rescales by sign, so it commutes with the temperature division
+            x = apply_repetition_penalty(x.float(), history, params.repetition_penalty)
+        k = params.top_k if draw == "full" else (params.top_k or x.shape[-1])
+        return fused_sample(x, temperature=0.0 if params.greedy else params.temperature, top_k=k,
+                            top_p=params.top_p if draw == "full" else 1.0, bias=bias, generator=generator)
     x = last_logits
     if bias is not None:
         x = x + bias.to(x.dtype)
@@ -107,4 +145,4 @@ def next_token(last_logits: Tensor, params: SamplingParams, *, history: Tensor |
 
 
 __all__ = ["SamplingParams", "apply_repetition_penalty", "bias_vector", "filter_top_k", "filter_top_p",
-           "next_token", "sample_from_topk"]
+           "fused_sample", "next_token", "sample_from_topk"]

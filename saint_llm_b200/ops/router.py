@@ -1,10 +1,10 @@
-"""Fused MoE router forward (``csrc/router.cu``) with its backward in PyTorch.
+"""Fused MoE router (``csrc/router.cu``): one forward kernel and one backward kernel.
 
-One kernel computes the affinity (``sqrt(softplus(z))`` or ``sigmoid(z)``), the bias-adjusted
-top-k selection and the renormalised gates.  The backward is a few element-wise ops on
-(T, E): the gates' renormalisation, the affinity's derivative, and the affinity gradient
-coming from the sequence-balance loss.  The biases only steer the selection, so they get no
-gradient (as with ``topk`` indices in the eager router).
+The forward computes the affinity (``sqrt(softplus(z))`` or ``sigmoid(z)``), the
+bias-adjusted top-k selection and the renormalised gates.  The backward (one warp per
+token) folds the gates' renormalisation, the affinity gradient coming from the
+sequence-balance loss and the affinity's derivative into dz.  The biases only steer the
+selection, so they get no gradient (as with ``topk`` indices in the eager router).
 """
 
 from __future__ import annotations
@@ -37,17 +37,24 @@ class _RouteFn(torch.autograd.Function):
     def backward(ctx, d_idx, d_gate: Tensor | None, d_aff: Tensor | None):  # type: ignore[override]
         z2, aff, idx, gate = ctx.saved_tensors
         e = aff.shape[-1]
-        da = torch.zeros_like(aff) if d_aff is None else d_aff.reshape(-1, e).float().clone()
-        if d_gate is not None:
-            dg = d_gate.reshape(-1, gate.shape[-1]).float()
-            s = aff.gather(-1, idx).sum(-1, keepdim=True) + 1.0e-12
-            d_raw = (dg - (dg * gate).sum(-1, keepdim=True)) / s
-            da.scatter_add_(-1, idx, d_raw)
-        if ctx.mode == 0:   # aff = sqrt(softplus(z) + eps): d aff / dz = sigmoid(z) / (2 aff)
-            dz = da * torch.sigmoid(z2) / (2.0 * aff)
-        else:               # aff = sigmoid(z)
-            dz = da * aff * (1.0 - aff)
+        dz = torch.empty_like(z2)
+        dg = None if d_gate is None else d_gate.reshape(-1, gate.shape[-1]).float().contiguous()
+        da = None if d_aff is None else d_aff.reshape(-1, e).float().contiguous()
+        backend.ext().router_bwd(z2, aff, idx, gate, dg, da, ctx.mode, dz)
         return dz.view(*ctx.lead, e), None, None, None, None, None
+
+
+def route_backward_reference(z: Tensor, aff: Tensor, idx: Tensor, gate: Tensor, d_gate: Tensor | None,
+                             d_aff: Tensor | None, mode: int) -> Tensor:
+    """PyTorch statement of the backward kernel (its test oracle)."""
+    da = torch.zeros_like(aff) if d_aff is None else d_aff.float().clone()
+    if d_gate is not None:
+        s = aff.gather(-1, idx).sum(-1, keepdim=True) + 1.0e-12
+        d_raw = (d_gate - (d_gate * gate).sum(-1, keepdim=True)) / s
+        da.scatter_add_(-1, idx, d_raw)
+    if mode == 0:   # aff = sqrt(softplus(z) + eps): d aff / dz = sigmoid(z) / (2 aff)
+        return da * torch.sigmoid(z) / (2.0 * aff)
+    return da * aff * (1.0 - aff)
 
 
 def fused_route(logits: Tensor, k: int, affinity_fn: str, bias: Tensor | None, modality_bias: Tensor | None,
@@ -58,4 +65,4 @@ def fused_route(logits: Tensor, k: int, affinity_fn: str, bias: Tensor | None, m
     return _RouteFn.apply(logits, k, mode, bias, modality_bias if vis is not None else None, vis)
 
 
-__all__ = ["fused_route"]
+__all__ = ["fused_route", "route_backward_reference"]

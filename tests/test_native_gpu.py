@@ -195,16 +195,13 @@ def test_fused_ce(cuda):
         assert _rel(gh1, gh0) < 3e-2 and _rel(gw1, gw0) < 3e-2
 
 
-def test_tiny_model_native_step(cuda):
-    """Whole tiny model on the native path: loss close to the eager oracle, grads aligned."""
-    from saint_llm_b200.config import ModelConfig
+def _tiny_native_vs_eager(cuda, cfg):
     from saint_llm_b200.models import SaintLLM
     from saint_llm_b200.ops import backend
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.losses import make_loss_fn
 
     torch.manual_seed(0)
-    cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
     model = SaintLLM(cfg).to(cuda)
     x = torch.randint(0, cfg.vocab_size, (2, 64), device=cuda)
     with backend.eager_mode():
@@ -216,14 +213,44 @@ def test_tiny_model_native_step(cuda):
     l1.backward()
     torch.cuda.synchronize()
     check_errors(cuda)
-    assert torch.isfinite(l1) and abs(l1.item() - l0.item()) < 0.05 * abs(l0.item())
-    cos = []
+    params = dict(model.named_parameters())
+    rel = {}
     for k, ref in g0.items():
-        p = dict(model.named_parameters())[k]
-        assert p.grad is not None and torch.isfinite(p.grad).all(), k
+        g = params[k].grad
+        assert g is not None and torch.isfinite(g).all(), k
         if ref.norm() > 1e-6:
-            cos.append(F.cosine_similarity(p.grad.flatten().float(), ref.flatten(), dim=0).item())
-    assert sum(c > 0.9 for c in cos) >= 0.8 * len(cos), sorted(cos)[:10]
+            rel[k] = ((g.float() - ref.float()).norm() / ref.float().norm()).item()
+    return l0.item(), l1.item(), rel
+
+
+def test_tiny_model_native_step_per_parameter(cuda):
+    """Whole tiny model, native path against the eager fp32 oracle, with every discrete
+    choice pinned (hash routing in every MoE layer, CSA top-k covering every block): the
+    loss agrees to bf16 precision and EVERY parameter's gradient to a few percent."""
+    from saint_llm_b200.config import CSAConfig, ModelConfig
+
+    base = ModelConfig.tiny()
+    cfg = base.model_copy(update={
+        "moe_use_grouped_gemm": True,
+        "moe": base.moe.model_copy(update={"hash_routed_layers": base.n_layers}),
+        "csa": CSAConfig(compression_rate=2, indexer_query_heads=2, indexer_head_dim=16, attention_top_k=64),
+    })
+    l0, l1, rel = _tiny_native_vs_eager(cuda, cfg)
+    assert abs(l1 - l0) < 5e-3 * abs(l0), (l0, l1)
+    worst = sorted(rel.items(), key=lambda kv: -kv[1])[:5]
+    assert worst[0][1] < 0.05, worst
+
+
+def test_tiny_model_native_step_learned_routing(cuda):
+    """Learned routing and indexer selection (discrete choices that bf16 rounding can flip
+    for a few tokens): loss within 1 %, 95 % of the parameters within 5 % and none beyond 50 %."""
+    from saint_llm_b200.config import ModelConfig
+
+    cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+    l0, l1, rel = _tiny_native_vs_eager(cuda, cfg)
+    assert abs(l1 - l0) < 1e-2 * abs(l0), (l0, l1)
+    vals = sorted(rel.values())
+    assert vals[int(0.95 * (len(vals) - 1))] < 0.05 and vals[-1] < 0.5, sorted(rel.items(), key=lambda kv: -kv[1])[:5]
 
 
 def test_smoke_entry(cuda):

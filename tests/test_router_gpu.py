@@ -37,3 +37,24 @@ def test_fused_router_matches_eager(cuda, fn, E, k):
     assert torch.allclose(aff, a, atol=1e-6, rtol=1e-5)
     assert torch.allclose(gate, rgate, atol=1e-6, rtol=1e-5)
     assert torch.allclose(dz, z.grad, atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("with_gate,with_aff", [(True, True), (True, False), (False, True)])
+def test_router_backward_kernel_matches_oracle(cuda, mode, with_gate, with_aff):
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.router import route_backward_reference
+
+    torch.manual_seed(mode)
+    T, E, k = 300, 64, 6
+    z = torch.randn(T, E, device=cuda)
+    aff = torch.sqrt(torch.nn.functional.softplus(z) + 1e-12) if mode == 0 else torch.sigmoid(z)
+    idx = torch.stack([torch.randperm(E)[:k] for _ in range(T)]).to(cuda)
+    gate = aff.gather(-1, idx)
+    gate = gate / (gate.sum(-1, keepdim=True) + 1e-12)
+    dg = torch.randn(T, k, device=cuda) if with_gate else None
+    da = torch.randn(T, E, device=cuda) if with_aff else None
+    dz = torch.empty_like(z)
+    backend.ext().router_bwd(z, aff, idx, gate, dg, da, mode, dz)
+    want = route_backward_reference(z, aff, idx, gate, dg, da, mode)
+    torch.testing.assert_close(dz, want, rtol=1e-5, atol=1e-6)

@@ -95,18 +95,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def count_native_launches(fn) -> tuple[int, float]:
-    """Kernels of this framework (namespace sv4) launched by one call of fn, and the summed
+def count_native_launches(fn) -> tuple[int, float, list]:
+    """Kernels of this framework (namespace sv4) launched by one call of fn, the summed
     device time of every kernel of that call in ms (compared with the step time it shows how
-    much of the step the GPU spends between kernels)."""
+    much of the step the GPU spends between kernels), and the 15 kernels with the largest
+    total time (name, launches, ms)."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         fn()
         torch.cuda.synchronize()
-    kernels = [ev for ev in prof.events() if ev.device_type == torch.autograd.DeviceType.CUDA]
-    busy_us = sum(ev.time_range.elapsed_us() for ev in kernels if "Memcpy" not in ev.name and "Memset" not in ev.name)
-    return sum(1 for ev in kernels if "sv4::" in ev.name), busy_us / 1000.0
+    kernels = [ev for ev in prof.events() if ev.device_type == torch.autograd.DeviceType.CUDA
+               and "Memcpy" not in ev.name and "Memset" not in ev.name]
+    busy_us = sum(ev.time_range.elapsed_us() for ev in kernels)
+    per: dict[str, list[float]] = {}
+    for ev in kernels:
+        key = ev.name.split("(")[0][:80]
+        rec = per.setdefault(key, [0, 0.0])
+        rec[0] += 1
+        rec[1] += ev.time_range.elapsed_us()
+    top = sorted(per.items(), key=lambda kv: -kv[1][1])[:15]
+    return (sum(1 for ev in kernels if "sv4::" in ev.name), busy_us / 1000.0,
+            [[k, v[0], round(v[1] / 1000.0, 2)] for k, v in top])
 
 
 def run_config(args, world: int):
@@ -220,7 +230,7 @@ def run_ours(args) -> dict:
     with PhaseRecorder(device) as rec:
         device_step()
     phases = rec.summary()
-    n_native, busy_ms = count_native_launches(device_step)
+    n_native, busy_ms, top_kernels = count_native_launches(device_step)
     launches = n_native * args.steps
     tokens_per_step = world * args.seqs_per_gpu * args.seq_len
     result = {
@@ -244,6 +254,7 @@ def run_ours(args) -> dict:
                    "final_loss": final_loss,
                    "phases_ms": phases,
                    "kernel_busy_ms_per_step": round(busy_ms, 1),
+                   "top_kernels_ms_per_step": top_kernels,
                    "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",

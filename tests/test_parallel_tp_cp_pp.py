@@ -19,27 +19,49 @@ def _port():
         return s.getsockname()[1]
 
 
-def _run(fn, ws=2):
+def _run(fn, ws=2, nccl=False):
+    """Run ``fn(rank, ws)`` on ``ws`` spawned ranks: gloo on CPU, or (``nccl``) one GPU per
+    rank over NCCL with the model's math on the eager fp32 path (the comparison against one
+    process stays exact; the collectives and p2p exchanges are the real NCCL ones)."""
     ctx = mp.get_context("spawn")
     q, port = ctx.Queue(), _port()
-    ps = [ctx.Process(target=_entry, args=(fn, r, ws, port, q)) for r in range(ws)]
+    ps = [ctx.Process(target=_entry, args=(fn, r, ws, port, q, nccl)) for r in range(ws)]
     for p in ps:
         p.start()
-    res = [q.get(timeout=240) for _ in range(ws)]
+    res = [q.get(timeout=300) for _ in range(ws)]
     for p in ps:
         p.join(timeout=60)
     return res
 
 
-def _entry(fn, rank, ws, port, q):
+DEV = torch.device("cpu")
+
+
+def _entry(fn, rank, ws, port, q, nccl=False):
+    import datetime
+
+    global DEV
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    if nccl:
+        DEV = torch.device("cuda", rank)
+        torch.cuda.set_device(DEV)
+        dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=120),
+                                device_id=DEV)
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
-        q.put(fn(rank, ws))
+        from saint_llm_b200.ops import backend
+
+        with backend.eager_mode(nccl):
+            q.put(fn(rank, ws))
     except Exception as e:  # noqa: BLE001
         q.put((rank, f"error: {type(e).__name__}: {e}"))
     finally:
         dist.destroy_process_group()
+
+
+def _ids(*shape, vocab):
+    return torch.randint(0, vocab, shape).to(DEV)
 
 
 def _model(**upd):
@@ -48,7 +70,7 @@ def _model(**upd):
 
     cfg = ModelConfig.tiny().model_copy(update=upd)
     torch.manual_seed(0)
-    return SaintLLM(cfg)
+    return SaintLLM(cfg).to(DEV)
 
 
 def _close(a, b, tol=2e-4):
@@ -63,7 +85,7 @@ def _tp(rank, ws):
     tp = copy.deepcopy(full)
     sync = apply_tensor_parallel(tp)
     torch.manual_seed(5)
-    ids = torch.randint(0, full.cfg.vocab_size, (2, 24))
+    ids = _ids(2, 24, vocab=full.cfg.vocab_size)
     lf = full(ids)["logits"]
     lf.square().mean().backward()
     lt = tp(ids)["logits"]
@@ -107,7 +129,7 @@ def _cp(rank, ws):
         full = _model(**upd)
         cp = copy.deepcopy(full)
         torch.manual_seed(7)
-        ids = torch.randint(0, full.cfg.vocab_size, (2, 64))
+        ids = _ids(2, 64, vocab=full.cfg.vocab_size)
         h, _ = full.backbone(ids)
         logits = full.logits(h).float()
         ref = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
@@ -141,7 +163,7 @@ def _pp(rank, ws):
     full = _model()
     pp = copy.deepcopy(full)
     torch.manual_seed(9)
-    micro = [torch.randint(0, full.cfg.vocab_size, (1, 16)) for _ in range(4)]
+    micro = [_ids(1, 16, vocab=full.cfg.vocab_size) for _ in range(4)]
     ref_losses = []
     for ids in micro:
         h, _ = full.backbone(ids)
@@ -203,7 +225,7 @@ def _dualpipe(rank, ws):
     full = _model()
     pp = copy.deepcopy(full)
     torch.manual_seed(9)
-    micro = [torch.randint(0, full.cfg.vocab_size, (1, 16)) for _ in range(5)]
+    micro = [_ids(1, 16, vocab=full.cfg.vocab_size) for _ in range(5)]
     ref_losses = []
     for ids in micro:
         h, _ = full.backbone(ids)
@@ -229,3 +251,21 @@ def test_dualpipe_v_matches_single_process(ws):
     res = _run(_dualpipe, ws)
     for r in res:
         assert r[1] is True and r[2] >= 3, r
+
+
+# ------------------------------------------------------------------ the same on GPUs over NCCL
+_two_gpus = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                               reason="needs 2 GPUs")
+
+
+@pytest.mark.gpu
+@_two_gpus
+@pytest.mark.parametrize("name", ["tp", "cp", "pp", "dualpipe"])
+def test_parallel_layouts_on_gpus_over_nccl(name):
+    """TP, CP, 1F1B and DualPipe-V with NCCL collectives and p2p between two GPUs, checked
+    against the same model run in one process (NCCL_NVLS_ENABLE=0 as for every multi-GPU test)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    fn = {"tp": _tp, "cp": _cp, "pp": _pp, "dualpipe": _dualpipe}[name]
+    res = _run(fn, 2, nccl=True)
+    for r in res:
+        assert r[1] is True, r

@@ -793,4 +793,126 @@ void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel, torch::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Indexer top-k straight to the CSA selection bitmask: per query row, the k highest finite
+// scores among n blocks (masked blocks are -inf and never picked; ties at the k-th score are
+// taken lowest block index first), written as bits of sel (B*T rows of `words` uint32).  The
+// k-th largest score is found by radix selection over an order-preserving integer key, 8 bits
+// per pass, reading the row from L2; no (rows, k) index tensor and no sort.
+namespace {
+__device__ __forceinline__ uint32_t score_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+}  // namespace
+
+__global__ void __launch_bounds__(256) indexer_select_kernel(const float* __restrict__ scores, int n, int k,
+                                                            int words, uint32_t* __restrict__ sel) {
+  __shared__ unsigned hist[256];
+  __shared__ unsigned s_cnt[8];
+  __shared__ uint32_t s_prefix;
+  __shared__ unsigned s_need;
+  __shared__ unsigned wsum[512 + 1];
+  const int row = blockIdx.x;
+  const float* sr = scores + static_cast<int64_t>(row) * n;
+  uint32_t* out = sel + static_cast<int64_t>(row) * words;
+  // finite scores only
+  unsigned fin = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) fin += isfinite(sr[i]) ? 1u : 0u;
+  for (int o = 16; o > 0; o >>= 1) fin += __shfl_xor_sync(0xffffffffu, fin, o);
+  if ((threadIdx.x & 31) == 0) s_cnt[threadIdx.x >> 5] = fin;
+  __syncthreads();
+  fin = 0;
+  for (int w = 0; w < 8; ++w) fin += s_cnt[w];
+  const bool all = static_cast<unsigned>(k) >= fin;
+  uint32_t tau = 0;  // keep keys > tau, plus `need` ties at tau (lowest index first)
+  unsigned need = 0;
+  if (!all) {
+    uint32_t prefix = 0, mask = 0;
+    unsigned want = static_cast<unsigned>(k);
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = sr[i];
+        if (!isfinite(v)) continue;
+        const uint32_t key = score_key(v);
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned acc = 0;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (acc + hist[b] >= want) break;
+          acc += hist[b];
+        }
+        s_prefix = prefix | (static_cast<uint32_t>(b) << shift);
+        s_need = want - acc;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      want = s_need;
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    tau = prefix;
+    need = want;  // how many of the keys equal to tau are kept
+  }
+  // per-word tie counts, exclusive scan in word order, then the bits
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    unsigned ties = 0;
+    if (!all) {
+      for (int j = 0; j < 32; ++j) {
+        const int i = w * 32 + j;
+        if (i < n && isfinite(sr[i]) && score_key(sr[i]) == tau) ++ties;
+      }
+    }
+    wsum[w] = ties;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned acc = 0;
+    for (int w = 0; w < words; ++w) {
+      const unsigned t = wsum[w];
+      wsum[w] = acc;
+      acc += t;
+    }
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    uint32_t bits = 0;
+    unsigned rank = wsum[w];
+    for (int j = 0; j < 32; ++j) {
+      const int i = w * 32 + j;
+      if (i >= n) break;
+      const float v = sr[i];
+      if (!isfinite(v)) continue;
+      if (all) {
+        bits |= 1u << j;
+        continue;
+      }
+      const uint32_t key = score_key(v);
+      if (key > tau || (key == tau && rank++ < need)) bits |= 1u << j;
+    }
+    out[w] = bits;
+  }
+}
+
+// scores (B, T, n) fp32 (block-causally masked with -inf) -> sel (B, T, words) int32 bitmask of
+// the top-k finite blocks per row.
+void indexer_select_mask(torch::Tensor scores, int64_t k, torch::Tensor sel) {
+  c10::cuda::CUDAGuard guard(scores.device());
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.is_contiguous(), "scores: contiguous fp32");
+  const int64_t n = scores.size(-1);
+  const int64_t rows = scores.numel() / std::max<int64_t>(n, 1);
+  const int64_t words = sel.size(-1);
+  TORCH_CHECK(sel.scalar_type() == at::kInt && sel.is_contiguous() && sel.numel() == rows * words &&
+                  words * 32 >= n && words <= 512, "sel: (rows, words) int32, n <= 16384");
+  if (rows == 0) return;
+  indexer_select_kernel<<<static_cast<unsigned>(rows), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      scores.data_ptr<float>(), static_cast<int>(n), static_cast<int>(k), static_cast<int>(words),
+      reinterpret_cast<uint32_t*>(sel.data_ptr<int32_t>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace sv4

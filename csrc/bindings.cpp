@@ -58,10 +58,14 @@ void moe_route_plan(torch::Tensor idx, int64_t n_experts, int64_t k, torch::Tens
 void moe_gather(torch::Tensor h, torch::Tensor row_token, torch::Tensor out, torch::Tensor err);
 void moe_combine(torch::Tensor y, torch::Tensor pos, c10::optional<torch::Tensor> w, torch::Tensor out,
                  torch::Tensor err);
-void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor dy,
-                     torch::Tensor dw, torch::Tensor err);
+void moe_combine_bwd(torch::Tensor dout, c10::optional<torch::Tensor> y, torch::Tensor pos, torch::Tensor w,
+                     torch::Tensor dy, c10::optional<torch::Tensor> dw, torch::Tensor err);
+void swiglu_bwd_gate(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi,
+                     torch::Tensor act, torch::Tensor row_pair, torch::Tensor gate, torch::Tensor dgate,
+                     torch::Tensor err);
 void moe_zero_pad_rows(torch::Tensor row_token, torch::Tensor buf);
-void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi);
+void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi,
+                c10::optional<torch::Tensor> act);
 // norm.cu
 void rmsnorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor rstd, double eps);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dx);
@@ -93,6 +97,7 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor k
               torch::Tensor o_c, torch::Tensor lse, torch::Tensor dout, torch::Tensor dq, torch::Tensor dk,
               torch::Tensor dv, torch::Tensor dkv, torch::Tensor dsink, torch::Tensor err);
 void csa_select_mask(torch::Tensor top, int64_t n, torch::Tensor sel, torch::Tensor err);
+void indexer_select_mask(torch::Tensor scores, int64_t k, torch::Tensor sel);
 // sampling.cu
 void sample_tokens(torch::Tensor logits, c10::optional<torch::Tensor> bias, double temperature, int64_t top_k,
                    double top_p, torch::Tensor u, torch::Tensor out, c10::optional<torch::Tensor> thr);
@@ -136,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &sv4::attn_fwd);
   m.def("attn_bwd", &sv4::attn_bwd);
   m.def("csa_select_mask", &sv4::csa_select_mask);
+  m.def("indexer_select_mask", &sv4::indexer_select_mask);
   m.def("sample_tokens", &sv4::sample_tokens);
   m.def("ce_fwd", &sv4::ce_fwd);
   m.def("ce_bwd", &sv4::ce_bwd);
@@ -168,6 +174,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &sv4::moe_combine_bwd);
   m.def("moe_zero_pad_rows", &sv4::moe_zero_pad_rows);
   m.def("swiglu_bwd", &sv4::swiglu_bwd);
+  m.def("swiglu_bwd_gate", &sv4::swiglu_bwd_gate);
   m.def("rmsnorm_fwd", &sv4::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &sv4::rmsnorm_bwd);
   m.def("rope_norm_fwd", &sv4::rope_norm_fwd);

@@ -208,42 +208,56 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const
   const int p = pos[pair];
   const bool ok = lane == 0 ? index_ok(p, 0, rows, err) : (p >= 0 && p < rows);
   if (!ok) {  // the pair's gradient row cannot be placed: no write, zero gate gradient
-    if (lane == 0) dw[pair] = 0.f;
+    if (lane == 0 && dw != nullptr) dw[pair] = 0.f;
     return;
   }
   const float g = w[pair];
   float dot = 0.f;
   for (int d = lane * 8; d < D; d += 32 * 8) {
     const uint4 a = *reinterpret_cast<const uint4*>(dout + static_cast<int64_t>(t) * D + d);
-    const uint4 b = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(p) * D + d);
     const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
-    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
     uint4 o;
     __nv_bfloat162* ho = reinterpret_cast<__nv_bfloat162*>(&o);
+    if (y != nullptr) {
+      const uint4 b = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(p) * D + d);
+      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 fa = __bfloat1622float2(ha[q]);
-      const float2 fb = __bfloat1622float2(hb[q]);
-      dot += fa.x * fb.x + fa.y * fb.y;
-      ho[q] = __floats2bfloat162_rn(fa.x * g, fa.y * g);
+      for (int q = 0; q < 4; ++q) {
+        const float2 fa = __bfloat1622float2(ha[q]);
+        const float2 fb = __bfloat1622float2(hb[q]);
+        dot += fa.x * fb.x + fa.y * fb.y;
+        ho[q] = __floats2bfloat162_rn(fa.x * g, fa.y * g);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fa = __bfloat1622float2(ha[q]);
+        ho[q] = __floats2bfloat162_rn(fa.x * g, fa.y * g);
+      }
     }
     *reinterpret_cast<uint4*>(dy + static_cast<int64_t>(p) * D + d) = o;
   }
+  if (y == nullptr || dw == nullptr) return;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
   if (lane == 0) dw[pair] = dot;
 }
 
-void moe_combine_bwd(torch::Tensor dout, torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor dy,
-                     torch::Tensor dw, torch::Tensor err) {
+// y / dw omitted: only the gate-scaled output gradient rows are written (the gate gradient
+// then comes from swiglu_bwd_gate, which needs no saved expert outputs).
+void moe_combine_bwd(torch::Tensor dout, c10::optional<torch::Tensor> y, torch::Tensor pos, torch::Tensor w,
+                     torch::Tensor dy, c10::optional<torch::Tensor> dw, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(dout.device());
   const int n_pairs = pos.numel(), k = pos.size(1), D = dout.size(1);
   TORCH_CHECK(D % 8 == 0, "D % 8");
+  TORCH_CHECK(y.has_value() == dw.has_value(), "y and dw come together");
   if (n_pairs == 0) return;
+  const int64_t rows = y.has_value() ? std::min(y->size(0), dy.size(0)) : dy.size(0);
   combine_bwd_kernel<<<(n_pairs * 32 + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()),
-      pos.data_ptr<int>(), w.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()),
-      dw.data_ptr<float>(), n_pairs, k, D, static_cast<int>(std::min(y.size(0), dy.size(0))), err.data_ptr<int>());
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+      y.has_value() ? reinterpret_cast<const __nv_bfloat16*>(y->data_ptr()) : nullptr, pos.data_ptr<int>(),
+      w.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()),
+      dw.has_value() ? dw->data_ptr<float>() : nullptr, n_pairs, k, D, static_cast<int>(rows), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -269,9 +283,12 @@ void moe_zero_pad_rows(torch::Tensor row_token, torch::Tensor buf) {
 
 // d_pre = [d_gate | d_up] from d_act and pre = [gate | up] (rows x 2I).
 //   act = silu(min(g, gmax)) * clamp(u, lo, hi)
+// With act != nullptr the forward activation act = silu(min(g, gmax)) * clamp(u, lo, hi) is
+// recomputed from the saved pre-activations and written too (the forward does not keep it).
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dact, int64_t ld_dact,
                                   const __nv_bfloat16* __restrict__ pre, __nv_bfloat16* __restrict__ dpre,
-                                  int64_t rows, int I, float gmax, float lo, float hi) {
+                                  int64_t rows, int I, float gmax, float lo, float hi,
+                                  __nv_bfloat16* __restrict__ act) {
   const int64_t n = rows * I;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -289,21 +306,113 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dact, int64_
     const float du = (u >= lo && u <= hi) ? da * silu : 0.0f;
     dpre[r * 2 * I + c] = __float2bfloat16(dg);
     dpre[r * 2 * I + I + c] = __float2bfloat16(du);
+    if (act != nullptr) act[r * I + c] = __float2bfloat16(silu * uc);
   }
 }
 
-void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi) {
+void swiglu_bwd(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi,
+                c10::optional<torch::Tensor> act) {
   c10::cuda::CUDAGuard guard(dact.device());
   const int64_t rows = dact.size(0);
   const int I = dact.size(1);
   TORCH_CHECK(dact.stride(1) == 1 && pre.is_contiguous() && dpre.is_contiguous(), "swiglu_bwd layout");
+  TORCH_CHECK(!act.has_value() || (act->is_contiguous() && act->size(0) == rows && act->size(1) == I &&
+                                   act->scalar_type() == at::kBFloat16), "act: contiguous (rows, I) bf16");
   if (rows == 0) return;
   const int64_t n = rows * I;
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16));
   swiglu_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dact.data_ptr()), dact.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(pre.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()),
-      rows, I, static_cast<float>(gmax), static_cast<float>(lo), static_cast<float>(hi));
+      rows, I, static_cast<float>(gmax), static_cast<float>(lo), static_cast<float>(hi),
+      act.has_value() ? reinterpret_cast<__nv_bfloat16*>(act->data_ptr()) : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// SwiGLU backward of the routed experts with the gate gradient folded in, one warp per row:
+// dpre from d(act) and the saved pre-activations, act recomputed (for the down projection's
+// weight gradient), and for the (token, slot) pair p that owns the row
+//   dgate[p] = <dout_t, y_row> = <dout_t Wd, act_row> = <dact_row, act_row> / gate[p]
+// because dact_row = (gate[p] dout_t) Wd.  The expert outputs y therefore need not be kept
+// for the backward.  row_pair[r] = p, or -1 for padding rows (whose dgate is not written).
+__global__ void swiglu_bwd_gate_kernel(const __nv_bfloat16* __restrict__ dact, const __nv_bfloat16* __restrict__ pre,
+                                       __nv_bfloat16* __restrict__ dpre, __nv_bfloat16* __restrict__ act, int64_t rows,
+                                       int I, float gmax, float lo, float hi, const int* __restrict__ row_pair,
+                                       const float* __restrict__ gate, float* __restrict__ dgate, int n_pairs,
+                                       int* err) {
+  const int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __nv_bfloat16* dr = dact + r * I;
+  const __nv_bfloat16* pg = pre + r * 2 * I;
+  float dot = 0.f;
+  for (int c = lane * 8; c < I; c += 256) {
+    const uint4 va = *reinterpret_cast<const uint4*>(dr + c);
+    const uint4 vg = *reinterpret_cast<const uint4*>(pg + c);
+    const uint4 vu = *reinterpret_cast<const uint4*>(pg + I + c);
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&va);
+    const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&vg);
+    const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&vu);
+    uint4 og, ou, oa;
+    __nv_bfloat162* pog = reinterpret_cast<__nv_bfloat162*>(&og);
+    __nv_bfloat162* pou = reinterpret_cast<__nv_bfloat162*>(&ou);
+    __nv_bfloat162* poa = reinterpret_cast<__nv_bfloat162*>(&oa);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 da = __bfloat1622float2(ha[q]);
+      const float2 g2 = __bfloat1622float2(hg[q]);
+      const float2 u2 = __bfloat1622float2(hu[q]);
+      float dg[2], du[2], a[2];
+      const float dav[2] = {da.x, da.y}, gv[2] = {g2.x, g2.y}, uv[2] = {u2.x, u2.y};
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float gc = fminf(gv[e], gmax);
+        const float uc = fminf(fmaxf(uv[e], lo), hi);
+        const float sig = 1.0f / (1.0f + __expf(-gc));
+        const float silu = gc * sig;
+        const float dsilu = sig * (1.0f + gc * (1.0f - sig));
+        dg[e] = (gv[e] <= gmax) ? dav[e] * uc * dsilu : 0.0f;
+        du[e] = (uv[e] >= lo && uv[e] <= hi) ? dav[e] * silu : 0.0f;
+        a[e] = silu * uc;
+      }
+      pog[q] = __floats2bfloat162_rn(dg[0], dg[1]);
+      pou[q] = __floats2bfloat162_rn(du[0], du[1]);
+      poa[q] = __floats2bfloat162_rn(a[0], a[1]);
+      const float2 ar = __bfloat1622float2(poa[q]);  // the act the weight gradient will read
+      dot += dav[0] * ar.x + dav[1] * ar.y;
+    }
+    *reinterpret_cast<uint4*>(dpre + r * 2 * I + c) = og;
+    *reinterpret_cast<uint4*>(dpre + r * 2 * I + I + c) = ou;
+    *reinterpret_cast<uint4*>(act + r * I + c) = oa;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+  if (lane == 0) {
+    const int p = row_pair[r];
+    if (p >= 0 && index_ok(p, 0, n_pairs, err)) {
+      const float g = gate[p];
+      dgate[p] = g != 0.f ? dot / g : 0.f;
+    }
+  }
+}
+
+void swiglu_bwd_gate(torch::Tensor dact, torch::Tensor pre, torch::Tensor dpre, double gmax, double lo, double hi,
+                     torch::Tensor act, torch::Tensor row_pair, torch::Tensor gate, torch::Tensor dgate,
+                     torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(dact.device());
+  const int64_t rows = dact.size(0);
+  const int I = dact.size(1);
+  TORCH_CHECK(dact.is_contiguous() && pre.is_contiguous() && dpre.is_contiguous() && act.is_contiguous() &&
+                  I % 8 == 0 && act.size(0) == rows && act.size(1) == I, "swiglu_bwd_gate layout (I % 8 == 0)");
+  TORCH_CHECK(row_pair.scalar_type() == at::kInt && row_pair.numel() >= rows && gate.scalar_type() == at::kFloat &&
+                  dgate.scalar_type() == at::kFloat && gate.numel() == dgate.numel(), "row_pair / gate / dgate");
+  if (rows == 0) return;
+  swiglu_bwd_gate_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0,
+                           at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dact.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(pre.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()), reinterpret_cast<__nv_bfloat16*>(act.data_ptr()), rows, I,
+      static_cast<float>(gmax), static_cast<float>(lo), static_cast<float>(hi), row_pair.data_ptr<int>(),
+      gate.data_ptr<float>(), dgate.data_ptr<float>(), static_cast<int>(gate.numel()), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -165,10 +165,10 @@ def fused_attention(q: Tensor, k: Tensor, v: Tensor, *, window: int, sink: Tenso
 
 
 @torch.no_grad()
-def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
-    """Lightning-indexer top-k block ids (B, T, k) with -1 for invalid picks.  The scores
-    (sum over heads of the weighted ReLU'd dot products, masked block-causally) come from
-    the fused ``indexer_scores`` kernel in one pass; only (B, T, blocks) is written."""
+def _indexer_scores(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> tuple[Tensor | None, int, int]:
+    """(scores (B, T, blocks) with -inf where block-causally masked, k_eff, n_blocks) from
+    the fused ``indexer_scores`` kernel (one pass; only the (B, T, blocks) scores are
+    written).  scores is None when no block exists yet."""
     b, t, _ = h.shape
     comp = idx.compressor
     y = lin.linear(h, torch.cat([_bf16(idx.w_dq.weight), _bf16(idx.w_w.weight), _bf16(comp.w_b_kv.weight),
@@ -179,7 +179,7 @@ def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
     n_blocks = keys.shape[1]
     k_eff = min(idx.top_k, n_blocks)
     if k_eff == 0:
-        return torch.full((b, t, 0), -1, dtype=torch.long, device=h.device)
+        return None, 0, n_blocks
     m_eff = t // n_blocks
     vis_bias = None
     if is_visual is not None:
@@ -196,8 +196,30 @@ def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
     backend.ext().indexer_scores(q.contiguous(), keys_b.contiguous(), w.float().contiguous(),
                                  None if vis_bias is None else vis_bias.contiguous(), m_eff, 0, scores,
                                  gemm.error_word(h.device))
+    return scores, k_eff, n_blocks
+
+
+def indexer_topk(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor:
+    """Lightning-indexer top-k block ids (B, T, k) with -1 for invalid picks."""
+    b, t, _ = h.shape
+    scores, k_eff, _ = _indexer_scores(idx, h, is_visual)
+    if scores is None:
+        return torch.full((b, t, 0), -1, dtype=torch.long, device=h.device)
     vals, ids = scores.topk(k_eff, dim=-1)
     return torch.where(torch.isfinite(vals), ids, torch.full_like(ids, -1))
+
+
+def indexer_select(idx: nn.Module, h: Tensor, is_visual: Tensor | None) -> Tensor | None:
+    """The CSA selection bitmask (B, T, ceil(blocks / 32)) int32 of the indexer's top-k
+    finite blocks per query, straight from the scores by one native kernel (radix selection
+    of the k-th score; ties at it taken lowest block index first); None when no block exists."""
+    b, t, _ = h.shape
+    scores, k_eff, n_blocks = _indexer_scores(idx, h, is_visual)
+    if scores is None:
+        return None
+    sel = torch.empty(b, t, (n_blocks + 31) // 32, dtype=torch.int32, device=h.device)
+    backend.ext().indexer_select_mask(scores, k_eff, sel)
+    return sel
 
 
 def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor | None) -> Tensor:
@@ -234,10 +256,8 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
         if n_blocks > 0:
             kvn = rms_norm(_bf16(comp), layer.k_norm.weight, layer.k_norm.eps)
             if kind == "csa":
-                top = indexer_topk(layer.indexer, hb, is_visual)
-                if top.shape[-1] > 0:
-                    sel = torch.empty(b, t, (n_blocks + 31) // 32, dtype=torch.int32, device=h.device)
-                    backend.ext().csa_select_mask(top.contiguous(), n_blocks, sel, gemm.error_word(h.device))
+                sel = indexer_select(layer.indexer, hb, is_visual)
+                if sel is not None:
                     mode = 2
             else:
                 mode = 1
@@ -248,4 +268,4 @@ def attention_forward(layer: nn.Module, kind: str, h: Tensor, is_visual: Tensor 
     return layer.output.forward_flat(flat)
 
 
-__all__ = ["attention_forward", "fused_linear", "indexer_topk"]
+__all__ = ["attention_forward", "fused_linear", "indexer_select", "indexer_topk"]

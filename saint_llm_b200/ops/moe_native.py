@@ -57,6 +57,14 @@ class RoutePlan:
         ext.moe_route_plan(idx.reshape(-1).to(torch.int64).contiguous(), n_experts, k, self.counts, self.seg_start,
                            self.seg_rows, self.total, self.pos, self.row_token, gemm.error_word(dev))
 
+    def row_pair(self) -> Tensor:
+        """(m_cap,) int32: the (token, slot) pair index t * k + j of each expert row, -1 for
+        padding rows."""
+        rp = torch.full((self.m_cap,), -1, dtype=torch.int32, device=self.pos.device)
+        n = self.pos.numel()
+        rp.index_put_((self.pos.reshape(-1).long(),), torch.arange(n, dtype=torch.int32, device=rp.device))
+        return rp
+
     def problems(self, mode: int, D: int, I: int) -> tuple[Tensor, Tensor, int]:
         n = self.n_experts * (2 if mode == 4 else 1)
         probs = _prob_table(n, self.pos.device)
@@ -158,17 +166,19 @@ class _RoutedExpertsFn(torch.autograd.Function):
             pr, tot, n = plan.problems(1, D, I)
             ext.grouped_gemm(1, act, wdb, wdb, y, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
             del x_p
+        del act  # recomputed from pre in the backward (saves rows x I bf16 per layer)
         out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
         gf = gate.float().contiguous()
         ext.moe_combine(y, plan.pos, gf, out, err)
-        ctx.save_for_backward(hb, gf, act, pre, y, wg, wu, wd)
+        del y  # the gate gradient is recovered in the backward without the expert outputs
+        ctx.save_for_backward(hb, gf, pre, wg, wu, wd)
         ctx.plan = plan
         ctx.clamps = clamps
         return out
 
     @staticmethod
     def backward(ctx, dout: Tensor):  # type: ignore[override]
-        hb, gf, act, pre, y, wg, wu, wd = ctx.saved_tensors
+        hb, gf, pre, wg, wu, wd = ctx.saved_tensors
         plan: RoutePlan = ctx.plan
         ext = backend.ext()
         dev = hb.device
@@ -178,23 +188,28 @@ class _RoutedExpertsFn(torch.autograd.Function):
         err = gemm.error_word(dev)
         e0 = _empty(dev)
         dy = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
-        dgate = torch.empty_like(gf)
-        ext.moe_combine_bwd(_bf16c(dout), y, plan.pos, gf, dy, dgate, err)
+        dgate = torch.zeros_like(gf)
+        ext.moe_combine_bwd(_bf16c(dout), None, plan.pos, gf, dy, None, err)
         ext.moe_zero_pad_rows(plan.row_token, dy)
         wgb, wub, wdb = _bf16c(wg), _bf16c(wu), _bf16c(wd)
-        # down projection: d_act = dy Wd ; dWd += dy^T act
+        # down projection: d_act = dy Wd
         dact = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
         pr, tot, n = plan.problems(2, D, I)
         ext.grouped_gemm(2, dy, wdb, wdb, dact, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+        # SwiGLU backward, recomputing the activation from the saved pre-activations; the
+        # gate gradient <dout, y> = <dact, act> / gate of each (token, slot) row comes along
+        dpre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
+        act = torch.empty(plan.m_cap, I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_bwd_gate(dact, pre, dpre, gmax, lo, hi, act, plan.row_pair(), gf, dgate, err)
+        del dact
+        # dWd += dy^T act
         dwd_buf = getattr(wd, "main_grad", None)
         acc_d = dwd_buf is not None
         if dwd_buf is None:
             dwd_buf = torch.zeros(E, D, I, dtype=torch.float32, device=dev)
         pr, tot, n = plan.problems(5, D, I)
         ext.grouped_gemm(4, dy, act, act, dwd_buf, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
-        # SwiGLU backward
-        dpre = torch.empty(plan.m_cap, 2 * I, dtype=torch.bfloat16, device=dev)
-        ext.swiglu_bwd(dact, pre, dpre, gmax, lo, hi)
+        del act
         # gate/up: dx_p = dpre [Wg; Wu] ; d[Wg|Wu] += dpre^T x_p
         dxp = torch.empty(plan.m_cap, D, dtype=torch.bfloat16, device=dev)
         pr, tot, n = plan.problems(3, D, I)
@@ -228,21 +243,22 @@ class _SharedSwiGLUFn(torch.autograd.Function):
         pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
         ext.swiglu_dense(hb, _bf16c(wg), _bf16c(wu), act, pre, *clamps, gemm.error_word(dev))
         y = gemm.gemm_nt(act, _bf16c(wd))
-        ctx.save_for_backward(hb, act, pre, wg, wu, wd)
+        ctx.save_for_backward(hb, pre, wg, wu, wd)  # act is recomputed from pre
         ctx.clamps = clamps
         return y
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
-        hb, act, pre, wg, wu, wd = ctx.saved_tensors
+        hb, pre, wg, wu, wd = ctx.saved_tensors
         ext = backend.ext()
         dev = hb.device
         I = wg.shape[0]
         dyb = _bf16c(dy)
         dact = gemm.gemm_nt(dyb, _bf16c(wd).t())
-        dwd = accumulate_weight_grad(wd, dyb, act)
         dpre = torch.empty_like(pre)
-        ext.swiglu_bwd(dact, pre, dpre, *ctx.clamps)
+        act = torch.empty(pre.shape[0], I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_bwd(dact, pre, dpre, *ctx.clamps, act)
+        dwd = accumulate_weight_grad(wd, dyb, act)
         dh = torch.empty_like(hb)
         ext.swiglu_dense_dgrad(dpre, _bf16c(wg), _bf16c(wu), dh, gemm.error_word(dev))
         dwg = accumulate_weight_grad(wg, dpre[:, :I], hb)
@@ -294,14 +310,14 @@ def shared_group_forward(h: Tensor, clamps: tuple[float, float, float], fp8_owne
         pre = torch.empty(T, 2 * I, dtype=torch.bfloat16, device=dev)
         ext.swiglu_dense(hb, wg, wu, act, pre, *clamps, gemm.error_word(dev))
         y = gemm.gemm_nt(act, wd)
-    return y, (hb, act, pre)
+    return y, (hb, pre)  # act is recomputed from pre in the backward
 
 
 def shared_group_backward(saved: tuple, ws: list[Tensor], clamps: tuple[float, float, float],
                           dy: Tensor) -> tuple[Tensor, list[Tensor | None]]:
     """Backward of ``shared_group_forward``: (dh, weight gradients in ``ws`` order; None
     where they went into ``main_grad``)."""
-    hb, act, pre = saved
+    hb, pre = saved
     n = len(ws) // 3
     wgs, wus, wds = ws[:n], ws[n:2 * n], ws[2 * n:]
     ext = backend.ext()
@@ -311,7 +327,9 @@ def shared_group_backward(saved: tuple, ws: list[Tensor], clamps: tuple[float, f
     dyb = _bf16c(dy)
     dact = gemm.gemm_nt(dyb, wd.t())
     dpre = torch.empty_like(pre)
-    ext.swiglu_bwd(dact, pre, dpre, *clamps)
+    act = torch.empty(pre.shape[0], I, dtype=torch.bfloat16, device=dev)
+    ext.swiglu_bwd(dact, pre, dpre, *clamps, act)
+    del dact
     dh = torch.empty_like(hb)
     ext.swiglu_dense_dgrad(dpre, wg, wu, dh, gemm.error_word(dev))
     off = 0
@@ -345,8 +363,8 @@ class _SharedGroupFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
-        hb, act, pre, *ws = ctx.saved_tensors
-        dh, grads = shared_group_backward((hb, act, pre), list(ws), ctx.clamps, dy)
+        hb, pre, *ws = ctx.saved_tensors
+        dh, grads = shared_group_backward((hb, pre), list(ws), ctx.clamps, dy)
         return (dh, None, None, *grads)
 
 

@@ -282,19 +282,20 @@ class EPCall:
             from saint_llm_b200.ops.moe_native import fp8_expert_weights, fp8_swiglu_experts
 
             gu, down = fp8_expert_weights(self.fp8_pool)
-            self.act, self.pre, _ = fp8_swiglu_experts(fp8.quantize_rows(x_rows), gu, down, plan, D, I, self.clamps,
-                                                       self.err, y_out=c.rows(c.y)[:self.R])
+            _, self.pre, _ = fp8_swiglu_experts(fp8.quantize_rows(x_rows), gu, down, plan, D, I, self.clamps,
+                                                self.err, y_out=c.rows(c.y)[:self.R])
         else:
             e0 = _empty(self.dev)
-            self.act = torch.empty(self.R, I, dtype=torch.bfloat16, device=self.dev)
+            act = torch.empty(self.R, I, dtype=torch.bfloat16, device=self.dev)
             self.pre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=self.dev)
             pr, tot, n = plan.problems(0, D, I)
-            ext.grouped_gemm(0, x_rows, _bf16c(self.wg), _bf16c(self.wu), self.act, self.pre, e0, pr, tot, n, gmax,
+            ext.grouped_gemm(0, x_rows, _bf16c(self.wg), _bf16c(self.wu), act, self.pre, e0, pr, tot, n, gmax,
                              lo, hi, 0, False, self.err)
             wdb = _bf16c(self.wd)
             pr, tot, n = plan.problems(1, D, I)
-            ext.grouped_gemm(1, self.act, wdb, wdb, c.rows(c.y), e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False,
+            ext.grouped_gemm(1, act, wdb, wdb, c.rows(c.y), e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False,
                              self.err)
+            del act  # recomputed from pre in the backward
         self.e_y = c.next_epoch(PH_Y)
         ext.ep_signal(c.flags.ptrs, PH_Y, c.rank, self.e_y)
 
@@ -332,15 +333,18 @@ class EPCall:
         dact = torch.empty(self.R, I, dtype=torch.bfloat16, device=dev)
         pr, tot, n = plan.problems(2, D, I)
         ext.grouped_gemm(2, dy, wdb, wdb, dact, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, False, err)
+        # SwiGLU backward, recomputing the activation from the saved pre-activations
+        dpre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=dev)
+        act = torch.empty(self.R, I, dtype=torch.bfloat16, device=dev)
+        ext.swiglu_bwd(dact, self.pre, dpre, gmax, lo, hi, act)
+        del self.pre, dact
         dwd_buf = getattr(self.wd, "main_grad", None)
         self.acc_d = dwd_buf is not None
         if dwd_buf is None:
             dwd_buf = torch.zeros(E_loc, D, I, dtype=torch.float32, device=dev)
         pr, tot, n = plan.problems(5, D, I)
-        ext.grouped_gemm(4, dy, self.act, self.act, dwd_buf, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
-        dpre = torch.empty(self.R, 2 * I, dtype=torch.bfloat16, device=dev)
-        ext.swiglu_bwd(dact, self.pre, dpre, gmax, lo, hi)
-        del self.act, self.pre, dact
+        ext.grouped_gemm(4, dy, act, act, dwd_buf, e0, e0, pr, tot, n, 0.0, 0.0, 0.0, 0, True, err)
+        del act
         pr, tot, n = plan.problems(3, D, I)
         ext.grouped_gemm(3, dpre, _bf16c(self.wg), _bf16c(self.wu), c.rows(c.dx), e0, e0, pr, tot, n, 0.0, 0.0, 0.0,
                          I, False, err)

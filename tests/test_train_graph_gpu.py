@@ -1,5 +1,5 @@
 """The CUDA-graph training step (one captured micro-batch replayed per micro-batch)
-trains like the eager step: the same losses over three steps, and the same accumulated
+trains like the eager step (routing pinned): the same losses over three steps, and the same accumulated
 gradients at every step -- within the spread of two eager runs (some backward kernels add
 partial results with atomics, so two eager runs are not bit-identical either) plus bf16
 rounding, floored at a small fraction of the median gradient norm (a few mHC gate
@@ -16,7 +16,10 @@ def _run(dev, graph, data):
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.launch import build_training
 
-    cfg = ModelConfig.bench_16b().model_copy(update={"n_layers": 2})
+    base = ModelConfig.bench_16b()
+    # hash routing in both MoE layers and a CSA top-k above the block count (512 > 128 at
+    # T = 512): no discrete choice can flip between runs, so later steps stay comparable
+    cfg = base.model_copy(update={"n_layers": 2, "moe": base.moe.model_copy(update={"hash_routed_layers": 2})})
     run = RunConfig(grad_accum=2, micro_batch=1, seq_len=512, cuda_graphs=graph, seed=0)
     job = build_training(cfg, run, dev)
     grads: list[dict] = []

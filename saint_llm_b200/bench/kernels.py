@@ -91,6 +91,13 @@ def bench_gemm(args: argparse.Namespace) -> None:
     from saint_llm_b200.ops import gemm
 
     m, n, k = args.m, args.n, args.k
+    if args.wgrad:  # weight-gradient layout: dW (m, n) += dY^T X with the tokens (k) as reduction
+        dy = torch.randn(k, m, device="cuda", dtype=torch.bfloat16)
+        x = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)
+        acc = torch.zeros(m, n, device="cuda", dtype=torch.float32)
+        _run(args, f"gemm_wgrad_acc {m}x{n}x{k}", lambda: gemm.gemm_nt(dy.t(), x.t(), out=acc, accumulate=True),
+             flops=2.0 * m * n * k, bytes_=2.0 * (m * k + n * k) + 8.0 * m * n)
+        return
     a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
     b = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
@@ -176,13 +183,16 @@ def bench_moe(args: argparse.Namespace) -> None:
     experts = GroupedSwiGLUExperts(dim, inter, e, device=torch.device("cuda"), dtype=torch.bfloat16)
     for p in experts.parameters():
         torch.nn.init.normal_(p, std=0.02)
+    if args.fp8:  # the training forward on block-scaled FP8 (cached weight copies)
+        experts.linear_quant = "fp8"
+        experts.fp8_weight_cache = "always"
     x = torch.randn(tok, dim, device="cuda", dtype=torch.bfloat16)
     idx = torch.stack([torch.randperm(e, device="cuda")[:k] for _ in range(tok)])
     w = torch.softmax(torch.randn(tok, k, device="cuda"), -1)
     flops = 2.0 * tok * k * 3 * dim * inter
     with torch.no_grad():
-        _run(args, f"moe_routed_fwd T={tok} D={dim} I={inter} E={e} k={k}",
-             lambda: routed_experts(x, idx, w, experts), flops=flops,
+        _run(args, f"moe_routed_fwd{'_fp8' if args.fp8 else ''} T={tok} D={dim} I={inter} E={e} k={k}",
+             lambda: routed_experts(x, idx, w, experts), flops=flops, peak_mult=2.0 if args.fp8 else 1.0,
              bytes_=2.0 * (3 * e * dim * inter + 2 * tok * dim))
 
 
@@ -250,6 +260,8 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--launches", type=int, default=0, help="run N launches and exit (profiler captures)")
     ap.add_argument("--backward", action="store_true")
+    ap.add_argument("--fp8", action="store_true", help="moe: block-scaled FP8 forward")
+    ap.add_argument("--wgrad", action="store_true", help="gemm: weight-gradient layout with fp32 accumulate")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=8192)

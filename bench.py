@@ -14,6 +14,15 @@ far beyond the 126 MB L2, so no explicit L2 flush is used.
 ``e2e`` repeats the measurement through the public ``TrainStep`` call (host batch in,
 Python float loss out) timed by the host clock around the whole call.
 
+After the timed regions: one step with per-phase CUDA events and one under the torch
+profiler (kernel counts, device-busy time, top kernels); at N = 1 with the bf16 headline a
+short measurement of the block-scaled FP8 recipe (``fp8_variant``); and the decode
+measurement of config 5 (``decode``: one replica per GPU, 64 prompts of 4096 tokens, 512
+greedy steps).
+
+The headline dtype is bf16 (at least the reference's precision): on this implementation the
+bf16 step is faster than the FP8 recipe, whose number is reported next to it.
+
 Rank 0 prints one JSON line.
 """
 
@@ -265,16 +274,56 @@ def run_ours(args) -> dict:
         comm = getattr(model, "ep_comm", None)
         if comm is not None:
             comm.close()  # collective: peers stop touching each other's buffers first
-    if not args.no_decode:
-        import gc
+    import gc
 
-        del step, model
+    del step, model
+    gc.collect()
+    torch.cuda.empty_cache()
+    if world == 1 and args.linear_quant == "bf16" and not args.no_fp8_variant:
+        result["fp8_variant"] = run_fp8_variant(args, device)
         gc.collect()
         torch.cuda.empty_cache()
+    if not args.no_decode:
         result["decode"] = run_decode(args, device, world)
     if world > 1:
         torch.distributed.destroy_process_group()
     return result if rank == 0 else {}
+
+
+def run_fp8_variant(args, device) -> dict:
+    """The same single-GPU training step with the block-scaled FP8 recipe (config 3's
+    precision): every linear the reference routes through its quantisation factory and the
+    routed experts run their forward GEMMs in FP8 (bf16 straight-through backward).  Timed
+    the same way as the headline (CUDA events, W warm-up steps) over min(K, 3) steps."""
+    torch.cuda.reset_peak_memory_stats(device)
+    fargs = argparse.Namespace(**vars(args))
+    fargs.linear_quant = "fp8"
+    cfg, model, step = build_ours(fargs, device, 1)
+    from saint_llm_b200.train.engine import SyntheticTokens
+
+    n_micro = args.seqs_per_gpu // args.micro_batch
+    data = SyntheticTokens(cfg.vocab_size, args.micro_batch, args.seq_len, n_micro, seed=0, n_batches=2)
+    it = iter(range(1 << 30))
+    k = max(1, min(args.steps, 3))
+    for _ in range(args.warmup):
+        step.run_device(data.batch(next(it)).to(device, non_blocking=True))
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(k):
+        loss = step.run_device(data.batch(next(it)).to(device, non_blocking=True))
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / k
+    out = {"value": args.seqs_per_gpu * args.seq_len / (ms / 1000.0), "unit": "tokens/s", "ms_per_step": ms,
+           "steps": k, "warmup": args.warmup, "dtype": "fp8",
+           "recipe": "block-scaled FP8 forward (1x128 activations, 128x128 weights) for the attention projections, "
+                     "shared and routed experts; bf16 straight-through backward",
+           "fp8_expert_cache": args.fp8_expert_cache, "cuda_graph": step._graph is not None,
+           "final_loss": float(loss.item()),
+           "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)}
+    del step, model
+    return out
 
 
 def run_decode(args, device, world: int) -> dict:
@@ -323,6 +372,8 @@ def main() -> None:
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (config 5) measurement")
+    ap.add_argument("--no-fp8-variant", action="store_true",
+                    help="N = 1, bf16 headline: skip the extra FP8-recipe measurement")
     ap.add_argument("--decode-batch", type=int, default=64)
     ap.add_argument("--decode-steps", type=int, default=512)
     ap.add_argument("--data-pool", type=int, default=8,

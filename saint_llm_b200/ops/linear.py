@@ -28,11 +28,14 @@ def _bf16(t: Tensor) -> Tensor:
 
 def accumulate_weight_grad(weight: Tensor, dy2: Tensor, x2: Tensor) -> Tensor | None:
     """dW = dy2^T @ x2 into weight.main_grad (returns None) or as a new tensor."""
+    from saint_llm_b200.utils.profiling import phase
+
     mg = getattr(weight, "main_grad", None)
-    if mg is not None:
-        gemm.gemm_nt(dy2.t(), x2.t(), out=mg, accumulate=True)
-        return None
-    return gemm.gemm_nt(dy2.t(), x2.t(), out_dtype=torch.float32).to(weight.dtype)
+    with phase(f"wgrad.{dy2.shape[-1]}x{x2.shape[-1]}"):
+        if mg is not None:
+            gemm.gemm_nt(dy2.t(), x2.t(), out=mg, accumulate=True)
+            return None
+        return gemm.gemm_nt(dy2.t(), x2.t(), out_dtype=torch.float32).to(weight.dtype)
 
 
 class _LinearFn(torch.autograd.Function):

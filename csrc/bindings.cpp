@@ -20,6 +20,15 @@ void fp8_quant_rows(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::opt
 void fp8_gather_quant_rows(torch::Tensor h, torch::Tensor row_token, torch::Tensor q, torch::Tensor sf,
                            torch::Tensor err);
 void fp8_quant_blocks_gu(torch::Tensor wg, torch::Tensor wu, torch::Tensor q, torch::Tensor sf);
+void fake_quant_fp4(torch::Tensor x, torch::Tensor out);
+int64_t gemm_peer_push(torch::Tensor x, torch::Tensor w, torch::Tensor out, std::vector<int64_t> peer_slots,
+                       std::vector<int64_t> peer_cnts, torch::Tensor err);
+int64_t tp_push(torch::Tensor x, std::vector<int64_t> peer_slots, std::vector<int64_t> peer_cnts);
+void tp_reduce(torch::Tensor x, torch::Tensor recv_parity, int64_t slot_elems, torch::Tensor counters,
+               std::vector<int64_t> expect, int64_t rank, int64_t timeout_ns, torch::Tensor err);
+void compress_pool_fwd(torch::Tensor c, torch::Tensor z, torch::Tensor bias, int64_t m, torch::Tensor out);
+void compress_pool_bwd(torch::Tensor c, torch::Tensor z, torch::Tensor bias, int64_t m, torch::Tensor out,
+                       torch::Tensor dout, torch::Tensor dc, torch::Tensor dz, torch::Tensor dz_f32);
 void fp8_quant_blocks(torch::Tensor w, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> scale);
 void gemm_fp8(torch::Tensor a, torch::Tensor sfa, torch::Tensor b, torch::Tensor sfb, torch::Tensor out,
               torch::Tensor err);
@@ -154,6 +163,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quant_rows", &sv4::fp8_quant_rows);
   m.def("fp8_gather_quant_rows", &sv4::fp8_gather_quant_rows);
   m.def("fp8_quant_blocks_gu", &sv4::fp8_quant_blocks_gu);
+  m.def("fake_quant_fp4", &sv4::fake_quant_fp4);
+  m.def("compress_pool_fwd", &sv4::compress_pool_fwd);
+  m.def("gemm_peer_push", &sv4::gemm_peer_push);
+  m.def("tp_push", &sv4::tp_push);
+  m.def("tp_reduce", &sv4::tp_reduce);
+  m.def("compress_pool_bwd", &sv4::compress_pool_bwd);
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);

@@ -197,6 +197,7 @@ static void dispatch(bool a_mn, bool b_mn, int bmode, int epi, const CUtensorMap
       {false, true, kBSingle, kEpiF32Acc},
       {false, false, kBSingle, kEpiAxpbyBF16},
       {false, true, kBSingle, kEpiAxpbyBF16},
+      {false, false, kBSingle, kEpiPeerBF16},
   };
   for (int i = 0; i < int(sizeof(table) / sizeof(table[0])); ++i) {
     const V& v = table[i];
@@ -353,6 +354,51 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b
   }
   const int grid = std::min<int>(tiles, sms);
   dispatch(a_mn, b_mn, kBSingle, epi, ma, mb, mb, md, p, grid, at::cuda::getCurrentCUDAStream());
+}
+
+// Row-parallel projection whose output tiles also go to the tensor-parallel peers while the
+// GEMM runs: out = x w^T (bf16, contiguous (M, N)), and every tile's bf16 values are stored into
+// each peer's receive slot (`peer_slots[i]`: the address of this rank's slot on peer i, laid out
+// like out) from the epilogue; each CTA then adds 1 to `peer_cnts[i]` (this rank's arrival
+// counter on peer i).  Returns the grid, i.e. the arrivals each peer waits for.
+int64_t gemm_peer_push(torch::Tensor x, torch::Tensor w, torch::Tensor out, std::vector<int64_t> peer_slots,
+                       std::vector<int64_t> peer_cnts, torch::Tensor err) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16, "bf16 operands and output");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2 && out.is_contiguous(), "x (M, K), w (N, K), out (M, N)");
+  TORCH_CHECK(peer_slots.size() == peer_cnts.size() && peer_slots.size() <= kGemmMaxPeers, "1..7 peers");
+  c10::cuda::CUDAGuard guard(x.device());
+  OperandView va = view_of(x), vb = view_of(w);
+  const int64_t M = va.outer, K = va.inner, N = vb.outer;
+  TORCH_CHECK(vb.inner == K && K % 64 == 0, "K mismatch or not a multiple of 64");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N && N % 8 == 0, "out (M, N), N % 8 == 0");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "out 16-byte aligned");
+  for (auto a : peer_slots) TORCH_CHECK((a & 15) == 0, "peer slots 16-byte aligned");
+  GemmParams p{};
+  p.n_probs = 1;
+  GemmProblem& s = p.single;
+  s.m = M; s.n = N; s.k = K;
+  s.batch = 1;
+  s.d_ld = N;
+  p.d = out.data_ptr();
+  p.alpha = 1.0f;
+  p.err = err.data_ptr<int>();
+  p.splitk = 1;
+  p.kc = static_cast<int>(K);
+  p.n_peers = static_cast<int>(peer_slots.size());
+  for (size_t i = 0; i < peer_slots.size(); ++i) {
+    p.peer_d[i] = static_cast<unsigned long long>(peer_slots[i]);
+    p.peer_cnt[i] = static_cast<unsigned long long>(peer_cnts[i]);
+  }
+  const int tiles = static_cast<int>(((M + 127) / 128) * ((N + 255) / 256));
+  if (tiles == 0) return 0;
+  CUtensorMap ma = map_for(va, 128);
+  CUtensorMap mb = map_for(vb, 256);
+  CUtensorMap md = ma;
+  p.tma_d = map_d_for(out.data_ptr(), false, N, M, 1, N, 0, md) ? 1 : 0;
+  const int grid = std::min<int>(tiles, num_sms(x.get_device()));
+  dispatch(false, false, kBSingle, kEpiPeerBF16, ma, mb, mb, md, p, grid, at::cuda::getCurrentCUDAStream());
+  return grid;
 }
 
 // out = alpha * (A B^T) + beta * C, bf16 out and bf16 C with identical layout to out

@@ -39,7 +39,14 @@ struct GemmProblem {
 
 enum BMode : int { kBSingle = 0, kBSplitN = 1, kBSplitK = 2 };
 // kEpiAxpbyBF16: D = alpha * acc + beta * C with C (bf16) laid out exactly like D (pointer `aux`).
-enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiSwiGLU = 3, kEpiRowScaleBF16 = 4, kEpiAxpbyBF16 = 5 };
+// kEpiPeerBF16: D (bf16) as kEpiBF16, and the same tile values stored into every peer's receive
+// slot (`peer_d`, D's layout, peer memory over NVLink) as the tile is written; when all of a CTA's
+// tiles are out, one thread adds 1 to every peer's arrival counter (`peer_cnt`, release at system
+// scope after a system fence), so a peer's consumer waits for gridDim.x arrivals per source.
+enum Epi : int {
+  kEpiBF16 = 0, kEpiF32 = 1, kEpiF32Acc = 2, kEpiSwiGLU = 3, kEpiRowScaleBF16 = 4, kEpiAxpbyBF16 = 5, kEpiPeerBF16 = 6
+};
+constexpr int kGemmMaxPeers = 7;
 
 struct GemmParams {
   const GemmProblem* probs;   // device table or nullptr (single mode)
@@ -57,6 +64,9 @@ struct GemmParams {
   int kc;
   int sym;                    // single mode: D is symmetric; tiles strictly below the diagonal are skipped
   int* err;
+  int n_peers;                // kEpiPeerBF16
+  unsigned long long peer_d[kGemmMaxPeers];
+  unsigned long long peer_cnt[kGemmMaxPeers];
 };
 
 constexpr int kBM = 128;
@@ -110,6 +120,35 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
   __nv_bfloat162 h3 = __floats2bfloat162_rn(v[6], v[7]);
   return make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
                     *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+}
+
+// kEpiPeerBF16: copy one staged 32-row x 64-column bf16 chunk (128B-swizzled, as stage_store
+// wrote it) to every peer's slot.  Eight lanes per row, so each store instruction writes four
+// whole 128-byte row segments (coalesced NVLink writes).  `off0`: element offset of the chunk's
+// first row and column in D's layout; rows past `rows` / columns past `cols` are not written.
+__device__ __forceinline__ void push_chunk_to_peers(const GemmParams& P, const uint8_t* b, int lane, long long off0,
+                                                    long long ld, int rows, int cols) {
+  const int q = lane & 7;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    if (r >= rows || q * 8 >= cols) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(b + r * 128 + ((q ^ (r & 7)) << 4));
+    const long long off = off0 + r * ld + q * 8;
+    for (int p = 0; p < P.n_peers; ++p) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(P.peer_d[p]) + off;
+      if (q * 8 + 8 <= cols) {
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+        for (int j = 0; j < cols - q * 8; ++j) dst[j] = e[j];
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void red_release_sys_add(unsigned long long addr, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ int tiles_m(const GemmProblem& p) { return (p.m + kBM - 1) / kBM; }
@@ -458,6 +497,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           }
           // Boxes starting past the problem are skipped (never issue a fully clipped store).
           const bool issue = col0 < pr.n && mt * kBM + quarter * 32 < pr.m;
+          const uint8_t* staged = stg + sbuf * kEpiStageBytes;
           stage_store(stg, sbuf, lane, [&](int q) {
             if constexpr (kF32) {
               return make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
@@ -466,6 +506,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               return pack_bf16x8(v + 8 * q);
             }
           }, &map_d, EPI == kEpiF32Acc, col0, drow, bt, issue);
+          if constexpr (EPI == kEpiPeerBF16) {
+            if (issue) {
+              const int r0 = mt * kBM + quarter * 32;
+              push_chunk_to_peers(P, staged, lane, pr.d_off + static_cast<long long>(bt) * pr.d_bstride +
+                                  r0 * pr.d_ld + col0, pr.d_ld, min(32, pr.m - r0), min(kCW, pr.n - col0));
+            }
+          }
         }
       } else {
         const float rs = (EPI == kEpiRowScaleBF16 && row_ok) ? P.rowscale[pr.aux_off + row] : 1.0f;
@@ -499,7 +546,15 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
             }
           }
-          if constexpr (EPI == kEpiBF16 || EPI == kEpiRowScaleBF16 || EPI == kEpiAxpbyBF16) {
+          if constexpr (EPI == kEpiPeerBF16) {  // fallback path: per-lane row stores to the peers
+            for (int p = 0; p < P.n_peers; ++p) {
+              __nv_bfloat16* po = reinterpret_cast<__nv_bfloat16*>(P.peer_d[p]) + dbase + col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < pr.n) po[j] = __float2bfloat16(v[j]);
+            }
+          }
+          if constexpr (EPI == kEpiBF16 || EPI == kEpiRowScaleBF16 || EPI == kEpiAxpbyBF16 || EPI == kEpiPeerBF16) {
             __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(P.d) + dbase + col0;
             if (full_chunk && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
 #pragma unroll
@@ -544,6 +599,14 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
     if (lane == 0) bulk_wait_all();  // TMA stores of this warp are complete before exit
+    if constexpr (EPI == kEpiPeerBF16) {
+      // every epilogue thread's peer stores are ordered before the arrival (system fence,
+      // then a barrier over the four epilogue warps, then one release-add per peer)
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0)
+        for (int p = 0; p < P.n_peers; ++p) red_release_sys_add(P.peer_cnt[p], 1u);
+    }
   }
 
   tc_fence_before();

@@ -679,6 +679,76 @@ void grouped_gemm_fp8(int64_t mode, torch::Tensor a, torch::Tensor sfa, torch::T
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------- MXFP4 fake quantisation (QAT)
+// The reference's MX FP4 straight-through quantiser (kernels/quant/fp4.py) over blocks of 32
+// along the last axis, one warp per block: scale = 2^ceil(log2(max(amax / 6, 2^-126))) (an
+// E8M0 value), each element rounded to the nearest E2M1 magnitude {0, .5, 1, 1.5, 2, 3, 4, 6}
+// of |x| / scale clamped to 6 (an exact tie goes to the smaller magnitude), times the scale and
+// the sign; the output is x + (q - x) evaluated in x's dtype, as the PyTorch expression does.
+namespace {
+__device__ __forceinline__ float e2m1_round(float mag) {
+  const float lv[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  float best = lv[0], bd = fabsf(mag - lv[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    const float d = fabsf(mag - lv[i]);
+    if (d < bd) { bd = d; best = lv[i]; }
+  }
+  return best;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+
+template <typename T>
+__global__ void fake_quant_fp4_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t n_blocks) {
+  const int64_t blk = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (blk >= n_blocks) return;
+  const T xv = x[blk * 32 + lane];
+  const float v = to_f<T>(xv);
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float raw = fmaxf(amax / 6.0f, 1.17549435e-38f);
+  const float scale = exp2f(ceilf(log2f(raw)));
+  const float q = copysignf(e2m1_round(fminf(fabsf(v / scale), 6.0f)), v) * scale;
+  const T qd = from_f<T>(q);
+  const T diff = from_f<T>(to_f<T>(qd) - v);
+  out[blk * 32 + lane] = from_f<T>(v + to_f<T>(diff));
+}
+}  // namespace
+
+void fake_quant_fp4(torch::Tensor x, torch::Tensor out) {
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.sizes() == out.sizes() &&
+                  x.scalar_type() == out.scalar_type(), "fake_quant_fp4: contiguous, same shape / dtype");
+  TORCH_CHECK(x.size(-1) % 32 == 0, "last dimension must be a multiple of 32");
+  const int64_t n_blocks = x.numel() / 32;
+  if (n_blocks == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  const unsigned grid = static_cast<unsigned>((n_blocks * 32 + 255) / 256);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (x.scalar_type() == at::kFloat) {
+    fake_quant_fp4_kernel<float><<<grid, 256, 0, stream>>>(x.data_ptr<float>(), out.data_ptr<float>(), n_blocks);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "fake_quant_fp4: fp32 or bf16");
+    fake_quant_fp4_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+        n_blocks);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 int64_t fp8_sf_bytes(int64_t rows, int64_t k) { return (rows + 127) / 128 * sf_groups(k) * kSfChunk; }
 
 }  // namespace sv4

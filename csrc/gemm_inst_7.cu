@@ -18,6 +18,7 @@ bool gemm_launch_group7(int variant, const CUtensorMap& ma, const CUtensorMap& m
   switch (variant) {
     case 15: launch_one<256, false, false, kBSingle, kEpiAxpbyBF16>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
     case 16: launch_one<256, false, true, kBSingle, kEpiAxpbyBF16>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
+    case 17: launch_one<256, false, false, kBSingle, kEpiPeerBF16>(ma, mb0, mb1, md, mx, p, grid, stream); return true;
     default: return false;
   }
 }

@@ -84,14 +84,59 @@ def uses_fp8(linear: nn.Module) -> bool:
     return bool(getattr(linear, "use_real_fp8_gemm", False))
 
 
-def _pool(c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int) -> Tensor:
-    """Softmax-over-m pooling (B, T, c) -> (B, T//m, c), fp32 math."""
+def _pool_torch(c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int) -> Tensor:
+    """Softmax-over-m pooling (B, T, c) -> (B, T//m, c), fp32 math (CPU path and test oracle)."""
     b, t, c = c_b.shape
     n = t // m
     if n == 0:
         return c_b.new_zeros(b, 0, c, dtype=torch.float32)
     z = z_b[:, : n * m].float().reshape(b, n, m, c) + bias_b.float()
     return (torch.softmax(z, dim=-2) * c_b[:, : n * m].float().reshape(b, n, m, c)).sum(-2)
+
+
+class _PoolFn(torch.autograd.Function):
+    """``compress_pool_fwd`` / ``compress_pool_bwd`` (``csrc/pool.cu``): one kernel each way
+    instead of the ~25 elementwise launches of the eager softmax pooling.  c_b / z_b are bf16
+    column slices of the fused projection output; the bias gradient is the (b, s) sum of the
+    kernel's fp32 dz."""
+
+    @staticmethod
+    def forward(ctx, c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int):  # type: ignore[override]
+        b, t, c = c_b.shape
+        out = torch.empty(b, t // m, c, dtype=torch.float32, device=c_b.device)
+        backend.ext().compress_pool_fwd(c_b, z_b, bias_b.contiguous(), m, out)
+        ctx.save_for_backward(c_b, z_b, bias_b, out)
+        ctx.m = m
+        return out
+
+    @staticmethod
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
+        c_b, z_b, bias_b, out = ctx.saved_tensors
+        m = ctx.m
+        b, t, c = c_b.shape
+        n = t // m
+        if n * m == t:
+            dc = torch.empty(b, t, c, dtype=c_b.dtype, device=c_b.device)
+            dz = torch.empty_like(dc)
+        else:
+            dc = torch.zeros(b, t, c, dtype=c_b.dtype, device=c_b.device)
+            dz = torch.zeros_like(dc)
+        dz32 = torch.empty(b, n, m, c, dtype=torch.float32, device=c_b.device)
+        backend.ext().compress_pool_bwd(c_b, z_b, bias_b.contiguous(), m, out, dout.float().contiguous(), dc, dz,
+                                        dz32)
+        dbias = dz32.sum((0, 1)).to(bias_b.dtype)
+        return dc, dz, dbias, None
+
+
+def _pool(c_b: Tensor, z_b: Tensor, bias_b: Tensor, m: int) -> Tensor:
+    """Softmax-over-m pooling (B, T, c) -> (B, T//m, c) fp32 (reference
+    core/attention/csa.py TokenLevelCompressor): the fused kernel on CUDA for bf16 inputs."""
+    b, t, c = c_b.shape
+    if (c_b.is_cuda and c_b.dtype == torch.bfloat16 and z_b.dtype == torch.bfloat16 and t // m > 0
+            and c_b.stride(-1) == 1 and z_b.stride(-1) == 1 and c_b.stride(0) == t * c_b.stride(1)
+            and z_b.stride(0) == t * z_b.stride(1)):
+        return _PoolFn.apply(c_b, z_b, bias_b, m)
+    return _pool_torch(c_b, z_b, bias_b, m)
 
 
 def _pad_head(t: Tensor, hd: int) -> Tensor:

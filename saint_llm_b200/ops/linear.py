@@ -102,9 +102,33 @@ def fp8_linear(x: Tensor, weight: Tensor, bias: Tensor | None = None) -> Tensor:
     return _Fp8LinearFn.apply(x, weight, bias)
 
 
+class _FakeQuantFp4Fn(torch.autograd.Function):
+    """MX FP4 straight-through fake quantisation in one native kernel (blocks of 32 along
+    the last axis); the gradient passes through unchanged."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor) -> Tensor:  # type: ignore[override]
+        from saint_llm_b200.ops import backend
+
+        xc = x.contiguous()
+        out = torch.empty_like(xc)
+        backend.ext().fake_quant_fp4(xc, out)
+        return out.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g: Tensor) -> Tensor:  # type: ignore[override]
+        return g
+
+
 def fake_quant_fp4(x: Tensor, block_size: int) -> Tensor:
+    """MX FP4 QAT quantiser of the last axis: the native kernel on CUDA (block 32, fp32 /
+    bf16), the PyTorch statement (``ops.quant.fake_quant_fp4_mx``) otherwise."""
+    from saint_llm_b200.ops import backend
     from saint_llm_b200.ops.quant import fake_quant_fp4_mx
 
+    if (backend.native_for(x) and block_size == 32 and x.shape[-1] % 32 == 0
+            and x.dtype in (torch.float32, torch.bfloat16)):
+        return _FakeQuantFp4Fn.apply(x)
     return fake_quant_fp4_mx(x, block_size=block_size, axis=-1)
 
 

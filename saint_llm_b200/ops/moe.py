@@ -20,7 +20,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-from saint_llm_b200.ops.quant import Fp8Format, fake_quant_fp4_mx, fake_quant_fp8
+from saint_llm_b200.ops.quant import Fp8Format, fake_quant_fp8
 
 GroupedQuantMode = Literal["bf16", "fp8", "fp4"]
 
@@ -75,7 +75,9 @@ class GroupedSwiGLUExperts(nn.Module):
         if self.linear_quant == "fp8":
             return fake_quant_fp8(x, fmt=Fp8Format.E4M3, axis=0)
         if self.linear_quant == "fp4":
-            return fake_quant_fp4_mx(x, block_size=self.fp4_block_size, axis=-1)
+            from saint_llm_b200.ops.linear import fake_quant_fp4
+
+            return fake_quant_fp4(x, self.fp4_block_size)  # native kernel on CUDA
         return x
 
     def _q_weight(self, w: Tensor) -> Tensor:
@@ -85,7 +87,9 @@ class GroupedSwiGLUExperts(nn.Module):
         if self.linear_quant == "fp8":
             q = fake_quant_fp8(flat, fmt=Fp8Format.E4M3, axis=0)
         else:
-            q = fake_quant_fp4_mx(flat, block_size=self.fp4_block_size, axis=-1)
+            from saint_llm_b200.ops.linear import fake_quant_fp4
+
+            q = fake_quant_fp4(flat, self.fp4_block_size)  # native kernel on CUDA
         return q.reshape(w.shape)
 
     def forward(self, flat_h: Tensor, flat_idx: Tensor, flat_gate: Tensor) -> Tensor:

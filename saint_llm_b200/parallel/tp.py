@@ -155,10 +155,15 @@ def _tp_post_hook(group: dist.ProcessGroup | None):
     return hook
 
 
-def shard_attention_heads(attn: nn.Module, group: dist.ProcessGroup | None = None) -> list[Tensor]:
+def shard_attention_heads(attn: nn.Module, group: dist.ProcessGroup | None = None, comm: Any = None) -> list[Tensor]:
     """Shard one SWA/CSA/HCA/NSA module's heads over ``group`` in place (the module keeps
     its class; the input copy and output all-reduce are forward hooks); returns the
-    replicated parameters whose gradients need ``TPGradSync``."""
+    replicated parameters whose gradients need ``TPGradSync``.
+
+    ``comm`` (a ``tp_p2p.PeerTPComm``): the NVLink peer-memory transport.  The output
+    projection then runs as one GEMM that pushes its tiles to the peer while it computes
+    (``PeerRowParallelLinear``), the input gradient is reduced by the peer kernels, and no
+    NCCL call is made for the block's activations."""
     rank, ws = dist.get_rank(group), _ws(group)
     cfg = attn.attn_cfg
     H, g = cfg.query_heads, cfg.output_proj_groups
@@ -185,8 +190,15 @@ def shard_attention_heads(attn: nn.Module, group: dist.ProcessGroup | None = Non
     fp.weight = nn.Parameter(fp.weight.data[:, cols].clone())
     fp.in_features = fp.weight.shape[1]
     sharded.add(id(fp.weight))
-    attn.register_forward_pre_hook(_tp_pre_hook(group), with_kwargs=True)
-    attn.register_forward_hook(_tp_post_hook(group), with_kwargs=True)
+    if comm is not None:
+        from saint_llm_b200.parallel.tp_p2p import PeerRowParallelLinear, peer_copy_to_tp
+
+        out.final_proj = PeerRowParallelLinear(fp.weight, comm)
+        attn.register_forward_pre_hook(
+            lambda m, args, kwargs: ((peer_copy_to_tp(args[0], comm), *args[1:]), kwargs), with_kwargs=True)
+    else:
+        attn.register_forward_pre_hook(_tp_pre_hook(group), with_kwargs=True)
+        attn.register_forward_hook(_tp_post_hook(group), with_kwargs=True)
     attn.tp_group = group
     return [p for p in attn.parameters() if id(p) not in sharded and p.requires_grad]
 
@@ -226,15 +238,36 @@ class TPGradSync:
                 off += x.numel()
 
 
-def apply_tensor_parallel(model: nn.Module, group: dist.ProcessGroup | None = None) -> TPGradSync:
+def apply_tensor_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *,
+                          transport: str = "nccl", max_tokens: int | None = None,
+                          timeout_s: float = 30.0) -> TPGradSync:
     """Shard the heads of every block's attention over ``group``; returns the gradient sync
-    of the replicated attention parameters (call it after backward, before the optimizer)."""
+    of the replicated attention parameters (call it after backward, before the optimizer).
+
+    ``transport``: "nccl" (autograd all-reduces through ``torch.distributed``) or "p2p" (the
+    NVLink peer-memory kernels of ``parallel.tp_p2p``; CUDA, bf16 activations, one node;
+    ``max_tokens`` sizes the receive buffer: tokens per rank per call)."""
+    comm = None
+    if transport == "p2p":
+        from saint_llm_b200.parallel.tp_p2p import PeerTPComm
+
+        dev = next(model.parameters()).device
+        if dev.type != "cuda":
+            raise ValueError("the p2p TP transport needs CUDA parameters")
+        if max_tokens is None:
+            raise ValueError("the p2p TP transport needs max_tokens (tokens per rank per call)")
+        hidden = model.cfg.hidden_dim  # type: ignore[attr-defined]
+        comm = PeerTPComm.create(group, dev, max_tokens * hidden, timeout_s=timeout_s)
+    elif transport != "nccl":
+        raise ValueError(f"unknown TP transport {transport!r}")
     replicated: list[Tensor] = []
     mods = []
     for block in model.blocks:  # type: ignore[attr-defined]
-        replicated += shard_attention_heads(block.attention, group)
+        replicated += shard_attention_heads(block.attention, group, comm)
         mods.append(block.attention)
-    return TPGradSync(replicated, group, attn_modules=mods)
+    sync = TPGradSync(replicated, group, attn_modules=mods)
+    sync.comm = comm  # type: ignore[attr-defined]
+    return sync
 
 
 __all__ = ["ColumnParallelLinear", "RowParallelLinear", "TPGradSync", "all_gather_seq", "apply_tensor_parallel",

@@ -165,3 +165,27 @@ def test_indexer_select_mask_matches_topk(cuda, n, k):
     backend.ext().indexer_select_mask(flat, k, sel)
     bits = torch.stack([(sel.view(-1, words)[:, i // 32] >> (i % 32)) & 1 for i in range(n)], -1)
     assert bits.sum(-1).tolist() == [min(k, n)] * 2 and bits[:, :min(k, n)].all()
+
+
+@pytest.mark.parametrize("B,T,c,m,bias_dtype", [(2, 512, 128, 4, torch.float32), (1, 1000, 64, 128, torch.float32),
+                                                (3, 96, 96, 8, torch.bfloat16)])
+def test_compressor_pool_kernel_matches_fp32(cuda, B, T, c, m, bias_dtype):
+    """compress_pool_fwd / _bwd against the fp32 eager pooling on strided column slices of one
+    projection output (T not a multiple of m leaves a tail that gets zero gradient)."""
+    from saint_llm_b200.ops.attention import _PoolFn, _pool_torch
+
+    torch.manual_seed(T + m)
+    y = (torch.randn(B, T, 3 * c, device=cuda) * 2).to(torch.bfloat16).requires_grad_()
+    bias = (torch.randn(m, c, device=cuda) * 0.5).to(bias_dtype).requires_grad_()
+    cb, zb = y[..., c:2 * c], y[..., 2 * c:]
+    out = _PoolFn.apply(cb, zb, bias, m)
+    yr = y.detach().float().requires_grad_()
+    br = bias.detach().float().requires_grad_()
+    ref = _pool_torch(yr[..., c:2 * c], yr[..., 2 * c:], br, m)
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    g = torch.randn_like(ref)
+    out.backward(g)
+    ref.backward(g)
+    torch.testing.assert_close(y.grad.float(), yr.grad, rtol=2e-2, atol=2e-2)
+    tol = 2e-2 if bias_dtype == torch.bfloat16 else 1e-3
+    torch.testing.assert_close(bias.grad.float(), br.grad, rtol=tol, atol=tol * max(1.0, br.grad.abs().max().item()))

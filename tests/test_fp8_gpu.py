@@ -118,3 +118,25 @@ def test_fp8_routed_experts_match_bf16(cuda, used):
     assert torch.isfinite(got).all()
     rel = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
     assert rel < 0.08, rel
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fake_quant_fp4_kernel_matches_oracle(cuda, dtype):
+    """Native MX FP4 straight-through quantiser against the PyTorch statement on the same
+    device (same scale rule, E2M1 rounding with ties to the smaller magnitude)."""
+    from saint_llm_b200.ops.linear import fake_quant_fp4
+    from saint_llm_b200.ops.quant import fake_quant_fp4_mx
+
+    torch.manual_seed(9)
+    x = (torch.randn(64, 256, device=cuda) * torch.exp2(torch.randint(-8, 8, (64, 1), device=cuda).float()))
+    x[0, :32] = 0.0                                   # an all-zero block
+    x[1, :32] = torch.linspace(-6, 6, 32, device=cuda)  # exact E2M1 levels and ties
+    x = x.to(dtype).requires_grad_(True)
+    got = fake_quant_fp4(x, 32)
+    want = fake_quant_fp4_mx(x.detach(), block_size=32, axis=-1)
+    torch.cuda.synchronize()
+    mismatch = (got.detach() != want).float().mean().item()
+    assert mismatch < 1e-3, mismatch  # at most a rare log2 rounding edge
+    g = torch.randn_like(got)
+    got.backward(g)
+    assert torch.equal(x.grad, g)  # straight-through

@@ -133,7 +133,8 @@ def run_config(args, world: int):
     from saint_llm_b200.config import RunConfig
 
     return RunConfig(ep=world, zero="dp" if args.no_zero else "hybrid_zero", fused_ep=args.ep_transport == "p2p",
-                     fused_zero=not args.no_overlap_reduce, cuda_graphs=not args.no_cuda_graph,
+                     fused_zero=not args.no_overlap_reduce, zero_transport=args.zero_transport,
+                     cuda_graphs=not args.no_cuda_graph,
                      fp8_expert_cache=args.fp8_expert_cache,
                      micro_batch=args.micro_batch, seq_len=args.seq_len,
                      grad_accum=args.seqs_per_gpu // args.micro_batch, lr=2.7e-4, adamw_lr=2.7e-4,
@@ -252,6 +253,7 @@ def run_ours(args) -> dict:
                    "parallelism": (f"ep{world}+dp{world}" + ("" if args.no_zero else "+zero")) if world > 1
                    else "single-gpu",
                    "ep_transport": args.ep_transport if world > 1 else None,
+                   "zero_transport": args.zero_transport if world > 1 and not args.no_zero else None,
                    "cuda_graph": bool(getattr(step, "_graph", None) is not None),
                    "cuda_graph_error": getattr(step, "graph_error", None),
                    "linear_quant": args.linear_quant, "activation_checkpointing": args.ckpt,
@@ -368,6 +370,8 @@ def main() -> None:
                     help="FP8: keep the routed experts' FP8 weight copies between steps (auto: when sharded by EP)")
     ap.add_argument("--no-cuda-graph", action="store_true",
                     help="N = 1: launch every kernel eagerly instead of replaying the captured micro-batch graph")
+    ap.add_argument("--zero-transport", default="nccl", choices=["nccl", "p2p"],
+                    help="N > 1 with hybrid ZeRO: NCCL reduce/broadcast or the peer-memory pull kernels")
     ap.add_argument("--no-overlap-reduce", action="store_true",
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)

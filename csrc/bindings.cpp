@@ -26,6 +26,12 @@ int64_t gemm_peer_push(torch::Tensor x, torch::Tensor w, torch::Tensor out, std:
 int64_t tp_push(torch::Tensor x, std::vector<int64_t> peer_slots, std::vector<int64_t> peer_cnts);
 void tp_reduce(torch::Tensor x, torch::Tensor recv_parity, int64_t slot_elems, torch::Tensor counters,
                std::vector<int64_t> expect, int64_t rank, int64_t timeout_ns, torch::Tensor err);
+void zero_signal(std::vector<int64_t> flag_ptrs, int64_t slot, int64_t rank, int64_t epoch);
+void zero_pull_reduce(torch::Tensor chunks, std::vector<int64_t> grad_ptrs, int64_t rank, double scale,
+                      torch::Tensor my_flags, int64_t slot, int64_t epoch, int64_t timeout_ns, int64_t blocks,
+                      torch::Tensor err);
+void zero_pull_params(torch::Tensor chunks, std::vector<int64_t> param_ptrs, int64_t rank, torch::Tensor my_flags,
+                      int64_t slot, int64_t epoch, int64_t timeout_ns, int64_t blocks, torch::Tensor err);
 void compress_pool_fwd(torch::Tensor c, torch::Tensor z, torch::Tensor bias, int64_t m, torch::Tensor out);
 void compress_pool_bwd(torch::Tensor c, torch::Tensor z, torch::Tensor bias, int64_t m, torch::Tensor out,
                        torch::Tensor dout, torch::Tensor dc, torch::Tensor dz, torch::Tensor dz_f32);
@@ -168,6 +174,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_peer_push", &sv4::gemm_peer_push);
   m.def("tp_push", &sv4::tp_push);
   m.def("tp_reduce", &sv4::tp_reduce);
+  m.def("zero_signal", &sv4::zero_signal);
+  m.def("zero_pull_reduce", &sv4::zero_pull_reduce);
+  m.def("zero_pull_params", &sv4::zero_pull_params);
   m.def("compress_pool_bwd", &sv4::compress_pool_bwd);
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);

@@ -245,7 +245,8 @@ class ParallelSync:
     loss is the global mean)."""
 
     def __init__(self, model: nn.Module, expert_params: list[Tensor], group: dist.ProcessGroup | None,
-                 *, zero: bool, overlap_reduce: bool = False) -> None:
+                 *, zero: bool, overlap_reduce: bool = False, zero_transport: str = "nccl",
+                 timeout_s: float = 30.0) -> None:
         self.model, self.group = model, group
         self.ws = dist.get_world_size(group)
         self.expert_ids = {id(p) for p in expert_params}
@@ -260,7 +261,15 @@ class ParallelSync:
             muon, adamw = split_for_muon_adamw(model)
             kinds = {id(p): "muon" for p in muon} | {id(p): "adamw" for p in adamw}
             rep = [p for p in model.parameters() if id(p) not in self.expert_ids and p.requires_grad]
-            self.zero = ZeroOptimizerSync(rep, [kinds.get(id(p), "adamw") for p in rep], group=group)
+            rep_kinds = [kinds.get(id(p), "adamw") for p in rep]
+            if zero_transport == "p2p":
+                from saint_llm_b200.parallel.zero_p2p import PeerZeroSync
+
+                self.zero = PeerZeroSync(rep, rep_kinds, group=group, timeout_s=timeout_s)
+            elif zero_transport == "nccl":
+                self.zero = ZeroOptimizerSync(rep, rep_kinds, group=group)
+            else:
+                raise ValueError(f"unknown ZeRO transport {zero_transport!r}")
             blocks = list(getattr(model, "blocks", []))
             if overlap_reduce and blocks:
                 self._hook_blocks(blocks)
@@ -314,7 +323,7 @@ class ParallelSync:
 
 def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",
                           capacity_factor: float | None = None, zero: bool = False, timeout_s: float = 30.0,
-                          overlap_reduce: bool = False) -> ParallelSync:
+                          overlap_reduce: bool = False, zero_transport: str = "nccl") -> ParallelSync:
     """Shard the experts over ``group`` and return the gradient synchroniser.
 
     ``transport``: "p2p" moves tokens with the peer-memory kernels of ``parallel.ep_p2p``
@@ -322,12 +331,13 @@ def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
     ``zero``: hybrid ZeRO for the replicated parameters (see ``ParallelSync``); call
     ``sync.configure_optimizer(opt)`` once and ``sync.post_step()`` after every step.
     ``overlap_reduce`` (with ``zero``): issue each block's owner reductions from its
-    backward hook during the last micro-batch.  ``timeout_s``: bound of every cross-GPU
-    flag wait of the peer-memory kernels."""
+    backward hook during the last micro-batch.  ``zero_transport`` (with ``zero``): "nccl"
+    reduce / broadcast, or "p2p" (``parallel.zero_p2p``: owners pull over NVLink peer
+    memory).  ``timeout_s``: bound of every cross-GPU flag wait of the peer-memory kernels."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
     sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero,
-                        overlap_reduce=overlap_reduce)
+                        overlap_reduce=overlap_reduce, zero_transport=zero_transport, timeout_s=timeout_s)
     dev = next(model.parameters()).device
     if transport not in ("auto", "p2p", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")

@@ -119,10 +119,12 @@ class ZeroOptimizerSync:
     """
 
     def __init__(self, params: Sequence[Tensor], kinds: Sequence[Literal["muon", "adamw"]], *,
-                 group: dist.ProcessGroup | None = None, bucket_bytes: int = 256 << 20) -> None:
+                 group: dist.ProcessGroup | None = None, bucket_bytes: int = 256 << 20,
+                 world: int | None = None, rank: int | None = None) -> None:
+        # world / rank override the process group's (ranks emulated in one process)
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = world if world is not None else (dist.get_world_size(group) if dist.is_initialized() else 1)
+        self.rank = rank if rank is not None else (dist.get_rank(group) if dist.is_initialized() else 0)
         self.params = list(params)
         self.plan = hybrid_zero_assign(self.params, kinds, self.world)
         owner = self.plan.owner_of()

@@ -16,6 +16,8 @@ What each ``RunConfig`` field selects here:
   are issued from a backward hook during the step's last micro-batch, so they run on
   NCCL's stream while the backward of the earlier blocks continues (True), or all after
   the backward (False).
+* ``zero_transport``: with hybrid ZeRO, NCCL ``reduce`` / ``broadcast`` ("nccl") or this
+  framework's peer-memory pull kernels ("p2p", ``parallel.zero_p2p``).
 * ``cuda_graphs``: on one GPU, each micro-batch's forward + backward replays one captured
   CUDA graph (``TrainStep(cuda_graph=True)``); ignored when gradients are synchronised
   across ranks (the expert-parallel step reads routing sizes on the host).
@@ -140,7 +142,8 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
 
         grad_sync = ep_mod.setup_expert_parallel(
             model, group, transport="p2p" if run.fused_ep else "nccl", zero=run.zero == "hybrid_zero",
-            timeout_s=run.device_wait_timeout_ms / 1000.0, overlap_reduce=run.fused_zero)
+            timeout_s=run.device_wait_timeout_ms / 1000.0, overlap_reduce=run.fused_zero,
+            zero_transport=run.zero_transport)
         if device.type == "cuda":
             torch.cuda.empty_cache()
     params = attach_main_grads(model)

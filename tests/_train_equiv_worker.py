@@ -4,7 +4,8 @@
 global token set (G sequences, one micro-batch per sequence, gradient accumulation) for S
 steps.  ``--mode ep`` (under torch.distributed.run, one rank per GPU): the same model and
 seed with the experts sharded over the ranks (EP = world size), hybrid ZeRO for the
-replicated weights and the chosen token transport; rank r trains on sequences
+replicated weights (NCCL or peer-memory transport, optionally reduced from the blocks'
+backward hooks) and the chosen token transport; rank r trains on sequences
 [r*G/N, (r+1)*G/N) with the same micro-batch size.  The same global batch is used every
 step, so the loss falls visibly and a wrong update shows.  Each run writes its per-step
 global-mean losses as JSON to ``--out``."""
@@ -20,7 +21,7 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
-def build(dev, world, transport, zero):
+def build(dev, world, transport, zero, zero_transport="nccl", overlap=False):
     from saint_llm_b200.config import ModelConfig
     from saint_llm_b200.models import SaintLLM
     from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
@@ -35,7 +36,8 @@ def build(dev, world, transport, zero):
     if world > 1:
         from saint_llm_b200.parallel import ep
 
-        sync = ep.setup_expert_parallel(model, transport=transport, zero=zero)
+        sync = ep.setup_expert_parallel(model, transport=transport, zero=zero, zero_transport=zero_transport,
+                                        overlap_reduce=overlap)
     params = attach_main_grads(model)
     muon, adamw = split_for_muon_adamw(model)
     opt = MuonAdamW(muon, adamw, lr=2.7e-4, qk_clip_layers=model.attention_layers())
@@ -49,6 +51,8 @@ def main() -> None:
     ap.add_argument("--mode", choices=["single", "ep"], required=True)
     ap.add_argument("--transport", default="p2p")
     ap.add_argument("--no-zero", action="store_true")
+    ap.add_argument("--zero-transport", default="nccl", choices=["nccl", "p2p"])
+    ap.add_argument("--overlap", action="store_true", help="reduce gradients from the blocks' backward hooks")
     ap.add_argument("--seqs", type=int, default=8)
     ap.add_argument("--seq-len", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=10)
@@ -62,7 +66,7 @@ def main() -> None:
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.step import TrainStep
 
-    cfg, model, opt, params, sync = build(dev, world, a.transport, not a.no_zero)
+    cfg, model, opt, params, sync = build(dev, world, a.transport, not a.no_zero, a.zero_transport, a.overlap)
     g = torch.Generator().manual_seed(1234)
     tokens = torch.randint(0, cfg.vocab_size, (a.seqs, 1, a.seq_len), generator=g)
     per = a.seqs // world

@@ -1,6 +1,6 @@
 """Training-step equivalence: N ranks with expert parallelism + hybrid ZeRO follow the
 same loss curve as one GPU that accumulates gradients over the same global token set.
-(2+ GPUs; both EP token transports.)"""
+(2+ GPUs; both EP token transports, and both ZeRO transports.)"""
 
 import json
 import os
@@ -42,11 +42,12 @@ def compare(single, multi, tol=0.02):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["p2p", "nccl"])
-def test_ep_zero_step_matches_single_gpu(tmp_path, transport):
+@pytest.mark.parametrize("transport,extra", [("p2p", []), ("nccl", []),
+                                             ("p2p", ["--zero-transport", "p2p", "--overlap"])])
+def test_ep_zero_step_matches_single_gpu(tmp_path, transport, extra):
     n = min(torch.cuda.device_count(), 8)
     single = _run([sys.executable, WORKER, "--mode", "single"], str(tmp_path / "single.json"))
     multi = _run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
                   "--master-addr=127.0.0.1", f"--master-port={_port()}", WORKER, "--mode", "ep", "--transport",
-                  transport], str(tmp_path / f"ep_{transport}.json"))
+                  transport, *extra], str(tmp_path / f"ep_{transport}_{len(extra)}.json"))
     compare(single, multi)

@@ -48,6 +48,12 @@ void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win,
                       c10::optional<torch::Tensor> comp, c10::optional<torch::Tensor> norm_w, double eps, int64_t m,
                       c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c, double scale,
                       torch::Tensor out);
+void decode_attention_paged(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_table,
+                            torch::Tensor k_len, int64_t window, c10::optional<torch::Tensor> sink_sw, double softcap,
+                            int64_t mode, c10::optional<torch::Tensor> e_pool, c10::optional<torch::Tensor> e_table,
+                            c10::optional<torch::Tensor> e_len, c10::optional<torch::Tensor> norm_w, double eps,
+                            int64_t m, c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c,
+                            double scale, int64_t max_rows, torch::Tensor out, torch::Tensor err);
 // router.cu
 void router_bwd(torch::Tensor z, torch::Tensor aff, torch::Tensor idx, torch::Tensor gate,
                 c10::optional<torch::Tensor> d_gate, c10::optional<torch::Tensor> d_aff, int64_t mode,
@@ -181,6 +187,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quant_blocks", &sv4::fp8_quant_blocks);
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);
+  m.def("decode_attention_paged", &sv4::decode_attention_paged);
   m.def("router_fwd", &sv4::router_fwd);
   m.def("router_bwd", &sv4::router_bwd);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);

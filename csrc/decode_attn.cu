@@ -28,6 +28,8 @@
 
 #include <cuda_bf16.h>
 
+#include "common.cuh"
+
 namespace sv4 {
 namespace {
 
@@ -65,9 +67,10 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
 // (K = V = w * x * rsqrt(mean(x^2) + eps), w folded into the queries by the caller); adds
 // (p @ x * rsqrt) / denominator into acc[4] for dimension t.  key_row(j) returns the raw
 // row or null when key j is not visible.
-template <bool NORM, typename RowFn>
-__device__ void branch(const float (*qs)[kD], float4* s, float* rs, float* red, int L, RowFn key_row,
-                       const float* sink, int h0, float scale, float softcap, float eps, float* acc) {
+template <bool NORM, typename RowFn, typename ValFn>
+__device__ void branch_kv(const float (*qs)[kD], float4* s, float* rs, float* red, int L, RowFn key_row,
+                          ValFn val_row, const float* sink, int h0, float scale, float softcap, float eps,
+                          float* acc) {
   const int t = threadIdx.x, warp = t / 32, lane = t % 32;
   // scores
   for (int j = t; j < L; j += kThreads) {
@@ -143,7 +146,7 @@ __device__ void branch(const float (*qs)[kD], float4* s, float* rs, float* red, 
       p.x *= rn; p.y *= rn; p.z *= rn; p.w *= rn;
     }
     if (p.x == 0.f && p.y == 0.f && p.z == 0.f && p.w == 0.f) continue;  // also skips invisible rows
-    const __nv_bfloat16* row = key_row(j);
+    const __nv_bfloat16* row = val_row(j);
     const float v = __bfloat162float(row[t]);
     o0 = fmaf(p.x, v, o0);
     o1 = fmaf(p.y, v, o1);
@@ -156,6 +159,12 @@ __device__ void branch(const float (*qs)[kD], float4* s, float* rs, float* red, 
   acc[2] += o2 * red[2];
   acc[3] += o3 * red[3];
   __syncthreads();  // scores / probabilities are reused by the next branch
+}
+
+template <bool NORM, typename RowFn>
+__device__ void branch(const float (*qs)[kD], float4* s, float* rs, float* red, int L, RowFn key_row,
+                       const float* sink, int h0, float scale, float softcap, float eps, float* acc) {
+  branch_kv<NORM>(qs, s, rs, red, L, key_row, key_row, sink, h0, scale, softcap, eps, acc);
 }
 
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeArgs a) {
@@ -285,6 +294,95 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeArgs 
     a.out[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t] = __float2bfloat16(acc[h]);
 }
 
+// ------------------------------------------------------------------ paged variant
+// Sequences of different lengths decode together; every cache stream lives in pages of a
+// shared pool (page_rows rows of 128) addressed through per-sequence block tables.
+//   K / V stream (B tables into kpool / vpool): len[b] rows including the current token; the
+//        window branch attends to the last min(window, len) rows (window 0: all of them).
+//   entries stream (mode 1 / 2, tables into epool): elen[b] compressed entries; mode 1 sees
+//        entry s iff s*m + m - 1 < len - 1 (the contiguous kernel's rule at pos = len - 1);
+//        mode 2 sees the entries listed in top[b, :] that are < elen[b].
+struct PagedArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* kpool;
+  const __nv_bfloat16* vpool;
+  const int* ktab;             // (B, kmaxp)
+  const int* klen;             // (B)
+  const __nv_bfloat16* epool;  // or null
+  const int* etab;             // (B, emaxp)
+  const int* elen;             // (B)
+  const float* norm_w;
+  const int64_t* top;          // (B, ktop) or null
+  const float* sink_sw;
+  const float* sink_c;
+  __nv_bfloat16* out;
+  int H, page_rows, kmaxp, emaxp, n_pages_k, n_pages_e, window, m, ktop, mode, lmax;
+  float scale, softcap, eps;
+  int* err;
+};
+
+__device__ __forceinline__ const __nv_bfloat16* paged_row(const __nv_bfloat16* pool, const int* tab, int maxp,
+                                                           int n_pages, int page_rows, int64_t r, int* err) {
+  const int slot = static_cast<int>(r / page_rows);
+  if (slot < 0 || slot >= maxp) { record_error(err, kErrBounds); return nullptr; }
+  const int page = tab[slot];
+  if (page < 0 || page >= n_pages) { record_error(err, kErrBounds); return nullptr; }
+  return pool + (static_cast<int64_t>(page) * page_rows + r % page_rows) * kD;
+}
+
+__global__ void __launch_bounds__(kThreads) decode_attn_paged_kernel(const PagedArgs a) {
+  extern __shared__ __align__(16) float dsm[];
+  __shared__ float qs[kHeads][kD];
+  __shared__ float red[kHeads];
+  float4* s = reinterpret_cast<float4*>(dsm);
+  float* rs = dsm + 4 * a.lmax;
+  const int b = blockIdx.x, h0 = blockIdx.y * kHeads, t = threadIdx.x;
+  const int len = a.klen[b];
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) qs[h][t] = __bfloat162float(a.q[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t]);
+  __syncthreads();
+  float acc[kHeads] = {0.f, 0.f, 0.f, 0.f};
+  {
+    int L = a.window > 0 ? min(a.window, len) : len;
+    L = max(0, min(L, a.lmax));
+    const int64_t first = static_cast<int64_t>(len) - L;
+    const int* kt = a.ktab + static_cast<int64_t>(b) * a.kmaxp;
+    auto krow = [&](int j) { return paged_row(a.kpool, kt, a.kmaxp, a.n_pages_k, a.page_rows, first + j, a.err); };
+    auto vrow = [&](int j) { return paged_row(a.vpool, kt, a.kmaxp, a.n_pages_k, a.page_rows, first + j, a.err); };
+    branch_kv<false>(qs, s, rs, red, L, krow, vrow, a.sink_sw, h0, a.scale, a.softcap, a.eps, acc);
+  }
+  if (a.mode != 0) {
+    const float w_t = a.norm_w[t];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) qs[h][t] *= w_t;
+    __syncthreads();
+    const int ne = a.elen[b];
+    const int* et = a.etab + static_cast<int64_t>(b) * a.emaxp;
+    float cacc[kHeads] = {0.f, 0.f, 0.f, 0.f};
+    if (a.mode == 1) {
+      const int64_t pos = static_cast<int64_t>(len) - 1, m = a.m;
+      const int L = max(0, min(ne, a.lmax));
+      auto row = [&](int j) -> const __nv_bfloat16* {
+        return static_cast<int64_t>(j) * m + m - 1 < pos
+                   ? paged_row(a.epool, et, a.emaxp, a.n_pages_e, a.page_rows, j, a.err) : nullptr;
+      };
+      branch<true>(qs, s, rs, red, L, row, a.sink_c, h0, a.scale, 0.f, a.eps, cacc);
+    } else {
+      const int64_t* tb = a.top + static_cast<int64_t>(b) * a.ktop;
+      auto row = [&](int j) -> const __nv_bfloat16* {
+        const int64_t e = tb[j];
+        return (e >= 0 && e < ne) ? paged_row(a.epool, et, a.emaxp, a.n_pages_e, a.page_rows, e, a.err) : nullptr;
+      };
+      branch<true>(qs, s, rs, red, a.ktop, row, nullptr, h0, a.scale, 0.f, a.eps, cacc);
+    }
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) acc[h] += cacc[h] * w_t;
+  }
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h)
+    a.out[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t] = __float2bfloat16(acc[h]);
+}
+
 const __nv_bfloat16* bf16_ptr(const torch::Tensor& t) {
   return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
 }
@@ -354,6 +452,91 @@ void decode_attention(torch::Tensor q, torch::Tensor k_win, torch::Tensor v_win,
     cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   decode_attn_kernel<<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(H / kHeads)), kThreads, smem,
                        at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Paged decode attention (see PagedArgs).  q (B, H, 128); k_pool / v_pool (pages, page_rows, 128);
+// k_table (B, kmaxp) int32; k_len (B) int32; max_rows: the longest branch any sequence may
+// attend to (sizes shared memory; longer branches are cut to it, which the caller avoids).
+void decode_attention_paged(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_table,
+                            torch::Tensor k_len, int64_t window, c10::optional<torch::Tensor> sink_sw, double softcap,
+                            int64_t mode, c10::optional<torch::Tensor> e_pool, c10::optional<torch::Tensor> e_table,
+                            c10::optional<torch::Tensor> e_len, c10::optional<torch::Tensor> norm_w, double eps,
+                            int64_t m, c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c,
+                            double scale, int64_t max_rows, torch::Tensor out, torch::Tensor err) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3 && q.size(2) == kD,
+              "q: contiguous (B, H, 128) bf16");
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(H % kHeads == 0, "heads must be a multiple of 4");
+  TORCH_CHECK(k_pool.is_contiguous() && v_pool.sizes() == k_pool.sizes() && v_pool.is_contiguous() &&
+                  k_pool.dim() == 3 && k_pool.size(2) == kD && k_pool.scalar_type() == at::kBFloat16 &&
+                  v_pool.scalar_type() == at::kBFloat16, "K / V pools: contiguous (pages, rows, 128) bf16");
+  TORCH_CHECK(k_table.scalar_type() == at::kInt && k_table.is_contiguous() && k_table.dim() == 2 &&
+                  k_table.size(0) == B, "k_table: (B, pages) int32");
+  TORCH_CHECK(k_len.scalar_type() == at::kInt && k_len.numel() == B, "k_len: (B) int32");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == q.numel(), "out");
+  TORCH_CHECK(max_rows > 0, "max_rows");
+  PagedArgs a{};
+  a.q = bf16_ptr(q);
+  a.kpool = bf16_ptr(k_pool);
+  a.vpool = bf16_ptr(v_pool);
+  a.ktab = k_table.data_ptr<int>();
+  a.klen = k_len.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.H = static_cast<int>(H);
+  a.page_rows = static_cast<int>(k_pool.size(1));
+  a.kmaxp = static_cast<int>(k_table.size(1));
+  a.n_pages_k = static_cast<int>(k_pool.size(0));
+  a.window = static_cast<int>(window);
+  a.scale = static_cast<float>(scale);
+  a.softcap = static_cast<float>(softcap);
+  a.eps = static_cast<float>(eps);
+  a.mode = static_cast<int>(mode);
+  a.err = err.data_ptr<int>();
+  if (sink_sw.has_value()) {
+    TORCH_CHECK(sink_sw->scalar_type() == at::kFloat && sink_sw->numel() == H && sink_sw->is_contiguous(), "sink");
+    a.sink_sw = sink_sw->data_ptr<float>();
+  }
+  int lmax = static_cast<int>(max_rows);
+  if (mode != 0) {
+    TORCH_CHECK(e_pool.has_value() && e_table.has_value() && e_len.has_value() && norm_w.has_value(),
+                "entry pool, table, lengths and norm weight required");
+    TORCH_CHECK(e_pool->is_contiguous() && e_pool->scalar_type() == at::kBFloat16 && e_pool->dim() == 3 &&
+                    e_pool->size(1) == k_pool.size(1) && e_pool->size(2) == kD, "entry pool: (pages, rows, 128) bf16");
+    TORCH_CHECK(e_table->scalar_type() == at::kInt && e_table->is_contiguous() && e_table->size(0) == B, "e_table");
+    TORCH_CHECK(e_len->scalar_type() == at::kInt && e_len->numel() == B, "e_len");
+    TORCH_CHECK(norm_w->scalar_type() == at::kFloat && norm_w->numel() == kD && norm_w->is_contiguous(), "norm w");
+    a.epool = bf16_ptr(*e_pool);
+    a.etab = e_table->data_ptr<int>();
+    a.elen = e_len->data_ptr<int>();
+    a.emaxp = static_cast<int>(e_table->size(1));
+    a.n_pages_e = static_cast<int>(e_pool->size(0));
+    a.norm_w = norm_w->data_ptr<float>();
+    a.m = static_cast<int>(m);
+    if (sink_c.has_value()) {
+      TORCH_CHECK(sink_c->scalar_type() == at::kFloat && sink_c->numel() == H && sink_c->is_contiguous(), "sink");
+      a.sink_c = sink_c->data_ptr<float>();
+    }
+    if (mode == 2) {
+      TORCH_CHECK(top.has_value() && top->scalar_type() == at::kLong && top->is_contiguous() && top->size(0) == B,
+                  "top: contiguous (B, k) int64");
+      a.top = top->data_ptr<int64_t>();
+      a.ktop = static_cast<int>(top->numel() / std::max<int64_t>(B, 1));
+      lmax = std::max(lmax, a.ktop);
+    } else {
+      TORCH_CHECK(m > 0, "compression rate");
+    }
+  }
+  a.lmax = lmax;
+  if (B == 0) return;
+  const size_t smem = static_cast<size_t>(lmax) * 5 * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "too many keys for one CTA");
+  c10::cuda::CUDAGuard guard(q.device());
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(decode_attn_paged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+  decode_attn_paged_kernel<<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(H / kHeads)), kThreads, smem,
+                             at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -5,6 +5,11 @@ branch (ring of W slots, live iff the slot's age is <= pos, softcap, optional si
 the compressed branch (HCA: every visible entry, optional sink; CSA: the listed top-k
 entries), with K = V = RMSNorm(entry) applied on the fly.  The eager composition it
 replaces is ``infer.static_decode._attend_layer_eager``.
+
+``decode_attention_paged`` is the serving variant: sequences of different lengths decode in
+one launch, and the K / V stream and the compressed entries are read through per-sequence
+block tables from the shared page pools of ``infer.paged_kv`` (no gather into contiguous
+buffers first).
 """
 
 from __future__ import annotations
@@ -39,4 +44,42 @@ def decode_attention(q: Tensor, k_win: Tensor, v_win: Tensor, pos: Tensor, *, si
     return out
 
 
-__all__ = ["decode_attention", "supported"]
+def decode_attention_paged(q: Tensor, k_pool: Tensor, v_pool: Tensor, k_table: Tensor, k_len: Tensor, *,
+                           window: int = 0, sink: Tensor | None = None, softcap: float | None = None,
+                           mode: int = 0, e_pool: Tensor | None = None, e_table: Tensor | None = None,
+                           e_len: Tensor | None = None, norm_weight: Tensor | None = None, norm_eps: float = 1e-6,
+                           m: int = 0, top: Tensor | None = None, comp_sink: Tensor | None = None,
+                           max_rows: int | None = None) -> Tensor:
+    """q (B, H, 128) or (B, H, 1, 128); k_pool / v_pool (pages, page_rows, 128) bf16 storages;
+    k_table (B, P) int32 block tables (-1 padded), k_len (B,) int32 rows per sequence (the
+    current token included).  The window branch attends to the last ``window`` rows (0: all).
+    mode 1 / 2 add the compressed branch over the entry stream (``e_pool`` / ``e_table`` /
+    ``e_len``): HCA with compression rate ``m``, or the CSA entries listed in ``top`` (B, k).
+    ``max_rows`` bounds any branch's length (default: the longest ``k_len`` / ``e_len``, read
+    on the host).  Returns (B, H, 128) bf16.  A page id outside the pool records the bounds
+    error (``gemm.check_errors``) and the row is skipped."""
+    from saint_llm_b200.ops.gemm import error_word
+
+    b, h = q.shape[0], q.shape[1]
+    d = q.shape[-1]
+    if max_rows is None:
+        rows = [int(k_len.max().item()) if k_len.numel() else 1]
+        if window > 0:
+            rows = [min(rows[0], window)]
+        if mode == 1 and e_len is not None and e_len.numel():
+            rows.append(int(e_len.max().item()))
+        max_rows = max(1, *rows)
+    out = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
+    backend.ext().decode_attention_paged(
+        q.reshape(b, h, d).to(torch.bfloat16).contiguous(), k_pool, v_pool, k_table.int().contiguous(),
+        k_len.int().contiguous(), int(window), None if sink is None else sink.float().contiguous(),
+        float(softcap or 0.0), mode, e_pool, None if e_table is None else e_table.int().contiguous(),
+        None if e_len is None else e_len.int().contiguous(),
+        None if norm_weight is None else norm_weight.float().contiguous(), float(norm_eps), int(m),
+        None if top is None else top.reshape(b, -1).long().contiguous(),
+        None if comp_sink is None else comp_sink.float().contiguous(), 1.0 / math.sqrt(d), int(max_rows), out,
+        error_word(q.device))
+    return out
+
+
+__all__ = ["decode_attention", "decode_attention_paged", "supported"]

@@ -61,3 +61,89 @@ def test_decode_attention_matches_eager(cuda, pos_val):
             err = (got.float() - want.float()).abs().max().item()
             assert err <= 3e-2 * want.float().abs().max().item() + 1e-3, (type(st.attn).__name__, err)
     assert {"CSA", "HCA"} <= kinds
+
+
+def _pages(rows_per_seq, page_rows, n_pages, gen, cuda):
+    """Scatter each sequence's rows into shuffled pages of one pool: (pool, table, lengths)."""
+    B = len(rows_per_seq)
+    pool = torch.zeros(n_pages, page_rows, 128, dtype=torch.bfloat16)
+    perm = torch.randperm(n_pages, generator=gen).tolist()
+    maxp = max(1, max((x.shape[0] + page_rows - 1) // page_rows for x in rows_per_seq))
+    table = torch.full((B, maxp), -1, dtype=torch.int32)
+    for b, x in enumerate(rows_per_seq):
+        for p in range((x.shape[0] + page_rows - 1) // page_rows):
+            pid = perm.pop()
+            table[b, p] = pid
+            chunk = x[p * page_rows:(p + 1) * page_rows]
+            pool[pid, :chunk.shape[0]] = chunk
+    lens = torch.tensor([x.shape[0] for x in rows_per_seq], dtype=torch.int32)
+    return pool.to(cuda), table.to(cuda), lens.to(cuda)
+
+
+@pytest.mark.parametrize("window,softcap,sink", [(0, None, True), (64, 30.0, True), (200, None, False)])
+def test_paged_decode_window_matches_fp32(cuda, window, softcap, sink):
+    """Variable-length sequences over shuffled pages against fp32 attention over the last
+    ``window`` rows of each contiguous history (+ sink, softcap)."""
+    import math
+
+    from saint_llm_b200.ops.decode import decode_attention_paged
+
+    gen = torch.Generator().manual_seed(window)
+    lens = [1, 37, 300, 129, 64]
+    H, P = 8, 16
+    ks = [torch.randn(n, 128, generator=gen).to(torch.bfloat16) for n in lens]
+    vs = [torch.randn(n, 128, generator=gen).to(torch.bfloat16) for n in lens]
+    kp, table, kl = _pages(ks, P, 64, torch.Generator().manual_seed(5), cuda)
+    vp, table_v, _ = _pages(vs, P, 64, torch.Generator().manual_seed(5), cuda)
+    assert torch.equal(table, table_v)
+    q = torch.randn(len(lens), H, 128, generator=gen).to(cuda, torch.bfloat16)
+    sk = torch.randn(H, generator=gen).to(cuda) if sink else None
+    out = decode_attention_paged(q, kp, vp, table, kl, window=window, sink=sk, softcap=softcap)
+    for b, n in enumerate(lens):
+        lo = max(0, n - window) if window else 0
+        k, v = ks[b][lo:].to(cuda).float(), vs[b][lo:].to(cuda).float()
+        s = q[b].float() @ k.t() / math.sqrt(128)
+        if softcap:
+            s = softcap * torch.tanh(s / softcap)
+        if sk is not None:
+            s = torch.cat([s, sk[:, None].float()], -1)
+        p = torch.softmax(s, -1)[:, :k.shape[0]]
+        want = p @ v
+        torch.testing.assert_close(out[b].float(), want, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_paged_decode_compressed_matches_contiguous_kernel(cuda, mode):
+    """Same caches laid out as ring + contiguous entries (decode_attention) and as pages
+    (decode_attention_paged), all sequences at one position."""
+    from saint_llm_b200.ops.decode import decode_attention, decode_attention_paged
+    from saint_llm_b200.ops.gemm import check_errors
+
+    gen = torch.Generator().manual_seed(mode)
+    B, H, W, m, pos = 3, 8, 128, 4, 517
+    n = 160
+    kh = torch.randn(B, pos + 1, 128, generator=gen).to(torch.bfloat16)
+    vh = torch.randn(B, pos + 1, 128, generator=gen).to(torch.bfloat16)
+    ring_k = torch.zeros(B, W, 128, dtype=torch.bfloat16)
+    ring_v = torch.zeros(B, W, 128, dtype=torch.bfloat16)
+    for r in range(max(0, pos - W + 1), pos + 1):
+        ring_k[:, r % W] = kh[:, r]
+        ring_v[:, r % W] = vh[:, r]
+    ent = torch.randn(B, n, 128, generator=gen).to(torch.bfloat16)
+    ne = (pos + 1) // m if mode == 1 else n
+    q = torch.randn(B, H, 1, 128, generator=gen).to(cuda, torch.bfloat16)
+    sink = torch.randn(H, generator=gen).to(cuda)
+    csink = torch.randn(H, generator=gen).to(cuda) if mode == 1 else None
+    w = (1 + 0.1 * torch.randn(128, generator=gen)).to(cuda)
+    top = torch.randint(-1, ne, (B, 24), generator=gen).to(cuda) if mode == 2 else None
+    want = decode_attention(q, ring_k.to(cuda), ring_v.to(cuda), torch.tensor(pos, device=cuda), sink=sink,
+                            softcap=None, mode=mode, entries=ent[:, :ne].contiguous().to(cuda), norm_weight=w,
+                            m=m, top=top, comp_sink=csink)
+    kp, kt, kl = _pages([kh[b] for b in range(B)], 32, 64, torch.Generator().manual_seed(7), cuda)
+    vp, _, _ = _pages([vh[b] for b in range(B)], 32, 64, torch.Generator().manual_seed(7), cuda)
+    ep, et, el = _pages([ent[b, :ne] for b in range(B)], 32, 32, torch.Generator().manual_seed(8), cuda)
+    got = decode_attention_paged(q, kp, vp, kt, kl, window=W, sink=sink, mode=mode, e_pool=ep, e_table=et,
+                                 e_len=el, norm_weight=w, m=m, top=top, comp_sink=csink)
+    torch.cuda.synchronize()
+    check_errors(cuda)
+    torch.testing.assert_close(got.float(), want.reshape(B, H, 128).float(), rtol=2e-2, atol=2e-2)

@@ -205,12 +205,16 @@ def run_ours(args) -> dict:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clk:
         start.record()
-        for _ in range(args.steps):
+        marks[0].record()
+        for i in range(args.steps):
             loss = device_step()
+            marks[i + 1].record()  # per-step spread (no sync: steps still queue back to back)
         end.record()
         torch.cuda.synchronize()
+        per_step = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
         if world > 1:
             torch.distributed.barrier()
         t_ms = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
@@ -220,8 +224,10 @@ def run_ours(args) -> dict:
         final_loss = _rank_mean(loss, world)
         check_errors(device)
 
-        # end-to-end through the public call: host batch in, float loss out (same clock
-        # sampling as the device-timed loop, so both run under the same host load)
+    # end-to-end through the public call: host batch in, float loss out, timed on the host
+    # around the calls; its own clock record (the power-capped SM clock differs between the
+    # two loops by a few percent, which is what separates the two numbers)
+    with ClockSampler(local) as clk_e:
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
@@ -264,12 +270,16 @@ def run_ours(args) -> dict:
                             "note": "mean over ranks; main CE + MTP-weighted CE + balance term"},
                    "final_loss": final_loss,
                    "phases_ms": phases,
+                   "step_ms_min_max_this_rank": [round(min(per_step), 1), round(max(per_step), 1)],
                    "kernel_busy_ms_per_step": round(busy_ms, 1),
                    "top_kernels_ms_per_step": top_kernels,
                    "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 1e9, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(data.bytes_per_step), "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": int(data.bytes_per_step), "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms, "clocks": clk_e.summary(),
+                "timing": "host perf_counter around TrainStep.__call__ (pinned host batch -> device, loss -> "
+                          "host float), after a device sync and barrier; max over ranks"},
         "gpu_launches": launches,
     }
     if world > 1:

@@ -147,6 +147,29 @@ __device__ __forceinline__ void push_chunk_to_peers(const GemmParams& P, const u
   }
 }
 
+// Symmetric outputs (P.sym): tiles entirely below the diagonal are skipped, and the tiles that
+// are computed write the transposes of their values into those skipped tiles, so no separate
+// mirror pass is needed.  For this lane's row r, the target (c, r) lies in a skipped tile exactly
+// when c >= c_min = (floor(((r / BN) * BN + BN - 1) / 128) + 1) * 128 (tile (c / 128, r / BN)
+// has all its columns left of its first row); those c are strictly above the diagonal.  Lanes
+// hold consecutive rows, so each store instruction writes 32 consecutive elements of row c.
+template <int BN, int W, bool F32>
+__device__ __forceinline__ void sym_store_transposed(const GemmParams& P, const GemmProblem& pr, int bt, int row,
+                                                     int col0, const float* v) {
+  if (row >= pr.m) return;
+  const int c_min = (((row / BN) * BN + BN - 1) / kBM + 1) * kBM;
+  if (col0 + W <= c_min) return;
+  const long long base = pr.d_off + static_cast<long long>(bt) * pr.d_bstride + row;
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    const int c = col0 + j;
+    if (c >= c_min && c < pr.n) {
+      if constexpr (F32) reinterpret_cast<float*>(P.d)[base + static_cast<long long>(c) * pr.d_ld] = v[j];
+      else reinterpret_cast<__nv_bfloat16*>(P.d)[base + static_cast<long long>(c) * pr.d_ld] = __float2bfloat16(v[j]);
+    }
+  }
+}
+
 __device__ __forceinline__ void red_release_sys_add(unsigned long long addr, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
@@ -495,6 +518,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               }
             }
           }
+          if (P.sym) sym_store_transposed<BN, kCW, kF32>(P, pr, bt, row, col0, v);
           // Boxes starting past the problem are skipped (never issue a fully clipped store).
           const bool issue = col0 < pr.n && mt * kBM + quarter * 32 < pr.m;
           const uint8_t* staged = stg + sbuf * kEpiStageBytes;
@@ -527,6 +551,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = zero_k ? 0.f : __uint_as_float(r[j]) * P.alpha * rs;
           const bool full_chunk = col0 + 32 <= pr.n;
+          const bool sym_here = P.sym != 0;
           if constexpr (EPI == kEpiAxpbyBF16) {
             const __nv_bfloat16* cin = reinterpret_cast<const __nv_bfloat16*>(P.aux) + dbase + col0;
             if (full_chunk && ((reinterpret_cast<uintptr_t>(cin) & 15) == 0)) {
@@ -545,6 +570,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               for (int j = 0; j < 32; ++j)
                 if (col0 + j < pr.n) v[j] += P.beta * __bfloat162float(cin[j]);
             }
+          }
+          if (sym_here) {
+            constexpr bool kF32o = (EPI == kEpiF32 || EPI == kEpiF32Acc);
+            sym_store_transposed<BN, 32, kF32o>(P, pr, bt, row, col0, v);
           }
           if constexpr (EPI == kEpiPeerBF16) {  // fallback path: per-lane row stores to the peers
             for (int p = 0; p < P.n_peers; ++p) {

@@ -55,12 +55,28 @@ __device__ __forceinline__ unsigned tp_ld_acquire(const unsigned* a) {
   return v;
 }
 
-// x (n bf16, n % 8 == 0) -> every peer's slot; then one release-add per CTA per peer.
+// x (n bf16, n % 8 == 0) -> every peer's slot; then one release-add per CTA per peer.  Each
+// thread moves 4 independent 16-byte vectors per iteration (loads issued before the stores), so
+// enough remote stores are in flight to fill the link.
+constexpr int kTpUnroll = 4;
+
 __global__ void tp_push_kernel(const uint4* __restrict__ x, int64_t n8, TpPeers slots, TpPeers cnts, int n_peers) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint4 v = x[i];
-    for (int p = 0; p < n_peers; ++p) reinterpret_cast<uint4*>(slots.p[p])[i] = v;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n8; i0 += stride * kTpUnroll) {
+    uint4 v[kTpUnroll];
+#pragma unroll
+    for (int u = 0; u < kTpUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < n8) v[u] = x[i];
+    }
+    for (int p = 0; p < n_peers; ++p) {
+      uint4* dst = reinterpret_cast<uint4*>(slots.p[p]);
+#pragma unroll
+      for (int u = 0; u < kTpUnroll; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i < n8) dst[i] = v[u];
+      }
+    }
   }
   __threadfence_system();
   __syncthreads();
@@ -94,26 +110,41 @@ __global__ void tp_reduce_kernel(uint4* __restrict__ x, int64_t n8, const __nv_b
   }
   __syncthreads();
   if (!ok) return;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float acc[8];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n8; i0 += stride * kTpUnroll) {
+    float acc[kTpUnroll][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int u = 0; u < kTpUnroll; ++u)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
     for (int s = 0; s < ws; ++s) {
-      const uint4 v = s == rank ? x[i] : __ldcg(reinterpret_cast<const uint4*>(recv + s * slot_elems) + i);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      uint4 v[kTpUnroll];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
+      for (int u = 0; u < kTpUnroll; ++u) {  // all loads of this source first
+        const int64_t i = i0 + u * stride;
+        if (i < n8) v[u] = s == rank ? x[i] : __ldcg(reinterpret_cast<const uint4*>(recv + s * slot_elems) + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kTpUnroll; ++u) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(h[j]);
+          acc[u][2 * j] += f.x;
+          acc[u][2 * j + 1] += f.y;
+        }
       }
     }
-    uint4 o;
-    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-    x[i] = o;
+    for (int u = 0; u < kTpUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n8) continue;
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[u][2 * j], acc[u][2 * j + 1]);
+      x[i] = o;
+    }
   }
 }
 

@@ -68,7 +68,8 @@ def _as_operand(x: Tensor) -> tuple[Tensor, bool]:
 def gemm_nt(a: Tensor, b: Tensor, *, out: Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
             accumulate: bool = False, alpha: float = 1.0, symmetric: bool = False) -> Tensor:
     """``symmetric=True``: the caller guarantees ``a @ b^T`` is symmetric (e.g. ``b is a``);
-    only tiles on or above the diagonal are computed and the rest is mirrored."""
+    only tiles on or above the diagonal are multiplied, and their epilogue writes the
+    transposed values into the skipped tiles below it."""
     if a.dtype != torch.bfloat16:
         a = a.to(torch.bfloat16)
     if b.dtype != torch.bfloat16:
@@ -100,9 +101,9 @@ def gemm_nt(a: Tensor, b: Tensor, *, out: Tensor | None = None, out_dtype: torch
     if av.dim() == 2 and a.dim() == 2:
         squeeze = False
     sym = symmetric and not accumulate
+    # symmetric: the GEMM computes the tiles on and above the diagonal and writes their
+    # transposes into the skipped ones from its epilogue (no mirror pass)
     backend.ext().gemm(av, bv, out, a_mn, b_mn, accumulate, float(alpha), error_word(a.device), sym)
-    if sym:
-        backend.ext().sym_mirror(out)
     del squeeze
     return out
 
@@ -121,8 +122,6 @@ def gemm_axpby(a: Tensor, b: Tensor, c: Tensor, *, alpha: float = 1.0, beta: flo
     av, a_mn = _as_operand(a)
     bv, b_mn = _as_operand(b)
     backend.ext().gemm_axpby(av, bv, c, out, a_mn, b_mn, float(alpha), float(beta), error_word(a.device), symmetric)
-    if symmetric:
-        backend.ext().sym_mirror(out)
     return out
 
 

@@ -91,7 +91,7 @@ def native_newton_schulz(y: Tensor, n_iter_stage1: int = 8, n_iter_stage2: int =
     The "+ b G" and "+ a Y" terms ride in the GEMM epilogue (no element-wise passes),
     and neither orientation needs a transpose copy: the tensor cores read Y^T directly.
     G and P are symmetric: their GEMMs skip the tiles below the diagonal (~40 % of the
-    tiles of a 1408 x 1408 Gram) and a transpose kernel mirrors them.
+    tiles of a 1408 x 1408 Gram) and fill them from the epilogue of the tiles they mirror.
     """
     from saint_llm_b200.ops import gemm
 

@@ -120,7 +120,9 @@ def test_gemm_bf16_output_view_with_row_stride(cuda):
 
 @pytest.mark.parametrize("batch,r,k", [(3, 1408, 2048), (2, 200, 256), (1, 520, 64)])
 def test_symmetric_gemm_and_axpby(cuda, batch, r, k):
-    """Symmetric outputs computed on the upper tiles only and mirrored."""
+    """Symmetric outputs computed on the upper tiles only; the skipped tiles are filled from the
+    epilogue with the transposed values, so the result is exactly symmetric and its upper
+    triangle equals the full product's."""
     from saint_llm_b200.ops.gemm import gemm_axpby, gemm_nt
 
     torch.manual_seed(0)
@@ -133,3 +135,6 @@ def test_symmetric_gemm_and_axpby(cuda, batch, r, k):
     pref = -1.5 * g.float() @ g.float() + 0.5 * g.float()
     assert torch.equal(p, p.transpose(-1, -2))
     assert ((p.float() - pref).norm() / pref.norm()).item() < 1e-2
+    full = gemm_nt(y, y)
+    up = torch.triu(torch.ones(r, r, dtype=torch.bool, device=cuda))
+    assert torch.equal(g[:, up], full[:, up])

@@ -53,7 +53,12 @@ class TokenLevelCompressor(nn.Module):
         self.bias_b = nn.Parameter(torch.zeros(m, c))
 
     def pool(self, c_b: Tensor, z_b: Tensor) -> Tensor:
-        """Softmax-pool (B, n*m, c) value/score projections into (B, n, c)."""
+        """Softmax-pool (B, n*m, c) value/score projections into (B, n, c).  bf16 inputs on
+        CUDA run the fused pooling kernel (fp32 math, one launch instead of ~25)."""
+        if backend.native_for(c_b) and c_b.dtype == torch.bfloat16 and z_b.dtype == torch.bfloat16:
+            from saint_llm_b200.ops.attention import _pool
+
+            return _pool(c_b, z_b, self.bias_b, self.m).to(c_b.dtype)
         b, t, c = c_b.shape
         n = t // self.m
         z = z_b.reshape(b, n, self.m, c) + self.bias_b

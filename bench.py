@@ -243,9 +243,18 @@ def run_ours(args) -> dict:
     # one more step with per-phase CUDA events (outside the timed regions), max over ranks
     if world > 1:
         torch.distributed.barrier()
+    comm = getattr(model, "ep_comm", None)
+    rows0 = getattr(comm, "rows_received", 0)
     with PhaseRecorder(device) as rec:
         device_step()
     phases = rec.summary()
+    expert_rows = None
+    if comm is not None and world > 1:
+        # expert rows (128-padded) each rank owned in that step: the load spread the EP waits absorb
+        mine = torch.tensor([comm.rows_received - rows0], dtype=torch.int64, device=device)
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        torch.distributed.all_gather(allr, mine)
+        expert_rows = [int(x.item()) for x in allr]
     n_native, busy_ms, top_kernels = count_native_launches(device_step)
     launches = n_native * args.steps
     tokens_per_step = world * args.seqs_per_gpu * args.seq_len
@@ -270,6 +279,7 @@ def run_ours(args) -> dict:
                             "note": "mean over ranks; main CE + MTP-weighted CE + balance term"},
                    "final_loss": final_loss,
                    "phases_ms": phases,
+                   "expert_rows_per_rank": expert_rows,
                    "step_ms_min_max_this_rank": [round(min(per_step), 1), round(max(per_step), 1)],
                    "kernel_busy_ms_per_step": round(busy_ms, 1),
                    "top_kernels_ms_per_step": top_kernels,

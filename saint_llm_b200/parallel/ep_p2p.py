@@ -175,6 +175,7 @@ class P2PExpertComm:
         self.tokens = 0
         self.C = 0
         self.y = self.dy = self.dx = self.xr = None
+        self.rows_received = 0  # expert rows this rank owned, summed over calls (host count)
         # side stream for the token traffic that overlaps the shared experts (see moe_forward_p2p)
         dev = heap.device
         self.side = torch.cuda.Stream(dev) if torch.device(dev).type == "cuda" else None
@@ -274,6 +275,7 @@ class EPCall:
         # rows this owner received (expert segments are contiguous and 128-padded): one host
         # read per layer sizes the saved input and the activations by the actual routing
         self.R = int((self.seg_start[-1] + self.seg_pad[-1]).item()) if E_loc else 0
+        c.rows_received += self.R
         x_rows = xr[:self.R].clone()
         self.x_saved = x_rows
         plan = _SegPlan(self.seg_start, self.seg_pad)

@@ -109,6 +109,8 @@ void mhc_combine_bwd(torch::Tensor dY, torch::Tensor X, torch::Tensor o, torch::
 void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t n);
 void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
+void mhc_split_bwd2(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
+                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
 // attention.cu
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
               int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
@@ -234,4 +236,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_combine_bwd", &sv4::mhc_combine_bwd);
   m.def("mhc_premix_da", &sv4::mhc_premix_da);
   m.def("mhc_split_bwd", &sv4::mhc_split_bwd);
+  m.def("mhc_split_bwd2", &sv4::mhc_split_bwd2);
 }

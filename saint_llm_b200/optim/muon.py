@@ -297,6 +297,30 @@ class MuonAdamW(_QKClipMixin, torch.optim.Optimizer):
         return loss
 
     @torch.no_grad()
+    def init_state(self) -> int:
+        """Allocate every state buffer the first ``step`` would create (Muon momentum, AdamW
+        moments) now, for the parameters this rank updates (``param_filter``), so memory
+        planning done before the first step -- a CUDA-graph capture -- sees them.  Returns
+        the bytes allocated."""
+        flt = self.param_filter
+        n = 0
+        for group in self.param_groups:
+            for p in group["params"]:
+                if not p.requires_grad or (flt is not None and not flt(p)):
+                    continue
+                st = self.state[p]
+                if group["kind"] == "muon":
+                    if "momentum_buffer" not in st:
+                        st["momentum_buffer"] = torch.zeros_like(p)
+                        n += p.numel() * p.element_size()
+                elif not st:
+                    st["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                    st["exp_avg"] = torch.zeros_like(p, dtype=torch.float32)
+                    st["exp_avg_sq"] = torch.zeros_like(p, dtype=torch.float32)
+                    n += 8 * p.numel()
+        return n
+
+    @torch.no_grad()
     def _adamw_group_step(self, group: dict[str, Any]) -> None:
         params = [p for p in group["params"] if _active_grad(self, p) is not None]
         if not params:

@@ -67,6 +67,9 @@ class TrainStep:
         longer reuse it between steps), so the capture is skipped when the warm-up's
         activation peak would not fit again next to what is allocated now plus a margin
         for the optimizer's temporaries."""
+        init_state = getattr(self.optimizer, "init_state", None)
+        if init_state is not None:
+            init_state()  # the optimizer's buffers exist before the free memory is measured
         self._tok = torch.zeros_like(tok)
         self._total = torch.zeros((), dtype=torch.float32, device=self.device)
         self._tok.copy_(tok)

@@ -266,3 +266,35 @@ def test_build_training_consumes_run_config():
     for bad in ({"tp": 2}, {"grad_dtype": "bfloat16"}, {"zero": "fsdp"}):
         with pytest.raises(ValueError):
             build_training(cfg, run.model_copy(update=bad), torch.device("cpu"))
+
+
+def test_init_state_preallocates_without_changing_the_update():
+    """``MuonAdamW.init_state`` creates exactly the buffers the first step would (so a graph
+    capture can plan memory with them) and the updates stay identical; ``param_filter``
+    excludes parameters another rank owns."""
+    from saint_llm_b200.optim import MuonAdamW
+
+    torch.manual_seed(0)
+    mats = [nn.Parameter(torch.randn(16, 8)) for _ in range(3)]
+    vecs = [nn.Parameter(torch.randn(8)) for _ in range(2)]
+    grads = [torch.randn_like(p) for p in mats + vecs]
+
+    def run(pre: bool, flt=None):
+        ps = [nn.Parameter(p.detach().clone()) for p in mats + vecs]
+        opt = MuonAdamW(ps[:3], ps[3:], lr=0.01, qk_clip_enabled=False, ns_impl="torch")
+        opt.param_filter = flt
+        if pre:
+            n = opt.init_state()
+            assert n > 0
+        for p, g in zip(ps, grads, strict=True):
+            p.grad = g.clone()
+        opt.step()
+        return ps, opt
+
+    a, _ = run(False)
+    b, opt_b = run(True)
+    for x, y in zip(a, b, strict=True):
+        assert torch.equal(x, y)
+    assert len(opt_b.state) == 5
+    _, opt_c = run(True, flt=lambda p: p.dim() == 1)  # this rank owns only the vectors
+    assert len(opt_c.state) == 2 and all(p.dim() == 1 for p in opt_c.state)

@@ -381,7 +381,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seqs-per-gpu", type=int, default=32)
-    ap.add_argument("--micro-batch", type=int, default=2)
+    ap.add_argument("--micro-batch", type=int, default=None,
+                    help="sequences per micro-batch (default: 2 on one GPU, where the CUDA-graph pool must fit "
+                         "next to the unsharded expert pool; 4 with N > 1, where expert parallelism frees the "
+                         "memory and halves the per-micro-batch gradient read-modify-writes and EP calls; the "
+                         "reference arm uses 2)")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel token transport for N > 1 (peer-memory kernels or NCCL all-to-all)")
     ap.add_argument("--no-zero", action="store_true",
@@ -406,6 +410,9 @@ def main() -> None:
     ap.add_argument("--ckpt", action="store_true", help="activation checkpointing per block")
     ap.add_argument("--layers", type=int, default=0, help="(development only) override n_layers")
     args = ap.parse_args()
+    if args.micro_batch is None:
+        world = int(os.environ.get("WORLD_SIZE", args.gpus))
+        args.micro_batch = 2 if args.impl == "reference" or world == 1 else 4
     res = run_reference(args) if args.impl == "reference" else run_ours(args)
     if res:
         print(json.dumps(res), flush=True)

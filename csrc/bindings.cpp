@@ -54,6 +54,11 @@ void decode_attention_paged(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             c10::optional<torch::Tensor> e_len, c10::optional<torch::Tensor> norm_w, double eps,
                             int64_t m, c10::optional<torch::Tensor> top, c10::optional<torch::Tensor> sink_c,
                             double scale, int64_t max_rows, torch::Tensor out, torch::Tensor err);
+void decode_window_split(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_table,
+                         torch::Tensor k_len, int64_t window, double softcap, double scale, int64_t splits,
+                         int64_t max_rows, torch::Tensor pm, torch::Tensor pl, torch::Tensor po, torch::Tensor err);
+void lse_merge(torch::Tensor m, torch::Tensor l, torch::Tensor o, c10::optional<torch::Tensor> extra,
+               torch::Tensor out, c10::optional<torch::Tensor> out_m, c10::optional<torch::Tensor> out_l);
 // router.cu
 void router_bwd(torch::Tensor z, torch::Tensor aff, torch::Tensor idx, torch::Tensor gate,
                 c10::optional<torch::Tensor> d_gate, c10::optional<torch::Tensor> d_aff, int64_t mode,
@@ -109,8 +114,6 @@ void mhc_combine_bwd(torch::Tensor dY, torch::Tensor X, torch::Tensor o, torch::
 void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t n);
 void mhc_split_bwd(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
-void mhc_split_bwd2(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
-                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n);
 // attention.cu
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor kv, torch::Tensor sel, int64_t mode,
               int64_t m, int64_t window, torch::Tensor sink, double softcap, double scale, torch::Tensor o_sw,
@@ -190,6 +193,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &sv4::gemm_fp8);
   m.def("decode_attention", &sv4::decode_attention);
   m.def("decode_attention_paged", &sv4::decode_attention_paged);
+  m.def("decode_window_split", &sv4::decode_window_split);
+  m.def("lse_merge", &sv4::lse_merge);
   m.def("router_fwd", &sv4::router_fwd);
   m.def("router_bwd", &sv4::router_bwd);
   m.def("fp8_sf_bytes", &sv4::fp8_sf_bytes);
@@ -236,5 +241,4 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_combine_bwd", &sv4::mhc_combine_bwd);
   m.def("mhc_premix_da", &sv4::mhc_premix_da);
   m.def("mhc_split_bwd", &sv4::mhc_split_bwd);
-  m.def("mhc_split_bwd2", &sv4::mhc_split_bwd2);
 }

@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_paged_kernel(const Paged
   __syncthreads();
   float acc[kHeads] = {0.f, 0.f, 0.f, 0.f};
   {
-    int L = a.window > 0 ? min(a.window, len) : len;
+    int L = a.window < 0 ? 0 : (a.window > 0 ? min(a.window, len) : len);  // window < 0: compressed only
     L = max(0, min(L, a.lmax));
     const int64_t first = static_cast<int64_t>(len) - L;
     const int* kt = a.ktab + static_cast<int64_t>(b) * a.kmaxp;
@@ -381,6 +381,131 @@ __global__ void __launch_bounds__(kThreads) decode_attn_paged_kernel(const Paged
 #pragma unroll
   for (int h = 0; h < kHeads; ++h)
     a.out[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t] = __float2bfloat16(acc[h]);
+}
+
+// ------------------------------------------------------ split-K window + LSE merge
+// Long windows (or window 0 = the whole stream) at small batch leave most SMs idle with one CTA
+// per (sequence, 4 heads); the split variant gives each of S CTAs a contiguous slice of the
+// window rows and writes the partial (m, l, o): row max of the scores, sum of exp(s - m) and the
+// normalised output, which lse_merge combines (the associative merge of tree attention).
+__global__ void __launch_bounds__(kThreads) decode_window_split_kernel(const PagedArgs a, int splits, float* pm,
+                                                                       float* pl, float* po) {
+  extern __shared__ __align__(16) float dsm[];
+  __shared__ float qs[kHeads][kD];
+  const int b = blockIdx.x, h0 = blockIdx.y * kHeads, z = blockIdx.z, t = threadIdx.x;
+  const int warp = t / 32, lane = t % 32;
+  const int len = a.klen[b];
+  int L = a.window > 0 ? min(a.window, len) : len;
+  const int64_t first = static_cast<int64_t>(len) - L;
+  const int chunk = (L + splits - 1) / splits;
+  const int lo = min(L, z * chunk), n = min(L, lo + chunk) - lo;
+  float4* sc = reinterpret_cast<float4*>(dsm);
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) qs[h][t] = __bfloat162float(a.q[(static_cast<int64_t>(b) * a.H + h0 + h) * kD + t]);
+  __syncthreads();
+  const int* kt = a.ktab + static_cast<int64_t>(b) * a.kmaxp;
+  for (int j = t; j < n; j += kThreads) {
+    const __nv_bfloat16* row = paged_row(a.kpool, kt, a.kmaxp, a.n_pages_k, a.page_rows, first + lo + j, a.err);
+    float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    if (row != nullptr) {
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < kD; c += 8) {
+        float x[8];
+        load8(row + c, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          d0 = fmaf(qs[0][c + e], x[e], d0);
+          d1 = fmaf(qs[1][c + e], x[e], d1);
+          d2 = fmaf(qs[2][c + e], x[e], d2);
+          d3 = fmaf(qs[3][c + e], x[e], d3);
+        }
+      }
+      v = make_float4(d0 * a.scale, d1 * a.scale, d2 * a.scale, d3 * a.scale);
+      if (a.softcap > 0.f) {
+        v.x = a.softcap * tanhf(v.x / a.softcap);
+        v.y = a.softcap * tanhf(v.y / a.softcap);
+        v.z = a.softcap * tanhf(v.z / a.softcap);
+        v.w = a.softcap * tanhf(v.w / a.softcap);
+      }
+    }
+    sc[j] = v;
+  }
+  __syncthreads();
+  __shared__ float sm[kHeads], sl[kHeads];
+  {  // warp h: max and sum of exponentials of head h0 + h
+    float* sh = reinterpret_cast<float*>(sc) + warp;
+    float mx = -INFINITY;
+    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sh[4 * j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float p = mx == -INFINITY ? 0.f : __expf(sh[4 * j] - mx);
+      sh[4 * j] = p;
+      sum += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      sm[warp] = mx;
+      sl[warp] = sum;
+    }
+  }
+  __syncthreads();
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+  for (int j = 0; j < n; ++j) {
+    const float4 p = sc[j];
+    if (p.x == 0.f && p.y == 0.f && p.z == 0.f && p.w == 0.f) continue;
+    const __nv_bfloat16* row = paged_row(a.vpool, kt, a.kmaxp, a.n_pages_k, a.page_rows, first + lo + j, nullptr);
+    if (row == nullptr) continue;
+    const float v = __bfloat162float(row[t]);
+    o0 = fmaf(p.x, v, o0);
+    o1 = fmaf(p.y, v, o1);
+    o2 = fmaf(p.z, v, o2);
+    o3 = fmaf(p.w, v, o3);
+  }
+  const float acc[kHeads] = {o0, o1, o2, o3};
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    const int64_t row = (static_cast<int64_t>(z) * gridDim.x + b) * a.H + h0 + h;  // (split, b, head)
+    po[row * kD + t] = sl[h] > 0.f ? acc[h] / sl[h] : 0.f;
+    if (t == 0) {
+      pm[row] = sm[h];
+      pl[row] = sl[h];
+    }
+  }
+}
+
+// out[r] = merge over s of (m[s, r], l[s, r], o[s, r, :]); an optional extra logit per row (a
+// sink) joins the denominator only.  Rows whose every partial is empty (and no sink) give 0.
+__global__ void lse_merge_kernel(const float* __restrict__ m, const float* __restrict__ l,
+                                 const float* __restrict__ o, int S, int64_t rows, int D,
+                                 const float* __restrict__ extra, int64_t extra_mod, float* __restrict__ out,
+                                 float* __restrict__ out_m, float* __restrict__ out_l) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * D) return;
+  const int64_t r = i / D;
+  const int d = static_cast<int>(i % D);
+  float mx = extra != nullptr ? extra[r % extra_mod] : -INFINITY;
+  for (int s = 0; s < S; ++s)
+    if (l[s * rows + r] > 0.f) mx = fmaxf(mx, m[s * rows + r]);
+  float den = 0.f, num = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < S; ++s) {
+      const float ls = l[s * rows + r];
+      if (ls <= 0.f) continue;
+      const float w = __expf(m[s * rows + r] - mx) * ls;
+      den += w;
+      num += w * o[(s * rows + r) * D + d];
+    }
+    if (extra != nullptr) den += __expf(extra[r % extra_mod] - mx);
+  }
+  out[i] = den > 0.f ? num / den : 0.f;
+  if (d == 0 && out_m != nullptr) {
+    out_m[r] = mx;
+    out_l[r] = den;
+  }
 }
 
 const __nv_bfloat16* bf16_ptr(const torch::Tensor& t) {
@@ -537,6 +662,85 @@ void decode_attention_paged(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                          static_cast<int>(smem));
   decode_attn_paged_kernel<<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(H / kHeads)), kThreads, smem,
                              at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Window branch of paged decode split over `splits` CTAs per (sequence, 4 heads): partial
+// (m, l, o) into pm / pl (splits, B, H) and po (splits, B, H, 128), fp32.
+void decode_window_split(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool, torch::Tensor k_table,
+                         torch::Tensor k_len, int64_t window, double softcap, double scale, int64_t splits,
+                         int64_t max_rows, torch::Tensor pm, torch::Tensor pl, torch::Tensor po, torch::Tensor err) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3 && q.size(2) == kD, "q");
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(H % kHeads == 0 && splits >= 1 && max_rows > 0, "heads % 4, splits >= 1, max_rows > 0");
+  TORCH_CHECK(k_pool.is_contiguous() && v_pool.sizes() == k_pool.sizes() && v_pool.is_contiguous() &&
+                  k_pool.dim() == 3 && k_pool.size(2) == kD, "pools");
+  TORCH_CHECK(k_table.scalar_type() == at::kInt && k_table.is_contiguous() && k_table.size(0) == B, "k_table");
+  TORCH_CHECK(k_len.scalar_type() == at::kInt && k_len.numel() == B, "k_len");
+  TORCH_CHECK(pm.numel() == splits * B * H && pl.numel() == pm.numel() && po.numel() == pm.numel() * kD &&
+                  pm.scalar_type() == at::kFloat && po.is_contiguous(), "partials");
+  PagedArgs a{};
+  a.q = bf16_ptr(q);
+  a.kpool = bf16_ptr(k_pool);
+  a.vpool = bf16_ptr(v_pool);
+  a.ktab = k_table.data_ptr<int>();
+  a.klen = k_len.data_ptr<int>();
+  a.H = static_cast<int>(H);
+  a.page_rows = static_cast<int>(k_pool.size(1));
+  a.kmaxp = static_cast<int>(k_table.size(1));
+  a.n_pages_k = static_cast<int>(k_pool.size(0));
+  a.window = static_cast<int>(window);
+  a.scale = static_cast<float>(scale);
+  a.softcap = static_cast<float>(softcap);
+  a.err = err.data_ptr<int>();
+  if (B == 0) return;
+  const int chunk = static_cast<int>((max_rows + splits - 1) / splits);
+  const size_t smem = static_cast<size_t>(std::max(chunk, 1)) * 4 * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "too many rows per split");
+  c10::cuda::CUDAGuard guard(q.device());
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(decode_window_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+  decode_window_split_kernel<<<dim3(static_cast<unsigned>(B), static_cast<unsigned>(H / kHeads),
+                                    static_cast<unsigned>(splits)),
+                               kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a, static_cast<int>(splits),
+                                                                                   pm.data_ptr<float>(),
+                                                                                   pl.data_ptr<float>(),
+                                                                                   po.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Log-sum-exp merge of S partials: m, l (S, R), o (S, R, D) fp32 -> out (R, D) fp32 (and the
+// merged m, l when given).  extra: optional logit per row (row r uses extra[r % extra.numel()]).
+void lse_merge(torch::Tensor m, torch::Tensor l, torch::Tensor o, c10::optional<torch::Tensor> extra,
+               torch::Tensor out, c10::optional<torch::Tensor> out_m, c10::optional<torch::Tensor> out_l) {
+  TORCH_CHECK(m.scalar_type() == at::kFloat && l.scalar_type() == at::kFloat && o.scalar_type() == at::kFloat &&
+                  out.scalar_type() == at::kFloat, "fp32 partials and output");
+  TORCH_CHECK(m.is_contiguous() && l.is_contiguous() && o.is_contiguous() && out.is_contiguous() && m.dim() == 2 &&
+                  l.sizes() == m.sizes() && o.dim() == 3 && o.size(0) == m.size(0) && o.size(1) == m.size(1),
+              "m, l (S, R); o (S, R, D)");
+  const int64_t S = m.size(0), R = m.size(1), D = o.size(2);
+  TORCH_CHECK(out.numel() == R * D, "out (R, D)");
+  const float* ex = nullptr;
+  int64_t ex_mod = 1;
+  if (extra.has_value()) {
+    TORCH_CHECK(extra->scalar_type() == at::kFloat && extra->is_contiguous() && extra->numel() > 0, "extra");
+    ex = extra->data_ptr<float>();
+    ex_mod = extra->numel();
+  }
+  float* om = nullptr;
+  float* ol = nullptr;
+  if (out_m.has_value()) {
+    TORCH_CHECK(out_l.has_value() && out_m->numel() == R && out_l->numel() == R, "out_m / out_l (R)");
+    om = out_m->data_ptr<float>();
+    ol = out_l->data_ptr<float>();
+  }
+  const int64_t total = R * D;
+  if (total == 0) return;
+  c10::cuda::CUDAGuard guard(m.device());
+  lse_merge_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      m.data_ptr<float>(), l.data_ptr<float>(), o.data_ptr<float>(), static_cast<int>(S), R, static_cast<int>(D),
+      ex, ex_mod, out.data_ptr<float>(), om, ol);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

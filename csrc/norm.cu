@@ -709,100 +709,6 @@ __global__ void mhc_premix_da_kernel(const __nv_bfloat16* __restrict__ X, const 
 // Backward of split (pre-mix + norm-projection), accumulated onto dX (which holds the carry grad):
 //   dX[t,h] = a[t,h] * dinner[t]  +  r * (dp_t W)_h  -  (r^3 / F) * X[t,h] * sum_j dp_tj q_tj
 // where q = p / r.  CTA per 32 tokens; each thread owns 4 features.
-// Same result as mhc_split_bwd_kernel with two features per thread (the projection column W[:, f]
-// stays in 2P registers instead of 4P) and the next 8 tokens' loads issued before the current 8
-// are computed: about half the registers, so more warps per SM, and memory latency overlapped
-// with the FMAs inside each warp.  CTA: 32 tokens x 256 features, 128 threads.
-constexpr int kMhc2Feat = 256;
-template <int N>
-__global__ void __launch_bounds__(128) mhc_split_bwd2_kernel(__nv_bfloat16* __restrict__ dX,
-                                                             const __nv_bfloat16* __restrict__ X,
-                                                             const __nv_bfloat16* __restrict__ din,
-                                                             const float* __restrict__ a,
-                                                             const float* __restrict__ dp,
-                                                             const float* __restrict__ p,
-                                                             const float* __restrict__ r,
-                                                             const float* __restrict__ W, int T, int D) {
-  constexpr int P = 2 * N + N * N;
-  constexpr int S = 8;  // tokens per batch
-  const int F = N * D;
-  __shared__ __align__(16) float sdp[kMhcTok][P];
-  __shared__ float scoef[kMhcTok][2];
-  __shared__ float sa[kMhcTok][N];
-  const int t0 = blockIdx.x * kMhcTok;
-  for (int i = threadIdx.x; i < kMhcTok * P; i += blockDim.x) {
-    const int tt = i / P, j = i % P;
-    sdp[tt][j] = (t0 + tt < T) ? dp[static_cast<int64_t>(t0 + tt) * P + j] : 0.f;
-  }
-  for (int i = threadIdx.x; i < kMhcTok * N; i += blockDim.x) {
-    const int tt = i / N;
-    sa[tt][i % N] = (t0 + tt < T) ? a[static_cast<int64_t>(t0 + tt) * N + i % N] : 0.f;
-  }
-  __syncthreads();
-  for (int tt0 = threadIdx.x; tt0 < kMhcTok; tt0 += blockDim.x) {
-    const int t = t0 + tt0;
-    float rr = 0.f, sum = 0.f;
-    if (t < T) {
-      rr = r[t];
-      for (int j = 0; j < P; ++j) sum += sdp[tt0][j] * p[static_cast<int64_t>(t) * P + j] / rr;
-    }
-    scoef[tt0][0] = rr;
-    scoef[tt0][1] = rr * rr * rr / F * sum;
-  }
-  __syncthreads();
-  const int f0 = (blockIdx.y * blockDim.x + threadIdx.x) * 2;
-  if (f0 >= F) return;
-  float wv[P][2];
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    const float2 w2 = *reinterpret_cast<const float2*>(W + static_cast<int64_t>(j) * F + f0);
-    wv[j][0] = w2.x;
-    wv[j][1] = w2.y;
-  }
-  const int h = f0 / D, d = f0 % D;
-  const int n_tok = min(kMhcTok, T - t0);
-  // two register buffers (compile-time indexed: the four 8-token batches are unrolled)
-  uint32_t xa[S], ga[S], xb[S], gb[S];
-  auto issue = [&](uint32_t (&xr)[S], uint32_t (&gr)[S], int tt) {
-    if (tt >= n_tok) return;
-#pragma unroll
-    for (int u = 0; u < S; ++u) {
-      const int t = t0 + min(tt + u, n_tok - 1);
-      xr[u] = __ldcs(reinterpret_cast<const unsigned int*>(X + static_cast<int64_t>(t) * F + f0));
-      gr[u] = *reinterpret_cast<const uint32_t*>(din + static_cast<int64_t>(t) * D + d);
-    }
-  };
-  auto compute = [&](const uint32_t (&xr)[S], const uint32_t (&gr)[S], int tt) {
-#pragma unroll
-    for (int u = 0; u < S; ++u) {
-      if (tt + u >= n_tok) break;
-      const int ti = tt + u;
-      const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xr[u]));
-      const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr[u]));
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        const float q = sdp[ti][j];
-        s0 += q * wv[j][0];
-        s1 += q * wv[j][1];
-      }
-      const float ah = sa[ti][h], rr = scoef[ti][0], cc = scoef[ti][1];
-      const __nv_bfloat162 o = __floats2bfloat162_rn(ah * g.x + rr * s0 - cc * x.x, ah * g.y + rr * s1 - cc * x.y);
-      __stcs(reinterpret_cast<unsigned int*>(dX + static_cast<int64_t>(t0 + ti) * F + f0),
-             *reinterpret_cast<const unsigned int*>(&o));
-    }
-  };
-  static_assert(kMhcTok == 4 * S, "four token batches per CTA");
-  issue(xa, ga, 0);
-  issue(xb, gb, S);
-  compute(xa, ga, 0);
-  issue(xa, ga, 2 * S);
-  compute(xb, gb, S);
-  issue(xb, gb, 3 * S);
-  compute(xa, ga, 2 * S);
-  compute(xb, gb, 3 * S);
-}
-
 template <int N>
 __global__ void mhc_split_bwd_kernel(__nv_bfloat16* __restrict__ dX, const __nv_bfloat16* __restrict__ X,
                                      const __nv_bfloat16* __restrict__ din, const float* __restrict__ a,
@@ -928,22 +834,6 @@ void mhc_premix_da(torch::Tensor X, torch::Tensor din, torch::Tensor da, int64_t
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   SV4_MHC_N(n, T, mhc_premix_da_kernel, reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()),
             reinterpret_cast<const __nv_bfloat16*>(din.data_ptr()), da.data_ptr<float>(), D);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-// variant 2: mhc_split_bwd2_kernel (2 features per thread, prefetched token batches)
-void mhc_split_bwd2(torch::Tensor dX, torch::Tensor X, torch::Tensor din, torch::Tensor a, torch::Tensor dp,
-                    torch::Tensor p, torch::Tensor r, torch::Tensor W, int64_t n) {
-  c10::cuda::CUDAGuard guard(X.device());
-  const int T = din.size(0), D = din.size(1);
-  TORCH_CHECK(D % 2 == 0, "mhc_split_bwd2: D % 2 == 0");
-  if (T == 0) return;
-  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const dim3 grid((T + kMhcTok - 1) / kMhcTok, (static_cast<int>(n) * D + kMhc2Feat - 1) / kMhc2Feat);
-  SV4_MHC_N(n, grid, mhc_split_bwd2_kernel, reinterpret_cast<__nv_bfloat16*>(dX.data_ptr()),
-            reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()),
-            reinterpret_cast<const __nv_bfloat16*>(din.data_ptr()), a.data_ptr<float>(), dp.data_ptr<float>(),
-            p.data_ptr<float>(), r.data_ptr<float>(), W.data_ptr<float>(), T, D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

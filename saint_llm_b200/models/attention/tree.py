@@ -38,6 +38,14 @@ def attention_partial(q: Tensor, k: Tensor, v: Tensor, mask: Tensor | None = Non
 
 
 def merge_partials(parts: list[tuple[Tensor, Tensor, Tensor]]) -> tuple[Tensor, Tensor, Tensor]:
+    """Merge partials ``(m, l, o)``; on CUDA one ``lse_merge`` kernel (``ops.decode``)."""
+    from saint_llm_b200.ops import backend
+
+    if parts and backend.native_for(parts[0][2]):
+        from saint_llm_b200.ops.decode import lse_merge
+
+        return lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
+                         torch.stack([p[2] for p in parts]))
     m = torch.stack([p[0] for p in parts]).amax(0)
     m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
     l = torch.zeros_like(m)  # noqa: E741

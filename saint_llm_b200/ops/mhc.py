@@ -90,7 +90,7 @@ class _SplitFn(torch.autograd.Function):
         dzs = dz.sum(0)
         d_s_pre, d_s_res, d_s_post = dzs[:n], dzs[n:n + n * n].view(n, n), dzs[n + n * n:]
         dXf = torch.empty_like(Xf)
-        ext.mhc_split_bwd2(dXf, Xf, din, a, dp.contiguous(), p, r, wf, n)
+        ext.mhc_split_bwd(dXf, Xf, din, a, dp.contiguous(), p, r, wf, n)
         dq = (dp * r[:, None]).to(torch.bfloat16)
         dW = gemm.gemm_nt(dq.t(), Xf.t(), out_dtype=torch.float32)
         return dXf.view(b_, t_, n, d), dW, d_alpha, d_s_pre, d_s_res, d_s_post, None, None, None

@@ -67,9 +67,6 @@ class TrainStep:
         longer reuse it between steps), so the capture is skipped when the warm-up's
         activation peak would not fit again next to what is allocated now plus a margin
         for the optimizer's temporaries."""
-        init_state = getattr(self.optimizer, "init_state", None)
-        if init_state is not None:
-            init_state()  # the optimizer's buffers exist before the free memory is measured
         self._tok = torch.zeros_like(tok)
         self._total = torch.zeros((), dtype=torch.float32, device=self.device)
         self._tok.copy_(tok)
@@ -85,6 +82,11 @@ class TrainStep:
         zero_main_grads(self.params)  # the warm-up gradients are not part of any step
         torch.cuda.synchronize(self.device)
         act_peak = torch.cuda.max_memory_allocated(self.device) - base
+        init_state = getattr(self.optimizer, "init_state", None)
+        if init_state is not None:
+            # the optimizer's buffers exist before the free memory is measured (created after
+            # the warm-up, so they do not add to its peak)
+            init_state()
         torch.cuda.empty_cache()
         free, _ = torch.cuda.mem_get_info(self.device)
         margin = 8 << 30

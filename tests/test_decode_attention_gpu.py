@@ -147,3 +147,66 @@ def test_paged_decode_compressed_matches_contiguous_kernel(cuda, mode):
     torch.cuda.synchronize()
     check_errors(cuda)
     torch.testing.assert_close(got.float(), want.reshape(B, H, 128).float(), rtol=2e-2, atol=2e-2)
+
+
+def test_lse_merge_matches_eager_merge(cuda):
+    """The one-kernel merge of attention partials against the eager associative merge (tree
+    attention's), with empty partials and an extra sink logit."""
+    from saint_llm_b200.models.attention.tree import attention_partial, merge_partials
+    from saint_llm_b200.ops import backend
+    from saint_llm_b200.ops.decode import lse_merge
+
+    torch.manual_seed(0)
+    q = torch.randn(2, 4, 5, 64, device=cuda)
+    k = torch.randn(2, 4, 90, 64, device=cuda)
+    v = torch.randn(2, 4, 90, 64, device=cuda)
+    mask = torch.ones(5, 90, dtype=torch.bool, device=cuda)
+    mask[:, 30:60] = False  # the middle chunk is empty for every row
+    parts = [attention_partial(q, k[..., s:s + 30, :], v[..., s:s + 30, :], mask[:, s:s + 30]) for s in (0, 30, 60)]
+    with backend.eager_mode():
+        m0, l0, o0 = merge_partials(parts)
+    m1, l1, o1 = lse_merge(torch.stack([p[0] for p in parts]), torch.stack([p[1] for p in parts]),
+                           torch.stack([p[2] for p in parts]))
+    torch.testing.assert_close(o1, o0, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(l1, l0, rtol=1e-4, atol=1e-4)
+    full = torch.softmax((q @ k.transpose(-1, -2) / 8).masked_fill(~mask, float("-inf")), -1) @ v
+    torch.testing.assert_close(o1, full, rtol=1e-3, atol=1e-3)
+    # a sink joins the denominator only
+    sink = torch.randn(4, device=cuda)
+    _, _, o2 = lse_merge(torch.stack([p[0] for p in parts]).reshape(3, -1), torch.stack([p[1] for p in parts]).reshape(3, -1),
+                         torch.stack([p[2] for p in parts]).reshape(3, -1, 64),
+                         extra=sink.repeat_interleave(5).contiguous())
+    s = (q @ k.transpose(-1, -2) / 8).masked_fill(~mask, float("-inf"))
+    s = torch.cat([s, sink.view(1, 4, 1, 1).expand(2, 4, 5, 1)], -1)
+    want = torch.softmax(s, -1)[..., :90] @ v
+    torch.testing.assert_close(o2.view(2, 4, 5, 64), want, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("mode,window", [(0, 0), (0, 64), (1, 128), (2, 128)])
+def test_paged_decode_split_matches_single_pass(cuda, mode, window):
+    from saint_llm_b200.ops.decode import decode_attention_paged
+    from saint_llm_b200.ops.gemm import check_errors
+
+    gen = torch.Generator().manual_seed(10 + mode)
+    lens = [700, 1, 513, 64]
+    H, P, m = 8, 32, 4
+    ks = [torch.randn(n, 128, generator=gen).to(torch.bfloat16) for n in lens]
+    vs = [torch.randn(n, 128, generator=gen).to(torch.bfloat16) for n in lens]
+    kp, kt, kl = _pages(ks, P, 128, torch.Generator().manual_seed(3), cuda)
+    vp, _, _ = _pages(vs, P, 128, torch.Generator().manual_seed(3), cuda)
+    q = torch.randn(len(lens), H, 128, generator=gen).to(cuda, torch.bfloat16)
+    kw = {"window": window, "sink": torch.randn(H, generator=gen).to(cuda), "softcap": 30.0}
+    if mode:
+        ne = [max(1, n // m) for n in lens]
+        ents = [torch.randn(x, 128, generator=gen).to(torch.bfloat16) for x in ne]
+        ep, et, el = _pages(ents, P, 64, torch.Generator().manual_seed(4), cuda)
+        kw.update(mode=mode, e_pool=ep, e_table=et, e_len=el, norm_weight=torch.ones(128, device=cuda), m=m)
+        if mode == 1:
+            kw["comp_sink"] = torch.randn(H, generator=gen).to(cuda)
+        else:
+            kw["top"] = torch.randint(-1, min(ne), (len(lens), 16), generator=gen).to(cuda)
+    one = decode_attention_paged(q, kp, vp, kt, kl, **kw)
+    four = decode_attention_paged(q, kp, vp, kt, kl, splits=4, **kw)
+    torch.cuda.synchronize()
+    check_errors(cuda)
+    torch.testing.assert_close(four.float(), one.float(), rtol=2e-2, atol=2e-2)

@@ -339,25 +339,3 @@ def test_shared_expert_group_matches_separate(cuda):
     for got, want in zip([h.grad] + [p.grad for e in ex for p in e.parameters()], ref, strict=True):
         assert _rel(got, want) < 2e-2
 
-
-@pytest.mark.parametrize("n,T,d", [(4, 8192, 2048), (4, 77, 256), (2, 100, 512), (3, 40, 128)])
-def test_mhc_split_bwd_variants_agree(cuda, n, T, d):
-    """The two-feature prefetching backward kernel against the four-feature one (same sums in
-    the same order) on random inputs, ragged token counts included."""
-    from saint_llm_b200.ops import backend
-
-    torch.manual_seed(n * T)
-    F, P = n * d, 2 * n + n * n
-    X = torch.randn(T, F, device=cuda).to(torch.bfloat16)
-    din = torch.randn(T, d, device=cuda).to(torch.bfloat16)
-    a = torch.rand(T, n, device=cuda)
-    dp = torch.randn(T, P, device=cuda)
-    p = torch.randn(T, P, device=cuda)
-    r = torch.rand(T, device=cuda) + 0.5
-    W = torch.randn(P, F, device=cuda) * 0.02
-    out1, out2 = torch.empty_like(X), torch.empty_like(X)
-    backend.ext().mhc_split_bwd(out1, X, din, a, dp, p, r, W, n)
-    backend.ext().mhc_split_bwd2(out2, X, din, a, dp, p, r, W, n)
-    torch.cuda.synchronize()
-    diff = (out1.float() - out2.float()).abs().max().item()
-    assert diff <= 1e-2 * out1.float().abs().max().item(), diff

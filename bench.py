@@ -5,7 +5,8 @@
 One process per GPU (``torchrun`` for N > 1, expert parallel EP = N, data parallel for
 the replicated weights).  Per GPU a step is one optimizer step over ``seqs_per_gpu`` x
 4096 uniform-random tokens (weak scaling: 32 sequences per GPU, i.e. global batch
-256 x 4096 at N = 8).  The W warm-up steps are untimed; exactly K steps are timed with
+256 x 4096 at N = 8), in micro-batches of 2 sequences on one GPU and 4 with N > 1.  The W
+warm-up steps are untimed; exactly K steps are timed with
 CUDA events between a barrier + synchronize on both sides; the per-rank time is
 max-reduced over ranks.  Every step copies its token batch from pinned host memory
 inside the timed region.  The model weights (tens of GB) stream through HBM every step,

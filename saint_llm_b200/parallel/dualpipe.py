@@ -1,7 +1,7 @@
 """DualPipe-V: a V-shaped pipeline schedule (absent in the reference, which lists
 DualPipe / DualPipeV as planned in ``distributed/__init__.py:9-13``).  Pipeline traffic is
-NCCL (or gloo) point-to-point; the exchange of a tick runs between ticks, not yet
-overlapped with the next tick's compute.
+NCCL (or gloo) point-to-point, posted at the end of each tick and waited for only by the
+op that consumes the tensor, so a tick's exchange overlaps the following ticks' compute.
 
 Placement.  The block stack is cut into ``2P`` virtual stages for ``P`` ranks; rank ``r``
 holds virtual stage ``r`` (chunk 0) and virtual stage ``2P-1-r`` (chunk 1).  A micro-batch
@@ -20,9 +20,13 @@ Ready backwards go first (oldest micro-batch first), then forwards, preferring c
 finished activations leave the pipeline early; a new micro-batch enters rank ``r`` only
 while fewer than ``2P - r`` micro-batches are between its chunk-0 forward and backward,
 which bounds the activations alive on a rank.  After each tick the activations and input
-gradients that cross ranks are exchanged in one grouped ``batch_isend_irecv``: every rank
-posts its sends and receives of that tick in one canonical order, so matching pairs always
-meet and no ordering of point-to-point calls can deadlock.
+gradients that cross ranks are posted in one grouped ``batch_isend_irecv``: every rank posts
+its sends and receives of that tick in one canonical order, so matching pairs always meet.
+Nothing waits at the end of the tick: a receive is waited for by the op that consumes it
+(always in a later tick), and the sends are waited for after the last tick (their tensors
+are kept alive until then).  No deadlock: posting never blocks, and an op at tick t waits only
+for a message its peer posted at the end of a tick before t, which the peer reaches after
+waits of the same kind for even earlier ticks.
 
 Gradients accumulate in the parameters as with ``run_1f1b`` (each micro-batch's loss is
 divided by ``M``); the result equals the non-pipelined step.
@@ -155,6 +159,15 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
     dev = micro_ids[0].device
     ticks = build_schedule(P, M)
     inbox: dict[tuple[str, int, int], Tensor] = {}   # (kind, virtual stage that consumes it, i)
+    arriving: dict[tuple[str, int, int], object] = {}  # pending receive of an inbox entry
+    in_flight: list[tuple[object, Tensor]] = []        # posted sends and the tensors they read
+
+    def take(key: tuple[str, int, int]) -> Tensor:
+        w = arriving.pop(key, None)
+        if w is not None:
+            w.wait()  # type: ignore[attr-defined]
+        return inbox.pop(key)
+
     saved: dict[tuple[int, int], tuple[Tensor | None, Tensor | tuple[Tensor, Tensor]]] = {}
     losses: list[Tensor] = []
     dist.barrier(group=pipe.group)  # every rank's communicator exists before the first grouped p2p
@@ -170,7 +183,7 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
             ids = micro_ids[op.i]
             x_in = None
             if op.v > 0:
-                x_in = inbox.pop(("act", op.v, op.i)).detach().requires_grad_(True)
+                x_in = take(("act", op.v, op.i)).detach().requires_grad_(True)
             out = pipe._forward(op.v, ids, x_in)
             aux = aux_losses(m, *pipe.bounds[op.v])
             if op.v == S - 1:
@@ -187,7 +200,7 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
         elif op is not None:
             x_in, out = saved.pop((op.v, op.i))
             y, aux = out if isinstance(out, tuple) else (out, None)
-            outs, grads = [y], [None if op.v == S - 1 else inbox.pop(("grad", op.v, op.i))]
+            outs, grads = [y], [None if op.v == S - 1 else take(("grad", op.v, op.i))]
             if aux is not None:
                 outs.append(aux)
                 grads.append(None)
@@ -198,11 +211,12 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
                     inbox[("grad", op.v - 1, op.i)] = x_in.grad
                 else:
                     produced[("grad", op.i)] = x_in.grad.contiguous()
-        # grouped exchange of this tick's cross-rank tensors
-        p2p = []
+        # grouped exchange of this tick's cross-rank tensors, posted now, waited for by consumers
+        p2p, keys = [], []
         for src, dst, kind, i in messages(row, P):
             if src == rank:
                 p2p.append(dist.P2POp(dist.isend, produced[(kind, i)], pipe._peer(dst), pipe.group))
+                keys.append(("send", produced[(kind, i)]))
             elif dst == rank:
                 buf = torch.empty(shape(i), dtype=dtype, device=dev)
                 # the consumer: the next virtual stage of a forward, the previous of a backward
@@ -211,9 +225,17 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
                 v_dst = src_op.v + 1 if kind == "act" else src_op.v - 1
                 inbox[(kind, v_dst, i)] = buf
                 p2p.append(dist.P2POp(dist.irecv, buf, pipe._peer(src), pipe.group))
+                keys.append(("recv", (kind, v_dst, i)))
         if p2p:
-            for req in dist.batch_isend_irecv(p2p):
-                req.wait()
+            for req, (what, ref) in zip(dist.batch_isend_irecv(p2p), keys, strict=True):
+                if what == "recv":
+                    arriving[ref] = req  # type: ignore[index]
+                else:
+                    in_flight.append((req, ref))  # type: ignore[arg-type]
+    for req, _ in in_flight:
+        req.wait()  # type: ignore[attr-defined]
+    for req in arriving.values():  # every receive has a consumer, so none is left; kept for safety
+        req.wait()  # type: ignore[attr-defined]
     return torch.stack(losses).mean() if losses else None
 
 

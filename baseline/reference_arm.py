@@ -201,7 +201,19 @@ def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make
     need = n_params * 12 / world
     fits = need <= 0.9 * have
     cuts = [full_layers]
-    if not fits:
+    if world > 1:
+        # FSDP2 shards the fp32 state, but the reference's per-layer working set stays ~135 GB
+        # per GPU (measured on one GPU: 167 GB peak at a 4-layer cut holding ~33 GB of state),
+        # so the state may take what is left; every rank picks the same cut (no OOM retries:
+        # ranks would have to agree on them)
+        per_layer = (n_params - _param_count(SaintLLM, _reference_config(ModelConfig, args, 1))) / max(
+            full_layers - 1, 1)
+        base = n_params - per_layer * full_layers
+        budget_params = max(0.0, (have - 150e9)) * world / 12
+        run = int(max(1, min(full_layers, (budget_params - base) // per_layer)))
+        fits = run == full_layers
+        cuts = [run]
+    elif not fits:
         # layer cuts whose fp32 state takes at most a third of the memory (the reference's
         # activations and optimizer temporaries take the rest: 133 GB at 2 layers and 2 x 4096
         # tokens); on an out-of-memory error the next smaller cut is tried.  The measured
@@ -216,7 +228,7 @@ def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make
         try:
             return _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn, rank, world, dev,
                             t_arm, budget, run_layers, full_layers, fits, n_params, need, have)
-        except torch.OutOfMemoryError as e:  # only the layer-cut probe retries
+        except torch.OutOfMemoryError as e:  # only the one-GPU layer-cut probe retries
             if fits or world > 1:
                 raise
             last_err = str(e).splitlines()[0][:120]  # keep no traceback: it would pin the model
@@ -235,9 +247,11 @@ def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_
     with torch.device(dev):
         model = SaintLLM(cfg)
     if world > 1:
-        from saint_llm_distributed.fsdp import fsdp2_wrap
+        from saint_llm_distributed.fsdp import fsdp2_wrap, init_default_mesh
 
-        model = fsdp2_wrap(model)
+        # the reference's production setting: a CUDA device mesh over the NCCL group (its
+        # default mesh is "cpu", for its gloo tests)
+        model = fsdp2_wrap(model, mesh=init_default_mesh(device="cuda"))
     muon_params, adamw_params = split_for_muon_adamw(model)
     muon = Muon(muon_params, lr=2.7e-4)
     adamw = torch.optim.AdamW(adamw_params, lr=2.7e-4, betas=(0.9, 0.95), eps=1e-20, weight_decay=0.1)
@@ -293,10 +307,11 @@ def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_
         "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "elapsed_s": round(elapsed, 1),
     }
     if not fits:
-        return _unavailable(
-            f"reference keeps fp32 weights, grads and Muon momentum: {n_params / 1e9:.1f}B params x 12 B / "
-            f"{world} GPU(s) = {need / 1e9:.0f} GB > {have / 1e9:.0f} GB per GPU; micro-batches timed on a "
-            f"{run_layers}-layer cut", measured) if rank == 0 else {}
+        why = (f"reference keeps fp32 weights, grads and Muon momentum: {n_params / 1e9:.1f}B params x 12 B / "
+               f"{world} GPU(s) = {need / 1e9:.0f} GB > {have / 1e9:.0f} GB per GPU" if world == 1 else
+               f"reference under FSDP2: {need / 1e9:.0f} GB of fp32 state per GPU plus its ~135 GB per-GPU "
+               f"working set exceed {have / 1e9:.0f} GB")
+        return _unavailable(f"{why}; micro-batches timed on a {run_layers}-layer cut", measured) if rank == 0 else {}
     remaining = (args.warmup + args.steps) * est_step_ms / 1000.0
     if elapsed + remaining > budget:
         return _unavailable(

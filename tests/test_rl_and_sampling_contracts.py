@@ -177,3 +177,66 @@ def test_paged_manager_tables_gather_and_release():
     assert pools["k"].free_pages == used + 2
     with pytest.raises(PoolExhausted):
         PagePool(1, 2, 3).alloc_many(2)
+
+
+# ---------------------------------------------------------- surrogate loss
+def _batch(B=4, T=6, seed=0):
+    from saint_llm_b200.posttrain.grpo import RolloutBatch
+
+    g = torch.Generator().manual_seed(seed)
+    mask = torch.zeros(B, T, dtype=torch.bool)
+    mask[:, 2:] = True
+    old = -torch.rand(B, T, generator=g)
+    return RolloutBatch(torch.zeros(B, T, dtype=torch.long), mask, old, old.clone(), torch.tensor([1.0, 0.0, 0.5, 0.5]))
+
+
+def test_surrogate_on_policy_equals_minus_mean_advantage():
+    from saint_llm_b200.posttrain.grpo import GRPOConfig, policy_surrogate_loss
+
+    b = _batch()
+    adv = torch.tensor([1.0, -1.0, 0.5, 0.0])
+    loss, met = policy_surrogate_loss(b.old_logprobs.clone(), b, adv, GRPOConfig(kl_coef=0.0))
+    torch.testing.assert_close(loss, -adv.mean())  # ratio 1 everywhere, KL 0
+    assert met["clip_frac"].item() == 0.0 and abs(met["ratio_mean"].item() - 1.0) < 1e-6
+
+
+def test_surrogate_clipping_stops_the_gradient():
+    from saint_llm_b200.posttrain.grpo import GRPOConfig, policy_surrogate_loss
+
+    b = _batch()
+    adv = torch.tensor([1.0, 1.0, -1.0, -1.0])
+    new = (b.old_logprobs + torch.tensor([0.5, 0.0, -0.5, 0.0]).view(4, 1)).requires_grad_(True)
+    loss, met = policy_surrogate_loss(new, b, adv, GRPOConfig(kl_coef=0.0))
+    loss.backward()
+    g = new.grad
+    # row 0: ratio e^0.5 > 1.2 with a positive advantage -> clipped, no gradient;
+    # row 2: ratio e^-0.5 < 0.8 with a negative advantage -> clipped, no gradient
+    assert g[0, 2:].abs().max() == 0 and g[2, 2:].abs().max() == 0
+    assert g[1, 2:].abs().min() > 0 and g[3, 2:].abs().min() > 0
+    assert g[:, :2].abs().max() == 0  # prompt tokens never get a gradient
+    assert abs(met["clip_frac"].item() - 0.5) < 1e-6
+
+
+def test_surrogate_kl_is_nonnegative_and_zero_at_reference():
+    from saint_llm_b200.posttrain.grpo import GRPOConfig, policy_surrogate_loss
+
+    b = _batch()
+    zero = torch.zeros(4)
+    _, met0 = policy_surrogate_loss(b.ref_logprobs.clone(), b, zero, GRPOConfig())
+    assert abs(met0["kl_penalty"].item()) < 1e-7
+    _, met1 = policy_surrogate_loss(b.ref_logprobs + 0.3, b, zero, GRPOConfig())
+    assert met1["kl_penalty"].item() > 0
+
+
+def test_clip_higher_bounds_and_sequence_ratio():
+    from saint_llm_b200.posttrain.grpo import GRPOConfig, policy_surrogate_loss
+
+    assert GRPOConfig().clip_bounds == (0.8, 1.2)
+    assert GRPOConfig(use_clip_higher=True).clip_bounds == (0.8, 1.28)
+    b = _batch()
+    new = b.old_logprobs + 0.1
+    loss_tok, _ = policy_surrogate_loss(new, b, torch.ones(4), GRPOConfig(kl_coef=0.0))
+    loss_seq, _ = policy_surrogate_loss(new, b, torch.ones(4), GRPOConfig(kl_coef=0.0,
+                                                                           importance_ratio_level="sequence"))
+    # a uniform shift of 0.1 gives the same ratio per token and per sequence
+    torch.testing.assert_close(loss_tok, loss_seq)

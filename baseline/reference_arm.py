@@ -182,6 +182,9 @@ def _run(args) -> dict:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # no NVLink multicast objects: a rank stopped by the driver's time limit must not leave
+        # peers' memory bound to one
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
     try:
         return _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn, rank, world,
@@ -239,6 +242,38 @@ def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make
     raise RuntimeError(f"every layer cut ran out of memory ({last_err})")
 
 
+def _probe_fsdp(args, micro, toks, n_micro, rank, world, dev, t_arm, run_layers, full_layers, n_params, need,
+                have) -> dict:
+    """N > 1: time one micro-batch under FSDP2 and report it with a lower bound of the step.  The
+    optimizer step is not run: the reference's Muon orthogonalises FSDP2 DTensor shards with
+    per-operation collectives, and a probe that included one such step did not finish within
+    600 s on 2 x B200 (the driver would kill the arm before it printed anything)."""
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    micro(toks, min(1, n_micro - 1))
+    ev[1].record()
+    torch.cuda.synchronize()
+    mb_ms = _max_over_ranks(ev[0].elapsed_time(ev[1]), dev, world)
+    elapsed = _max_over_ranks(time.perf_counter() - t_arm, dev, world)
+    scale = full_layers / run_layers
+    low_ms = n_micro * mb_ms * scale
+    tokens = world * args.seqs_per_gpu * args.seq_len
+    measured = {
+        "layers_run": run_layers, "layers_config": full_layers, "micro_batch_tokens": args.micro_batch * args.seq_len,
+        "micro_batch_ms": round(mb_ms, 1), "micro_batches_per_step": n_micro,
+        "step_ms_lower_bound": round(low_ms, 1),
+        "tokens_per_s_upper_bound": round(tokens / (low_ms / 1000.0), 1),
+        "extrapolation": "micro-batches only (no optimizer step), linear in layers" if scale != 1 else
+                         "micro-batches only (no optimizer step)",
+        "n_gpus": world, "parallelism": f"fsdp2 dp{world}",
+        "peak_mem_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "elapsed_s": round(elapsed, 1),
+    }
+    return _unavailable(
+        f"reference under FSDP2 ({need / 1e9:.0f} GB fp32 state per GPU, {run_layers} of {full_layers} layers "
+        f"timed): its Muon step over DTensor shards did not finish within the 600 s arm budget on 2 GPUs, so "
+        f"only the micro-batch is timed", measured) if rank == 0 else {}
+
+
 def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn,  # noqa: N803
              rank, world, dev, t_arm, budget, run_layers, full_layers, fits, n_params, need, have) -> dict:
     cfg = _reference_config(ModelConfig, args, run_layers)
@@ -284,6 +319,9 @@ def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_
     toks = host.to(dev, non_blocking=True)
     micro(toks, 0)
     torch.cuda.synchronize()
+    if world > 1:
+        return _probe_fsdp(args, micro, toks, n_micro, rank, world, dev, t_arm, run_layers, full_layers, n_params,
+                           need, have)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     ev[0].record()
     micro(toks, min(1, n_micro - 1))

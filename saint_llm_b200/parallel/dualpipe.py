@@ -159,13 +159,12 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
     dev = micro_ids[0].device
     ticks = build_schedule(P, M)
     inbox: dict[tuple[str, int, int], Tensor] = {}   # (kind, virtual stage that consumes it, i)
-    arriving: dict[tuple[str, int, int], object] = {}  # pending receive of an inbox entry
-    in_flight: list[tuple[object, Tensor]] = []        # posted sends and the tensors they read
+    arriving: dict[tuple[str, int, int], list] = {}  # pending receive(s) of an inbox entry
+    in_flight: list[tuple[list, Tensor]] = []         # posted sends and the tensors they read
 
     def take(key: tuple[str, int, int]) -> Tensor:
-        w = arriving.pop(key, None)
-        if w is not None:
-            w.wait()  # type: ignore[attr-defined]
+        for w in arriving.pop(key, []):
+            w.wait()
         return inbox.pop(key)
 
     saved: dict[tuple[int, int], tuple[Tensor | None, Tensor | tuple[Tensor, Tensor]]] = {}
@@ -227,15 +226,22 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
                 p2p.append(dist.P2POp(dist.irecv, buf, pipe._peer(src), pipe.group))
                 keys.append(("recv", (kind, v_dst, i)))
         if p2p:
-            for req, (what, ref) in zip(dist.batch_isend_irecv(p2p), keys, strict=True):
+            reqs = dist.batch_isend_irecv(p2p)
+            # gloo returns one work per op; NCCL coalesces the group into fewer works, each of
+            # which then stands for every op of the tick
+            per_op = len(reqs) == len(p2p)
+            for j, (what, ref) in enumerate(keys):
+                ws = [reqs[j]] if per_op else list(reqs)
                 if what == "recv":
-                    arriving[ref] = req  # type: ignore[index]
+                    arriving[ref] = ws  # type: ignore[index]
                 else:
-                    in_flight.append((req, ref))  # type: ignore[arg-type]
-    for req, _ in in_flight:
-        req.wait()  # type: ignore[attr-defined]
-    for req in arriving.values():  # every receive has a consumer, so none is left; kept for safety
-        req.wait()  # type: ignore[attr-defined]
+                    in_flight.append((ws, ref))  # type: ignore[arg-type]
+    for ws, _ in in_flight:
+        for w in ws:
+            w.wait()
+    for ws in arriving.values():  # every receive has a consumer, so none is left; kept for safety
+        for w in ws:
+            w.wait()
     return torch.stack(losses).mean() if losses else None
 
 

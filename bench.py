@@ -395,8 +395,8 @@ def main() -> None:
                     help="FP8: keep the routed experts' FP8 weight copies between steps (auto: when sharded by EP)")
     ap.add_argument("--no-cuda-graph", action="store_true",
                     help="N = 1: launch every kernel eagerly instead of replaying the captured micro-batch graph")
-    ap.add_argument("--zero-transport", default="nccl", choices=["nccl", "p2p"],
-                    help="N > 1 with hybrid ZeRO: NCCL reduce/broadcast or the peer-memory pull kernels")
+    ap.add_argument("--zero-transport", default="p2p", choices=["nccl", "p2p"],
+                    help="N > 1 with hybrid ZeRO: the peer-memory pull kernels (default) or NCCL reduce/broadcast")
     ap.add_argument("--no-overlap-reduce", action="store_true",
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
     ap.add_argument("--seq-len", type=int, default=4096)

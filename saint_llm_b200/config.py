@@ -316,9 +316,9 @@ class RunConfig(_Frozen):
     kernels: Literal["native", "torch"] = "native"
     fused_ep: bool = True
     fused_zero: bool = True
-    # hybrid ZeRO transport: "nccl" (reduce / broadcast) or "p2p" (owners pull gradients and
-    # parameters over NVLink peer memory, parallel.zero_p2p)
-    zero_transport: Literal["nccl", "p2p"] = "nccl"
+    # hybrid ZeRO transport: "nccl" (reduce / broadcast), "p2p" (owners pull gradients and
+    # parameters over NVLink peer memory, parallel.zero_p2p) or "auto" (p2p on CUDA)
+    zero_transport: Literal["auto", "nccl", "p2p"] = "auto"
     # single GPU: replay each micro-batch's forward + backward from one captured CUDA graph
     cuda_graphs: bool = True
     # FP8 training (linear_quant="fp8"): keep the routed experts' FP8 weight copies between

@@ -262,6 +262,8 @@ class ParallelSync:
             kinds = {id(p): "muon" for p in muon} | {id(p): "adamw" for p in adamw}
             rep = [p for p in model.parameters() if id(p) not in self.expert_ids and p.requires_grad]
             rep_kinds = [kinds.get(id(p), "adamw") for p in rep]
+            if zero_transport == "auto":
+                zero_transport = "p2p" if rep and rep[0].is_cuda else "nccl"
             if zero_transport == "p2p":
                 from saint_llm_b200.parallel.zero_p2p import PeerZeroSync
 
@@ -332,8 +334,8 @@ def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
     ``sync.configure_optimizer(opt)`` once and ``sync.post_step()`` after every step.
     ``overlap_reduce`` (with ``zero``): issue each block's owner reductions from its
     backward hook during the last micro-batch.  ``zero_transport`` (with ``zero``): "nccl"
-    reduce / broadcast, or "p2p" (``parallel.zero_p2p``: owners pull over NVLink peer
-    memory).  ``timeout_s``: bound of every cross-GPU flag wait of the peer-memory kernels."""
+    reduce / broadcast, "p2p" (``parallel.zero_p2p``: owners pull over NVLink peer memory),
+    or "auto" (p2p for CUDA parameters).  ``timeout_s``: bound of every cross-GPU flag wait of the peer-memory kernels."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
     sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero,

@@ -16,8 +16,8 @@ What each ``RunConfig`` field selects here:
   are issued from a backward hook during the step's last micro-batch, so they run on
   NCCL's stream while the backward of the earlier blocks continues (True), or all after
   the backward (False).
-* ``zero_transport``: with hybrid ZeRO, NCCL ``reduce`` / ``broadcast`` ("nccl") or this
-  framework's peer-memory pull kernels ("p2p", ``parallel.zero_p2p``).
+* ``zero_transport``: with hybrid ZeRO, NCCL ``reduce`` / ``broadcast`` ("nccl"), this
+  framework's peer-memory pull kernels ("p2p", ``parallel.zero_p2p``), or "auto" (p2p on CUDA).
 * ``cuda_graphs``: on one GPU, each micro-batch's forward + backward replays one captured
   CUDA graph (``TrainStep(cuda_graph=True)``); ignored when gradients are synchronised
   across ranks (the expert-parallel step reads routing sizes on the host).

@@ -39,6 +39,11 @@ from saint_llm_b200.models.linear import LinearFactory, default_linear
 from saint_llm_b200.ops import backend
 
 
+def _key_offset(kv_cache: Any | None) -> int:
+    """Global position of the first window key a cache returns (0: it returns all of them)."""
+    return int(getattr(kv_cache, "key_offset", 0)) if kv_cache is not None else 0
+
+
 class TokenLevelCompressor(nn.Module):
     def __init__(self, hidden_dim: int, c: int, m: int, *,
                  linear_factory: LinearFactory = default_linear) -> None:
@@ -209,13 +214,15 @@ class _AttentionBase(nn.Module):
             k = self.k_norm(apply_partial_rope(k, cos, sin, rd))
         return k, self.v_proj(h)
 
-    def _sw_branch(self, q: Tensor, k: Tensor, v: Tensor, q_start: int) -> Tensor:
+    def _sw_branch(self, q: Tensor, k: Tensor, v: Tensor, q_start: int, k_start: int = 0) -> Tensor:
+        """Window branch for queries at global positions ``q_start..`` over keys at global
+        positions ``k_start..`` (a cache may hold only the keys a window can reach)."""
         cfg = self.attn_cfg
         b, n_heads, t, d = q.shape
-        # with a cache only the last `window` keys before the first query can be visible
-        lo = max(0, q_start - cfg.sliding_window_size + 1) if k.shape[1] > t else 0
+        # only the last `window` keys before the first query can be visible
+        lo = max(0, q_start - cfg.sliding_window_size + 1 - k_start)
         k, v = k[:, lo:], v[:, lo:]
-        mask = window_mask_at(q_start - lo, t, k.shape[1], cfg.sliding_window_size, q.device)
+        mask = window_mask_at(q_start - k_start - lo, t, k.shape[1], cfg.sliding_window_size, q.device)
         return scaled_dot_product(
             q, k.unsqueeze(1), v.unsqueeze(1), mask=mask, sink_logit=self.sink_logit,
             score_observer=self._observe, logit_softcap=cfg.logit_softcap,
@@ -281,7 +288,7 @@ class CSA(_AttentionBase):
             _, top_idx = self.indexer(h, is_visual=is_visual)
             compressed = self.kv_compressor(h)
             k, v = k_new, v_new
-        out = self.sparse_branch(q, compressed, top_idx) + self._sw_branch(q, k, v, off)
+        out = self.sparse_branch(q, compressed, top_idx) + self._sw_branch(q, k, v, off, _key_offset(kv_cache))
         return self.output(out)
 
     def topk_cached(self, h: Tensor, idx_keys: Tensor, q_start: int, m: int) -> Tensor:

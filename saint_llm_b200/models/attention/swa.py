@@ -19,7 +19,7 @@ from torch import Tensor
 
 from saint_llm_b200.config import AttentionConfig, HCAConfig
 from saint_llm_b200.models.attention.common import scaled_dot_product
-from saint_llm_b200.models.attention.csa import TokenLevelCompressor, _AttentionBase
+from saint_llm_b200.models.attention.csa import TokenLevelCompressor, _AttentionBase, _key_offset
 from saint_llm_b200.models.linear import LinearFactory, default_linear
 from saint_llm_b200.ops import backend
 
@@ -43,7 +43,7 @@ class SWAttention(_AttentionBase):
         k, v = self._sw_kv(h, cos, sin)
         if kv_cache is not None:
             k, v = kv_cache.append(k, v)
-        return self.output(self._sw_branch(q, k, v, off))
+        return self.output(self._sw_branch(q, k, v, off, _key_offset(kv_cache)))
 
 
 class HCA(_AttentionBase):
@@ -84,7 +84,7 @@ class HCA(_AttentionBase):
             compressed, k, v = kv_cache.append(h, k, v, compressor=self.kv_compressor)
         else:
             compressed = self.kv_compressor(h)
-        out = self.compressed_branch(q, compressed, off) + self._sw_branch(q, k, v, off)
+        out = self.compressed_branch(q, compressed, off) + self._sw_branch(q, k, v, off, _key_offset(kv_cache))
         return self.output(out)
 
 

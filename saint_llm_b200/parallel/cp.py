@@ -19,9 +19,11 @@ another.
 The attention modules are run unchanged through their KV-cache entry point: a
 ``CPLayerView`` presents "the context before this shard" exactly as a cache would
 (``length`` = the shard's start, so RoPE and every block-causal / window mask use
-global positions).  The window K/V are presented at full length with zeros before the
-halo (outside every query's window, so never attended); with the MQA layout (one K/V
-head) that costs two (B, T, head_dim) buffers per layer.
+global positions).  For SWA / CSA / HCA layers the window K/V are only the halo and the
+local rows, with ``key_offset`` = the global position of the first halo row (the window
+branch reads keys from there), so no rank holds K/V for the whole sequence.  NSA, whose
+compressed and selective branches index keys from position 0, gets the keys at full length
+with zeros before the halo (outside every query's window, so never attended).
 """
 
 from __future__ import annotations
@@ -61,12 +63,14 @@ class CPLayerView:
     all-gather gives each rank the previous rank's tail (the halo) and every rank's
     compressed entries in global block order."""
 
-    def __init__(self, group: dist.ProcessGroup | None, shard_len: int, window: int) -> None:
+    def __init__(self, group: dist.ProcessGroup | None, shard_len: int, window: int, *, compact: bool = True) -> None:
         self.group = group
         self.rank = dist.get_rank(group)
         self.ws = dist.get_world_size(group)
         self.length = self.rank * shard_len
         self.window = min(window, shard_len)
+        self.compact = compact
+        self.key_offset = 0
 
     def append(self, *args: Tensor, compressor=None, indexer_compressor=None):  # noqa: ANN001, ANN201
         if compressor is None:  # SWA / NSA: (k, v)
@@ -89,6 +93,11 @@ class CPLayerView:
         if self.rank == 0:  # no halo; the empty slice keeps the gather in the graph on every rank
             empty = outs[0][0][:, :0]
             k_all, v_all = torch.cat([empty[..., :d], k], 1), torch.cat([empty[..., d:], v], 1)
+        elif self.compact:  # halo + local rows; the window branch starts at key_offset
+            halo = outs[0][self.rank - 1]
+            self.key_offset = self.length - w
+            k_all = torch.cat([halo[..., :d], k], 1)
+            v_all = torch.cat([halo[..., d:], v], 1)
         else:
             halo = outs[0][self.rank - 1]
             z = k.new_zeros(b, self.length - w, d)
@@ -116,8 +125,9 @@ class CPBundle:
                 raise ValueError(f"shard length {shard_len} must be a multiple of every compression rate ({m})")
         if shard_len < cfg.attention.sliding_window_size:
             raise ValueError("shard length must be at least the sliding window")
-        self.views = [CPLayerView(group, shard_len, cfg.attention.sliding_window_size)
-                      for _ in model.blocks]  # type: ignore[attr-defined]
+        self.views = [CPLayerView(group, shard_len, cfg.attention.sliding_window_size,
+                                  compact=cfg.layer_kind(i) != "nsa")
+                      for i in range(len(model.blocks))]  # type: ignore[arg-type]
         self.length = self.views[0].length
 
     def for_layer(self, i: int) -> CPLayerView:

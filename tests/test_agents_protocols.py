@@ -276,3 +276,56 @@ def test_file_memory_persists_across_instances(tmp_path):
     again = FileMemoryStore(tmp_path / "m")
     assert again.view("k").value == "v1"
     assert [e.key for e in again.list()] == ["k"]
+
+
+# --------------------------------------------------------------- Code Mode
+def test_api_stub_documents_every_tool():
+    from saint_llm_b200.agents.code_mode import generate_api_stub
+
+    stub = generate_api_stub([ToolSpec("add", "add ints", {"type": "object", "properties": {
+        "a": {"type": "integer", "description": "left"}, "b": {"type": "integer"}}, "required": ["a"]}),
+        ToolSpec("noop", "nothing")], namespace="api")
+    assert stub.names == ("add", "noop")
+    assert "class api:" in stub.source and "a (integer) (required): left" in stub.source
+    assert "No parameters." in stub.source
+    compile(stub.source, "<stub>", "exec")  # valid Python
+    assert generate_api_stub([]).names == ()
+
+
+def test_in_process_executor_logs_calls_and_reports_errors():
+    from saint_llm_b200.agents.code_mode import InProcessExecutor
+
+    ex = InProcessExecutor()
+    ok = ex.execute("x = tools.echo(text='hi')\nprint(x)\nRESULT = x * 2", registry=_registry())
+    assert ok.ok and ok.stdout.strip() == "hi" and ok.return_value == "hihi"
+    assert ok.tool_calls == [{"name": "echo", "arguments": {"text": "hi"}}]
+    bad = ex.execute("1 / 0", registry=_registry())
+    assert not bad.ok and bad.error_type == "ZeroDivisionError" and "ZeroDivisionError" in bad.stderr
+    missing = ex.execute("tools.nope()", registry=_registry())
+    assert not missing.ok and missing.error_type == "AttributeError"
+
+
+# ------------------------------------------------------------------ skills
+def test_skill_front_matter_and_loading(tmp_path):
+    from saint_llm_b200.agents.skills import SkillLoadError, load_skill, load_skills, parse_front_matter
+
+    meta = parse_front_matter("name: demo\n# comment\ntags:\n  - a\n  - 'b c'\ndescription: \"quoted\"\n")
+    assert meta == {"name": "demo", "tags": ["a", "b c"], "description": "quoted"}
+    with pytest.raises(SkillLoadError):
+        parse_front_matter("no colon here")
+    root = tmp_path / "skills"
+    (root / "one").mkdir(parents=True)
+    (root / "one" / "SKILL.md").write_text("---\nname: one\ndescription: first\nallowed-tools: a, b\n---\nDo it.\n")
+    (root / "two").mkdir()
+    (root / "two" / "SKILL.md").write_text("---\nname: two\n---\nbody\n")
+    (root / ".hidden").mkdir()
+    (root / "notaskill").mkdir()
+    skills = load_skills(root)
+    assert [s.name for s in skills] == ["one", "two"]
+    assert skills[0].allowed_tools == ("a", "b") and skills[0].instructions == "Do it."
+    (root / "bad").mkdir()
+    (root / "bad" / "SKILL.md").write_text("---\nname: bad\n")
+    with pytest.raises(SkillLoadError, match="unterminated"):
+        load_skill(root / "bad")
+    with pytest.raises(SkillLoadError):
+        load_skills(tmp_path / "missing")

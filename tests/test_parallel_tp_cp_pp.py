@@ -156,6 +156,33 @@ def test_context_parallel_two_ranks():
         assert r[1] is True, r
 
 
+def _cp_compact(rank, ws):
+    """A CP view hands a window layer only the halo plus the local rows, with the halo's global
+    start as key_offset; the full-length form (NSA) pads with zeros before the halo."""
+    from saint_llm_b200.parallel.cp import CPLayerView
+
+    tl, w, d = 16, 4, 8
+    k = torch.full((1, tl, d), float(rank + 1))
+    v = -k
+    compact = CPLayerView(None, tl, w)
+    kc, vc = compact.append(k, v)
+    full = CPLayerView(None, tl, w, compact=False)
+    kf, _ = full.append(k, v)
+    if rank == 0:
+        ok = kc.shape[1] == tl and compact.key_offset == 0 and kf.shape[1] == tl
+    else:
+        ok = (kc.shape[1] == w + tl and compact.key_offset == rank * tl - w and bool((kc[:, :w] == rank).all())
+              and bool((vc[:, :w] == -rank).all()) and kf.shape[1] == rank * tl + tl
+              and bool((kf[:, :rank * tl - w] == 0).all()) and torch.equal(kf[:, rank * tl - w:], kc))
+    return rank, ok or f"shapes {tuple(kc.shape)} / {tuple(kf.shape)}, key_offset {compact.key_offset}"
+
+
+def test_context_parallel_view_holds_only_halo_and_local_rows():
+    res = _run(_cp_compact)
+    for r in res:
+        assert r[1] is True, r
+
+
 # ------------------------------------------------------------------ PP
 def _pp(rank, ws):
     from saint_llm_b200.parallel.pipeline import PipelineStage, default_lm_loss, run_1f1b, sync_tied_embedding

@@ -162,9 +162,18 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
     arriving: dict[tuple[str, int, int], list] = {}  # pending receive(s) of an inbox entry
     in_flight: list[tuple[list, Tensor]] = []         # posted sends and the tensors they read
 
+    # a work is waited for once (gloo's p2p waits are not idempotent); the dict keeps every
+    # waited work alive, so no later work can reuse its id
+    waited: dict[int, object] = {}
+
+    def wait(w: object) -> None:
+        if id(w) not in waited:
+            waited[id(w)] = w
+            w.wait()  # type: ignore[attr-defined]
+
     def take(key: tuple[str, int, int]) -> Tensor:
         for w in arriving.pop(key, []):
-            w.wait()
+            wait(w)
         return inbox.pop(key)
 
     saved: dict[tuple[int, int], tuple[Tensor | None, Tensor | tuple[Tensor, Tensor]]] = {}
@@ -238,10 +247,10 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
                     in_flight.append((ws, ref))  # type: ignore[arg-type]
     for ws, _ in in_flight:
         for w in ws:
-            w.wait()
+            wait(w)
     for ws in arriving.values():  # every receive has a consumer, so none is left; kept for safety
         for w in ws:
-            w.wait()
+            wait(w)
     return torch.stack(losses).mean() if losses else None
 
 

@@ -280,6 +280,37 @@ def test_dualpipe_v_matches_single_process(ws):
         assert r[1] is True and r[2] >= 3, r
 
 
+class _OneWork:
+    """The whole group's transfers behind one handle, as NCCL returns them."""
+
+    def __init__(self, works):
+        self.works = works
+
+    def wait(self):
+        for w in self.works:
+            w.wait()
+        return True
+
+
+def _dualpipe_coalesced(rank, ws):
+    """DualPipe-V when the backend returns one work for a tick's whole group of transfers
+    (NCCL's coalescing), emulated over gloo by wrapping the per-op works."""
+    import saint_llm_b200.parallel.dualpipe as dp
+
+    real = dist.batch_isend_irecv
+    dp.dist.batch_isend_irecv = lambda ops: [_OneWork(real(ops))]
+    try:
+        return _dualpipe(rank, ws)
+    finally:
+        dp.dist.batch_isend_irecv = real
+
+
+def test_dualpipe_v_with_coalesced_group_works():
+    res = _run(_dualpipe_coalesced, 2)
+    for r in res:
+        assert r[1] is True and r[2] >= 3, r
+
+
 # ------------------------------------------------------------------ the same on GPUs over NCCL
 _two_gpus = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                                reason="needs 2 GPUs")

@@ -66,3 +66,19 @@ def test_ulysses_and_ring_attention_match_single_process(ws):
         p.join(timeout=60)
     for r in res:
         assert r[1] is True, r
+
+
+@pytest.mark.parametrize("ws", [1, 2, 4, 8])
+def test_sharding_positions_partition_the_sequence(ws):
+    """Every token lands on exactly one rank; zigzag pairs an early chunk with a late one, so
+    each rank's causal work (sum of query positions + 1) is the same."""
+    from saint_llm_b200.parallel import sp
+
+    T = 64
+    for fn in (sp.contiguous_positions, sp.zigzag_positions):
+        parts = [fn(T, r, ws) for r in range(ws)]
+        allpos = torch.cat(parts).sort().values
+        assert torch.equal(allpos, torch.arange(T)), fn.__name__
+        assert all(p.numel() == T // ws for p in parts)
+    work = [int((sp.zigzag_positions(T, r, ws) + 1).sum()) for r in range(ws)]
+    assert max(work) == min(work)

@@ -24,13 +24,20 @@ the budget.  Otherwise -- and when the model's fp32 training state does not fit 
 all, in which case the micro-batches are timed on the largest layer cut that fits and scaled
 linearly to the full depth -- it prints its ``unavailable`` line carrying those measured
 times and the extrapolated step time, so the record shows that the reference ran on the box.
+
+Watchdog (N > 1, ``SV4_REF_WATCHDOG_S``, default 720 s): if the probe itself has not finished by
+then, rank 0 prints an ``unavailable`` line naming the stage it reached and every rank exits,
+so the driver records a line instead of killing a silent arm at its own limit.  NVLink
+multicast (NVLS) is off in the arm's NCCL group, so an exit leaves no peer memory bound.
 """
 
 from __future__ import annotations
 
 import datetime
+import json
 import os
 import sys
+import threading
 import time
 
 import torch
@@ -181,6 +188,7 @@ def _run(args) -> dict:
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    dog = _watchdog(float(os.environ.get("SV4_REF_WATCHDOG_S", "720")), rank) if world > 1 else None
     if world > 1:
         # no NVLink multicast objects: a rank stopped by the driver's time limit must not leave
         # peers' memory bound to one
@@ -190,8 +198,33 @@ def _run(args) -> dict:
         return _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn, rank, world,
                               dev, t_arm, budget)
     finally:
+        if dog is not None:
+            dog.cancel()
         if world > 1:
             torch.distributed.destroy_process_group()
+
+
+STAGE = {"name": "start"}
+
+
+def _stage(name: str) -> None:
+    STAGE["name"] = name
+
+
+def _watchdog(limit_s: float, rank: int) -> threading.Timer:
+    """After ``limit_s`` seconds: rank 0 prints the unavailable line with the stage reached,
+    then the process exits (every rank runs its own timer from the same start)."""
+    def fire() -> None:
+        if rank == 0:
+            print(json.dumps(_unavailable(f"reference probe did not finish within {limit_s:.0f} s "
+                                          f"(stage reached: {STAGE['name']})")), flush=True)
+        sys.stdout.flush()
+        os._exit(0)
+
+    t = threading.Timer(limit_s, fire)
+    t.daemon = True
+    t.start()
+    return t
 
 
 def _run_on_device(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn,  # noqa: N803
@@ -248,6 +281,7 @@ def _probe_fsdp(args, micro, toks, n_micro, rank, world, dev, t_arm, run_layers,
     optimizer step is not run: the reference's Muon orthogonalises FSDP2 DTensor shards with
     per-operation collectives, and a probe that included one such step did not finish within
     600 s on 2 x B200 (the driver would kill the arm before it printed anything)."""
+    _stage("timed micro-batch")
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     ev[0].record()
     micro(toks, min(1, n_micro - 1))
@@ -277,6 +311,7 @@ def _probe_fsdp(args, micro, toks, n_micro, rank, world, dev, t_arm, run_layers,
 def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_fn,  # noqa: N803
              rank, world, dev, t_arm, budget, run_layers, full_layers, fits, n_params, need, have) -> dict:
     cfg = _reference_config(ModelConfig, args, run_layers)
+    _stage(f"building the {run_layers}-layer model")
     torch.cuda.reset_peak_memory_stats(dev)
     torch.manual_seed(0)
     with torch.device(dev):
@@ -317,6 +352,7 @@ def _measure(args, SaintLLM, ModelConfig, Muon, split_for_muon_adamw, make_loss_
 
     # --- probe: one untimed micro-batch, one timed micro-batch, one timed optimizer step
     toks = host.to(dev, non_blocking=True)
+    _stage("first (untimed) micro-batch")
     micro(toks, 0)
     torch.cuda.synchronize()
     if world > 1:

@@ -12,7 +12,6 @@ only and the LM-head GEMM, optional softcap, log-sum-exp and CE run chunk by chu
 
 from __future__ import annotations
 
-import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 

@@ -99,3 +99,30 @@ def test_fp8_per_axis_cast_and_fake_quant():
     xr = x.clone().requires_grad_(True)
     fake_quant_fp8(xr).sum().backward()
     assert torch.equal(xr.grad, torch.ones_like(x))
+
+
+@pytest.mark.parametrize("mode", ["fp8", "fp4"])
+def test_qat_linears_track_the_plain_linear(mode):
+    """The QAT linears of the factory (eager CPU path) stay close to the plain linear they are
+    built from, pass gradients to input, weight and bias, and keep the layer's shape / repr."""
+    from torch import nn
+
+    from saint_llm_b200.models.linear import Fp4Linear, Fp8Linear, make_linear_factory
+
+    torch.manual_seed(3)
+    base = nn.Linear(64, 32)
+    layer = (Fp8Linear if mode == "fp8" else Fp4Linear).from_linear(base)
+    x = torch.randn(5, 64, requires_grad=True)
+    y, ref = layer(x), base(x)
+    rel = ((y - ref).norm() / ref.norm()).item()
+    assert rel < (0.05 if mode == "fp8" else 0.25), rel
+    y.sum().backward()
+    assert x.grad is not None and layer.weight.grad is not None and layer.bias.grad is not None
+    assert "in_features=64" in repr(layer)
+    made = make_linear_factory(mode)(64, 32, bias=False)
+    assert made.bias is None and made.weight.shape == (32, 64)
+    with pytest.raises(ValueError):
+        make_linear_factory("int4")  # type: ignore[arg-type]
+    if mode == "fp4":
+        with pytest.raises(ValueError):
+            Fp4Linear(50, 8)

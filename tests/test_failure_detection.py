@@ -106,3 +106,69 @@ def test_forged_gradient_is_rejected_and_reputation_drops():
     rnd = trust.DecentralizedTrainingRound(verifier=trust.GradientVerifier(m, loss_fn), tracker=tr)
     res = rnd.process([trust.PeerSubmission("rand", bad, names, x, y), trust.PeerSubmission("nan", nan, names, x, y)])
     assert res.n_accepted == 0 and tr.score("rand") < 0.5 and tr.score("nan") < 0.5
+
+
+def test_stale_ranks_with_a_local_store():
+    """A rank that never beat, one that beat long ago and one that is fresh, judged against an
+    explicit clock; the monitor raises naming the stale ranks."""
+    import time
+
+    import torch.distributed as dist
+
+    from saint_llm_b200.utils.heartbeat import Heartbeat, HeartbeatMonitor, stale_ranks
+
+    store = dist.HashStore()
+    Heartbeat(store, 0).beat()
+    store.set("hb/1", f"{time.time() - 100:.6f},3")
+    now = time.time()
+    assert stale_ranks(store, 3, timeout=10.0, now=now) == [1, 2]
+    assert stale_ranks(store, 3, timeout=1000.0, now=now) == [2]
+    store.set("hb/2", "garbage")
+    assert 2 in stale_ranks(store, 3, timeout=1000.0, now=now)
+    with pytest.raises(RuntimeError, match=r"ranks \[1, 2\]"):
+        HeartbeatMonitor(store, 3, timeout=10.0).raise_if_stale()
+    hb = Heartbeat(store, 1, interval=0.05).start()
+    time.sleep(0.2)
+    hb.stop()
+    assert 1 not in stale_ranks(store, 2, timeout=5.0)
+
+
+def test_checkpoint_rotator_keeps_the_last_n(tmp_path):
+    from saint_llm_b200.train.schedule import CheckpointRotator
+
+    class _T:
+        step = 0
+
+        def save(self, path, extra=None):
+            path.write_text(str(extra))
+
+    rot = CheckpointRotator(tmp_path / "ckpt.pt", keep_last_n=2)
+    t = _T()
+    for s in range(4):
+        t.step = s
+        rot.save(t, extra={"s": s})
+    names = [p.name for p in rot.saved_paths]
+    assert names == ["ckpt.step2.pt", "ckpt.step3.pt"]
+    assert sorted(p.name for p in tmp_path.iterdir()) == names
+    with pytest.raises(ValueError):
+        CheckpointRotator(tmp_path / "x.pt", keep_last_n=0)
+
+
+def test_warmup_cosine_schedule_shape_and_validation():
+    from saint_llm_b200.train.schedule import warmup_cosine_schedule
+
+    p = torch.nn.Parameter(torch.zeros(1))
+    opt = torch.optim.SGD([p], lr=1.0)
+    sched = warmup_cosine_schedule(opt, warmup_steps=4, total_steps=20, min_lr_ratio=0.1)
+    lrs = []
+    for _ in range(20):
+        lrs.append(opt.param_groups[0]["lr"])
+        opt.step()
+        sched.step()
+    assert lrs[0] < 1e-6 and abs(max(lrs) - 1.0) < 1e-6 and lrs.index(max(lrs)) == 4
+    assert all(a >= b - 1e-9 for a, b in zip(lrs[4:], lrs[5:]))  # monotone decay after warm-up
+    assert min(lrs[4:]) >= 0.1 - 1e-6
+    for kw in ({"warmup_steps": -1, "total_steps": 5}, {"warmup_steps": 5, "total_steps": 5},
+               {"warmup_steps": 1, "total_steps": 5, "min_lr_ratio": 2.0}):
+        with pytest.raises(ValueError):
+            warmup_cosine_schedule(opt, **kw)

@@ -329,3 +329,22 @@ def test_skill_front_matter_and_loading(tmp_path):
         load_skill(root / "bad")
     with pytest.raises(SkillLoadError):
         load_skills(tmp_path / "missing")
+
+
+def test_history_rendering_for_the_model_policy():
+    from saint_llm_b200.agents.core import Message, ToolSpec
+    from saint_llm_b200.agents.model_policy import TOOL_FORMAT_HINT, to_chat_turns, tools_prompt
+
+    assert tools_prompt(()) == ""
+    spec = ToolSpec("add", "adds", {"type": "object"})
+    cat = tools_prompt([spec])
+    assert cat.startswith(TOOL_FORMAT_HINT) and '- add: adds parameters={"type": "object"}' in cat
+    msgs = [Message(role="system", content="rule one"), Message(role="user", content="hi"),
+            Message(role="assistant", content="calling"), Message(role="tool", content="3", tool_call_id="c1"),
+            Message(role="system", content="rule two")]
+    turns = to_chat_turns(msgs, [spec])
+    # every system message is folded into one leading system turn, followed by the catalogue
+    assert turns[0].role == "system" and turns[0].content == "rule one\n\nrule two\n\n" + cat
+    assert [(t.role, t.content) for t in turns[1:]] == [("user", "hi"), ("assistant", "calling"),
+                                                         ("user", "[tool c1] 3")]
+    assert to_chat_turns([Message(role="user", content="x")], [])[0].role == "user"

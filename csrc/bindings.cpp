@@ -5,7 +5,6 @@ namespace sv4 {
 // gemm.cu
 void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate,
           double alpha, torch::Tensor err, bool symmetric);
-void sym_mirror(torch::Tensor d);
 void grouped_gemm(int64_t mode, torch::Tensor a, torch::Tensor b0, torch::Tensor b1, torch::Tensor out,
                   torch::Tensor aux, torch::Tensor rowscale, torch::Tensor probs, torch::Tensor total_tiles,
                   int64_t n_probs, double gate_max, double lin_lo, double lin_hi, int64_t ksplit,
@@ -176,7 +175,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("build_moe_problems", &sv4::build_moe_problems);
   m.def("problem_bytes", &sv4::problem_bytes);
   m.def("gemm_axpby", &sv4::gemm_axpby);
-  m.def("sym_mirror", &sv4::sym_mirror);
   m.def("fp8_quant_rows", &sv4::fp8_quant_rows);
   m.def("fp8_gather_quant_rows", &sv4::fp8_gather_quant_rows);
   m.def("fp8_quant_blocks_gu", &sv4::fp8_quant_blocks_gu);

@@ -438,72 +438,6 @@ void gemm_axpby(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor
            at::cuda::getCurrentCUDAStream());
 }
 
-// Completes a symmetric GEMM output: element (i, j) below the diagonal <- (j, i).  The
-// GEMM skipped only tiles entirely below the diagonal, so every source element (j, i),
-// j < i, was computed.  One CTA per 64 x 64 destination tile on or below the diagonal
-// (triangular grid): 16-byte row loads of the source tile, a transpose through shared
-// memory, 16-byte row stores.
-template <typename T>
-__global__ void __launch_bounds__(256) sym_mirror_kernel(T* __restrict__ d, int r, int64_t bstride, int64_t ld,
-                                                         int nt) {
-  constexpr int kV = 16 / sizeof(T);  // elements per 16-byte vector
-  const int k = blockIdx.x;
-  int bi = static_cast<int>((sqrtf(8.f * k + 1.f) - 1.f) * 0.5f);
-  while ((bi + 1) * (bi + 2) / 2 <= k) ++bi;
-  while (bi * (bi + 1) / 2 > k) --bi;
-  const int bj = k - bi * (bi + 1) / 2;  // bi >= bj
-  __shared__ T tile[64][64 + kV];
-  T* base = d + static_cast<int64_t>(blockIdx.y) * bstride;
-  const bool vec = (ld % kV) == 0 && (reinterpret_cast<uintptr_t>(d) % 16) == 0 && (bstride % kV) == 0;
-  // source tile: rows bj*64 .., cols bi*64 .. ; stored transposed: tile[col][row]
-  for (int c = threadIdx.x; c < 64 * (64 / kV); c += blockDim.x) {
-    const int row = c / (64 / kV), col0 = (c % (64 / kV)) * kV;
-    const int sr = bj * 64 + row, sc = bi * 64 + col0;
-    T v[kV];
-    if (vec && sr < r && sc + kV <= r) {
-      *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(sr) * ld + sc);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kV; ++e) v[e] = (sr < r && sc + e < r) ? base[static_cast<int64_t>(sr) * ld + sc + e] : T(0);
-    }
-#pragma unroll
-    for (int e = 0; e < kV; ++e) tile[col0 + e][row] = v[e];
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < 64 * (64 / kV); c += blockDim.x) {
-    const int row = c / (64 / kV), col0 = (c % (64 / kV)) * kV;
-    const int dr = bi * 64 + row, dc = bj * 64 + col0;
-    if (dr >= r) continue;
-    if (vec && bi > bj && dc + kV <= r) {
-      *reinterpret_cast<uint4*>(base + static_cast<int64_t>(dr) * ld + dc) = *reinterpret_cast<const uint4*>(&tile[row][col0]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < kV; ++e)
-        if (dc + e < r && dr > dc + e) base[static_cast<int64_t>(dr) * ld + dc + e] = tile[row][col0 + e];
-    }
-  }
-  (void)nt;
-}
-
-void sym_mirror(torch::Tensor d) {
-  c10::cuda::CUDAGuard guard(d.device());
-  const int r = d.size(-1);
-  TORCH_CHECK(d.size(-2) == r && d.stride(-1) == 1, "sym_mirror: square, unit inner stride");
-  const int batch = d.dim() == 3 ? d.size(0) : 1;
-  const int64_t bstride = d.dim() == 3 ? d.stride(0) : 0;
-  const int nt = (r + 63) / 64;
-  dim3 grid(nt * (nt + 1) / 2, batch);
-  cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  if (d.scalar_type() == at::kBFloat16)
-    sym_mirror_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(d.data_ptr()), r, bstride,
-                                           d.stride(-2), nt);
-  else {
-    TORCH_CHECK(d.scalar_type() == at::kFloat, "sym_mirror: bf16 or fp32");
-    sym_mirror_kernel<<<grid, 256, 0, s>>>(d.data_ptr<float>(), r, bstride, d.stride(-2), nt);
-  }
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
 // Grouped GEMM driven by a device-side problem table (MoE).
 //   mode 0: SwiGLU fprop    A = x_perm (M_pad, D),    B0/B1 = W_gate/W_up (E, I, D)   -> out act (M_pad, I),
 //                                                                                       aux pre (M_pad, 2I)

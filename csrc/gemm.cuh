@@ -196,7 +196,8 @@ __device__ __forceinline__ bool locate_tile(const GemmParams& P, int t, int& hin
     const int local = t - bt * per;
     mt = local / tiles_n<BN, BMODE>(pr);
     nt = local % tiles_n<BN, BMODE>(pr);
-    // symmetric output: a tile whose every column is left of its first row is mirrored later
+    // symmetric output: a tile whose every column is left of its first row is skipped (the
+    // epilogue of its transpose tile fills it)
     return !(P.sym && nt * BN + BN - 1 < mt * kBM);
   }
   while (hint + 1 < P.n_probs && P.probs[hint + 1].tile_begin <= t) ++hint;

@@ -212,3 +212,42 @@ def test_engram_hashing_and_identity():
     assert torch.equal(hook(h, ids), h)  # zero-initialised projection
     torch.nn.init.ones_(hook.proj.weight)
     assert torch.allclose(hook(h, ids)[0, -1], h[0, -1] + 8.0)
+
+
+def test_multimodal_chat_session_feeds_features_and_records_history():
+    from saint_llm_b200.config import MultimodalConfig
+    from saint_llm_b200.data.multimodal import TokenSlots
+    from saint_llm_b200.data.multimodal_chat import render_multimodal_chat
+    from saint_llm_b200.infer.chat import MultimodalChatSession
+    from saint_llm_b200.infer.generate import decode
+    from saint_llm_b200.infer.sampling import SamplingParams
+
+    m = _model({"multimodal": MultimodalConfig(enable_vision_projector=True, vision_input_dim=8)})
+    tok = CharTokenizer(base_vocab=16, unicode_max=480)
+    slots = TokenSlots.from_model_config(m.cfg)
+    img = torch.randn(3, 8, generator=torch.Generator().manual_seed(4))
+    sess = MultimodalChatSession(model=m, tokenizer=tok, slots=slots, system="look")
+    with pytest.raises(ValueError):
+        sess.add_user()
+    sess.add_user("what is it", image_features=[img])
+    cfg = GenerationConfig(max_new_tokens=5, temperature=0.0)
+    r = render_multimodal_chat(sess.history, tok, slots, add_generation_prompt=True)
+    assert r.token_ids.count(slots.image_pad) == 3
+    text = sess.respond(cfg=cfg)
+    # the same prompt and features decoded without the session (full recomputation)
+    want = decode(m, torch.tensor([r.token_ids]), max_new_tokens=5, params=SamplingParams(),
+                  eos_token=tok.eos_token_id, vision_features=img)[0, len(r.token_ids):].tolist()
+    if tok.eos_token_id in want:
+        want = want[:want.index(tok.eos_token_id)]
+    assert text == "".join(tok.decode([t]) for t in want)
+    assert [t.role for t in sess.history] == ["system", "user", "assistant"]
+    assert sess.history[-1].content == tok.decode(want).strip()
+    # a different image changes what the model sees
+    with torch.no_grad():
+        a = m(torch.tensor([r.token_ids]), vision_features=img)["logits"][0, -1]
+        b = m(torch.tensor([r.token_ids]), vision_features=img + 1)["logits"][0, -1]
+    assert not torch.allclose(a, b)
+    sess.reset()
+    assert sess.history == []
+    with pytest.raises(ValueError):
+        next(sess.stream_response(cfg=cfg))

@@ -316,6 +316,9 @@ class RunConfig(_Frozen):
     kernels: Literal["native", "torch"] = "native"
     fused_ep: bool = True
     fused_zero: bool = True
+    # tensor parallelism (tp > 1): the attention block's output projection and input gradient
+    # reduced by the NVLink peer-memory kernels (True) or NCCL all-reduces (False)
+    fused_tp: bool = False
     # hybrid ZeRO transport: "nccl" (reduce / broadcast), "p2p" (owners pull gradients and
     # parameters over NVLink peer memory, parallel.zero_p2p) or "auto" (p2p on CUDA)
     zero_transport: Literal["auto", "nccl", "p2p"] = "auto"

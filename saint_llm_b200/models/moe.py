@@ -166,6 +166,11 @@ class DeepSeekMoE(nn.Module):
         self.ep_group = None
         self.ep_size = 1
         self.ep_rank = 0
+        # tensor parallelism (set by parallel.tp.split_moe_batches): the TP ranks hold the same
+        # sequences; each routes its own 1/tp of them and the outputs are gathered
+        self.tp_group = None
+        self.tp_size = 1
+        self.tp_rank = 0
 
     def route(self, h: Tensor, token_ids: Tensor | None, is_visual: Tensor | None
               ) -> tuple[Tensor, Tensor, Tensor]:
@@ -181,6 +186,28 @@ class DeepSeekMoE(nn.Module):
 
     def forward(self, x: Tensor, token_ids: Tensor | None = None,
                 is_visual: Tensor | None = None) -> Tensor:
+        if self.tp_size > 1:
+            return self._forward_tp_split(x, token_ids, is_visual)
+        return self._forward_local(x, token_ids, is_visual)
+
+    def _forward_tp_split(self, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
+        """This TP rank's share of the batch through the layer, then the shares gathered.  The
+        balance loss of a share is scaled by 1/tp: summed over the TP group (as its router
+        gradients are) it is the batch mean of the unsplit layer."""
+        from saint_llm_b200.parallel.tp import gather_batch_tp, split_batch_tp
+
+        b = x.shape[0]
+        if b % self.tp_size:
+            raise ValueError(f"batch {b} not divisible by the TP size {self.tp_size}")
+        n = b // self.tp_size
+        rows = slice(self.tp_rank * n, (self.tp_rank + 1) * n)
+        y = self._forward_local(split_batch_tp(x, self.tp_group), None if token_ids is None else token_ids[rows],
+                                None if is_visual is None else is_visual[rows])
+        if self._last_aux_loss is not None:
+            self._last_aux_loss = self._last_aux_loss / self.tp_size
+        return gather_batch_tp(y, self.tp_group)
+
+    def _forward_local(self, x: Tensor, token_ids: Tensor | None, is_visual: Tensor | None) -> Tensor:
         if self.ep_size > 1:
             from saint_llm_b200.parallel import ep
 

@@ -139,13 +139,44 @@ def _muon_defaults(lr: float, momentum: float, weight_decay: float, rms_rescale:
 
 
 @torch.no_grad()
+def _tp_shard_step(opt: torch.optim.Optimizer, p: Tensor, g: Tensor, group: dict[str, Any], impl: str,
+                   pg: Any, dim: int) -> None:
+    """Muon step of a tensor-parallel shard of a matrix (rows ``dim=0`` or columns ``dim=1``
+    split over the process group ``pg``): the momentum is element-wise, so it stays a shard,
+    but Newton-Schulz orthogonalises the WHOLE matrix -- the shards' updates are gathered,
+    orthogonalised identically on every rank, and each keeps its own slice."""
+    import torch.distributed as dist
+
+    lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
+    st = opt.state[p]
+    if "momentum_buffer" not in st:
+        st["momentum_buffer"] = torch.zeros_like(p)
+    buf = st["momentum_buffer"]
+    buf.mul_(mu).add_(g.to(buf.dtype))
+    upd = (buf.float() * mu + g.float()).contiguous()
+    ws, r = dist.get_world_size(pg), dist.get_rank(pg)
+    parts = [torch.empty_like(upd) for _ in range(ws)]
+    dist.all_gather(parts, upd, group=pg)
+    full = torch.cat(parts, dim)
+    o = _orthogonalize([full], group, "batched_bf16" if impl == "native" else impl)[0]
+    n = p.shape[dim]
+    local = o.narrow(dim, r * n, n)
+    rows, cols = full.shape
+    p.mul_(1.0 - lr * wd).add_((local * (math.sqrt(max(rows, cols)) * gamma)).to(p.dtype), alpha=-lr)
+
+
+@torch.no_grad()
 def _muon_group_step(opt: torch.optim.Optimizer, group: dict[str, Any], impl: str, strict_2d: bool,
                      chunk_elems: int = 1 << 28) -> None:
     lr, mu, wd, gamma = group["lr"], group["momentum"], group["weight_decay"], group["rms_rescale"]
     by_shape: dict[tuple[Any, ...], list[Tensor]] = {}
+    shards = getattr(opt, "tp_shards", None) or {}
     for p in group["params"]:
         g = _active_grad(opt, p)
         if g is None:
+            continue
+        if id(p) in shards:
+            _tp_shard_step(opt, p, g, group, impl, *shards[id(p)])
             continue
         if p.dim() != 2 and (strict_2d or p.dim() != 3):
             raise ValueError(f"Muon expects 2D matrix params; got shape {tuple(p.shape)}. "

@@ -192,13 +192,18 @@ def shard_grouped_experts(model: nn.Module, rank: int, ws: int, group: dist.Proc
 
 
 def make_grad_sync(expert_params: list[Tensor], group: dist.ProcessGroup | None,
-                   bucket_bytes: int = 256 << 20) -> Callable[[list[Tensor]], None]:
-    """Average replicated main_grads across ranks (bucketed all-reduce); scale expert grads by 1/N."""
+                   bucket_bytes: int = 256 << 20, *, exclude: set[int] | None = None,
+                   expert_div: int | None = None) -> Callable[[list[Tensor]], None]:
+    """Average replicated main_grads across ranks (bucketed all-reduce); scale expert grads by
+    1/``expert_div`` (default: the group size).  Parameters whose ids are in ``exclude`` are
+    left alone (another group reduces them)."""
     ws = dist.get_world_size(group)
     eids = {id(p) for p in expert_params}
+    skip = eids | (exclude or set())
+    ediv = expert_div or ws
 
     def sync(params: list[Tensor]) -> None:
-        rep = [p.main_grad for p in params if id(p) not in eids]  # type: ignore[attr-defined]
+        rep = [p.main_grad for p in params if id(p) not in skip]  # type: ignore[attr-defined]
         bucket: list[Tensor] = []
         size = 0
         for i, g in enumerate(rep):
@@ -215,9 +220,28 @@ def make_grad_sync(expert_params: list[Tensor], group: dist.ProcessGroup | None,
                 bucket, size = [], 0
         for p in params:
             if id(p) in eids:
-                p.main_grad.div_(ws)  # type: ignore[attr-defined]
+                p.main_grad.div_(ediv)  # type: ignore[attr-defined]
 
     return sync
+
+
+def _mean_over(grads: list[Tensor], group: dist.ProcessGroup | None, bucket_bytes: int = 256 << 20) -> None:
+    """In-place mean of ``grads`` over ``group`` (bucketed fp32 all-reduces)."""
+    ws = dist.get_world_size(group)
+    i = 0
+    while i < len(grads):
+        bucket, size = [], 0
+        while i < len(grads) and (not bucket or size < bucket_bytes):
+            bucket.append(grads[i])
+            size += grads[i].numel() * 4
+            i += 1
+        flat = torch.cat([x.reshape(-1).float() for x in bucket])
+        dist.all_reduce(flat, group=group)
+        flat.div_(ws)
+        off = 0
+        for x in bucket:
+            x.copy_(flat[off:off + x.numel()].view_as(x))
+            off += x.numel()
 
 
 def _sync_attention_logits(model: nn.Module, group: dist.ProcessGroup | None) -> None:
@@ -242,15 +266,32 @@ class ParallelSync:
     owner only, only the owner runs the optimizer on it (``optimizer.param_filter``), and
     the updated parameters are broadcast from their owners.  Expert parameters are local
     to their rank in both modes (their gradients are divided by the world size so the
-    loss is the global mean)."""
+    loss is the global mean).
+
+    With tensor parallelism composed in (``parallel.tp_ep``), three more sets: ``dp_params``
+    (head-sharded attention weights: each TP rank holds a different slice) are averaged over
+    ``dp_group`` (the ranks holding the same slice) and updated on every rank, outside ZeRO;
+    ``partial_params`` (gradients that are partial sums over the TP ranks of one replica:
+    replicated attention weights, MoE router / norm / shared experts) are scaled by
+    ``partial_scale`` after the group mean; the expert gradients are divided by
+    ``expert_div`` (the number of data replicas) instead of the group size."""
 
     def __init__(self, model: nn.Module, expert_params: list[Tensor], group: dist.ProcessGroup | None,
                  *, zero: bool, overlap_reduce: bool = False, zero_transport: str = "nccl",
-                 timeout_s: float = 30.0) -> None:
+                 timeout_s: float = 30.0, dp_params: list[Tensor] | None = None,
+                 dp_group: dist.ProcessGroup | None = None, partial_params: list[Tensor] | None = None,
+                 partial_scale: float = 1.0, expert_div: int | None = None) -> None:
         self.model, self.group = model, group
         self.ws = dist.get_world_size(group)
         self.expert_ids = {id(p) for p in expert_params}
         self.expert_params = expert_params
+        self.expert_div = expert_div or self.ws
+        self.dp_params = list(dp_params or [])
+        self.dp_ids = {id(p) for p in self.dp_params}
+        self.dp_group = dp_group
+        self.partial_params = list(partial_params or [])
+        self.partial_scale = partial_scale
+        self.tp_shards: dict[int, tuple[object, int]] = {}
         self.zero = None
         self._plain = None
         self.overlap = False
@@ -260,7 +301,8 @@ class ParallelSync:
 
             muon, adamw = split_for_muon_adamw(model)
             kinds = {id(p): "muon" for p in muon} | {id(p): "adamw" for p in adamw}
-            rep = [p for p in model.parameters() if id(p) not in self.expert_ids and p.requires_grad]
+            rep = [p for p in model.parameters()
+                   if id(p) not in self.expert_ids and id(p) not in self.dp_ids and p.requires_grad]
             rep_kinds = [kinds.get(id(p), "adamw") for p in rep]
             if zero_transport == "auto":
                 zero_transport = "p2p" if rep and rep[0].is_cuda else "nccl"
@@ -276,7 +318,7 @@ class ParallelSync:
             if overlap_reduce and blocks:
                 self._hook_blocks(blocks)
         else:
-            self._plain = make_grad_sync(expert_params, group)
+            self._plain = make_grad_sync(expert_params, group, exclude=self.dp_ids, expert_div=self.expert_div)
 
     def _hook_blocks(self, blocks: list[nn.Module]) -> None:
         """Overlapped reduce: block i's backward hook reduces block i + 1's group (one
@@ -294,25 +336,38 @@ class ParallelSync:
             self.zero.final_micro = True
 
     def is_updated_here(self, p: Tensor) -> bool:
-        return self.zero is None or id(p) in self.expert_ids or self.zero.is_owned(p)
+        return self.zero is None or id(p) in self.expert_ids or id(p) in self.dp_ids or self.zero.is_owned(p)
 
     def configure_optimizer(self, optimizer: torch.optim.Optimizer) -> None:
         if self.zero is not None:
             optimizer.param_filter = self.is_updated_here  # type: ignore[attr-defined]
+        if self.tp_shards:
+            optimizer.tp_shards = self.tp_shards  # type: ignore[attr-defined]
+
+    @staticmethod
+    def _grad(p: Tensor) -> Tensor:
+        g = getattr(p, "main_grad", None)
+        return g if g is not None else p.grad
 
     @torch.no_grad()
     def __call__(self, params: list[Tensor]) -> None:
         _sync_attention_logits(self.model, self.group)
         if self._plain is not None:
             self._plain(params)
-            return
-        if self.overlap:
-            self.zero.finish_reduce()
         else:
-            self.zero.reduce_grads()
-        for p in self.expert_params:
-            g = getattr(p, "main_grad", None)
-            (g if g is not None else p.grad).div_(self.ws)
+            if self.overlap:
+                self.zero.finish_reduce()
+            else:
+                self.zero.reduce_grads()
+            for p in self.expert_params:
+                self._grad(p).div_(self.expert_div)
+        if self.partial_scale != 1.0:
+            for p in self.partial_params:
+                g = self._grad(p)
+                if g is not None:
+                    g.mul_(self.partial_scale)
+        if self.dp_params:
+            _mean_over([g for p in self.dp_params if (g := self._grad(p)) is not None], self.dp_group)
 
     @torch.no_grad()
     def post_step(self) -> None:
@@ -325,7 +380,8 @@ class ParallelSync:
 
 def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = None, *, transport: str = "auto",
                           capacity_factor: float | None = None, zero: bool = False, timeout_s: float = 30.0,
-                          overlap_reduce: bool = False, zero_transport: str = "nccl") -> ParallelSync:
+                          overlap_reduce: bool = False, zero_transport: str = "nccl",
+                          **tp_sets: object) -> ParallelSync:
     """Shard the experts over ``group`` and return the gradient synchroniser.
 
     ``transport``: "p2p" moves tokens with the peer-memory kernels of ``parallel.ep_p2p``
@@ -335,11 +391,14 @@ def setup_expert_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
     ``overlap_reduce`` (with ``zero``): issue each block's owner reductions from its
     backward hook during the last micro-batch.  ``zero_transport`` (with ``zero``): "nccl"
     reduce / broadcast, "p2p" (``parallel.zero_p2p``: owners pull over NVLink peer memory),
-    or "auto" (p2p for CUDA parameters).  ``timeout_s``: bound of every cross-GPU flag wait of the peer-memory kernels."""
+    or "auto" (p2p for CUDA parameters).  ``timeout_s``: bound of every cross-GPU flag wait of the peer-memory kernels.
+    ``tp_sets``: the tensor-parallel parameter sets of ``ParallelSync`` (``dp_params``, ``dp_group``,
+    ``partial_params``, ``partial_scale``, ``expert_div``), given by ``parallel.tp_ep``."""
     rank = dist.get_rank(group)
     ws = dist.get_world_size(group)
     sync = ParallelSync(model, shard_grouped_experts(model, rank, ws, group), group, zero=zero,
-                        overlap_reduce=overlap_reduce, zero_transport=zero_transport, timeout_s=timeout_s)
+                        overlap_reduce=overlap_reduce, zero_transport=zero_transport, timeout_s=timeout_s,
+                        **tp_sets)  # type: ignore[arg-type]
     dev = next(model.parameters()).device
     if transport not in ("auto", "p2p", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")

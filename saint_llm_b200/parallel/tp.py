@@ -91,6 +91,49 @@ class _ScatterSeq(torch.autograd.Function):
         return _GatherSeq.apply(g, ctx.group, ctx.dim), None, None
 
 
+class _SplitBatch(torch.autograd.Function):
+    """This rank's 1/ws of dim 0 of a tensor that is identical on the group's ranks; the
+    backward gathers the shares' gradients, so every rank again holds the full gradient."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, group: Any) -> Tensor:  # type: ignore[override]
+        ctx.group = group
+        ws, r = _ws(group), dist.get_rank(group)
+        n = x.shape[0] // ws
+        return x[r * n:(r + 1) * n].contiguous()
+
+    @staticmethod
+    def backward(ctx, g: Tensor):  # type: ignore[override]
+        parts = [torch.empty_like(g) for _ in range(_ws(ctx.group))]
+        dist.all_gather(parts, g.contiguous(), group=ctx.group)
+        return torch.cat(parts, 0), None
+
+
+class _GatherBatch(torch.autograd.Function):
+    """Concatenate the ranks' shares along dim 0; the gradient arriving is identical on every
+    rank (replicated computation downstream), so each rank keeps its own share of it."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, group: Any) -> Tensor:  # type: ignore[override]
+        ctx.group, ctx.n = group, x.shape[0]
+        parts = [torch.empty_like(x) for _ in range(_ws(group))]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        return torch.cat(parts, 0)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):  # type: ignore[override]
+        r = dist.get_rank(ctx.group)
+        return g[r * ctx.n:(r + 1) * ctx.n].contiguous(), None
+
+
+def split_batch_tp(x: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+    return _SplitBatch.apply(x, group)
+
+
+def gather_batch_tp(x: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+    return _GatherBatch.apply(x, group)
+
+
 def copy_to_tp(x: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
     return _CopyToTP.apply(x, group)
 
@@ -203,6 +246,20 @@ def shard_attention_heads(attn: nn.Module, group: dist.ProcessGroup | None = Non
     return [p for p in attn.parameters() if id(p) not in sharded and p.requires_grad]
 
 
+def split_moe_batches(model: nn.Module, group: dist.ProcessGroup | None = None) -> list[nn.Module]:
+    """Make every MoE layer route only this TP rank's share of the batch (the TP ranks hold
+    the same sequences after the head-sharded attention) and gather the outputs, so the
+    routed experts see each token once per TP group.  Returns the MoE layers; the gradients
+    of their non-expert parameters are then partial sums over the TP ranks."""
+    from saint_llm_b200.models.moe import DeepSeekMoE
+
+    ws, rank = _ws(group), dist.get_rank(group)
+    layers = [m for m in model.modules() if isinstance(m, DeepSeekMoE)]
+    for m in layers:
+        m.tp_group, m.tp_size, m.tp_rank = group, ws, rank
+    return layers
+
+
 class TPGradSync:
     """Sum the gradients (``main_grad`` when present) of replicated attention parameters
     over the TP group, bucketed; and take the max of the attention-logit telemetry over
@@ -271,4 +328,5 @@ def apply_tensor_parallel(model: nn.Module, group: dist.ProcessGroup | None = No
 
 
 __all__ = ["ColumnParallelLinear", "RowParallelLinear", "TPGradSync", "all_gather_seq", "apply_tensor_parallel",
-           "copy_to_tp", "reduce_from_tp", "reduce_scatter_seq", "shard_attention_heads"]
+           "copy_to_tp", "gather_batch_tp", "reduce_from_tp", "reduce_scatter_seq", "shard_attention_heads",
+           "split_batch_tp", "split_moe_batches"]

@@ -33,9 +33,13 @@ What each ``RunConfig`` field selects here:
 * ``param_dtype`` / ``grad_dtype`` / ``compute_dtype``: parameters in bf16 (or fp32),
   gradients accumulated in fp32 ``main_grad`` buffers; bf16 parameters compute in bf16.
   Other combinations raise.
-* ``tp`` / ``cp`` / ``pp``: tensor, context and pipeline parallelism have their own
-  drivers (``parallel.tp`` / ``parallel.cp`` / ``parallel.pipeline`` / ``parallel.dualpipe``);
-  this builder accepts only 1 for them and says so.
+* ``tp``: attention heads sharded over groups of ``tp`` consecutive ranks, composed with EP over
+  the whole group and (hybrid ZeRO) data parallelism over the ``world / tp`` replicas
+  (``parallel.tp_ep``); the ranks of one TP group must be fed the same batch
+  (``TrainingJob.replica`` names it).  ``fused_tp`` selects the peer-memory TP kernels.
+* ``cp`` / ``pp``: context and pipeline parallelism have their own drivers (``parallel.cp`` /
+  ``parallel.pipeline`` / ``parallel.dualpipe``); this builder accepts only 1 for them and
+  says so.
 """
 
 from __future__ import annotations
@@ -58,12 +62,19 @@ class TrainingJob:
     step: TrainStepLike
     grad_sync: object | None
     run: RunConfig
+    # which shard of the global batch this rank reads, out of how many (ranks of one TP
+    # group read the same shard)
+    replica: int = 0
+    replicas: int = 1
 
     def close(self) -> None:
         """Collective release of the expert-parallel peer buffers (call on every rank)."""
         comm = getattr(self.model, "ep_comm", None)
         if comm is not None:
             comm.close()
+        tp_comm = getattr(self.grad_sync, "tp_comm", None)
+        if tp_comm is not None:
+            tp_comm.close()
 
 
 class TrainStepLike:  # typing helper: TrainStep or its eager wrapper
@@ -97,11 +108,15 @@ class _EagerStep:
 
 def _check(run: RunConfig, world: int) -> None:
     problems = []
-    for dim in ("tp", "cp", "pp"):
+    for dim in ("cp", "pp"):
         if getattr(run, dim) != 1:
             problems.append(f"{dim}={getattr(run, dim)} (use the parallel.{dim} driver)")
     if run.ep not in (1, world):
         problems.append(f"ep={run.ep} must be 1 or the world size {world}")
+    if run.tp < 1 or world % run.tp:
+        problems.append(f"tp={run.tp} must divide the world size {world}")
+    elif run.tp > 1 and run.ep != world:
+        problems.append(f"tp={run.tp} composes with expert parallelism over all ranks: ep must be {world}")
     if run.zero not in ("dp", "hybrid_zero", "none"):
         problems.append(f"zero={run.zero!r} (this builder runs 'dp' or 'hybrid_zero'; FSDP has parallel.fsdp)")
     if run.grad_dtype != "float32":
@@ -137,13 +152,21 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
         if hasattr(mod, "gate_weight") and hasattr(mod, "linear_quant"):
             mod.fp8_weight_cache = run.fp8_expert_cache
     grad_sync = None
+    replica, replicas = (dist.get_rank(group), world) if world > 1 else (0, 1)
     if world > 1:
-        from saint_llm_b200.parallel import ep as ep_mod
+        common = dict(transport="p2p" if run.fused_ep else "nccl", zero=run.zero == "hybrid_zero",
+                      timeout_s=run.device_wait_timeout_ms / 1000.0, overlap_reduce=run.fused_zero,
+                      zero_transport=run.zero_transport)
+        if run.tp > 1:
+            from saint_llm_b200.parallel.tp_ep import setup_tp_ep
 
-        grad_sync = ep_mod.setup_expert_parallel(
-            model, group, transport="p2p" if run.fused_ep else "nccl", zero=run.zero == "hybrid_zero",
-            timeout_s=run.device_wait_timeout_ms / 1000.0, overlap_reduce=run.fused_zero,
-            zero_transport=run.zero_transport)
+            grad_sync, lay = setup_tp_ep(model, run.tp, group, tp_transport="p2p" if run.fused_tp else "nccl",
+                                         max_tokens=run.micro_batch * run.seq_len, **common)
+            replica, replicas = lay.replica, lay.replicas
+        else:
+            from saint_llm_b200.parallel import ep as ep_mod
+
+            grad_sync = ep_mod.setup_expert_parallel(model, group, **common)
         if device.type == "cuda":
             torch.cuda.empty_cache()
     params = attach_main_grads(model)
@@ -155,7 +178,7 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
     step = TrainStep(model, opt, micro_batches=run.grad_accum, params=params, grad_sync=grad_sync,
                      cuda_graph=run.cuda_graphs and run.kernels == "native")
     wrapped = _EagerStep(step) if run.kernels == "torch" else step
-    return TrainingJob(model, opt, wrapped, grad_sync, run)
+    return TrainingJob(model, opt, wrapped, grad_sync, run, replica, replicas)
 
 
 __all__ = ["TrainingJob", "build_training", "init_distributed"]

@@ -87,6 +87,7 @@ def test_dispatch_simulation_mode():
 def _step_worker(rank: int, ws: int, port: int, zero: bool, q, overlap: bool = False, micro: int = 1) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // ws))  # the ranks share the host's cores
     dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
         import copy
@@ -112,6 +113,7 @@ def _step_worker(rank: int, ws: int, port: int, zero: bool, q, overlap: bool = F
         for d in data:
             for i in range(micro):
                 (rstep.loss_fn(ref, d[i]) / (ws * micro)).backward()
+        ref_grads = {n: p.main_grad.clone() for n, p in ref.named_parameters() if hasattr(p, "main_grad")}
         ropt.step()
         # expert + data parallel with (or without) hybrid ZeRO
         sync = ep.setup_expert_parallel(model, transport="nccl", zero=zero, overlap_reduce=overlap)
@@ -119,18 +121,33 @@ def _step_worker(rank: int, ws: int, port: int, zero: bool, q, overlap: bool = F
         opt = MuonAdamW(*split_for_muon_adamw(model), lr=0.02, qk_clip_enabled=False)
         sync.configure_optimizer(opt)
         step = TrainStep(model, opt, micro_batches=micro, params=params, grad_sync=sync)
+        grads: dict[str, torch.Tensor] = {}
+        real_step = opt.step
+
+        def step_and_record(*a, **k):  # the synchronised gradients the optimizer steps with
+            for n, p in model.named_parameters():
+                if sync.is_updated_here(p) and hasattr(p, "main_grad"):
+                    grads[n] = p.main_grad.clone()
+            return real_step(*a, **k)
+
+        opt.step = step_and_record
         step.run_device(data[rank])
         per = cfg.moe.routed_experts // ws
         refp = dict(ref.named_parameters())
         worst, moved = 0.0, 0.0
+        g_worst = 0.0
         for n, p in model.named_parameters():
-            r = refp[n]
+            r, rg = refp[n], ref_grads.get(n)
             if ".grouped_experts." in n:
                 r = r[rank * per:(rank + 1) * per]
+                rg = rg[rank * per:(rank + 1) * per] if rg is not None else None
             worst = max(worst, float((p.detach() - r.detach()).abs().max()))
+            if n in grads and rg is not None:
+                # floor: the mHC static biases' gradients are ~1e-7 cancelling sums
+                g_worst = max(g_worst, float((grads[n] - rg).abs().max() / rg.abs().max().clamp(min=1e-5)))
         for n, p1 in ref.named_parameters():
             moved = max(moved, float((p1.detach() - init[n]).abs().max()))
-        q.put((rank, worst, moved))
+        q.put((rank, worst, moved, g_worst, len(grads)))
     finally:
         dist.destroy_process_group()
 
@@ -149,7 +166,10 @@ def test_ep_dp_step_matches_single_process(zero, overlap, micro):
     res = [q.get(timeout=180) for _ in range(2)]
     for p in procs:
         p.join(timeout=60)
-    for rank, worst, moved in res:
+    for rank, worst, moved, g_worst, n_grads in res:
+        # the gradients each rank steps with equal the single process's (a wrong averaging
+        # factor hides in the weights: Muon and AdamW updates barely depend on the scale)
+        assert n_grads > 20 and g_worst < 1e-3, (zero, rank, g_worst, n_grads)
         # the step moved weights by ~`moved`; the parallel step must agree to fp32 noise.
         # Gradient sums run in a different order; parameters whose gradient is a heavily
         # cancelling sum (mHC gate biases) differ by ~0.5 % of their own size, and

@@ -42,6 +42,7 @@ def _entry(fn, rank, ws, port, q, nccl=False):
 
     global DEV
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // ws))  # the ranks share the host's cores
     if nccl:
         DEV = torch.device("cuda", rank)
         torch.cuda.set_device(DEV)

@@ -1,0 +1,186 @@
+"""Tensor parallelism on attention composed with expert parallelism and (hybrid ZeRO) data
+parallelism, on 4 gloo CPU ranks (TP=2 x 2 replicas, EP=4): one training step equals one
+process stepping on the mean of the replicas' losses."""
+
+import copy
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.distributed
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _global_name(n: str, rank: int, per: int) -> str:
+    """Local output group i of TP rank r is the full model's group r * per + i."""
+    if ".group_projs." not in n:
+        return n
+    head, tail = n.split(".group_projs.")
+    i, rest = tail.split(".", 1)
+    return f"{head}.group_projs.{rank * per + int(i)}.{rest}"
+
+
+def _slice_like(ref: torch.Tensor, p: torch.Tensor, n: str, tp_rank: int, ep_rank: int, e_per: int) -> torch.Tensor:
+    if ".grouped_experts." in n:
+        return ref[ep_rank * e_per:(ep_rank + 1) * e_per]
+    if p.shape == ref.shape:
+        return ref
+    if n.endswith("q_up.weight") or n.endswith("sink_logit"):
+        r = p.shape[0]
+        return ref[tp_rank * r:(tp_rank + 1) * r]
+    if n.endswith("final_proj.weight"):
+        c = p.shape[1]
+        return ref[:, tp_rank * c:(tp_rank + 1) * c]
+    raise AssertionError(f"unexpected shape for {n}: {tuple(p.shape)} vs {tuple(ref.shape)}")
+
+
+def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, micro: int, q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(2)  # four ranks share the host's cores
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        from saint_llm_b200.config import ModelConfig
+        from saint_llm_b200.models import SaintLLM
+        from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
+        from saint_llm_b200.parallel.tp_ep import setup_tp_ep
+        from saint_llm_b200.train.engine import attach_main_grads
+        from saint_llm_b200.train.step import TrainStep
+
+        cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+        torch.manual_seed(0)
+        ref = SaintLLM(cfg)
+        model = copy.deepcopy(ref)
+        replicas = ws // tp
+        torch.manual_seed(11)
+        data = [torch.randint(0, cfg.vocab_size, (micro, 2, 16)) for _ in range(replicas)]
+        init = {n: p.detach().clone() for n, p in ref.named_parameters()}
+        rp = attach_main_grads(ref)
+        ropt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, qk_clip_enabled=False)
+        rstep = TrainStep(ref, ropt, micro_batches=1, params=rp)
+        for d in data:
+            for i in range(micro):
+                (rstep.loss_fn(ref, d[i]) / (replicas * micro)).backward()
+        ref_grads = {n: p.main_grad.clone() for n, p in ref.named_parameters() if hasattr(p, "main_grad")}
+        ropt.step()
+
+        sync, lay = setup_tp_ep(model, tp, transport="nccl", zero=zero, overlap_reduce=overlap)
+        params = attach_main_grads(model)
+        opt = MuonAdamW(*split_for_muon_adamw(model), lr=0.02, qk_clip_enabled=False)
+        sync.configure_optimizer(opt)
+        step = TrainStep(model, opt, micro_batches=micro, params=params, grad_sync=sync)
+        # the synchronised gradients, as the optimizer sees them (Muon and AdamW updates are
+        # nearly invariant to a gradient's scale, so the weights alone would hide a wrong factor)
+        grads: dict[str, torch.Tensor] = {}
+        real_step = opt.step
+
+        def step_and_record(*a, **k):
+            for n, p in model.named_parameters():
+                if sync.is_updated_here(p) and hasattr(p, "main_grad"):
+                    grads[n] = p.main_grad.clone()
+            return real_step(*a, **k)
+
+        opt.step = step_and_record
+        loss = float(step.run_device(data[lay.replica]))
+        e_per = cfg.moe.routed_experts // ws
+        g_per = cfg.attention.output_proj_groups // tp
+        refp = dict(ref.named_parameters())
+        worst, moved, n_cmp = 0.0, 0.0, 0
+        g_worst = 0.0
+        for n, p in model.named_parameters():
+            gn = _global_name(n, lay.tp_rank, g_per)
+            r = _slice_like(refp[gn], p, n, lay.tp_rank, rank, e_per)
+            worst = max(worst, float((p.detach() - r.detach()).abs().max()))
+            n_cmp += 1
+            if n in grads:
+                rg = _slice_like(ref_grads[gn], p, n, lay.tp_rank, rank, e_per)
+                # the floor covers gradients that are heavily cancelling sums (the mHC static
+                # biases' are ~1e-7): their summation-order noise is ~1e-9 in absolute terms
+                g_worst = max(g_worst, float((grads[n] - rg).abs().max() / rg.abs().max().clamp(min=1e-5)))
+        for n, p1 in ref.named_parameters():
+            moved = max(moved, float((p1.detach() - init[n]).abs().max()))
+        heads = model.blocks[0].attention.attn_cfg.query_heads
+        q.put((rank, worst, moved, n_cmp, heads, loss, g_worst, len(grads)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("zero,overlap,micro", [(False, False, 1), (True, False, 1), (True, True, 2)])
+def test_tp_ep_step_matches_single_process(zero, overlap, micro):
+    ws, tp = 4, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, ws, tp, port, zero, overlap, micro, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(ws)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert len(r) == 8, r
+        rank, worst, moved, n_cmp, heads, loss, g_worst, n_grads = r
+        assert heads == 2 and n_cmp > 50 and n_grads > 20
+        # every gradient this rank steps with equals the single process's (its slice of it)
+        assert g_worst < 1e-3, (zero, overlap, rank, g_worst)
+        # as in the EP-only equivalence test: a wrong reduction, scale or slice would differ
+        # by about `moved`; different summation orders stay at fp32 noise
+        assert worst < 1e-2 * max(moved, 1e-3) + 2e-5, (zero, overlap, rank, worst, moved)
+    # the TP ranks of one replica report the same loss
+    losses = {r[0]: r[5] for r in res}
+    assert abs(losses[0] - losses[1]) < 1e-5 and abs(losses[2] - losses[3]) < 1e-5
+
+
+def _job_worker(rank: int, ws: int, port: int, q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(2)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        from saint_llm_b200.config import ModelConfig, RunConfig
+        from saint_llm_b200.train.launch import build_training
+
+        cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+        run = RunConfig(ep=ws, tp=2, zero="hybrid_zero", fused_ep=False, zero_transport="nccl", grad_accum=1,
+                        micro_batch=2, seq_len=16, lr=0.02, adamw_lr=3e-3, param_dtype="float32",
+                        compute_dtype="float32")
+        job = build_training(cfg, run, torch.device("cpu"))
+        torch.manual_seed(100 + job.replica)
+        batch = torch.randint(0, cfg.vocab_size, (1, 2, 16))
+        losses = [job.step(batch) for _ in range(4)]
+        q.put((rank, job.replica, job.replicas, losses))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_build_training_with_tensor_parallelism():
+    """``RunConfig(tp=2, ep=4)`` through the public builder: ranks 0-1 and 2-3 form the two
+    replicas, each TP pair reports the same losses, and training makes progress."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_job_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(4)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(len(r) == 4 for r in res), res
+    assert [(r[1], r[2]) for r in res] == [(0, 2), (0, 2), (1, 2), (1, 2)]
+    for a, b in ((0, 1), (2, 3)):
+        assert all(abs(x - y) < 1e-4 for x, y in zip(res[a][3], res[b][3], strict=True))
+    for r in res:
+        assert r[3][-1] < r[3][0]

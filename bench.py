@@ -24,6 +24,12 @@ greedy steps).
 The headline dtype is bf16 (at least the reference's precision): on this implementation the
 bf16 step is faster than the FP8 recipe, whose number is reported next to it.
 
+``--tp T`` (N divisible by T) adds config 3's tensor parallelism on attention: the T ranks
+of a TP group share a batch of T x micro-batch sequences (heads split over the group, each
+rank routing its micro-batch share through the MoE layers), so the tokens per GPU are
+unchanged; EP stays over all N ranks and ZeRO over the N / T replicas.  Not the default:
+this layout has only run on CPU ranks so far.
+
 Rank 0 prints one JSON line.
 """
 
@@ -133,11 +139,15 @@ def run_config(args, world: int):
     """The run layout of this bench as a ``RunConfig`` (consumed by ``build_training``)."""
     from saint_llm_b200.config import RunConfig
 
-    return RunConfig(ep=world, zero="dp" if args.no_zero else "hybrid_zero", fused_ep=args.ep_transport == "p2p",
+    tp = getattr(args, "tp", 1)
+    # with TP the ranks of one TP group share a batch of tp x micro_batch sequences: each routes
+    # micro_batch of them through the MoE layers, so the work per GPU matches tp = 1
+    return RunConfig(ep=world, tp=tp, zero="dp" if args.no_zero else "hybrid_zero",
+                     fused_ep=args.ep_transport == "p2p", fused_tp=getattr(args, "tp_transport", "nccl") == "p2p",
                      fused_zero=not args.no_overlap_reduce, zero_transport=args.zero_transport,
                      cuda_graphs=not args.no_cuda_graph,
                      fp8_expert_cache=args.fp8_expert_cache,
-                     micro_batch=args.micro_batch, seq_len=args.seq_len,
+                     micro_batch=args.micro_batch * tp, seq_len=args.seq_len,
                      grad_accum=args.seqs_per_gpu // args.micro_batch, lr=2.7e-4, adamw_lr=2.7e-4,
                      pg_timeout_s=600.0, seed=0)
 
@@ -152,7 +162,7 @@ def build_ours(args, device, world):
     cfg = ModelConfig.bench_16b().model_copy(update=upd)
     run = run_config(args, world)
     job = build_training(cfg, run, device)
-    return cfg, job.model, job.step
+    return cfg, job.model, job.step, job
 
 
 def _uniform_loss(cfg) -> float:
@@ -182,13 +192,14 @@ def run_ours(args) -> dict:
         from saint_llm_b200.train.launch import init_distributed
 
         init_distributed(run_config(args, world), device)
-    cfg, model, step = build_ours(args, device, world)
+    cfg, model, step, job = build_ours(args, device, world)
     from saint_llm_b200.ops.gemm import check_errors
     from saint_llm_b200.train.engine import SyntheticTokens
     from saint_llm_b200.utils.profiling import PhaseRecorder
 
     n_micro = args.seqs_per_gpu // args.micro_batch
-    data = SyntheticTokens(cfg.vocab_size, args.micro_batch, args.seq_len, n_micro, seed=rank,
+    # the ranks of one TP group read the same batch (job.replica == rank without TP)
+    data = SyntheticTokens(cfg.vocab_size, args.micro_batch * args.tp, args.seq_len, n_micro, seed=job.replica,
                            n_batches=args.data_pool)
     it = iter(range(1 << 30))
 
@@ -266,8 +277,10 @@ def run_ours(args) -> dict:
         "data": "synthetic uniform-random tokens; random-init weights N(0,0.02)",
         "config": {"model": MODEL_DESC, "n_layers": cfg.n_layers, "global_batch": world * args.seqs_per_gpu,
                    "seq_len": args.seq_len, "micro_batch": args.micro_batch,
-                   "parallelism": (f"ep{world}+dp{world}" + ("" if args.no_zero else "+zero")) if world > 1
+                   "parallelism": (f"ep{world}" + (f"+tp{args.tp}" if args.tp > 1 else "")
+                                   + f"+dp{world // args.tp}" + ("" if args.no_zero else "+zero")) if world > 1
                    else "single-gpu",
+                   "tp_transport": args.tp_transport if args.tp > 1 else None,
                    "ep_transport": args.ep_transport if world > 1 else None,
                    "zero_transport": args.zero_transport if world > 1 and not args.no_zero else None,
                    "cuda_graph": bool(getattr(step, "_graph", None) is not None),
@@ -297,6 +310,9 @@ def run_ours(args) -> dict:
         comm = getattr(model, "ep_comm", None)
         if comm is not None:
             comm.close()  # collective: peers stop touching each other's buffers first
+        tp_comm = getattr(job.grad_sync, "tp_comm", None)
+        if tp_comm is not None:
+            tp_comm.close()
     import gc
 
     del step, model
@@ -321,7 +337,8 @@ def run_fp8_variant(args, device) -> dict:
     torch.cuda.reset_peak_memory_stats(device)
     fargs = argparse.Namespace(**vars(args))
     fargs.linear_quant = "fp8"
-    cfg, model, step = build_ours(fargs, device, 1)
+    fargs.tp = 1
+    cfg, model, step, _ = build_ours(fargs, device, 1)
     from saint_llm_b200.train.engine import SyntheticTokens
 
     n_micro = args.seqs_per_gpu // args.micro_batch
@@ -399,6 +416,10 @@ def main() -> None:
                     help="N > 1 with hybrid ZeRO: the peer-memory pull kernels (default) or NCCL reduce/broadcast")
     ap.add_argument("--no-overlap-reduce", action="store_true",
                     help="N > 1 with hybrid ZeRO: reduce gradients after the backward instead of from block hooks")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor parallelism on attention (config 3 names TP=2), composed with EP over all ranks")
+    ap.add_argument("--tp-transport", default="nccl", choices=["nccl", "p2p"],
+                    help="TP reductions: NCCL all-reduce, or the peer-memory fused GEMM + reduce kernels")
     ap.add_argument("--seq-len", type=int, default=4096)
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (config 5) measurement")
     ap.add_argument("--no-fp8-variant", action="store_true",

@@ -24,15 +24,20 @@ Gradients (the loss of a step is the mean over the W / t replicas):
 
 Data: ``TPEPLayout.replica`` / ``replicas`` name the shard of the global batch a rank reads
 (TP ranks of one replica read the same one).
+
+Decoding uses the same layout without gradient state (``shard_for_inference`` +
+``parallel_decode``): config 5's TP x EP serving layout.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
 
+import torch
 import torch.distributed as dist
-from torch import nn
+from torch import Tensor, nn
 
+from saint_llm_b200.infer.sampling import SamplingParams
 from saint_llm_b200.parallel.ep import ParallelSync, setup_expert_parallel
 from saint_llm_b200.parallel.tp import shard_attention_heads, split_moe_batches
 
@@ -110,4 +115,37 @@ def setup_tp_ep(model: nn.Module, tp: int, group: dist.ProcessGroup | None = Non
     return sync, lay
 
 
-__all__ = ["TPEPLayout", "setup_tp_ep", "tp_dp_groups"]
+def shard_for_inference(model: nn.Module, tp: int, group: dist.ProcessGroup | None = None) -> TPEPLayout:
+    """The same layout for decoding (config 5's TP x EP): heads over each TP group, the routed
+    experts over all ranks, each TP rank routing its share of the batch (the decode batch of a
+    replica must divide by ``tp``).  Every rank of ``group`` calls this; no gradient state."""
+    from saint_llm_b200.parallel.ep import shard_grouped_experts
+
+    lay = tp_dp_groups(tp, group)
+    for block in model.blocks:  # type: ignore[attr-defined]
+        shard_attention_heads(block.attention, lay.tp_group)
+    split_moe_batches(model, lay.tp_group)
+    shard_grouped_experts(model, dist.get_rank(group), dist.get_world_size(group), group)
+    return lay
+
+
+def parallel_decode(model: nn.Module, prompt_ids: Tensor, *, max_new_tokens: int,
+                    params: SamplingParams | None = None, eos_token: int | None = None,
+                    generator: torch.Generator | None = None, use_cache: bool = True) -> Tensor:
+    """``infer.generate.decode`` for a model sharded by ``shard_for_inference``: this rank's
+    replica decodes ``prompt_ids`` (the TP ranks of a replica pass the same prompts and, for
+    sampling, identically seeded generators).  The expert exchange is a collective over all
+    ranks, so every rank runs all ``max_new_tokens`` steps: rows that produced ``eos_token``
+    are filled with it afterwards instead of ending the loop early (the output is the same)."""
+    from saint_llm_b200.infer.generate import decode
+
+    out = decode(model, prompt_ids, max_new_tokens=max_new_tokens, params=params or SamplingParams(),
+                 generator=generator, use_cache=use_cache)
+    if eos_token is not None:
+        gen = out[:, prompt_ids.shape[1]:]
+        hit = (gen == eos_token).long().cumsum(1) > 0
+        gen.masked_fill_(hit, eos_token)
+    return out
+
+
+__all__ = ["TPEPLayout", "parallel_decode", "setup_tp_ep", "shard_for_inference", "tp_dp_groups"]

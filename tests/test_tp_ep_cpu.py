@@ -184,3 +184,60 @@ def test_build_training_with_tensor_parallelism():
         assert all(abs(x - y) < 1e-4 for x, y in zip(res[a][3], res[b][3], strict=True))
     for r in res:
         assert r[3][-1] < r[3][0]
+
+
+def _decode_worker(rank: int, ws: int, port: int, q) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(2)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        from saint_llm_b200.config import ModelConfig
+        from saint_llm_b200.infer.generate import decode, last_logits
+        from saint_llm_b200.infer.sampling import SamplingParams
+        from saint_llm_b200.models import SaintLLM
+        from saint_llm_b200.parallel.tp_ep import parallel_decode, shard_for_inference
+
+        cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
+        torch.manual_seed(0)
+        full = SaintLLM(cfg).eval()
+        model = copy.deepcopy(full)
+        torch.manual_seed(21)
+        prompts = torch.randint(0, cfg.vocab_size, (4, 12))
+        with torch.no_grad():
+            want = decode(full, prompts, max_new_tokens=6, params=SamplingParams(), use_cache=True)
+            want_logits = last_logits(full, prompts)
+        lay = shard_for_inference(model, 2)
+        rows = slice(2 * lay.replica, 2 * lay.replica + 2)
+        with torch.no_grad():
+            got_logits = last_logits(model, prompts[rows])
+            got = parallel_decode(model, prompts[rows], max_new_tokens=6)
+            eos = int(got[0, 14])  # a token the first row produces: rows are cut after it
+            cut = parallel_decode(model, prompts[rows], max_new_tokens=6, eos_token=eos)
+        err = float((got_logits - want_logits[rows]).abs().max() / want_logits.abs().max())
+        first = int((cut[0, 12:] == eos).nonzero()[0])
+        ok_cut = bool((cut[0, 12 + first:] == eos).all()) and torch.equal(cut[0, :12 + first], got[0, :12 + first])
+        q.put((rank, err, torch.equal(got, want[rows]), ok_cut, model.blocks[0].attention.attn_cfg.query_heads))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_ep_decode_matches_single_process():
+    """Config 5's layout on 4 gloo ranks (TP=2 x EP=4, 2 replicas): each replica decodes its
+    two prompts through the KV cache with head-sharded attention and experts over all ranks;
+    prefill logits and greedy tokens equal one process decoding all four prompts."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decode_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(4)]
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert len(r) == 5, r
+        rank, err, same_tokens, ok_cut, heads = r
+        assert heads == 2 and err < 1e-4 and same_tokens and ok_cut, r

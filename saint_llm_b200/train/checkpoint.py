@@ -11,7 +11,9 @@ process killed mid-save leaves the previous checkpoint intact.
 
 v2 (sharded): a directory with ``manifest.json`` (format_version 2, step, world size,
 model config, per-rank file list), ``model.pt`` (the full model state dict, written by
-rank 0 after gathering expert shards) and ``optim.rank{r}.pt`` per rank.
+rank 0: ``parallel.state.gather_full_state_dict`` assembles it from expert- and
+tensor-parallel shards, ``load_full_state_dict`` slices it back) and ``optim.rank{r}.pt``
+per rank.
 ``load_sharded(..., into_v1=True)`` gathers everything back into the v1 layout so a
 run can resume at a different world size.
 

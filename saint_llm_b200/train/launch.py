@@ -47,6 +47,7 @@ from __future__ import annotations
 import contextlib
 import datetime
 from dataclasses import dataclass
+from pathlib import Path
 
 import torch
 import torch.distributed as dist
@@ -67,6 +68,52 @@ class TrainingJob:
     replica: int = 0
     replicas: int = 1
 
+    def save(self, directory: str | Path, *, step: int, extra: dict | None = None) -> Path:
+        """Sharded (v2) checkpoint, collective: every rank writes its optimizer state, rank 0
+        the full unsharded model (``parallel.state.gather_full_state_dict``) and the manifest
+        last, so a directory with a manifest is complete."""
+        from saint_llm_b200.parallel.state import gather_full_state_dict
+        from saint_llm_b200.train.checkpoint import save_sharded
+
+        world, rank = _world_rank()
+        full = gather_full_state_dict(self.model) if world > 1 else self.model.state_dict()
+        opt_state = self.optimizer.state_dict()
+        extra = {**(extra or {}), "layout": self._layout(world)}
+        if rank != 0:
+            save_sharded(directory, full, opt_state, step=step, rank=rank, world_size=world, extra=extra)
+        if world > 1:
+            dist.barrier()  # every optimizer shard is on disk before rank 0 writes the manifest
+        if rank == 0:
+            save_sharded(directory, full, opt_state, step=step, rank=0, world_size=world, extra=extra,
+                         model_config_json=self.model.cfg.model_dump_json())  # type: ignore[union-attr]
+        if world > 1:
+            dist.barrier()
+        return Path(directory)
+
+    def load(self, directory: str | Path, *, optimizer: bool = True) -> int:
+        """Resume from ``save``'s directory (or any v2 checkpoint): the full model state is
+        sliced into this rank's shards; the optimizer state is restored when the checkpoint
+        was written with the same layout (world size, TP, EP, ZeRO: its state is per rank and
+        per shard) and skipped otherwise (fresh moments).  Returns the step."""
+        from saint_llm_b200.ops.fp8 import bump_weight_epoch
+        from saint_llm_b200.parallel.state import load_full_state_dict
+        from saint_llm_b200.train.checkpoint import load_sharded
+
+        world, rank = _world_rank()
+        manifest = _manifest(directory)
+        saved = (manifest.get("extra") or {}).get("layout")
+        # optimizer states are per rank and per shard shape: only the same layout reuses them
+        same_layout = saved == self._layout(world) if saved is not None else manifest["world_size"] == world
+        data = load_sharded(directory, rank=rank if same_layout else 0)
+        load_full_state_dict(self.model, data["model"])
+        if optimizer and same_layout and data["optim"] is not None:
+            self.optimizer.load_state_dict(data["optim"])
+        bump_weight_epoch()  # cached FP8 weight copies must be re-quantised from the loaded weights
+        return int(data["step"])
+
+    def _layout(self, world: int) -> dict:
+        return {"world": world, "tp": self.run.tp, "ep": self.run.ep, "zero": self.run.zero}
+
     def close(self) -> None:
         """Collective release of the expert-parallel peer buffers (call on every rank)."""
         comm = getattr(self.model, "ep_comm", None)
@@ -75,6 +122,16 @@ class TrainingJob:
         tp_comm = getattr(self.grad_sync, "tp_comm", None)
         if tp_comm is not None:
             tp_comm.close()
+
+
+def _world_rank() -> tuple[int, int]:
+    return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
+
+
+def _manifest(directory: str | Path) -> dict:
+    import json
+
+    return json.loads((Path(directory) / "manifest.json").read_text())
 
 
 class TrainStepLike:  # typing helper: TrainStep or its eager wrapper

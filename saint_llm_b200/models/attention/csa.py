@@ -278,7 +278,16 @@ class CSA(_AttentionBase):
         q = self._queries(h, cos, sin)
         k_new, v_new = self._sw_kv(h, cos, sin)
         m = self.csa_cfg.compression_rate
-        if kv_cache is not None:
+        if kv_cache is not None and is_visual is not None and getattr(kv_cache, "carries_visual_bias", False):
+            # a context-parallel view: the sequence is whole, only sharded, so the indexer keeps
+            # the visual cohesion bias of its blocks (gathered with the compressed entries)
+            compressed, idx_keys, k, v, vis_bias = kv_cache.append(
+                h, k_new, v_new, compressor=self.kv_compressor,
+                indexer_compressor=self.indexer.compressor, is_visual=is_visual,
+            )
+            top_idx = self.indexer.select(self.indexer.scores(h, idx_keys, off, m, vis_bias), self.indexer.top_k)
+        elif kv_cache is not None:
+            # a decode cache: like the reference, the cached path has no visual bias
             compressed, idx_keys, k, v = kv_cache.append(
                 h, k_new, v_new, compressor=self.kv_compressor,
                 indexer_compressor=self.indexer.compressor,

@@ -63,6 +63,10 @@ class CPLayerView:
     all-gather gives each rank the previous rank's tail (the halo) and every rank's
     compressed entries in global block order."""
 
+    # CSA asks for the gathered per-block visual fractions (the indexer's cohesion bias) through
+    # ``append(..., is_visual=...)``; decode caches, which the reference leaves without it, do not
+    carries_visual_bias = True
+
     def __init__(self, group: dist.ProcessGroup | None, shard_len: int, window: int, *, compact: bool = True) -> None:
         self.group = group
         self.rank = dist.get_rank(group)
@@ -72,17 +76,23 @@ class CPLayerView:
         self.compact = compact
         self.key_offset = 0
 
-    def append(self, *args: Tensor, compressor=None, indexer_compressor=None):  # noqa: ANN001, ANN201
+    def append(self, *args: Tensor, compressor=None, indexer_compressor=None,  # noqa: ANN001, ANN201
+               is_visual: Tensor | None = None):
         if compressor is None:  # SWA / NSA: (k, v)
             h, (k, v) = None, args
         else:
             h, k, v = args
         b, d, w = k.shape[0], k.shape[-1], self.window
         parts = [torch.cat([k[:, -w:], v[:, -w:]], -1)]
+        visual = compressor is not None and indexer_compressor is not None and is_visual is not None
         if compressor is not None:
             parts.append(compressor(h))
             if indexer_compressor is not None:
                 parts.append(indexer_compressor(h))
+            if visual:  # the fraction of image tokens per local block, gathered with the entries
+                m = indexer_compressor.m
+                nb = h.shape[1] // m
+                parts.append(is_visual[:, :nb * m].reshape(b, nb, m).to(h.dtype).mean(-1, keepdim=True))
         sizes = [p.shape[1:] for p in parts]
         g = gather_stack(torch.cat([p.reshape(b, -1) for p in parts], 1), self.group)  # (ws, B, L)
         outs, off = [], 0
@@ -108,6 +118,8 @@ class CPLayerView:
         comp = [o.transpose(0, 1).reshape(b, -1, o.shape[-1]) for o in outs[1:]]
         if indexer_compressor is None:  # HCA
             return comp[0], k_all, v_all
+        if visual:
+            return comp[0], comp[1], k_all, v_all, comp[2].squeeze(-1)
         return comp[0], comp[1], k_all, v_all
 
 

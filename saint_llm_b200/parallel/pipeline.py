@@ -17,6 +17,15 @@ order, so matching pairs always meet.
 
 With tied embeddings the first and last stages both hold the embedding matrix;
 ``sync_tied_embedding`` sums its gradient over the two after the schedule.
+
+Context parallelism inside each stage (config 4's PP x CP layout): with ``cp_group`` every
+stage's sequence is split over that group as in ``parallel.cp`` (each rank holds a
+contiguous shard; attention exchanges the window halo and the compressed entries), the
+stage boundary carries the shard's residual stream to the same CP rank of the next stage
+(the pipeline group links the ranks with one CP index), and the last stage's loss is this
+shard's share of the global mean (``cp_lm_share``).  ``sync_cp_grads`` then sums the
+stage's gradients over the CP group.  Every CP rank of a stage runs the same schedule, so
+their attention collectives pair up in order.
 """
 
 from __future__ import annotations
@@ -37,8 +46,10 @@ def stage_bounds(n_layers: int, n_stages: int, stage: int) -> tuple[int, int]:
 
 
 class PipelineStage:
-    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None = None, *, prune: bool = False) -> None:
+    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None = None, *, prune: bool = False,
+                 cp_group: dist.ProcessGroup | None = None) -> None:
         self.model, self.group = model, group
+        self.cp_group = cp_group
         self.stage = dist.get_rank(group)
         self.n_stages = dist.get_world_size(group)
         self.first, self.last = self.stage == 0, self.stage == self.n_stages - 1
@@ -51,16 +62,32 @@ class PipelineStage:
     def _peer(self, s: int) -> int:
         return dist.get_global_rank(self.group, s) if self.group is not None else s
 
+    def local_ids(self, ids: Tensor) -> Tensor:
+        """The tokens this rank computes: its CP shard of ``ids`` (all of them without CP)."""
+        if self.cp_group is None:
+            return ids
+        from saint_llm_b200.parallel.cp import cp_shard
+
+        return cp_shard(ids, self.cp_group)
+
     def forward(self, ids: Tensor, x_in: Tensor | None) -> Tensor:
+        """``ids``: the micro-batch's full (B, T) token ids."""
         m = self.model
+        local = self.local_ids(ids)
         if self.first:
-            x = MHC.expand(m._embed_inputs(ids, None, None), m.cfg.mhc.expansion_factor)  # type: ignore[attr-defined]
+            x = MHC.expand(m._embed_inputs(local, None, None), m.cfg.mhc.expansion_factor)  # type: ignore[attr-defined]
         else:
             assert x_in is not None
             x = x_in
-        vis = ids == m.cfg.tokenizer_slots.image_pad  # type: ignore[attr-defined]
+        vis = local == m.cfg.tokenizer_slots.image_pad  # type: ignore[attr-defined]
+        bundle = None
+        if self.cp_group is not None:
+            from saint_llm_b200.parallel.cp import CPBundle
+
+            bundle = CPBundle(m, self.cp_group, local.shape[1])
         for i in range(self.lo, self.hi):
-            x = m.blocks[i](x, token_ids=ids, is_visual=vis)  # type: ignore[index]
+            view = bundle.for_layer(i) if bundle is not None else None
+            x = m.blocks[i](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
         return x
 
     def loss(self, ids: Tensor, x: Tensor, loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor]) -> Tensor:
@@ -84,12 +111,44 @@ def default_lm_loss(model: nn.Module, h: Tensor, ids: Tensor) -> Tensor:
     return torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
 
 
+def cp_lm_share(group: dist.ProcessGroup | None) -> Callable[[nn.Module, Tensor, Tensor], Tensor]:
+    """The main next-token CE for a CP-sharded last stage: ``h`` holds this rank's shard of the
+    positions, ``ids`` the full sequence (the shard's last target is the next shard's first
+    token); returns this shard's share of the global mean (the sum over the group is the loss)."""
+
+    def loss(model: nn.Module, h: Tensor, ids: Tensor) -> Tensor:
+        r = dist.get_rank(group)
+        b, t = ids.shape
+        tl = h.shape[1]
+        tgt = ids[:, r * tl + 1:(r + 1) * tl + 1]
+        logits = model.logits(h[:, :tgt.shape[1]]).float()  # type: ignore[attr-defined]
+        ce = torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1),
+                                               reduction="sum")
+        return ce / (b * (t - 1))
+
+    return loss
+
+
+@torch.no_grad()
+def sync_cp_grads(stage: PipelineStage) -> None:
+    """Sum the stage's parameter gradients over its CP group (each rank's are the share of
+    its own tokens)."""
+    if stage.cp_group is None:
+        return
+    for p in stage.model.parameters():
+        if p.grad is not None:
+            dist.all_reduce(p.grad, group=stage.cp_group)
+
+
 def run_1f1b(stage: PipelineStage, micro_ids: list[Tensor], *,
-             loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor] = default_lm_loss,
+             loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor] | None = None,
              aux_weight: float = 0.0) -> Tensor | None:
     """One pipelined forward+backward over ``micro_ids``; gradients accumulate in the
     stage's parameters (each micro-batch's loss is divided by M).  Returns the mean loss
-    on the last stage, None elsewhere."""
+    on the last stage (with CP: this rank's share of it), None elsewhere.  ``loss_fn``
+    defaults to ``default_lm_loss`` (``cp_lm_share`` with a CP group)."""
+    if loss_fn is None:
+        loss_fn = default_lm_loss if stage.cp_group is None else cp_lm_share(stage.cp_group)
     m = stage.model
     M = len(micro_ids)
     cfg = m.cfg  # type: ignore[attr-defined]
@@ -101,7 +160,8 @@ def run_1f1b(stage: PipelineStage, micro_ids: list[Tensor], *,
     losses: list[Tensor] = []
 
     def shape(ids: Tensor) -> tuple[int, ...]:
-        return (ids.shape[0], ids.shape[1], cfg.mhc.expansion_factor, cfg.hidden_dim)
+        local = stage.local_ids(ids)
+        return (local.shape[0], local.shape[1], cfg.mhc.expansion_factor, cfg.hidden_dim)
 
     def fwd(i: int) -> None:
         ids = micro_ids[i]
@@ -176,4 +236,5 @@ def sync_tied_embedding(stage: PipelineStage) -> None:
     g.copy_(mine + other)
 
 
-__all__ = ["PipelineStage", "aux_losses", "default_lm_loss", "run_1f1b", "stage_bounds", "sync_tied_embedding"]
+__all__ = ["PipelineStage", "aux_losses", "cp_lm_share", "default_lm_loss", "run_1f1b", "stage_bounds", "sync_cp_grads",
+           "sync_tied_embedding"]

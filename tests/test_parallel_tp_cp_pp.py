@@ -121,8 +121,8 @@ def test_tensor_parallel_attention_two_ranks():
 def _cp(rank, ws):
     from saint_llm_b200.parallel.cp import cp_lm_loss
 
-    for pattern in ("csa_hca_interleaved", "nsa"):
-        upd = {"attention_pattern": pattern}
+    for pattern in ("csa_hca_interleaved", "nsa", "visual"):
+        upd = {"attention_pattern": "csa_hca_interleaved" if pattern == "visual" else pattern}
         if pattern == "nsa":
             from saint_llm_b200.config import NSAConfig
 
@@ -131,6 +131,9 @@ def _cp(rank, ws):
         cp = copy.deepcopy(full)
         torch.manual_seed(7)
         ids = _ids(2, 64, vocab=full.cfg.vocab_size)
+        if pattern == "visual":  # image tokens on both shards: the indexer's cohesion bias must cross them
+            ids[:, 3:9] = full.cfg.tokenizer_slots.image_pad
+            ids[:, 40:41] = full.cfg.tokenizer_slots.image_pad
         h, _ = full.backbone(ids)
         logits = full.logits(h).float()
         ref = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
@@ -216,6 +219,51 @@ def _pp(rank, ws):
 
 def test_pipeline_1f1b_two_stages():
     res = _run(_pp)
+    for r in res:
+        assert r[1] is True and r[2] > 5, r
+
+
+def _pp_cp(rank, ws):
+    """Config 4's layout in miniature: 2 pipeline stages x 2 context-parallel ranks each."""
+    from saint_llm_b200.parallel.pipeline import (PipelineStage, default_lm_loss, run_1f1b, sync_cp_grads,
+                                                  sync_tied_embedding)
+
+    cp_n = 2
+    cp_groups = [dist.new_group([s * cp_n + c for c in range(cp_n)]) for s in range(ws // cp_n)]
+    pp_groups = [dist.new_group([s * cp_n + c for s in range(ws // cp_n)]) for c in range(cp_n)]
+    full = _model()
+    pp = copy.deepcopy(full)
+    torch.manual_seed(9)
+    micro = [_ids(1, 32, vocab=full.cfg.vocab_size) for _ in range(3)]
+    ref_losses = []
+    for ids in micro:
+        h, _ = full.backbone(ids)
+        loss = default_lm_loss(full, h, ids)
+        (loss / len(micro)).backward()
+        ref_losses.append(loss.detach())
+    stage = PipelineStage(pp, pp_groups[rank % cp_n], cp_group=cp_groups[rank // cp_n])
+    out = run_1f1b(stage, micro)
+    sync_cp_grads(stage)
+    sync_tied_embedding(stage)
+    ok = []
+    if stage.last:
+        tot = out.detach().clone()
+        dist.all_reduce(tot, group=stage.cp_group)
+        ok.append(_close(tot, torch.stack(ref_losses).mean(), 1e-5))
+    fp = dict(full.named_parameters())
+    own = [f"blocks.{i}." for i in range(stage.lo, stage.hi)]
+    for n, p in pp.named_parameters():
+        mine = any(n.startswith(o) for o in own) or (n.startswith("embed.") and (stage.first or stage.last)) or \
+            (n.startswith("final_norm.") and stage.last)
+        if mine and fp[n].grad is not None:
+            ok.append(_close(p.grad, fp[n].grad))
+    return rank, all(ok), len(ok)
+
+
+def test_pipeline_with_context_parallel_stages():
+    """PP=2 x CP=2 on 4 gloo ranks: each stage's sequence split over its CP pair, 1F1B between
+    the stages; losses and every owned gradient equal one process."""
+    res = _run(_pp_cp, ws=4)
     for r in res:
         assert r[1] is True and r[2] > 5, r
 

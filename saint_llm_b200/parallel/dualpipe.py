@@ -30,6 +30,12 @@ waits of the same kind for even earlier ticks.
 
 Gradients accumulate in the parameters as with ``run_1f1b`` (each micro-batch's loss is
 divided by ``M``); the result equals the non-pipelined step.
+
+Context parallelism inside the chunks (``cp_group``) works as in ``parallel.pipeline``: each
+chunk's sequence is this rank's CP shard, the loss on rank 0 is the shard's share
+(``cp_lm_share``), and ``pipeline.sync_cp_grads(pipe)`` sums the gradients over the CP group
+afterwards.  The CP ranks of one pipeline rank follow the same timetable, so their attention
+collectives pair up.
 """
 
 from __future__ import annotations
@@ -42,7 +48,7 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from saint_llm_b200.models.mhc import MHC
-from saint_llm_b200.parallel.pipeline import aux_losses, default_lm_loss, stage_bounds
+from saint_llm_b200.parallel.pipeline import aux_losses, cp_lm_share, default_lm_loss, stage_bounds
 
 
 @dataclass(frozen=True)
@@ -121,8 +127,10 @@ def messages(row: list[Op | None], n_ranks: int) -> list[tuple[int, int, str, in
 class DualPipeV:
     """One rank's two chunks of ``model`` (``prune=True`` drops the other ranks' blocks)."""
 
-    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None = None, *, prune: bool = False) -> None:
+    def __init__(self, model: nn.Module, group: dist.ProcessGroup | None = None, *, prune: bool = False,
+                 cp_group: dist.ProcessGroup | None = None) -> None:
         self.model, self.group = model, group
+        self.cp_group = cp_group
         self.rank = dist.get_rank(group)
         self.P = dist.get_world_size(group)
         n_layers = len(model.blocks)  # type: ignore[arg-type]
@@ -136,22 +144,40 @@ class DualPipeV:
     def _peer(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
+    def local_ids(self, ids: Tensor) -> Tensor:
+        if self.cp_group is None:
+            return ids
+        from saint_llm_b200.parallel.cp import cp_shard
+
+        return cp_shard(ids, self.cp_group)
+
     def _forward(self, v: int, ids: Tensor, x: Tensor | None) -> Tensor:
         m = self.model
+        local = self.local_ids(ids)
         if v == 0:
-            x = MHC.expand(m._embed_inputs(ids, None, None), m.cfg.mhc.expansion_factor)  # type: ignore[attr-defined]
-        vis = ids == m.cfg.tokenizer_slots.image_pad  # type: ignore[attr-defined]
+            x = MHC.expand(m._embed_inputs(local, None, None), m.cfg.mhc.expansion_factor)  # type: ignore[attr-defined]
+        vis = local == m.cfg.tokenizer_slots.image_pad  # type: ignore[attr-defined]
+        bundle = None
+        if self.cp_group is not None:
+            from saint_llm_b200.parallel.cp import CPBundle
+
+            bundle = CPBundle(m, self.cp_group, local.shape[1])
         lo, hi = self.bounds[v]
         for j in range(lo, hi):
-            x = m.blocks[j](x, token_ids=ids, is_visual=vis)  # type: ignore[index]
+            view = bundle.for_layer(j) if bundle is not None else None
+            x = m.blocks[j](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
         assert x is not None
         return x
 
 
 def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
-                 loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor] = default_lm_loss,
+                 loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor] | None = None,
                  aux_weight: float = 0.0) -> Tensor | None:
-    """One DualPipe-V forward+backward over ``micro_ids``; returns the mean loss on rank 0."""
+    """One DualPipe-V forward+backward over ``micro_ids``; returns the mean loss on rank 0
+    (with CP: this rank's share of it).  ``loss_fn`` defaults to ``default_lm_loss``
+    (``cp_lm_share`` with a CP group)."""
+    if loss_fn is None:
+        loss_fn = default_lm_loss if pipe.cp_group is None else cp_lm_share(pipe.cp_group)
     m = pipe.model
     P, S, M, rank = pipe.P, 2 * pipe.P, len(micro_ids), pipe.rank
     cfg = m.cfg  # type: ignore[attr-defined]
@@ -181,7 +207,7 @@ def run_dualpipe(pipe: DualPipeV, micro_ids: list[Tensor], *,
     dist.barrier(group=pipe.group)  # every rank's communicator exists before the first grouped p2p
 
     def shape(i: int) -> tuple[int, ...]:
-        ids = micro_ids[i]
+        ids = pipe.local_ids(micro_ids[i])
         return (ids.shape[0], ids.shape[1], cfg.mhc.expansion_factor, cfg.hidden_dim)
 
     for row in ticks:

@@ -322,6 +322,49 @@ def _dualpipe(rank, ws):
     return rank, all(ok), len(ok)
 
 
+def _dualpipe_cp(rank, ws):
+    """DualPipe-V over 2 pipeline ranks, each chunk's sequence split over a CP pair."""
+    from saint_llm_b200.parallel.dualpipe import DualPipeV, run_dualpipe
+    from saint_llm_b200.parallel.pipeline import default_lm_loss, sync_cp_grads
+
+    cp_n = 2
+    cp_groups = [dist.new_group([s * cp_n + c for c in range(cp_n)]) for s in range(ws // cp_n)]
+    pp_groups = [dist.new_group([s * cp_n + c for s in range(ws // cp_n)]) for c in range(cp_n)]
+    full = _model()
+    pp = copy.deepcopy(full)
+    torch.manual_seed(9)
+    micro = [_ids(1, 32, vocab=full.cfg.vocab_size) for _ in range(4)]
+    micro[1][:, 20:22] = full.cfg.tokenizer_slots.image_pad
+    ref_losses = []
+    for ids in micro:
+        h, _ = full.backbone(ids)
+        loss = default_lm_loss(full, h, ids)
+        (loss / len(micro)).backward()
+        ref_losses.append(loss.detach())
+    pipe = DualPipeV(pp, pp_groups[rank % cp_n], cp_group=cp_groups[rank // cp_n])
+    out = run_dualpipe(pipe, micro)
+    sync_cp_grads(pipe)
+    ok = []
+    if pipe.rank == 0:
+        tot = out.detach().clone()
+        dist.all_reduce(tot, group=pipe.cp_group)
+        ok.append(_close(tot, torch.stack(ref_losses).mean(), 1e-5))
+    fp = dict(full.named_parameters())
+    own = [f"blocks.{i}." for lo, hi in pipe.bounds.values() for i in range(lo, hi)]
+    for n, p in pp.named_parameters():
+        mine = any(n.startswith(o) for o in own) or (pipe.rank == 0 and n.startswith(("embed.", "final_norm.")))
+        if mine and fp[n].grad is not None:
+            ok.append(p.grad is not None and _close(p.grad, fp[n].grad))
+    return rank, all(ok), len(ok)
+
+
+def test_dualpipe_v_with_context_parallel_chunks():
+    """DualPipe-V (2 pipeline ranks) x CP=2 on 4 gloo ranks equals one process."""
+    res = _run(_dualpipe_cp, ws=4)
+    for r in res:
+        assert r[1] is True and r[2] > 5, r
+
+
 @pytest.mark.parametrize("ws", [2, 4])
 def test_dualpipe_v_matches_single_process(ws):
     res = _run(_dualpipe, ws)

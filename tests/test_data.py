@@ -8,7 +8,6 @@ import torch
 
 from saint_llm_b200.data import (
     CharTokenizer,
-    ChatTemplate,
     ChatTurn,
     CorpusSlice,
     MixedCorpus,

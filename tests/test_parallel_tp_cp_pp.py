@@ -419,3 +419,20 @@ def test_parallel_layouts_on_gpus_over_nccl(name):
     res = _run(fn, 2, nccl=True)
     for r in res:
         assert r[1] is True, r
+
+
+_four_gpus = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4,
+                                reason="needs 4 GPUs")
+
+
+@pytest.mark.gpu
+@_four_gpus
+@pytest.mark.parametrize("name", ["pp_cp", "dualpipe_cp"])
+def test_pipeline_with_context_parallel_on_four_gpus(name):
+    """Config 4's PP x CP layout (2 pipeline ranks x CP=2) over NCCL on four GPUs against one
+    process (NVLS off)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    fn = {"pp_cp": _pp_cp, "dualpipe_cp": _dualpipe_cp}[name]
+    res = _run(fn, 4, nccl=True)
+    for r in res:
+        assert r[1] is True, r

@@ -43,11 +43,28 @@ def _slice_like(ref: torch.Tensor, p: torch.Tensor, n: str, tp_rank: int, ep_ran
     raise AssertionError(f"unexpected shape for {n}: {tuple(p.shape)} vs {tuple(ref.shape)}")
 
 
-def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, micro: int, q) -> None:
+def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, micro: int, q,
+            nccl: bool = False) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.set_num_threads(2)  # four ranks share the host's cores
-    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    if nccl:  # one GPU per rank, NCCL collectives, the model's math on the eager fp32 path
+        import datetime
+
+        from saint_llm_b200.ops import backend
+
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        ctx = backend.eager_mode(True)
+    else:
+        import contextlib
+
+        dev = torch.device("cpu")
+        dist.init_process_group("gloo", rank=rank, world_size=ws)
+        ctx = contextlib.nullcontext()
+    ctx.__enter__()
     try:
         from saint_llm_b200.config import ModelConfig
         from saint_llm_b200.models import SaintLLM
@@ -58,14 +75,14 @@ def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, m
 
         cfg = ModelConfig.tiny().model_copy(update={"moe_use_grouped_gemm": True})
         torch.manual_seed(0)
-        ref = SaintLLM(cfg)
+        ref = SaintLLM(cfg).to(dev)
         model = copy.deepcopy(ref)
         replicas = ws // tp
         torch.manual_seed(11)
-        data = [torch.randint(0, cfg.vocab_size, (micro, 2, 16)) for _ in range(replicas)]
+        data = [torch.randint(0, cfg.vocab_size, (micro, 2, 16)).to(dev) for _ in range(replicas)]
         init = {n: p.detach().clone() for n, p in ref.named_parameters()}
         rp = attach_main_grads(ref)
-        ropt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, qk_clip_enabled=False)
+        ropt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, qk_clip_enabled=False, ns_impl="reference")
         rstep = TrainStep(ref, ropt, micro_batches=1, params=rp)
         for d in data:
             for i in range(micro):
@@ -75,7 +92,7 @@ def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, m
 
         sync, lay = setup_tp_ep(model, tp, transport="nccl", zero=zero, overlap_reduce=overlap)
         params = attach_main_grads(model)
-        opt = MuonAdamW(*split_for_muon_adamw(model), lr=0.02, qk_clip_enabled=False)
+        opt = MuonAdamW(*split_for_muon_adamw(model), lr=0.02, qk_clip_enabled=False, ns_impl="reference")
         sync.configure_optimizer(opt)
         step = TrainStep(model, opt, micro_batches=micro, params=params, grad_sync=sync)
         # the synchronised gradients, as the optimizer sees them (Muon and AdamW updates are
@@ -113,16 +130,30 @@ def _worker(rank: int, ws: int, tp: int, port: int, zero: bool, overlap: bool, m
     except Exception as e:  # noqa: BLE001
         q.put((rank, f"error: {type(e).__name__}: {e}"))
     finally:
+        ctx.__exit__(None, None, None)
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("zero,overlap,micro", [(False, False, 1), (True, False, 1), (True, True, 2)])
 def test_tp_ep_step_matches_single_process(zero, overlap, micro):
+    _check_tp_ep_step(zero, overlap, micro, nccl=False)
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_tp_ep_step_over_nccl_on_four_gpus():
+    """The same layout with NCCL collectives on four GPUs (TP and EP over NCCL, ZeRO with the
+    NCCL transport; NVLS off, as for every multi-GPU test)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    _check_tp_ep_step(True, True, 2, nccl=True)
+
+
+def _check_tp_ep_step(zero, overlap, micro, *, nccl):
     ws, tp = 4, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, ws, tp, port, zero, overlap, micro, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, tp, port, zero, overlap, micro, q, nccl)) for r in range(ws)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(ws)]

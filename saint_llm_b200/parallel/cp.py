@@ -153,21 +153,50 @@ def cp_shard(ids: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
     return ids[:, r * t:(r + 1) * t]
 
 
-def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
+def _ce_share(model: nn.Module, h: Tensor, ids: Tensor, start: int, shift: int) -> Tensor:
+    """Sum of CE(logits(h[:, j]), ids[:, start + j + shift]) over the local positions j whose
+    target exists, divided by the global count B * (T - shift): this shard's share of the
+    mean next-``shift``-token loss."""
+    b, t = ids.shape
+    n = max(0, min(h.shape[1], t - shift - start))
+    if n == 0:
+        return h.sum() * 0.0  # keeps the graph (and the CP collectives' backward) on every rank
+    logits = model.logits(h[:, :n]).float()  # type: ignore[attr-defined]
+    tgt = ids[:, start + shift:start + shift + n]
+    ce = torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1), reduction="sum")
+    return ce / (b * (t - shift))
+
+
+def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = None, *,
+               mtp: bool = False) -> Tensor:
     """Next-token cross-entropy of the full sequence ``ids`` (B, T) computed with its tokens
     sharded over ``group``; returns this rank's share of the global mean (the sum over
-    ranks is the loss)."""
+    ranks is the loss).
+
+    ``mtp``: add the multi-token-prediction heads' weighted losses (the training loss of
+    ``train.losses.cross_entropy_with_mtp`` without the balance term).  Head k combines the
+    hidden state at position p with the embedding of token p + k + 1, which for a shard's
+    last positions lies in the next shard: every rank holds all token ids, so it embeds the
+    few it needs itself and the heads need no communication."""
     r, ws = dist.get_rank(group), dist.get_world_size(group)
     b, t = ids.shape
     tl = t // ws
-    local = ids[:, r * tl:(r + 1) * tl]
+    start = r * tl
+    local = ids[:, start:start + tl]
     h, _ = model.backbone(local, kv_cache_bundle=CPBundle(model, group, tl))  # type: ignore[attr-defined]
-    logits = model.logits(h).float()  # type: ignore[attr-defined]
-    tgt = ids[:, r * tl + 1:(r + 1) * tl + 1]
-    n = tgt.shape[1]
-    loss = torch.nn.functional.cross_entropy(logits[:, :n].reshape(-1, logits.shape[-1]), tgt.reshape(-1),
-                                             reduction="sum")
-    return loss / (b * (t - 1))
+    loss = _ce_share(model, h, ids, start, 1)
+    depth = model.cfg.mtp.depth if mtp else 0  # type: ignore[attr-defined]
+    if depth > 0:
+        from saint_llm_b200.train.losses import mtp_weight
+
+        ahead = ids[:, start:min(t, start + tl + depth)]
+        emb = model._embed_inputs(ahead, None, None)  # type: ignore[attr-defined]
+        emb = torch.nn.functional.pad(emb, (0, 0, 0, tl + depth - emb.shape[1]))  # zeros past the end
+        cur = h
+        for k, mod in enumerate(model.mtp.modules_):  # type: ignore[attr-defined]
+            cur = mod(cur, emb[:, k + 1:k + 1 + tl])
+            loss = loss + mtp_weight(model.cfg.mtp, k) * _ce_share(model, cur, ids, start, k + 2)  # type: ignore[attr-defined]
+    return loss
 
 
 __all__ = ["CPBundle", "CPLayerView", "cp_lm_loss", "cp_shard", "gather_stack"]

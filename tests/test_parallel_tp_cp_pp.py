@@ -154,6 +154,41 @@ def _cp(rank, ws):
     return rank, True
 
 
+def _cp_mtp(rank, ws):
+    """The CP training loss with the MTP heads equals the single-process main + MTP loss."""
+    from saint_llm_b200.parallel.cp import cp_lm_loss
+    from saint_llm_b200.train.losses import cross_entropy_with_mtp
+
+    full = _model()
+    cp = copy.deepcopy(full)
+    torch.manual_seed(8)
+    ids = _ids(2, 64, vocab=full.cfg.vocab_size)
+    ref = cross_entropy_with_mtp(full(ids), ids, cfg=full.cfg.mtp)
+    ref.backward()
+    loss = cp_lm_loss(cp, ids, mtp=True)
+    loss.backward()
+    tot = loss.detach().clone()
+    dist.all_reduce(tot)
+    if not _close(tot, ref.detach(), 1e-5):
+        return rank, f"loss {tot.item()} vs {ref.item()}"
+    fp = dict(full.named_parameters())
+    n = 0
+    for name, p in cp.named_parameters():
+        g = p.grad if p.grad is not None else torch.zeros_like(p)
+        dist.all_reduce(g)
+        ref_g = fp[name].grad if fp[name].grad is not None else torch.zeros_like(p)
+        if not _close(g, ref_g):
+            return rank, f"grad {name} max err {(g - ref_g).abs().max().item()}"
+        n += name.startswith("mtp.")
+    return rank, n > 0
+
+
+def test_context_parallel_loss_with_mtp_heads():
+    res = _run(_cp_mtp)
+    for r in res:
+        assert r[1] is True, r
+
+
 def test_context_parallel_two_ranks():
     res = _run(_cp)
     for r in res:

@@ -308,6 +308,8 @@ class RunConfig(_Frozen):
     cp: int = 1
     pp: int = 1
     zero: ParallelMode = "dp"
+    # pipeline schedule with pp > 1: one-forward-one-backward, or the V-shaped DualPipe-V
+    pp_schedule: Literal["1f1b", "dualpipe"] = "1f1b"
     # precision
     compute_dtype: Literal["bfloat16", "float32"] = "bfloat16"
     param_dtype: Literal["bfloat16", "float32"] = "bfloat16"

@@ -88,7 +88,11 @@ class CPLayerView:
         if compressor is not None:
             parts.append(compressor(h))
             if indexer_compressor is not None:
-                parts.append(indexer_compressor(h))
+                # the indexer's keys only choose blocks (top-k has no gradient); without the
+                # no-grad they would still receive zeros through the packed gather and the
+                # optimizer would decay weights the unsharded model leaves untouched
+                with torch.no_grad():
+                    parts.append(indexer_compressor(h))
             if visual:  # the fraction of image tokens per local block, gathered with the entries
                 m = indexer_compressor.m
                 nb = h.shape[1] // m
@@ -179,11 +183,19 @@ def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = 
     last positions lies in the next shard: every rank holds all token ids, so it embeds the
     few it needs itself and the heads need no communication."""
     r, ws = dist.get_rank(group), dist.get_world_size(group)
-    b, t = ids.shape
-    tl = t // ws
+    tl = ids.shape[1] // ws
     start = r * tl
     local = ids[:, start:start + tl]
     h, _ = model.backbone(local, kv_cache_bundle=CPBundle(model, group, tl))  # type: ignore[attr-defined]
+    return shard_loss(model, h, ids, start, mtp=mtp)
+
+
+def shard_loss(model: nn.Module, h: Tensor, ids: Tensor, start: int, *, mtp: bool = False) -> Tensor:
+    """This shard's share of the training loss from its final-normed hidden states ``h``
+    (positions ``start ..``) and the full token ids: main next-token CE, plus (``mtp``) the
+    MTP heads' weighted CEs.  Summed over the shards it is the loss of the whole sequence."""
+    b, t = ids.shape
+    tl = h.shape[1]
     loss = _ce_share(model, h, ids, start, 1)
     depth = model.cfg.mtp.depth if mtp else 0  # type: ignore[attr-defined]
     if depth > 0:
@@ -199,4 +211,4 @@ def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = 
     return loss
 
 
-__all__ = ["CPBundle", "CPLayerView", "cp_lm_loss", "cp_shard", "gather_stack"]
+__all__ = ["CPBundle", "CPLayerView", "cp_lm_loss", "cp_shard", "gather_stack", "shard_loss"]

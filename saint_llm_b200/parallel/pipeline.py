@@ -132,12 +132,30 @@ def cp_lm_share(group: dist.ProcessGroup | None) -> Callable[[nn.Module, Tensor,
 @torch.no_grad()
 def sync_cp_grads(stage: PipelineStage) -> None:
     """Sum the stage's parameter gradients over its CP group (each rank's are the share of
-    its own tokens)."""
+    its own tokens).  A parameter can have a gradient on one shard and none on another (an
+    expert no token of that shard was routed to), so the ranks first agree on which
+    parameters take part; those nobody touched keep no gradient (the optimizer skips them)."""
     if stage.cp_group is None:
         return
-    for p in stage.model.parameters():
-        if p.grad is not None:
-            dist.all_reduce(p.grad, group=stage.cp_group)
+    params = [p for p in stage.model.parameters() if p.requires_grad]
+    if not params:
+        return
+    dev = params[0].device
+    used = torch.tensor([p.grad is not None for p in params], dtype=torch.int32, device=dev)
+    dist.all_reduce(used, group=stage.cp_group)
+    grads = []
+    for p, u in zip(params, used.tolist(), strict=True):
+        if u:
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+            grads.append(p.grad)
+    if grads:
+        flat = torch.cat([g.reshape(-1).float() for g in grads])
+        dist.all_reduce(flat, group=stage.cp_group)
+        off = 0
+        for g in grads:
+            g.copy_(flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
 
 
 def run_1f1b(stage: PipelineStage, micro_ids: list[Tensor], *,

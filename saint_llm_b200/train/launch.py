@@ -37,9 +37,10 @@ What each ``RunConfig`` field selects here:
   the whole group and (hybrid ZeRO) data parallelism over the ``world / tp`` replicas
   (``parallel.tp_ep``); the ranks of one TP group must be fed the same batch
   (``TrainingJob.replica`` names it).  ``fused_tp`` selects the peer-memory TP kernels.
-* ``cp`` / ``pp``: context and pipeline parallelism have their own drivers (``parallel.cp`` /
-  ``parallel.pipeline`` / ``parallel.dualpipe``); this builder accepts only 1 for them and
-  says so.
+* ``pp`` / ``cp`` (with ``ep = tp = 1``, ``world = pp x cp``): config 4's layout -- the block
+  stack in ``pp`` pipeline stages (``pp_schedule``: 1F1B or DualPipe-V), each sequence split
+  over the ``cp`` ranks of a stage; the step is ``train.pipeline_step.PipelineTrainStep``
+  (main + MTP loss) and every rank reads the same batch.
 """
 
 from __future__ import annotations
@@ -75,6 +76,9 @@ class TrainingJob:
         from saint_llm_b200.parallel.state import gather_full_state_dict
         from saint_llm_b200.train.checkpoint import save_sharded
 
+        if self.run.pp > 1:
+            raise NotImplementedError("checkpoints of pipeline-parallel jobs are not supported (each rank "
+                                      "holds only its stage's blocks)")
         world, rank = _world_rank()
         full = gather_full_state_dict(self.model) if world > 1 else self.model.state_dict()
         opt_state = self.optimizer.state_dict()
@@ -165,9 +169,11 @@ class _EagerStep:
 
 def _check(run: RunConfig, world: int) -> None:
     problems = []
-    for dim in ("cp", "pp"):
-        if getattr(run, dim) != 1:
-            problems.append(f"{dim}={getattr(run, dim)} (use the parallel.{dim} driver)")
+    if run.pp > 1 or run.cp > 1:
+        if run.pp * run.cp != world:
+            problems.append(f"pp x cp = {run.pp} x {run.cp} must equal the world size {world}")
+        if run.ep != 1 or run.tp != 1:
+            problems.append("pipeline / context parallelism runs with ep = tp = 1")
     if run.ep not in (1, world):
         problems.append(f"ep={run.ep} must be 1 or the world size {world}")
     if run.tp < 1 or world % run.tp:
@@ -208,6 +214,8 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
     for mod in model.modules():
         if hasattr(mod, "gate_weight") and hasattr(mod, "linear_quant"):
             mod.fp8_weight_cache = run.fp8_expert_cache
+    if run.pp > 1 or run.cp > 1:
+        return _build_pipeline(model, run, group, qk_clip)
     grad_sync = None
     replica, replicas = (dist.get_rank(group), world) if world > 1 else (0, 1)
     if world > 1:
@@ -238,4 +246,41 @@ def build_training(model_cfg: ModelConfig, run: RunConfig, device: torch.device,
     return TrainingJob(model, opt, wrapped, grad_sync, run, replica, replicas)
 
 
-__all__ = ["TrainingJob", "build_training", "init_distributed"]
+def pp_cp_groups(pp: int, cp: int, group: dist.ProcessGroup | None = None
+                 ) -> tuple[dist.ProcessGroup | None, dist.ProcessGroup | None]:
+    """(pipeline group, CP group) of this rank: rank r is CP rank r % cp of pipeline rank
+    r // cp.  Every rank of ``group`` calls this (new groups are created collectively)."""
+    rank = dist.get_rank(group)
+    glob = [dist.get_global_rank(group, r) if group is not None else r for r in range(pp * cp)]
+    pp_group = cp_group = None
+    for c in range(cp):
+        g = dist.new_group([glob[s * cp + c] for s in range(pp)])
+        if rank % cp == c:
+            pp_group = g
+    for s in range(pp):
+        g = dist.new_group([glob[s * cp + c] for c in range(cp)])
+        if rank // cp == s:
+            cp_group = g
+    return pp_group, cp_group
+
+
+def _build_pipeline(model: nn.Module, run: RunConfig, group: dist.ProcessGroup | None, qk_clip: bool) -> TrainingJob:
+    from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
+    from saint_llm_b200.parallel.dualpipe import DualPipeV
+    from saint_llm_b200.parallel.pipeline import PipelineStage
+    from saint_llm_b200.train.pipeline_step import PipelineTrainStep
+
+    pp_group, cp_group = pp_cp_groups(run.pp, run.cp, group)
+    # the stage drops the other stages' blocks before the optimizer sees any parameter
+    stage = (DualPipeV(model, pp_group, prune=True, cp_group=cp_group) if run.pp_schedule == "dualpipe"
+             else PipelineStage(model, pp_group, prune=True, cp_group=cp_group))
+    muon, adamw = split_for_muon_adamw(model)
+    layers = [b.attention for b in model.blocks if hasattr(b, "attention")]  # type: ignore[attr-defined]
+    opt = MuonAdamW(muon, adamw, lr=run.lr, adamw_lr=run.adamw_lr, qk_clip_enabled=qk_clip,
+                    qk_clip_layers=layers if qk_clip else None)
+    step = PipelineTrainStep(model, opt, micro_batches=run.grad_accum, pp_group=pp_group, cp_group=cp_group,
+                             schedule=run.pp_schedule, stage=stage)
+    return TrainingJob(model, opt, step, None, run, 0, 1)
+
+
+__all__ = ["TrainingJob", "build_training", "init_distributed", "pp_cp_groups"]

@@ -471,3 +471,71 @@ def test_pipeline_with_context_parallel_on_four_gpus(name):
     res = _run(fn, 4, nccl=True)
     for r in res:
         assert r[1] is True, r
+
+
+def _pp_cp_job(rank, ws):
+    """``build_training`` with RunConfig(pp=2, cp=2) on 4 ranks (1F1B, then DualPipe-V): one
+    step equals one process stepping on the main + MTP loss of the same micro-batches."""
+    from saint_llm_b200.config import ModelConfig, RunConfig
+    from saint_llm_b200.models import SaintLLM
+    from saint_llm_b200.optim import MuonAdamW, split_for_muon_adamw
+    from saint_llm_b200.train.launch import build_training
+    from saint_llm_b200.train.losses import make_loss_fn
+
+    cfg = ModelConfig.tiny()
+    torch.manual_seed(4)
+    batch = torch.randint(0, cfg.vocab_size, (2, 1, 32))
+    torch.manual_seed(0)
+    ref = SaintLLM(cfg)
+    opt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, adamw_lr=3e-3, qk_clip_enabled=False)
+    loss_fn = make_loss_fn(cfg.mtp, fused=False)
+    want = 0.0
+    for i in range(2):
+        loss = loss_fn(ref, batch[i]) / 2
+        loss.backward()
+        want += float(loss.detach())
+    ref_grads = {n: p.grad.clone() for n, p in ref.named_parameters() if p.grad is not None}
+    init = {n: p.detach().clone() for n, p in ref.named_parameters()}
+    opt.step()
+    refp = dict(ref.named_parameters())
+    out = []
+    for schedule in ("1f1b", "dualpipe"):
+        run = RunConfig(pp=2, cp=2, pp_schedule=schedule, grad_accum=2, micro_batch=1, seq_len=32, lr=0.02,
+                        adamw_lr=3e-3, seed=0, param_dtype="float32", compute_dtype="float32")
+        job = build_training(cfg, run, torch.device("cpu"), qk_clip=False)
+        grads: dict = {}
+        real_step = job.optimizer.step
+
+        def step_and_record(*a, _g=grads, _m=job.model, _s=real_step, **k):  # the synchronised gradients
+            _g.update({n: p.grad.clone() for n, p in _m.named_parameters() if p.grad is not None})
+            return _s(*a, **k)
+
+        job.optimizer.step = step_and_record
+        got = job.step(batch)
+        # the weights this rank updated (its blocks, and the ends it holds) match; the rest
+        # of its model copy is untouched
+        mine = [f"blocks.{i}." for i in range(len(job.model.blocks)) if hasattr(job.model.blocks[i], "attention")]
+        first = job.step.stage.first if schedule == "1f1b" else job.step.stage.rank == 0
+        last = job.step.stage.last if schedule == "1f1b" else job.step.stage.rank == 0
+        owned = [n for n, _ in job.model.named_parameters()
+                 if any(n.startswith(o) for o in mine) or (n.startswith("embed.") and (first or last))
+                 or (n.startswith(("final_norm.", "mtp.")) and last)]
+        cur = dict(job.model.named_parameters())
+        # gradients: exact up to summation order (floor: cancelling sums such as the mHC biases')
+        g_worst = max(float((grads[n] - ref_grads[n]).abs().max() / ref_grads[n].abs().max().clamp(min=1e-5))
+                      for n in owned if n in ref_grads)
+        # weights: Newton-Schulz amplifies that noise for experts that saw few tokens (low-rank
+        # gradients); a wrong reduction or a missed update would be off by the whole move
+        w_ok = all(float((cur[n].detach() - refp[n].detach()).abs().max())
+                   <= 5e-2 * float((refp[n].detach() - init[n]).abs().max()) + 2e-5 for n in owned)
+        n_blocks = sum(1 for b in job.model.blocks if hasattr(b, "attention"))
+        out.append((abs(got - want) < 1e-5, g_worst < 1e-3 and w_ok and set(grads) <= set(ref_grads), n_blocks))
+    return rank, out
+
+
+def test_build_training_pipeline_and_context_parallel():
+    res = _run(_pp_cp_job, ws=4)
+    for r in res:
+        assert isinstance(r[1], list), r
+        for ok_loss, ok_weights, n_blocks in r[1]:
+            assert ok_loss and ok_weights and n_blocks == 2, r

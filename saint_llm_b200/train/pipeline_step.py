@@ -13,6 +13,10 @@ left out: its per-sequence statistics would need an exchange of their own); grad
 summed over the CP group and the tied embedding's over its two pipeline ends; the
 attention-logit telemetry is max-reduced over the CP group (MuonClip acts on the same
 value on every shard); then the optimizer updates the parameters this rank holds.
+
+Gradients accumulate in the parameters' ``.grad`` (the parameter dtype: fp32 parameters keep
+fp32 sums; with bf16 parameters the micro-batch sums are bf16, unlike ``TrainStep``'s fp32
+``main_grad`` buffers).
 """
 
 from __future__ import annotations

@@ -279,7 +279,7 @@ def _build_pipeline(model: nn.Module, run: RunConfig, group: dist.ProcessGroup |
     opt = MuonAdamW(muon, adamw, lr=run.lr, adamw_lr=run.adamw_lr, qk_clip_enabled=qk_clip,
                     qk_clip_layers=layers if qk_clip else None)
     step = PipelineTrainStep(model, opt, micro_batches=run.grad_accum, pp_group=pp_group, cp_group=cp_group,
-                             schedule=run.pp_schedule, stage=stage)
+                             schedule=run.pp_schedule, stage=stage, group=group)
     return TrainingJob(model, opt, step, None, run, 0, 1)
 
 

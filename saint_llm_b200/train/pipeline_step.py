@@ -29,7 +29,9 @@ from torch import Tensor, nn
 class PipelineTrainStep:
     def __init__(self, model: nn.Module, optimizer: torch.optim.Optimizer, *, micro_batches: int,
                  pp_group: dist.ProcessGroup | None, cp_group: dist.ProcessGroup | None,
-                 schedule: str = "1f1b", mtp: bool = True, stage: object | None = None) -> None:
+                 schedule: str = "1f1b", mtp: bool = True, stage: object | None = None,
+                 group: dist.ProcessGroup | None = None) -> None:
+        """``group``: all ``pp x cp`` ranks of the job (the default group when None)."""
         from saint_llm_b200.parallel.dualpipe import DualPipeV
         from saint_llm_b200.parallel.pipeline import PipelineStage
 
@@ -37,7 +39,7 @@ class PipelineTrainStep:
             raise ValueError(f"unknown pipeline schedule {schedule!r}")
         self.model, self.optimizer = model, optimizer
         self.micro_batches, self.schedule, self.mtp = micro_batches, schedule, mtp
-        self.cp_group = cp_group
+        self.cp_group, self.group = cp_group, group
         self.device = next(model.parameters()).device
         if stage is not None:
             self.stage = stage
@@ -86,7 +88,7 @@ class PipelineTrainStep:
         total = (out.detach().float().reshape(()) if out is not None
                  else torch.zeros((), dtype=torch.float32, device=self.device)).clone()
         if dist.is_initialized():
-            dist.all_reduce(total)
+            dist.all_reduce(total, group=self.group)
         return total
 
     def __call__(self, host_tokens: Tensor) -> float:

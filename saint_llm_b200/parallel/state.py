@@ -114,4 +114,31 @@ def load_full_state_dict(model: nn.Module, full: dict[str, Tensor], *, strict: b
     model.load_state_dict(local, strict=strict)
 
 
-__all__ = ["gather_full_state_dict", "load_full_state_dict"]
+@torch.no_grad()
+def gather_pipeline_state_dict(model: nn.Module, stage: object) -> dict[str, Tensor]:
+    """The full state dict of a model split into pipeline stages (``parallel.pipeline`` /
+    ``parallel.dualpipe``, blocks of other stages dropped), on the CPU, on every rank
+    (collective over the pipeline group).  Each block comes from the stage that holds it; the
+    input embedding from the first stage, everything else outside the blocks (final norm, MTP
+    heads, LM head) from the stage that computes the loss, which is where they are updated.
+    ``load_full_state_dict`` loads the result back into any stage."""
+    group = stage.group  # type: ignore[attr-defined]
+    n = dist.get_world_size(group)
+    mine = {k: v.detach().cpu() for k, v in model.state_dict().items()}
+    parts: list = [None] * n
+    dist.all_gather_object(parts, mine, group=group)
+    dual = hasattr(stage, "bounds")  # DualPipe-V: both ends live on pipeline rank 0
+    first, last = 0, (0 if dual else n - 1)
+    full: dict[str, Tensor] = {}
+    for r, sd in enumerate(parts):
+        for k, v in sd.items():
+            if k.startswith("blocks."):
+                full.setdefault(k, v)
+            elif k.startswith("embed.") and r == first:
+                full[k] = v
+            elif not k.startswith("embed.") and r == last:
+                full[k] = v
+    return full
+
+
+__all__ = ["gather_full_state_dict", "gather_pipeline_state_dict", "load_full_state_dict"]

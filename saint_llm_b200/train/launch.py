@@ -76,11 +76,13 @@ class TrainingJob:
         from saint_llm_b200.parallel.state import gather_full_state_dict
         from saint_llm_b200.train.checkpoint import save_sharded
 
-        if self.run.pp > 1:
-            raise NotImplementedError("checkpoints of pipeline-parallel jobs are not supported (each rank "
-                                      "holds only its stage's blocks)")
         world, rank = _world_rank()
-        full = gather_full_state_dict(self.model) if world > 1 else self.model.state_dict()
+        if self.run.pp > 1 or self.run.cp > 1:
+            from saint_llm_b200.parallel.state import gather_pipeline_state_dict
+
+            full = gather_pipeline_state_dict(self.model, self.step.stage)  # type: ignore[attr-defined]
+        else:
+            full = gather_full_state_dict(self.model) if world > 1 else self.model.state_dict()
         opt_state = self.optimizer.state_dict()
         extra = {**(extra or {}), "layout": self._layout(world)}
         if rank != 0:
@@ -116,7 +118,8 @@ class TrainingJob:
         return int(data["step"])
 
     def _layout(self, world: int) -> dict:
-        return {"world": world, "tp": self.run.tp, "ep": self.run.ep, "zero": self.run.zero}
+        return {"world": world, "tp": self.run.tp, "ep": self.run.ep, "zero": self.run.zero, "pp": self.run.pp,
+                "cp": self.run.cp, "pp_schedule": self.run.pp_schedule}
 
     def close(self) -> None:
         """Collective release of the expert-parallel peer buffers (call on every rank)."""

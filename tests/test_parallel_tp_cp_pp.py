@@ -529,11 +529,25 @@ def _pp_cp_job(rank, ws):
         w_ok = all(float((cur[n].detach() - refp[n].detach()).abs().max())
                    <= 5e-2 * float((refp[n].detach() - init[n]).abs().max()) + 2e-5 for n in owned)
         n_blocks = sum(1 for b in job.model.blocks if hasattr(b, "attention"))
-        out.append((abs(got - want) < 1e-5, g_worst < 1e-3 and w_ok and set(grads) <= set(ref_grads), n_blocks))
+        # a checkpoint of the pipeline job holds the whole model; a job built with other
+        # weights loads its own stage back from it
+        path = os.path.join(os.environ["SV4_TEST_CKPT_DIR"], schedule)
+        job.save(path, step=1)
+        from saint_llm_b200.train.checkpoint import load_sharded
+
+        saved = load_sharded(path, rank=rank)["model"]
+        other = build_training(cfg, run.model_copy(update={"seed": 7}), torch.device("cpu"), qk_clip=False)
+        other.load(path)
+        theirs = dict(other.model.named_parameters())
+        same = all(torch.equal(theirs[n].detach(), cur[n].detach()) for n in owned)
+        ckpt_ok = set(saved) == set(ref.state_dict()) and same
+        out.append((abs(got - want) < 1e-5, g_worst < 1e-3 and w_ok and set(grads) <= set(ref_grads) and ckpt_ok,
+                    n_blocks))
     return rank, out
 
 
-def test_build_training_pipeline_and_context_parallel():
+def test_build_training_pipeline_and_context_parallel(tmp_path):
+    os.environ["SV4_TEST_CKPT_DIR"] = str(tmp_path)  # inherited by the spawned ranks
     res = _run(_pp_cp_job, ws=4)
     for r in res:
         assert isinstance(r[1], list), r

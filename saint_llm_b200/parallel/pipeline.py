@@ -117,14 +117,9 @@ def cp_lm_share(group: dist.ProcessGroup | None) -> Callable[[nn.Module, Tensor,
     token); returns this shard's share of the global mean (the sum over the group is the loss)."""
 
     def loss(model: nn.Module, h: Tensor, ids: Tensor) -> Tensor:
-        r = dist.get_rank(group)
-        b, t = ids.shape
-        tl = h.shape[1]
-        tgt = ids[:, r * tl + 1:(r + 1) * tl + 1]
-        logits = model.logits(h[:, :tgt.shape[1]]).float()  # type: ignore[attr-defined]
-        ce = torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1),
-                                               reduction="sum")
-        return ce / (b * (t - 1))
+        from saint_llm_b200.parallel.cp import shard_loss
+
+        return shard_loss(model, h, ids, dist.get_rank(group) * h.shape[1])
 
     return loss
 

@@ -127,6 +127,25 @@ def sequence_balance_loss(affinity: Tensor, expert_idx: Tensor) -> Tensor:
     return (freq * affinity.mean(dim=1)).sum(-1).mean() * n
 
 
+def sharded_balance_loss(affinity: Tensor, expert_idx: Tensor, group: object) -> Tensor:
+    """``sequence_balance_loss`` of sequences whose tokens are split over ``group`` (context
+    parallelism): the per-sequence expert counts and affinity sums are summed over the group
+    (the affinity sum through a differentiable all-reduce), and this rank returns its 1/ws
+    share, so the shares add up to the loss of the whole sequences and so do the gradients."""
+    import torch.distributed as dist
+    from torch.distributed.nn.functional import all_reduce
+
+    n = affinity.shape[-1]
+    b, t, k = expert_idx.shape
+    ws = dist.get_world_size(group)
+    counts = torch.zeros(b, n, device=affinity.device, dtype=torch.float32)
+    counts.scatter_add_(1, expert_idx.reshape(b, t * k), torch.ones(b, t * k, device=affinity.device))
+    dist.all_reduce(counts, group=group)
+    total = t * ws
+    aff_sum = all_reduce(affinity.float().sum(dim=1), group=group)
+    return ((counts / (total * k)) * (aff_sum / total)).sum(-1).mean() * n / ws
+
+
 class DeepSeekMoE(nn.Module):
     def __init__(self, hidden_dim: int, cfg: MoEConfig, layer_idx: int,
                  enable_modality_router_bias: bool = True, *,
@@ -171,6 +190,9 @@ class DeepSeekMoE(nn.Module):
         self.tp_group = None
         self.tp_size = 1
         self.tp_rank = 0
+        # context parallelism (set for the duration of a CP forward by parallel.cp.balance_over):
+        # the sequences are sharded over this group, so the balance loss pools its statistics
+        self.balance_group = None
 
     def route(self, h: Tensor, token_ids: Tensor | None, is_visual: Tensor | None
               ) -> tuple[Tensor, Tensor, Tensor]:
@@ -182,6 +204,8 @@ class DeepSeekMoE(nn.Module):
             return idx, gate, h.new_zeros(())
         assert self.router is not None
         idx, gate, aff = self.router(h, is_visual=is_visual)
+        if self.balance_group is not None:
+            return idx, gate, sharded_balance_loss(aff, idx, self.balance_group)
         return idx, gate, sequence_balance_loss(aff, idx)
 
     def forward(self, x: Tensor, token_ids: Tensor | None = None,
@@ -244,4 +268,4 @@ class DeepSeekMoE(nn.Module):
         return sequence_balance_loss(affinity, expert_idx)
 
 
-__all__ = ["DeepSeekMoE", "HashRouter", "LearnedRouter", "SwiGLU", "sequence_balance_loss"]
+__all__ = ["DeepSeekMoE", "HashRouter", "LearnedRouter", "SwiGLU", "sequence_balance_loss", "sharded_balance_loss"]

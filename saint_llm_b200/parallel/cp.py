@@ -28,6 +28,9 @@ with zeros before the halo (outside every query's window, so never attended).
 
 from __future__ import annotations
 
+import contextlib
+from collections.abc import Iterator
+
 import torch
 import torch.distributed as dist
 from torch import Tensor, nn
@@ -150,6 +153,21 @@ class CPBundle:
         return self.views[i]
 
 
+@contextlib.contextmanager
+def balance_over(model: nn.Module, group: dist.ProcessGroup | None) -> Iterator[None]:
+    """While active, every MoE layer of ``model`` computes its balance loss over sequences
+    sharded across ``group`` (``models.moe.sharded_balance_loss``): the loss's per-sequence
+    statistics span every shard."""
+    layers = [m for m in model.modules() if hasattr(m, "balance_group")]
+    for m in layers:
+        m.balance_group = group if group is not None else dist.group.WORLD  # None would mean "off"
+    try:
+        yield
+    finally:
+        for m in layers:
+            m.balance_group = None
+
+
 def cp_shard(ids: Tensor, group: dist.ProcessGroup | None = None) -> Tensor:
     """This rank's contiguous slice of (B, T) token ids."""
     r, ws = dist.get_rank(group), dist.get_world_size(group)
@@ -172,7 +190,7 @@ def _ce_share(model: nn.Module, h: Tensor, ids: Tensor, start: int, shift: int) 
 
 
 def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = None, *,
-               mtp: bool = False) -> Tensor:
+               mtp: bool = False, balance: bool = False) -> Tensor:
     """Next-token cross-entropy of the full sequence ``ids`` (B, T) computed with its tokens
     sharded over ``group``; returns this rank's share of the global mean (the sum over
     ranks is the loss).
@@ -181,13 +199,21 @@ def cp_lm_loss(model: nn.Module, ids: Tensor, group: dist.ProcessGroup | None = 
     ``train.losses.cross_entropy_with_mtp`` without the balance term).  Head k combines the
     hidden state at position p with the embedding of token p + k + 1, which for a shard's
     last positions lies in the next shard: every rank holds all token ids, so it embeds the
-    few it needs itself and the heads need no communication."""
+    few it needs itself and the heads need no communication.
+
+    ``balance``: add ``sequence_balance_weight`` x the MoE balance loss, computed over the whole
+    sequences (``balance_over``): with ``mtp`` too, the sum over ranks is the training loss of
+    ``cross_entropy_with_mtp`` with its balance term."""
     r, ws = dist.get_rank(group), dist.get_world_size(group)
     tl = ids.shape[1] // ws
     start = r * tl
     local = ids[:, start:start + tl]
-    h, _ = model.backbone(local, kv_cache_bundle=CPBundle(model, group, tl))  # type: ignore[attr-defined]
-    return shard_loss(model, h, ids, start, mtp=mtp)
+    with balance_over(model, group):
+        h, _ = model.backbone(local, kv_cache_bundle=CPBundle(model, group, tl))  # type: ignore[attr-defined]
+    loss = shard_loss(model, h, ids, start, mtp=mtp)
+    w = model.cfg.moe.sequence_balance_weight if balance else 0.0  # type: ignore[attr-defined]
+    aux = model.aux_loss() if w else None  # type: ignore[attr-defined]
+    return loss + w * aux if aux is not None else loss
 
 
 def shard_loss(model: nn.Module, h: Tensor, ids: Tensor, start: int, *, mtp: bool = False) -> Tensor:
@@ -211,4 +237,4 @@ def shard_loss(model: nn.Module, h: Tensor, ids: Tensor, start: int, *, mtp: boo
     return loss
 
 
-__all__ = ["CPBundle", "CPLayerView", "cp_lm_loss", "cp_shard", "gather_stack", "shard_loss"]
+__all__ = ["CPBundle", "CPLayerView", "balance_over", "cp_lm_loss", "cp_shard", "gather_stack", "shard_loss"]

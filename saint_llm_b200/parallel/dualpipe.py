@@ -40,6 +40,7 @@ collectives pair up.
 
 from __future__ import annotations
 
+import contextlib
 from collections.abc import Callable
 from dataclasses import dataclass
 
@@ -163,9 +164,12 @@ class DualPipeV:
 
             bundle = CPBundle(m, self.cp_group, local.shape[1])
         lo, hi = self.bounds[v]
-        for j in range(lo, hi):
-            view = bundle.for_layer(j) if bundle is not None else None
-            x = m.blocks[j](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
+        from saint_llm_b200.parallel.cp import balance_over
+
+        with balance_over(m, self.cp_group) if self.cp_group is not None else contextlib.nullcontext():
+            for j in range(lo, hi):
+                view = bundle.for_layer(j) if bundle is not None else None
+                x = m.blocks[j](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
         assert x is not None
         return x
 

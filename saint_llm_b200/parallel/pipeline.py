@@ -30,6 +30,7 @@ their attention collectives pair up in order.
 
 from __future__ import annotations
 
+import contextlib
 from collections.abc import Callable
 
 import torch
@@ -85,9 +86,12 @@ class PipelineStage:
             from saint_llm_b200.parallel.cp import CPBundle
 
             bundle = CPBundle(m, self.cp_group, local.shape[1])
-        for i in range(self.lo, self.hi):
-            view = bundle.for_layer(i) if bundle is not None else None
-            x = m.blocks[i](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
+        from saint_llm_b200.parallel.cp import balance_over
+
+        with balance_over(m, self.cp_group) if self.cp_group is not None else contextlib.nullcontext():
+            for i in range(self.lo, self.hi):
+                view = bundle.for_layer(i) if bundle is not None else None
+                x = m.blocks[i](x, token_ids=local, is_visual=vis, kv_cache_layer=view)  # type: ignore[index]
         return x
 
     def loss(self, ids: Tensor, x: Tensor, loss_fn: Callable[[nn.Module, Tensor, Tensor], Tensor]) -> Tensor:

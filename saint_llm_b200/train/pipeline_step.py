@@ -8,8 +8,9 @@ shards.  Each pipeline rank keeps only its own blocks (the others are dropped at
 
 A step: the micro-batches run through the 1F1B schedule (``parallel.pipeline``) or DualPipe-V
 (``parallel.dualpipe``), every CP rank computing its shard of each sequence; the loss is the
-main next-token CE plus the MTP heads (``parallel.cp.shard_loss``; the MoE balance term is
-left out: its per-sequence statistics would need an exchange of their own); gradients are
+main next-token CE plus the MTP heads (``parallel.cp.shard_loss``) plus the MoE balance term,
+whose per-sequence statistics are pooled over the CP group (``parallel.cp.balance_over``),
+so the objective is the single-process training loss; gradients are
 summed over the CP group and the tied embedding's over its two pipeline ends; the
 attention-logit telemetry is max-reduced over the CP group (MuonClip acts on the same
 value on every shard); then the optimizer updates the parameters this rank holds.
@@ -68,16 +69,18 @@ class PipelineTrainStep:
 
     def run_device(self, tokens: Tensor) -> Tensor:
         """tokens: (micro_batches, mb, T) on the device, the same on every rank.  Returns the
-        step's mean loss (device scalar, the same on every rank)."""
+        step's mean main + MTP loss (device scalar, the same on every rank); the balance term
+        is in the gradients but not in the reported value."""
         from saint_llm_b200.parallel.dualpipe import run_dualpipe
         from saint_llm_b200.parallel.pipeline import run_1f1b, sync_cp_grads, sync_tied_embedding
 
         self.model.train()
         micro = [tokens[i] for i in range(tokens.shape[0])]
+        aux_w = float(self.model.cfg.moe.sequence_balance_weight)  # type: ignore[attr-defined]
         if self.schedule == "dualpipe":
-            out = run_dualpipe(self.stage, micro, loss_fn=self._loss)  # type: ignore[arg-type]
+            out = run_dualpipe(self.stage, micro, loss_fn=self._loss, aux_weight=aux_w)  # type: ignore[arg-type]
         else:
-            out = run_1f1b(self.stage, micro, loss_fn=self._loss)  # type: ignore[arg-type]
+            out = run_1f1b(self.stage, micro, loss_fn=self._loss, aux_weight=aux_w)  # type: ignore[arg-type]
             sync_tied_embedding(self.stage)  # type: ignore[arg-type]
         sync_cp_grads(self.stage)  # type: ignore[arg-type]
         self._sync_logits()

@@ -159,13 +159,16 @@ def _cp_mtp(rank, ws):
     from saint_llm_b200.parallel.cp import cp_lm_loss
     from saint_llm_b200.train.losses import cross_entropy_with_mtp
 
-    full = _model()
+    from saint_llm_b200.config import ModelConfig
+
+    # a large balance weight, so a balance term computed per shard would show in the gradients
+    full = _model(moe=ModelConfig.tiny().moe.model_copy(update={"sequence_balance_weight": 0.5}))
     cp = copy.deepcopy(full)
     torch.manual_seed(8)
     ids = _ids(2, 64, vocab=full.cfg.vocab_size)
-    ref = cross_entropy_with_mtp(full(ids), ids, cfg=full.cfg.mtp)
+    ref = cross_entropy_with_mtp(full(ids), ids, cfg=full.cfg.mtp, moe_cfg=full.cfg.moe)
     ref.backward()
-    loss = cp_lm_loss(cp, ids, mtp=True)
+    loss = cp_lm_loss(cp, ids, mtp=True, balance=True)
     loss.backward()
     tot = loss.detach().clone()
     dist.all_reduce(tot)
@@ -483,17 +486,18 @@ def _pp_cp_job(rank, ws):
     from saint_llm_b200.train.losses import make_loss_fn
 
     cfg = ModelConfig.tiny()
+    cfg = cfg.model_copy(update={"moe": cfg.moe.model_copy(update={"sequence_balance_weight": 0.5})})
     torch.manual_seed(4)
     batch = torch.randint(0, cfg.vocab_size, (2, 1, 32))
     torch.manual_seed(0)
     ref = SaintLLM(cfg)
     opt = MuonAdamW(*split_for_muon_adamw(ref), lr=0.02, adamw_lr=3e-3, qk_clip_enabled=False)
-    loss_fn = make_loss_fn(cfg.mtp, fused=False)
-    want = 0.0
+    loss_fn = make_loss_fn(cfg.mtp, moe_cfg=cfg.moe, fused=False)
+    want = 0.0  # the reported value: main + MTP (the balance term only enters the gradients)
     for i in range(2):
         loss = loss_fn(ref, batch[i]) / 2
         loss.backward()
-        want += float(loss.detach())
+        want += float(loss.detach()) - cfg.moe.sequence_balance_weight * float(ref.aux_loss().detach()) / 2
     ref_grads = {n: p.grad.clone() for n, p in ref.named_parameters() if p.grad is not None}
     init = {n: p.detach().clone() for n, p in ref.named_parameters()}
     opt.step()

@@ -557,3 +557,25 @@ def test_build_training_pipeline_and_context_parallel(tmp_path):
         assert isinstance(r[1], list), r
         for ok_loss, ok_weights, n_blocks in r[1]:
             assert ok_loss and ok_weights and n_blocks == 2, r
+
+
+def _cp_job(rank, ws):
+    from saint_llm_b200.config import ModelConfig, RunConfig
+    from saint_llm_b200.train.launch import build_training
+
+    cfg = ModelConfig.tiny()
+    run = RunConfig(cp=ws, grad_accum=2, micro_batch=1, seq_len=32, lr=0.02, adamw_lr=3e-3,
+                    param_dtype="float32", compute_dtype="float32")
+    job = build_training(cfg, run, DEV)
+    torch.manual_seed(4)
+    batch = torch.randint(0, cfg.vocab_size, (2, 1, 32))
+    return rank, [job.step(batch) for _ in range(3)]
+
+
+def test_build_training_context_parallel_only():
+    """RunConfig(cp=2) alone (one pipeline stage, MuonClip on): both ranks report the same
+    decreasing losses."""
+    res = _run(_cp_job, ws=2)
+    assert all(isinstance(r[1], list) for r in res), res
+    a, b = res[0][1], res[1][1]
+    assert all(abs(x - y) < 1e-6 for x, y in zip(a, b, strict=True)) and a[-1] < a[0], res

@@ -506,12 +506,12 @@ def _pp_cp_job(rank, ws):
     for schedule in ("1f1b", "dualpipe"):
         run = RunConfig(pp=2, cp=2, pp_schedule=schedule, grad_accum=2, micro_batch=1, seq_len=32, lr=0.02,
                         adamw_lr=3e-3, seed=0, param_dtype="float32", compute_dtype="float32")
-        job = build_training(cfg, run, torch.device("cpu"), qk_clip=False)
+        job = build_training(cfg, run, DEV, qk_clip=False)
         grads: dict = {}
         real_step = job.optimizer.step
 
         def step_and_record(*a, _g=grads, _m=job.model, _s=real_step, **k):  # the synchronised gradients
-            _g.update({n: p.grad.clone() for n, p in _m.named_parameters() if p.grad is not None})
+            _g.update({n: p.grad.detach().cpu() for n, p in _m.named_parameters() if p.grad is not None})
             return _s(*a, **k)
 
         job.optimizer.step = step_and_record
@@ -524,7 +524,7 @@ def _pp_cp_job(rank, ws):
         owned = [n for n, _ in job.model.named_parameters()
                  if any(n.startswith(o) for o in mine) or (n.startswith("embed.") and (first or last))
                  or (n.startswith(("final_norm.", "mtp.")) and last)]
-        cur = dict(job.model.named_parameters())
+        cur = {n: p.detach().cpu() for n, p in job.model.named_parameters()}
         # gradients: exact up to summation order (floor: cancelling sums such as the mHC biases')
         g_worst = max(float((grads[n] - ref_grads[n]).abs().max() / ref_grads[n].abs().max().clamp(min=1e-5))
                       for n in owned if n in ref_grads)
@@ -540,9 +540,9 @@ def _pp_cp_job(rank, ws):
         from saint_llm_b200.train.checkpoint import load_sharded
 
         saved = load_sharded(path, rank=rank)["model"]
-        other = build_training(cfg, run.model_copy(update={"seed": 7}), torch.device("cpu"), qk_clip=False)
+        other = build_training(cfg, run.model_copy(update={"seed": 7}), DEV, qk_clip=False)
         other.load(path)
-        theirs = dict(other.model.named_parameters())
+        theirs = {n: p.detach().cpu() for n, p in other.model.named_parameters()}
         same = all(torch.equal(theirs[n].detach(), cur[n].detach()) for n in owned)
         ckpt_ok = set(saved) == set(ref.state_dict()) and same
         out.append((abs(got - want) < 1e-5, g_worst < 1e-3 and w_ok and set(grads) <= set(ref_grads) and ckpt_ok,
@@ -579,3 +579,17 @@ def test_build_training_context_parallel_only():
     assert all(isinstance(r[1], list) for r in res), res
     a, b = res[0][1], res[1][1]
     assert all(abs(x - y) < 1e-6 for x, y in zip(a, b, strict=True)) and a[-1] < a[0], res
+
+
+@pytest.mark.gpu
+@_four_gpus
+def test_build_training_pipeline_and_context_parallel_on_four_gpus(tmp_path):
+    """The builder-level PP=2 x CP=2 check with NCCL on four GPUs (the model math on the eager
+    fp32 path, compared with one CPU process; NVLS off)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["SV4_TEST_CKPT_DIR"] = str(tmp_path)
+    res = _run(_pp_cp_job, 4, nccl=True)
+    for r in res:
+        assert isinstance(r[1], list), r
+        for ok_loss, ok_weights, n_blocks in r[1]:
+            assert ok_loss and ok_weights and n_blocks == 2, r
